@@ -1,0 +1,209 @@
+/*
+ * pairformer_b200.h -- C ABI of the B200-native (sm_100a) Pairformer pair stack.
+ *
+ * Plain C: device pointers, sizes, element strides, dtype enums and a cudaStream_t passed
+ * as void*. Every entry point returns a pf_status code; a human-readable message for the
+ * last failure on the calling thread is available from pf_last_error_string(). No entry
+ * point allocates or frees device memory: the caller owns inputs, outputs and workspace
+ * (size it with the matching *_workspace_size call). All work is enqueued on the stream
+ * passed in; no entry point synchronises the host.
+ *
+ * Each entry point replaces one reference interface (OpenDDE 1.0.2, package `opendde`);
+ * the replaced function is cited beside it. Pair tensors are addressed through
+ * pf_pair_view so that the ending-node / incoming variants and the Fold-CP slabs are the
+ * same kernels on transposed or offset views (no physical transposes).
+ */
+#ifndef PAIRFORMER_B200_H
+#define PAIRFORMER_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PF_API __attribute__((visibility("default")))
+#else
+#define PF_API
+#endif
+
+typedef enum {
+  PF_OK = 0,
+  PF_EINVAL_SHAPE = 1,   /* sizes / strides / alignment rejected by host-side validation */
+  PF_EINVAL_DTYPE = 2,   /* unknown dtype enum */
+  PF_EUNSUPPORTED = 3,   /* valid request that this build does not implement */
+  PF_ECUDA = 4,          /* a CUDA runtime/driver call failed (message has the CUDA error) */
+  PF_ENCCL = 5,          /* reserved for collective entry points */
+  PF_ETIMEOUT = 6,       /* a bounded device-side wait gave up (status word set by a kernel) */
+  PF_EINVAL_ARG = 7,     /* null pointer or out-of-range scalar argument */
+  PF_EWORKSPACE = 8      /* workspace pointer null or smaller than *_workspace_size */
+} pf_status;
+
+typedef enum {
+  PF_F32 = 0,   /* fp32 storage, fp32 arithmetic (SIMT FFMA; the tolerance-1e-4 mode)        */
+  PF_BF16 = 1   /* bf16 storage, fp32 accumulation on tcgen05 tensor cores where shapes allow */
+} pf_dtype;
+
+/* A view of a pair tensor: element (r, s, ch) lives at ptr + r*row_stride + s*col_stride + ch
+ * (strides in elements; the channel dim is contiguous). A transposed view swaps the strides. */
+typedef struct {
+  void* ptr;
+  int64_t row_stride;
+  int64_t col_stride;
+} pf_pair_view;
+
+/* A view of an fp32 pair mask: mask(r, s) = ptr[r*row_stride + s*col_stride]. */
+typedef struct {
+  const float* ptr;
+  int64_t row_stride;
+  int64_t col_stride;
+} pf_mask_view;
+
+/* ---- library ------------------------------------------------------------------------ */
+
+PF_API int pf_abi_version(void);
+PF_API const char* pf_last_error_string(void);
+/* Options: PF_OPT_FORCE_SIMT=1 routes bf16 requests to the generic SIMT kernels (testing). */
+#define PF_OPT_FORCE_SIMT 1
+PF_API int pf_set_option(int option, int64_t value);
+/* Name of the kernel family the last call on this thread dispatched to ("tc" or "simt"). */
+PF_API const char* pf_last_path(void);
+
+/* ---- LayerNorm ------------------------------------------------------------------------
+ * y[r, :] = (x[r, :] - mean) / sqrt(var + eps) * gamma + beta over the last dim c.
+ * Replaces OpenFoldLayerNorm.forward (opendde/model/triangular/layers.py:255-269) and the
+ * fused extension FusedLayerNorm (opendde/model/layer_norm/layer_norm.py:233-288), launched
+ * on the caller's stream (the reference launches on the legacy default stream,
+ * layer_norm_cuda_kernel.cu:271). gamma/beta may be NULL (no scale / no offset). */
+PF_API int pf_layernorm_fwd(const void* x, void* y, const float* gamma, const float* beta,
+                     int64_t rows, int32_t c, float eps, int32_t dtype, void* stream);
+
+/* ---- Triangle multiplicative update -----------------------------------------------------
+ * Replaces TriangleMultiplicativeUpdate.forward (opendde/model/triangular/triangular.py:458-567,
+ * _combine_projections :112-139) and its Fold-CP adapter
+ * distributed_triangle_multiplication_update (opendde/distributed/foldcp/real_pairformer.py:1226).
+ *
+ *   a(i,k) = ma(i,k) * sigmoid(W_ag LN_in(za(i,k))) * (W_ap LN_in(za(i,k)))      i<n_i, k<n_k
+ *   b(j,k) = mb(j,k) * sigmoid(W_bg LN_in(zb(j,k))) * (W_bp LN_in(zb(j,k)))      j<n_j
+ *   x(i,j) = LN_out( sum_k a(i,k) * b(j,k) )
+ *   u(i,j) = (W_z x(i,j)) * sigmoid(W_g LN_in(zg(i,j)))
+ *   zo(i,j) = (accumulate ? zo(i,j) : 0) + u(i,j)
+ * Outgoing: za = zb = zg = z, ma = mb = mask. Incoming: za, zb, ma, mb are the transposed
+ * views of z and the mask, zg = z. All weights are [out, in] row-major in `dtype`; LayerNorm
+ * parameters are fp32. zo may alias za, zb and zg (each position of zg is read before the
+ * same position of zo is written, and the projections finish before zo is touched). */
+typedef struct {
+  const float* ln_in_w;  const float* ln_in_b;    /* [c_z] */
+  const void* w_ap; const void* w_ag;             /* [c_h, c_z] */
+  const void* w_bp; const void* w_bg;             /* [c_h, c_z] */
+  const float* ln_out_w; const float* ln_out_b;   /* [c_h] */
+  const void* w_z;                                /* [c_z, c_h] */
+  const void* w_g;                                /* [c_z, c_z] */
+} pf_trimul_params;
+
+PF_API int pf_trimul_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
+                             int32_t dtype, size_t* bytes);
+PF_API int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_view zb,
+                  pf_mask_view ma, pf_mask_view mb, pf_pair_view zg, pf_pair_view zo,
+                  int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
+                  int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* ---- Triangle attention (starting node; ending node = transposed views) ------------------
+ * Replaces TriangleAttention.forward (opendde/model/triangular/triangular.py:648-706) with
+ * Attention._prep_qkv/_attention/_wrap_up (opendde/model/triangular/layers.py:302-424), and
+ * the Fold-CP adapter distributed_triangle_attention_update (real_pairformer.py:2633).
+ *
+ * Rows i < n_rows of the slab zs attend over keys k < n_keys of the same row:
+ *   x = LN(zs(i,k));  q,k,v,g from x;  bias(h,j,k) = W_b LN(z(j,k))
+ *   logits(h,i,j,k) = q(i,j).k(i,k)/sqrt(d) + inf*(m(i,k)-1) + bias(h,j,k)
+ *   o(i,j) = W_o[ sigmoid(W_g x(i,j)) * softmax_k(logits) v(i,k) ]
+ * Queries are the slab columns j = q_col0 .. q_col0+n_q-1; the output goes to zo(i, j-q_col0).
+ * Keys with index >= n_valid_keys do not exist (Fold-CP padding); n_valid_keys <= n_keys.
+ * bias: NULL => computed from zs itself (requires q_col0==0 and n_q==n_keys==n_rows, the
+ * single-device case); otherwise a buffer written by pf_triatt_bias for the query rows,
+ * addressed bias + h*bias_head_stride + j*bias_row_stride + k.
+ * ending node: pass transposed views of z and the mask. */
+typedef struct {
+  const float* ln_w; const float* ln_b;   /* [c]          layer_norm           */
+  const void* w_bias;                     /* [H, c]       linear (triangle bias) */
+  const void* w_q; const void* w_k; const void* w_v;  /* [H*d, c]  mha.linear_{q,k,v} */
+  const void* w_g;                        /* [H*d, c]     mha.linear_g          */
+  const void* w_o;                        /* [c, H*d]     mha.linear_o          */
+} pf_triatt_params;
+
+/* bias(h, r, s) for positions r < n_rows, s < n_cols of z, written to
+ * bias + h*bias_head_stride + r*bias_row_stride + s. Format: fp32 natural units for PF_F32;
+ * bf16 scaled by log2(e) for PF_BF16 (the tensor-core attention works in base 2). */
+PF_API int pf_triatt_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c, int32_t heads,
+                                  int32_t dtype, size_t* bytes);
+PF_API int pf_triatt_bias(const pf_triatt_params* w, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                   void* bias, int64_t bias_head_stride, int64_t bias_row_stride,
+                   int32_t c, int32_t heads, int32_t dtype, void* workspace,
+                   size_t workspace_bytes, void* stream);
+PF_API int pf_triatt_workspace_size(int64_t n_rows, int64_t n_keys, int64_t n_q, int32_t c,
+                             int32_t heads, int32_t head_dim, int32_t dtype, size_t* bytes);
+PF_API int pf_triatt_fwd(const pf_triatt_params* w, pf_pair_view zs, pf_mask_view m,
+                  const void* bias, int64_t bias_head_stride, int64_t bias_row_stride,
+                  pf_pair_view zo, int64_t n_rows, int64_t n_keys, int64_t n_valid_keys,
+                  int64_t q_col0, int64_t n_q, int32_t c, int32_t heads, int32_t head_dim,
+                  float inf, int32_t accumulate, int32_t dtype,
+                  void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Transition (LN -> SiLU(W_a y) * (W_b y) -> W_out) ------------------------------------
+ * Replaces Transition.forward (opendde/model/modules/primitives.py:182-217) and the Fold-CP
+ * distributed_pair_transition_update (real_pairformer.py:1405, local in inference).
+ * x and out are [rows, c] with row strides x_stride/out_stride (elements); out may alias x.
+ * out = (accumulate ? out : 0) + Transition(x). */
+typedef struct {
+  const float* ln_w; const float* ln_b;   /* [c]        layernorm1        */
+  const void* w_a; const void* w_b;       /* [n*c, c]   linear_no_bias_a/b */
+  const void* w_o;                        /* [c, n*c]   linear_no_bias     */
+} pf_transition_params;
+
+PF_API int pf_transition_workspace_size(int64_t rows, int32_t c, int32_t n_mult, int32_t dtype,
+                                 size_t* bytes);
+PF_API int pf_transition_fwd(const pf_transition_params* w, const void* x, int64_t x_stride,
+                      void* out, int64_t out_stride, int64_t rows, int32_t c, int32_t n_mult,
+                      int32_t accumulate, int32_t dtype, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* ---- AttentionPairBias, single representation (has_s = False) -----------------------------
+ * Replaces AttentionPairBias.forward with standard_multihead_attention
+ * (opendde/model/modules/transformer.py:550-671) and Attention (primitives.py:645-857),
+ * and the Fold-CP distributed_attention_pair_bias_update (real_pairformer.py:1714).
+ * pf_apb_pair_bias: bias(h, r, s) = W_z LN_z(z(r, s)) for r < n_rows, s < n_cols, written
+ * to bias + h*head_stride + r*row_stride + s (fp32).
+ * pf_apb_fwd: s_out = (accumulate ? s_out : 0) + APB(s_in, bias) with the full [H, n, n]
+ * bias (bias == NULL => computed from z, which must then be given). */
+typedef struct {
+  const float* ln_a_w; const float* ln_a_b;   /* [c_s]   layernorm_a            */
+  const void* w_q; const float* b_q;          /* [c_s, c_s], [c_s] attention.linear_q */
+  const void* w_k; const void* w_v;           /* [c_s, c_s]                    */
+  const void* w_g; const void* w_o;           /* [c_s, c_s]                    */
+  const float* ln_z_w; const float* ln_z_b;   /* [c_z]   layernorm_z (b may be NULL) */
+  const void* w_z;                            /* [H, c_z] linear_nobias_z     */
+} pf_apb_params;
+
+PF_API int pf_apb_pair_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t heads,
+                                    int32_t dtype, size_t* bytes);
+PF_API int pf_apb_pair_bias(const pf_apb_params* w, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                     float* bias, int64_t head_stride, int64_t row_stride,
+                     int32_t c_z, int32_t heads, int32_t dtype, void* workspace,
+                     size_t workspace_bytes, void* stream);
+PF_API int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, int32_t dtype,
+                          size_t* bytes);
+PF_API int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_pair_view z,
+               const float* bias, int64_t n, int32_t c_s, int32_t c_z, int32_t heads,
+               int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PAIRFORMER_B200_H */

@@ -1,0 +1,147 @@
+"""ctypes binding of ``libpairformer_b200.so`` (the C ABI in ``include/pairformer_b200.h``).
+
+This is the only module that touches the shared library. Every call returns a status
+code; :func:`check` turns non-zero codes into Python exceptions carrying the library's
+thread-local message. The library never allocates device memory: callers pass
+workspaces (allocated here from torch's caching allocator).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpairformer_b200.so")
+
+PF_OK = 0
+PF_EINVAL_SHAPE = 1
+PF_EINVAL_DTYPE = 2
+PF_EUNSUPPORTED = 3
+PF_ECUDA = 4
+PF_ENCCL = 5
+PF_ETIMEOUT = 6
+PF_EINVAL_ARG = 7
+PF_EWORKSPACE = 8
+PF_F32 = 0
+PF_BF16 = 1
+PF_OPT_FORCE_SIMT = 1
+
+_STATUS_NAMES = {
+    PF_EINVAL_SHAPE: "PF_EINVAL_SHAPE", PF_EINVAL_DTYPE: "PF_EINVAL_DTYPE",
+    PF_EUNSUPPORTED: "PF_EUNSUPPORTED", PF_ECUDA: "PF_ECUDA", PF_ENCCL: "PF_ENCCL",
+    PF_ETIMEOUT: "PF_ETIMEOUT", PF_EINVAL_ARG: "PF_EINVAL_ARG", PF_EWORKSPACE: "PF_EWORKSPACE",
+}
+
+# Every symbol the header declares (checked by tests/test_abi_symbols.py).
+EXPORTED = (
+    "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path",
+    "pf_layernorm_fwd",
+    "pf_trimul_workspace_size", "pf_trimul_fwd",
+    "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
+    "pf_transition_workspace_size", "pf_transition_fwd",
+    "pf_apb_pair_bias_workspace_size", "pf_apb_pair_bias", "pf_apb_workspace_size", "pf_apb_fwd",
+)
+
+
+class PFError(RuntimeError):
+    """A non-zero pf_status from the library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"{_STATUS_NAMES.get(status, status)}: {message}")
+        self.status = status
+
+
+class PairView(Structure):
+    _fields_ = [("ptr", c_void_p), ("row_stride", c_int64), ("col_stride", c_int64)]
+
+
+class MaskView(Structure):
+    _fields_ = [("ptr", c_void_p), ("row_stride", c_int64), ("col_stride", c_int64)]
+
+
+class TrimulParams(Structure):
+    _fields_ = [(n, c_void_p) for n in (
+        "ln_in_w", "ln_in_b", "w_ap", "w_ag", "w_bp", "w_bg", "ln_out_w", "ln_out_b", "w_z", "w_g")]
+
+
+class TriattParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w_bias", "w_q", "w_k", "w_v", "w_g", "w_o")]
+
+
+class TransitionParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w_a", "w_b", "w_o")]
+
+
+class ApbParams(Structure):
+    _fields_ = [(n, c_void_p) for n in (
+        "ln_a_w", "ln_a_b", "w_q", "b_q", "w_k", "w_v", "w_g", "w_o", "ln_z_w", "ln_z_b", "w_z")]
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load the library once and declare the argument types of every entry point."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(
+            f"{path} is missing: build it with `make -C opendde_b200/csrc` "
+            "(or __graft_entry__.build()); there is no fallback implementation")
+    lib = ctypes.CDLL(path)
+    sz = POINTER(c_size_t)
+    sig = {
+        "pf_abi_version": ([], c_int),
+        "pf_last_error_string": ([], c_char_p),
+        "pf_last_path": ([], c_char_p),
+        "pf_set_option": ([c_int, c_int64], c_int),
+        "pf_layernorm_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p], c_int),
+        "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
+                           c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_triatt_bias_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_triatt_bias": ([POINTER(TriattParams), PairView, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                            c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_triatt_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_triatt_fwd": ([POINTER(TriattParams), PairView, MaskView, c_void_p, c_int64, c_int64, PairView,
+                           c_int64, c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_float,
+                           c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_transition_workspace_size": ([c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_transition_fwd": ([POINTER(TransitionParams), c_void_p, c_int64, c_void_p, c_int64, c_int64, c_int32,
+                               c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_apb_pair_bias_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_apb_pair_bias": ([POINTER(ApbParams), PairView, c_int64, c_int64, c_void_p, c_int64, c_int64,
+                              c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_apb_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_apb_fwd": ([POINTER(ApbParams), c_void_p, c_void_p, PairView, c_void_p, c_int64, c_int32, c_int32,
+                        c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+    }
+    for name, (args, res) in sig.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    _lib = lib
+    return lib
+
+
+def check(status: int) -> None:
+    if status != PF_OK:
+        msg = load().pf_last_error_string().decode(errors="replace")
+        raise PFError(status, msg)
+
+
+def last_path() -> str:
+    return load().pf_last_path().decode()
+
+
+def set_force_simt(flag: bool) -> None:
+    check(load().pf_set_option(PF_OPT_FORCE_SIMT, 1 if flag else 0))
+
+
+def workspace_bytes(fn_name: str, *args) -> int:
+    out = c_size_t(0)
+    check(getattr(load(), fn_name)(*args, ctypes.byref(out)))
+    return int(out.value)

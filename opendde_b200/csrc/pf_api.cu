@@ -1,0 +1,300 @@
+// pf_api.cu -- the extern "C" entry points declared in include/pairformer_b200.h.
+//
+// Host-side validation (shapes, dtypes, pointers, workspace size) happens here, before any
+// launch; failures return a status code and leave a message in a thread-local buffer.
+// Dispatch: bf16 requests with the tuned channel counts go to the tcgen05 kernels
+// (pf_tc_*.cu); fp32 requests and every other shape go to the SIMT kernels (pf_simt.cu).
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+
+#include "pf_common.cuh"
+#include "pf_simt.h"
+#include "pf_tc.h"
+
+namespace pf {
+
+static thread_local char g_err[1024] = "";
+static thread_local const char* g_path = "none";
+static int g_force_simt = 0;
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+}
+
+int fail(int status, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return status;
+}
+
+void set_path(const char* p) { g_path = p; }
+bool force_simt() { return g_force_simt != 0; }
+
+static int check_dtype(int dtype) {
+  if (dtype != PF_F32 && dtype != PF_BF16) return fail(PF_EINVAL_DTYPE, "unknown dtype %d", dtype);
+  return PF_OK;
+}
+
+static int check_ws(void* ws, size_t have, size_t need, const char* what) {
+  if (need == 0) return PF_OK;
+  if (ws == nullptr) return fail(PF_EWORKSPACE, "%s: workspace is NULL (need %zu bytes)", what, need);
+  if (have < need)
+    return fail(PF_EWORKSPACE, "%s: workspace too small (%zu < %zu bytes)", what, have, need);
+  if (((uintptr_t)ws) % 256 != 0) return fail(PF_EWORKSPACE, "%s: workspace not 256-byte aligned", what);
+  return PF_OK;
+}
+
+static bool view_ok(const pf_pair_view& v) { return v.ptr != nullptr && v.row_stride >= 0 && v.col_stride >= 0; }
+
+}  // namespace pf
+
+using namespace pf;
+
+extern "C" {
+
+int pf_abi_version(void) { return PF_ABI_VERSION; }
+const char* pf_last_error_string(void) { return g_err; }
+const char* pf_last_path(void) { return g_path; }
+
+int pf_set_option(int option, int64_t value) {
+  if (option == PF_OPT_FORCE_SIMT) {
+    g_force_simt = value ? 1 : 0;
+    return PF_OK;
+  }
+  return fail(PF_EINVAL_ARG, "unknown option %d", option);
+}
+
+// ------------------------------------------------------------------ LayerNorm
+int pf_layernorm_fwd(const void* x, void* y, const float* gamma, const float* beta, int64_t rows,
+                     int32_t c, float eps, int32_t dtype, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!x || !y) return fail(PF_EINVAL_ARG, "layernorm: null input/output");
+  if (rows < 0 || c <= 0 || c > 1024) return fail(PF_EINVAL_SHAPE, "layernorm: rows=%lld c=%d", (long long)rows, c);
+  if (rows == 0) return PF_OK;
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == PF_BF16 && !force_simt() && tc::layernorm_supported(c, x, y)) {
+    set_path("tc");
+    return tc::layernorm_bf16(x, y, gamma, beta, rows, c, eps, st);
+  }
+  set_path("simt");
+  return simt::layernorm(x, y, gamma, beta, rows, c, eps, dtype, st);
+}
+
+// ------------------------------------------------------------------ triangle multiplication
+static bool trimul_tc(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::trimul_supported(n_i, n_j, n_k, c_z, c_h);
+}
+
+int pf_trimul_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
+                             int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0)
+    return fail(PF_EINVAL_SHAPE, "trimul: bad sizes");
+  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h)
+                                                      : simt::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h);
+  return PF_OK;
+}
+
+int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+                  pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+                  int32_t c_z, int32_t c_h, int32_t accumulate, int32_t dtype, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_ap || !w->w_ag || !w->w_bp || !w->w_bg || !w->w_z || !w->w_g)
+    return fail(PF_EINVAL_ARG, "trimul: null weight pointer");
+  if (!view_ok(za) || !view_ok(zb) || !view_ok(zg) || !view_ok(zo))
+    return fail(PF_EINVAL_ARG, "trimul: bad pair view");
+  if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0 || c_z > 1024 || c_h > 1024)
+    return fail(PF_EINVAL_SHAPE, "trimul: bad sizes n_i=%lld n_j=%lld n_k=%lld c_z=%d c_h=%d",
+                (long long)n_i, (long long)n_j, (long long)n_k, c_z, c_h);
+  if (n_i == 0 || n_j == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_trimul_workspace_size(n_i, n_j, n_k, c_z, c_h, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "trimul"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype)) {
+    set_path("tc");
+    return tc::trimul(w, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, accumulate, workspace,
+                      workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::trimul(w, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, accumulate, dtype, workspace,
+                      workspace_bytes, st);
+}
+
+// ------------------------------------------------------------------ triangle attention
+static bool triatt_tc(int c, int H, int d, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::triatt_supported(c, H, d);
+}
+
+int pf_triatt_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c, int32_t heads,
+                                  int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  *bytes = (dtype == PF_BF16 && !force_simt() && tc::triatt_bias_supported(c, heads))
+               ? 0
+               : simt::triatt_bias_ws_bytes(n_rows, n_cols, c, heads);
+  return PF_OK;
+}
+
+int pf_triatt_bias(const pf_triatt_params* w, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                   void* bias, int64_t hs, int64_t rs, int32_t c, int32_t heads, int32_t dtype,
+                   void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_bias || !bias || !view_ok(z)) return fail(PF_EINVAL_ARG, "triatt_bias: null pointer");
+  if (n_rows < 0 || n_cols < 0 || c <= 0 || c > 1024 || heads <= 0)
+    return fail(PF_EINVAL_SHAPE, "triatt_bias: bad sizes");
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_triatt_bias_workspace_size(n_rows, n_cols, c, heads, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "triatt_bias"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == PF_BF16 && !force_simt() && tc::triatt_bias_supported(c, heads)) {
+    set_path("tc");
+    return tc::triatt_bias(w, z, n_rows, n_cols, bias, hs, rs, c, heads, st);
+  }
+  set_path("simt");
+  return simt::triatt_bias(w, z, n_rows, n_cols, bias, hs, rs, c, heads, dtype, workspace,
+                           workspace_bytes, st);
+}
+
+int pf_triatt_workspace_size(int64_t n_rows, int64_t n_keys, int64_t n_q, int32_t c, int32_t heads,
+                             int32_t head_dim, int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  *bytes = triatt_tc(c, heads, head_dim, dtype)
+               ? tc::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim)
+               : simt::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim);
+  return PF_OK;
+}
+
+int pf_triatt_fwd(const pf_triatt_params* w, pf_pair_view zs, pf_mask_view m, const void* bias,
+                  int64_t b_hs, int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys,
+                  int64_t n_valid_keys, int64_t q_col0, int64_t n_q, int32_t c, int32_t heads,
+                  int32_t head_dim, float inf, int32_t accumulate, int32_t dtype, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_q || !w->w_k || !w->w_v || !w->w_g || !w->w_o || !w->w_bias)
+    return fail(PF_EINVAL_ARG, "triatt: null weight pointer");
+  if (!view_ok(zs) || !view_ok(zo)) return fail(PF_EINVAL_ARG, "triatt: bad pair view");
+  if (n_rows < 0 || n_keys < 0 || n_q < 0 || c <= 0 || c > 1024 || heads <= 0 || head_dim <= 0)
+    return fail(PF_EINVAL_SHAPE, "triatt: bad sizes");
+  if (n_valid_keys < 0 || n_valid_keys > n_keys)
+    return fail(PF_EINVAL_SHAPE, "triatt: n_valid_keys=%lld outside [0, n_keys=%lld]",
+                (long long)n_valid_keys, (long long)n_keys);
+  if (q_col0 < 0 || q_col0 + n_q > n_keys)
+    return fail(PF_EINVAL_SHAPE, "triatt: query columns [%lld, %lld) outside the slab",
+                (long long)q_col0, (long long)(q_col0 + n_q));
+  if (bias == nullptr && !(q_col0 == 0 && n_q == n_keys && n_rows == n_keys))
+    return fail(PF_EINVAL_ARG, "triatt: bias may be NULL only for the square single-device case");
+  if (n_rows == 0 || n_q == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_triatt_workspace_size(n_rows, n_keys, n_q, c, heads, head_dim, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "triatt"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (triatt_tc(c, heads, head_dim, dtype)) {
+    set_path("tc");
+    return tc::triatt(w, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid_keys, q_col0, n_q,
+                      c, heads, head_dim, inf, accumulate, workspace, workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::triatt(w, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid_keys, q_col0, n_q, c,
+                      heads, head_dim, inf, accumulate, dtype, workspace, workspace_bytes, st);
+}
+
+// ------------------------------------------------------------------ transition
+static bool transition_tc(int c, int nm, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::transition_supported(c, nm);
+}
+
+int pf_transition_workspace_size(int64_t rows, int32_t c, int32_t n_mult, int32_t dtype,
+                                 size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  *bytes = transition_tc(c, n_mult, dtype) ? 0 : simt::transition_ws_bytes(rows, c, n_mult);
+  return PF_OK;
+}
+
+int pf_transition_fwd(const pf_transition_params* w, const void* x, int64_t x_stride, void* out,
+                      int64_t out_stride, int64_t rows, int32_t c, int32_t n_mult,
+                      int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_a || !w->w_b || !w->w_o || !x || !out) return fail(PF_EINVAL_ARG, "transition: null pointer");
+  if (rows < 0 || c <= 0 || c > 1024 || n_mult <= 0 || x_stride < c || out_stride < c)
+    return fail(PF_EINVAL_SHAPE, "transition: bad sizes");
+  if (rows == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_transition_workspace_size(rows, c, n_mult, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "transition"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (transition_tc(c, n_mult, dtype)) {
+    set_path("tc");
+    return tc::transition(w, x, x_stride, out, out_stride, rows, c, n_mult, accumulate, st);
+  }
+  set_path("simt");
+  return simt::transition(w, x, x_stride, out, out_stride, rows, c, n_mult, accumulate, dtype,
+                          workspace, workspace_bytes, st);
+}
+
+// ------------------------------------------------------------------ AttentionPairBias
+int pf_apb_pair_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t heads,
+                                    int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  *bytes = simt::apb_pair_bias_ws_bytes(n_rows * n_cols, c_z, heads);
+  return PF_OK;
+}
+
+int pf_apb_pair_bias(const pf_apb_params* w, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                     float* bias, int64_t hs, int64_t rs, int32_t c_z, int32_t heads, int32_t dtype,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_z || !bias || !view_ok(z)) return fail(PF_EINVAL_ARG, "apb_pair_bias: null pointer");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_z > 1024 || heads <= 0)
+    return fail(PF_EINVAL_SHAPE, "apb_pair_bias: bad sizes");
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_apb_pair_bias_workspace_size(n_rows, n_cols, c_z, heads, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "apb_pair_bias"));
+  set_path("simt");
+  return simt::apb_pair_bias(w, z, n_rows, n_cols, bias, hs, rs, c_z, heads, dtype, workspace,
+                             workspace_bytes, (cudaStream_t)stream);
+}
+
+int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, int32_t dtype,
+                          size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  *bytes = simt::apb_ws_bytes_full(n, c_s, c_z, heads);
+  return PF_OK;
+}
+
+int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_pair_view z,
+               const float* bias, int64_t n, int32_t c_s, int32_t c_z, int32_t heads,
+               int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_q || !w->w_k || !w->w_v || !w->w_g || !w->w_o || !s_in || !s_out)
+    return fail(PF_EINVAL_ARG, "apb: null pointer");
+  if (bias == nullptr && (!view_ok(z) || !w->w_z)) return fail(PF_EINVAL_ARG, "apb: need z or bias");
+  if (n < 0 || c_s <= 0 || c_s > 1024 || heads <= 0 || c_s % heads != 0)
+    return fail(PF_EINVAL_SHAPE, "apb: bad sizes n=%lld c_s=%d heads=%d", (long long)n, c_s, heads);
+  if (n == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_apb_workspace_size(n, c_s, c_z, heads, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "apb"));
+  set_path("simt");
+  return simt::apb(w, s_in, s_out, z, bias, n, c_s, c_z, heads, accumulate, dtype, workspace,
+                   workspace_bytes, (cudaStream_t)stream);
+}
+
+}  // extern "C"

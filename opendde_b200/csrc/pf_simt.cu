@@ -1,0 +1,728 @@
+// pf_simt.cu -- generic SIMT (FFMA) path of the pair stack.
+//
+// Serves two purposes:
+//  * the fp32 mode (PF_F32): fp32 storage and fp32 arithmetic, evaluated in the same
+//    operation order as the reference PyTorch modules so that the 1e-4 max-abs parity
+//    holds (no TF32 anywhere);
+//  * any shape the tcgen05 path does not cover (channel counts other than the tuned
+//    ones), in either dtype. Intermediates are fp32 in the caller's workspace.
+//
+// Every op is a short sequence of: a LayerNorm-of-a-view kernel, a strided batched
+// C = A * B^T GEMM, and small elementwise kernels.
+
+#include <cmath>
+
+#include "pf_common.cuh"
+#include "pf_simt.h"
+
+namespace pf {
+namespace simt {
+
+// ============================================================================ kernels
+
+// LayerNorm over channels of every position (r, s) of a pair view -> contiguous output
+// out[(r*n_cols + s) * c + ch]. One warp per position; two-pass (mean, then centred
+// variance) like torch's CPU layer_norm.
+template <class T, class TO>
+__global__ void k_ln_view(const T* __restrict__ x, int64_t rs, int64_t cs, int64_t n_rows,
+                          int64_t n_cols, int c, const float* __restrict__ gamma,
+                          const float* __restrict__ beta, float eps, TO* __restrict__ out,
+                          int64_t out_pos_stride) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t npos = n_rows * n_cols;
+  if (pos >= npos) return;
+  const int64_t r = pos / n_cols, s = pos - r * n_cols;
+  const T* xp = x + r * rs + s * cs;
+  constexpr int MAXV = 32;  // c <= 1024
+  float v[MAXV];
+  float sum = 0.f;
+  const int per = (c + 31) / 32;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (t < per) {
+      int ch = t * 32 + lane;
+      v[t] = ch < c ? to_f(xp[ch]) : 0.f;
+      sum += v[t];
+    }
+  }
+  const float mean = warp_sum(sum) / (float)c;
+  float sq = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (t < per) {
+      int ch = t * 32 + lane;
+      float d = ch < c ? v[t] - mean : 0.f;
+      sq += d * d;
+    }
+  }
+  const float var = warp_sum(sq) / (float)c;
+  const float rstd = 1.0f / sqrtf(var + eps);
+  TO* op = out + pos * out_pos_stride;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (t < per) {
+      int ch = t * 32 + lane;
+      if (ch < c) {
+        float y = (v[t] - mean) * rstd;
+        if (gamma) y = y * gamma[ch];
+        if (beta) y = y + beta[ch];
+        op[ch] = from_f<TO>(y);
+      }
+    }
+  }
+}
+
+// C[b](m, n) = alpha * sum_k A[b](m, k) * B[b](n, k)  (+ C if accumulate)
+// A(m,k) = A + b*sAb + m*sAm + k ; B(n,k) = B + b*sBb + n*sBn + k ;
+// C(m,n) = C + b*sCb + m*sCm + n*sCn.
+// 64x64 tile, K step 16, 256 threads, 4x4 outputs per thread, fp32 FFMA.
+template <class TA, class TB>
+__global__ void __launch_bounds__(256) k_gemm_nt(const TA* __restrict__ A, int64_t sAb, int64_t sAm,
+                                                 const TB* __restrict__ B, int64_t sBb, int64_t sBn,
+                                                 float* __restrict__ C, int64_t sCb, int64_t sCm,
+                                                 int64_t sCn, int64_t M, int64_t N, int64_t K,
+                                                 float alpha, int accumulate) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64 + 4];
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  const int64_t b = blockIdx.z;
+  const int64_t m0 = (int64_t)blockIdx.y * 64, n0 = (int64_t)blockIdx.x * 64;
+  const TA* Ab = A + b * sAb;
+  const TB* Bb = B + b * sBb;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+  for (int64_t k0 = 0; k0 < K; k0 += 16) {
+    // each thread loads 4 elements of A tile and 4 of B tile (64 rows x 16 k)
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      int idx = tid + t * 256;   // 0..1023
+      int row = idx >> 4, kk = idx & 15;
+      int64_t gm = m0 + row, gk = k0 + kk, gn = n0 + row;
+      As[kk][row] = (gm < M && gk < K) ? to_f(Ab[gm * sAm + gk]) : 0.f;
+      Bs[kk][row] = (gn < N && gk < K) ? to_f(Bb[gn * sBn + gk]) : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < 16; ++kk) {
+      float a[4], bb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bb[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], bb[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+  float* Cb = C + b * sCb;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int64_t gm = m0 + ty + 16 * i;
+    if (gm >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int64_t gn = n0 + tx + 16 * j;
+      if (gn >= N) continue;
+      float* cp = Cb + gm * sCm + gn * sCn;
+      float val = alpha * acc[i][j];
+      *cp = accumulate ? (*cp + val) : val;
+    }
+  }
+}
+
+// a(ch, r, k) = m(r, k) * sigmoid(pg[p, ch]) * pa[p, ch],  p = r*n_k + k  (channel-major out)
+__global__ void k_gate_to_cmajor(const float* __restrict__ pa, const float* __restrict__ pg,
+                                 pf_mask_view m, int64_t n_r, int64_t n_k, int c_h,
+                                 float* __restrict__ out) {
+  const int64_t P = n_r * n_k;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= P * c_h) return;
+  const int64_t ch = idx / P, p = idx - ch * P;
+  const int64_t r = p / n_k, k = p - r * n_k;
+  const float mv = m.ptr ? m.ptr[r * m.row_stride + k * m.col_stride] : 1.0f;
+  // reference order: a = mask; a = a * sigmoid(g); a = a * p   (triangular.py:539-541)
+  float v = mv * sigmoid_acc(pg[p * c_h + ch]);
+  out[idx] = v * pa[p * c_h + ch];
+}
+
+// x[p, ch] = LN_out over ch of p_cm[ch, p]   (channel-major input, one warp per position)
+__global__ void k_ln_cmajor(const float* __restrict__ pin, int64_t P, int c,
+                            const float* __restrict__ gamma, const float* __restrict__ beta,
+                            float eps, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pos >= P) return;
+  constexpr int MAXV = 32;
+  float v[MAXV];
+  const int per = (c + 31) / 32;
+  float sum = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t)
+    if (t < per) {
+      int ch = t * 32 + lane;
+      v[t] = ch < c ? pin[(int64_t)ch * P + pos] : 0.f;
+      sum += v[t];
+    }
+  const float mean = warp_sum(sum) / (float)c;
+  float sq = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t)
+    if (t < per) {
+      int ch = t * 32 + lane;
+      float d = ch < c ? v[t] - mean : 0.f;
+      sq += d * d;
+    }
+  const float rstd = 1.0f / sqrtf(warp_sum(sq) / (float)c + eps);
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t)
+    if (t < per) {
+      int ch = t * 32 + lane;
+      if (ch < c) {
+        float y = (v[t] - mean) * rstd;
+        if (gamma) y *= gamma[ch];
+        if (beta) y += beta[ch];
+        out[pos * c + ch] = y;
+      }
+    }
+}
+
+// dst(r, s, ch) = acc ? dst + y*sig(g) : y*sig(g) for positions of a view;
+// y, g are contiguous [P, c]; g == nullptr => no gate.
+template <class T>
+__global__ void k_combine_view(T* __restrict__ dst, int64_t rs, int64_t cs, int64_t n_rows,
+                               int64_t n_cols, int c, const float* __restrict__ y,
+                               const float* __restrict__ g, int accumulate) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t P = n_rows * n_cols;
+  if (idx >= P * c) return;
+  const int64_t p = idx / c;
+  const int ch = (int)(idx - p * c);
+  const int64_t r = p / n_cols, s = p - r * n_cols;
+  float u = y[idx];
+  if (g) u = u * sigmoid_acc(g[idx]);
+  T* d = dst + r * rs + s * cs + ch;
+  float base = accumulate ? to_f(*d) : 0.f;
+  *d = from_f<T>(base + u);
+}
+
+// o *= sigmoid(g), contiguous
+__global__ void k_gate_inplace(float* __restrict__ o, const float* __restrict__ g, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) o[i] = o[i] * sigmoid_acc(g[i]);
+}
+
+// h = silu(a) * b, contiguous (reference: a = silu(a); b *= a, primitives.py:205-210)
+__global__ void k_swiglu(const float* __restrict__ a, float* __restrict__ b, int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) b[i] = b[i] * silu_acc(a[i]);
+}
+
+// y += bias[col] for a row-major [rows, cols] matrix
+__global__ void k_add_bias(float* __restrict__ y, const float* __restrict__ bias, int64_t rows, int cols) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < rows * cols) y[i] += bias[i % cols];
+}
+
+// Online-softmax attention, one thread per query. Arithmetic order follows the
+// reference: s = (q / sqrt(d)) . k ; s += mask_bias ; s += bias ; softmax ; @ v.
+//   q(i, j)  = q + i*q_rs + (q_col0 + j)*q_ps + h*D      (projection, unscaled)
+//   k,v(i,k) = k + i*kv_rs + k*kv_ps + h*D
+//   bias(h, j, k) = bias[h*b_hs + j*b_rs + k] * bias_scale    (nullptr => 0)
+//   mask(i, k): mask_bias = inf * (mask - 1)                   (ptr == nullptr => 0)
+template <int D, class TB>
+__global__ void __launch_bounds__(64) k_attn_simt(
+    const float* __restrict__ q, int64_t q_rs, int64_t q_ps, int64_t q_col0,
+    const float* __restrict__ k, const float* __restrict__ v, int64_t kv_rs, int64_t kv_ps,
+    const TB* __restrict__ bias, int64_t b_hs, int64_t b_rs, float bias_scale,
+    pf_mask_view m, float inf, int64_t n_q, int64_t n_valid_keys, float inv_sqrt_d_div,
+    float* __restrict__ o, int64_t o_rs, int64_t o_ps) {
+  __shared__ float Ks[64][D + 1];
+  __shared__ float Vs[64][D + 1];
+  const int h = blockIdx.y;
+  const int64_t i = blockIdx.z;
+  const int64_t j = (int64_t)blockIdx.x * 64 + threadIdx.x;
+  const bool active = j < n_q;
+  float qv[D];
+  const float* qp = q + i * q_rs + (q_col0 + (active ? j : 0)) * q_ps + h * D;
+#pragma unroll
+  for (int t = 0; t < D; ++t) qv[t] = qp[t] / inv_sqrt_d_div;  // reference divides q by sqrt(d)
+  float mrun = -INFINITY, l = 0.f;
+  float acc[D];
+#pragma unroll
+  for (int t = 0; t < D; ++t) acc[t] = 0.f;
+  const float* kb = k + i * kv_rs + h * D;
+  const float* vb = v + i * kv_rs + h * D;
+  for (int64_t k0 = 0; k0 < n_valid_keys; k0 += 64) {
+    __syncthreads();
+    {
+      int64_t kk = k0 + threadIdx.x;
+      if (kk < n_valid_keys) {
+#pragma unroll
+        for (int t = 0; t < D; ++t) {
+          Ks[threadIdx.x][t] = kb[kk * kv_ps + t];
+          Vs[threadIdx.x][t] = vb[kk * kv_ps + t];
+        }
+      }
+    }
+    __syncthreads();
+    if (!active) continue;
+    const int64_t rem = n_valid_keys - k0;
+    const int nk = rem < 64 ? (int)rem : 64;
+    for (int t = 0; t < nk; ++t) {
+      const int64_t kk = k0 + t;
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < D; ++e) s = fmaf(qv[e], Ks[t][e], s);
+      if (m.ptr) s = s + inf * (m.ptr[i * m.row_stride + kk * m.col_stride] - 1.0f);
+      if (bias) s = s + to_f(bias[(int64_t)h * b_hs + j * b_rs + kk]) * bias_scale;
+      if (s > mrun) {
+        float corr = expf(mrun - s);  // exp(-inf) = 0 on the first key
+        l *= corr;
+#pragma unroll
+        for (int e = 0; e < D; ++e) acc[e] *= corr;
+        mrun = s;
+      }
+      float pexp = expf(s - mrun);
+      l += pexp;
+#pragma unroll
+      for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[t][e], acc[e]);
+    }
+  }
+  if (!active) return;
+  float* op = o + i * o_rs + j * o_ps + h * D;
+  const float inv = l > 0.f ? 1.0f / l : 0.f;
+#pragma unroll
+  for (int e = 0; e < D; ++e) op[e] = acc[e] * inv;
+}
+
+// ============================================================================ host side
+
+static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+template <class T, class TO>
+static int ln_view(const T* x, int64_t rs, int64_t cs, int64_t n_rows, int64_t n_cols, int c,
+                   const float* g, const float* b, float eps, TO* out, int64_t ops,
+                   cudaStream_t st) {
+  if (c > 1024) return fail(PF_EUNSUPPORTED, "LayerNorm channel count %d > 1024", c);
+  int64_t P = n_rows * n_cols;
+  if (P == 0) return PF_OK;
+  k_ln_view<T, TO><<<nblk(P, 8), 256, 0, st>>>(x, rs, cs, n_rows, n_cols, c, g, b, eps, out, ops);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+template <class TA, class TB>
+static int gemm(const TA* A, int64_t sAb, int64_t sAm, const TB* B, int64_t sBb, int64_t sBn,
+                float* C, int64_t sCb, int64_t sCm, int64_t sCn, int64_t batch, int64_t M,
+                int64_t N, int64_t K, float alpha, int acc, cudaStream_t st) {
+  if (M == 0 || N == 0 || batch == 0) return PF_OK;
+  if (batch > 65535 || (M + 63) / 64 > 65535)
+    return fail(PF_EUNSUPPORTED, "SIMT GEMM grid too large (batch %lld, M %lld)",
+                (long long)batch, (long long)M);
+  dim3 grid(nblk(N, 64), nblk(M, 64), (unsigned)batch);
+  k_gemm_nt<TA, TB><<<grid, 256, 0, st>>>(A, sAb, sAm, B, sBb, sBn, C, sCb, sCm, sCn, M, N, K,
+                                          alpha, acc);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int layernorm(const void* x, void* y, const float* g, const float* b, int64_t rows, int c,
+              float eps, int dtype, cudaStream_t st) {
+  if (dtype == PF_F32)
+    return ln_view<float, float>((const float*)x, c, 0, rows, 1, c, g, b, eps, (float*)y, c, st);
+  return ln_view<__nv_bfloat16, __nv_bfloat16>((const __nv_bfloat16*)x, c, 0, rows, 1, c, g, b,
+                                                eps, (__nv_bfloat16*)y, c, st);
+}
+
+// ---------------------------------------------------------------- triangle multiplication
+struct TrimulWs {
+  float *xa, *xb, *pa, *pg, *a, *b, *p, *xn, *y, *xo, *gg;
+};
+static void trimul_plan(Arena& ar, int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h,
+                        TrimulWs& w) {
+  int64_t Pa = n_i * n_k, Pb = n_j * n_k, Po = n_i * n_j;
+  int64_t Pm = Pa > Pb ? Pa : Pb;
+  w.xa = ar.take<float>(Pa * c_z);
+  w.xb = ar.take<float>(Pb * c_z);
+  w.pa = ar.take<float>(Pm * c_h);
+  w.pg = ar.take<float>(Pm * c_h);
+  w.a = ar.take<float>(Pa * c_h);
+  w.b = ar.take<float>(Pb * c_h);
+  w.p = ar.take<float>(Po * c_h);
+  w.xn = ar.take<float>(Po * c_h);
+  w.y = ar.take<float>(Po * c_z);
+  w.xo = ar.take<float>(Po * c_z);
+  w.gg = ar.take<float>(Po * c_z);
+}
+
+size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h) {
+  Arena ar(nullptr, 0);
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
+  return ar.used;
+}
+
+template <class T>
+static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+                    pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+                    int c_z, int c_h, int acc, Arena& ar, cudaStream_t st) {
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small (%zu < %zu)", ar.cap, ar.used);
+  const float eps = 1e-5f;
+  int64_t Pa = n_i * n_k, Pb = n_j * n_k, Po = n_i * n_j;
+  const T* W_ap = (const T*)p->w_ap; const T* W_ag = (const T*)p->w_ag;
+  const T* W_bp = (const T*)p->w_bp; const T* W_bg = (const T*)p->w_bg;
+  // a
+  PF_TRY((ln_view<T, float>((const T*)za.ptr, za.row_stride, za.col_stride, n_i, n_k, c_z,
+                            p->ln_in_w, p->ln_in_b, eps, w.xa, c_z, st)));
+  PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ap, 0, c_z, w.pa, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ag, 0, c_z, w.pg, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
+  k_gate_to_cmajor<<<nblk(Pa * c_h, 256), 256, 0, st>>>(w.pa, w.pg, ma, n_i, n_k, c_h, w.a);
+  PF_CHECK_LAUNCH();
+  // b
+  PF_TRY((ln_view<T, float>((const T*)zb.ptr, zb.row_stride, zb.col_stride, n_j, n_k, c_z,
+                            p->ln_in_w, p->ln_in_b, eps, w.xb, c_z, st)));
+  PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bp, 0, c_z, w.pa, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bg, 0, c_z, w.pg, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
+  k_gate_to_cmajor<<<nblk(Pb * c_h, 256), 256, 0, st>>>(w.pa, w.pg, mb, n_j, n_k, c_h, w.b);
+  PF_CHECK_LAUNCH();
+  // x[ch] = a[ch] b[ch]^T  (batched over channels)
+  PF_TRY((gemm<float, float>(w.a, Pa, n_k, w.b, Pb, n_k, w.p, Po, n_j, 1, c_h, n_i, n_j, n_k,
+                             1.f, 0, st)));
+  // LN_out, linear_z
+  k_ln_cmajor<<<nblk(Po, 8), 256, 0, st>>>(w.p, Po, c_h, p->ln_out_w, p->ln_out_b, eps, w.xn);
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(w.xn, 0, c_h, (const T*)p->w_z, 0, c_h, w.y, 0, c_z, 1, 1, Po, c_z, c_h,
+                         1.f, 0, st)));
+  // gate from LN_in(zg)
+  PF_TRY((ln_view<T, float>((const T*)zg.ptr, zg.row_stride, zg.col_stride, n_i, n_j, c_z,
+                            p->ln_in_w, p->ln_in_b, eps, w.xo, c_z, st)));
+  PF_TRY((gemm<float, T>(w.xo, 0, c_z, (const T*)p->w_g, 0, c_z, w.gg, 0, c_z, 1, 1, Po, c_z, c_z,
+                         1.f, 0, st)));
+  k_combine_view<T><<<nblk(Po * c_z, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
+                                                         n_i, n_j, c_z, w.y, w.gg, acc);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
+           int c_h, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return trimul_t<float>(p, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, acc, ar, st);
+  return trimul_t<__nv_bfloat16>(p, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, acc, ar, st);
+}
+
+// ---------------------------------------------------------------- triangle attention
+struct TriattWs {
+  float *x, *q, *k, *v, *bias, *o, *g, *y;
+};
+static void triatt_plan(Arena& ar, int64_t n_rows, int64_t n_keys, int64_t n_q, int c, int H,
+                        int d, bool own_bias, TriattWs& w) {
+  int64_t P = n_rows * n_keys, Pq = n_rows * n_q;
+  int hd = H * d;
+  w.x = ar.take<float>(P * c);
+  w.q = ar.take<float>(P * hd);
+  w.k = ar.take<float>(P * hd);
+  w.v = ar.take<float>(P * hd);
+  w.bias = own_bias ? ar.take<float>((int64_t)H * n_keys * n_keys) : nullptr;
+  w.o = ar.take<float>(Pq * hd);
+  w.g = ar.take<float>(Pq * hd);
+  w.y = ar.take<float>(Pq * c);
+}
+
+size_t triatt_ws_bytes(int64_t n_rows, int64_t n_keys, int64_t n_q, int c, int H, int d) {
+  Arena ar(nullptr, 0);
+  TriattWs w;
+  triatt_plan(ar, n_rows, n_keys, n_q, c, H, d, true, w);
+  return ar.used;
+}
+
+template <class T, class TB>
+static int launch_attn(int d, const float* q, int64_t q_rs, int64_t q_ps, int64_t q_col0,
+                       const float* k, const float* v, int64_t kv_rs, int64_t kv_ps,
+                       const TB* bias, int64_t b_hs, int64_t b_rs, float bias_scale,
+                       pf_mask_view m, float inf, int64_t n_rows, int64_t n_q, int H,
+                       int64_t n_valid, float* o, int64_t o_rs, int64_t o_ps, cudaStream_t st) {
+  if (n_rows > 65535) return fail(PF_EUNSUPPORTED, "too many attention rows (%lld)", (long long)n_rows);
+  dim3 grid(nblk(n_q, 64), H, (unsigned)n_rows);
+  float sd = sqrtf((float)d);
+#define PF_ATTN_CASE(DD)                                                                       \
+  case DD:                                                                                     \
+    k_attn_simt<DD, TB><<<grid, 64, 0, st>>>(q, q_rs, q_ps, q_col0, k, v, kv_rs, kv_ps, bias,  \
+                                             b_hs, b_rs, bias_scale, m, inf, n_q, n_valid, sd, \
+                                             o, o_rs, o_ps);                                   \
+    break;
+  switch (d) {
+    PF_ATTN_CASE(8)
+    PF_ATTN_CASE(16)
+    PF_ATTN_CASE(24)
+    PF_ATTN_CASE(32)
+    PF_ATTN_CASE(48)
+    PF_ATTN_CASE(64)
+    default:
+      return fail(PF_EUNSUPPORTED, "head dim %d not in {8,16,24,32,48,64}", d);
+  }
+#undef PF_ATTN_CASE
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+template <class T>
+static int triatt_bias_t(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                         void* bias, int64_t hs, int64_t rs, int c, int H, float scale,
+                         float* xbuf, cudaStream_t st) {
+  // xbuf: LN(z) [n_rows*n_cols, c] (fp32), then bias(h, r, s) = scale * x . W_b[h]
+  PF_TRY((ln_view<T, float>((const T*)z.ptr, z.row_stride, z.col_stride, n_rows, n_cols, c,
+                            p->ln_w, p->ln_b, 1e-5f, xbuf, c, st)));
+  return PF_OK;
+}
+
+template <class T>
+static int triatt_t(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias,
+                    int64_t b_hs, int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys,
+                    int64_t n_valid, int64_t q_col0, int64_t n_q, int c, int H, int d, float inf,
+                    int acc, Arena& ar, cudaStream_t st) {
+  TriattWs w;
+  triatt_plan(ar, n_rows, n_keys, n_q, c, H, d, bias == nullptr, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "triatt workspace too small (%zu < %zu)", ar.cap, ar.used);
+  const int hd = H * d;
+  const int64_t P = n_rows * n_keys, Pq = n_rows * n_q;
+  PF_TRY((ln_view<T, float>((const T*)zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys, c,
+                            p->ln_w, p->ln_b, 1e-5f, w.x, c, st)));
+  PF_TRY((gemm<float, T>(w.x, 0, c, (const T*)p->w_q, 0, c, w.q, 0, hd, 1, 1, P, hd, c, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(w.x, 0, c, (const T*)p->w_k, 0, c, w.k, 0, hd, 1, 1, P, hd, c, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(w.x, 0, c, (const T*)p->w_v, 0, c, w.v, 0, hd, 1, 1, P, hd, c, 1.f, 0, st)));
+  if (bias == nullptr) {
+    // square single-device case: bias(h, j, k) = W_b . x(j, k), written [H][n][n]
+    PF_TRY((gemm<float, T>(w.x, 0, c, (const T*)p->w_bias, 0, c, w.bias, 0, 1, n_keys * n_keys, 1,
+                           P, H, c, 1.f, 0, st)));
+    PF_TRY((launch_attn<T, float>(d, w.q, n_keys * hd, hd, q_col0, w.k, w.v, n_keys * hd, hd,
+                                  w.bias, n_keys * n_keys, n_keys, 1.0f, m, inf, n_rows, n_q, H,
+                                  n_valid, w.o, n_q * hd, hd, st)));
+  } else if (sizeof(T) == 4) {
+    PF_TRY((launch_attn<T, float>(d, w.q, n_keys * hd, hd, q_col0, w.k, w.v, n_keys * hd, hd,
+                                  (const float*)bias, b_hs, b_rs, 1.0f, m, inf, n_rows, n_q, H,
+                                  n_valid, w.o, n_q * hd, hd, st)));
+  } else {
+    // bf16 bias buffers hold log2-scaled values (the tensor-core path's format)
+    PF_TRY((launch_attn<T, __nv_bfloat16>(d, w.q, n_keys * hd, hd, q_col0, w.k, w.v, n_keys * hd,
+                                          hd, (const __nv_bfloat16*)bias, b_hs, b_rs,
+                                          0.69314718055994531f, m, inf, n_rows, n_q, H, n_valid,
+                                          w.o, n_q * hd, hd, st)));
+  }
+  // gate from LN'd query input, then output projection
+  PF_TRY((gemm<float, T>(w.x + q_col0 * c, n_keys * c, c, (const T*)p->w_g, 0, c, w.g, n_q * hd,
+                         hd, 1, n_rows, n_q, hd, c, 1.f, 0, st)));
+  k_gate_inplace<<<nblk(Pq * hd, 256), 256, 0, st>>>(w.o, w.g, Pq * hd);
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(w.o, 0, hd, (const T*)p->w_o, 0, hd, w.y, 0, c, 1, 1, Pq, c, hd, 1.f, 0, st)));
+  k_combine_view<T><<<nblk(Pq * c, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
+                                                       n_rows, n_q, c, w.y, nullptr, acc);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias,
+           int64_t b_hs, int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys,
+           int64_t n_valid, int64_t q_col0, int64_t n_q, int c, int H, int d, float inf, int acc,
+           int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return triatt_t<float>(p, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid, q_col0, n_q, c,
+                           H, d, inf, acc, ar, st);
+  return triatt_t<__nv_bfloat16>(p, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid, q_col0,
+                                 n_q, c, H, d, inf, acc, ar, st);
+}
+
+size_t triatt_bias_ws_bytes(int64_t n_rows, int64_t n_cols, int c, int H) {
+  return align_up((size_t)(n_rows * n_cols) * (c + H) * sizeof(float), 256);
+}
+
+// fp32 -> fp32 (scale 1) or -> bf16 scaled by log2(e)
+template <class TO>
+__global__ void k_bias_store(const float* __restrict__ src, int64_t n_rows, int64_t n_cols, int H,
+                             TO* __restrict__ dst, int64_t hs, int64_t rs, float scale) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t P = n_rows * n_cols;
+  if (idx >= P * H) return;
+  const int64_t h = idx / P, p = idx - h * P;
+  const int64_t r = p / n_cols, s = p - r * n_cols;
+  dst[h * hs + r * rs + s] = from_f<TO>(src[p * H + h] * scale);
+}
+
+int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                void* bias, int64_t hs, int64_t rs, int c, int H, int dtype, void* ws,
+                size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  int64_t P = n_rows * n_cols;
+  float* x = ar.take<float>(P * c);
+  float* bb = ar.take<float>(P * H);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "triatt_bias workspace too small");
+  if (dtype == PF_F32) {
+    PF_TRY(triatt_bias_t<float>(p, z, n_rows, n_cols, bias, hs, rs, c, H, 1.f, x, st));
+    PF_TRY((gemm<float, float>(x, 0, c, (const float*)p->w_bias, 0, c, bb, 0, H, 1, 1, P, H, c, 1.f, 0, st)));
+    k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, (float*)bias, hs, rs, 1.f);
+  } else {
+    PF_TRY(triatt_bias_t<__nv_bfloat16>(p, z, n_rows, n_cols, bias, hs, rs, c, H, 1.f, x, st));
+    PF_TRY((gemm<float, __nv_bfloat16>(x, 0, c, (const __nv_bfloat16*)p->w_bias, 0, c, bb, 0, H, 1, 1,
+                                       P, H, c, 1.f, 0, st)));
+    k_bias_store<__nv_bfloat16><<<nblk(P * H, 256), 256, 0, st>>>(
+        bb, n_rows, n_cols, H, (__nv_bfloat16*)bias, hs, rs, 1.4426950408889634f);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+// ---------------------------------------------------------------- transition
+size_t transition_ws_bytes(int64_t rows, int c, int nm) {
+  Arena ar(nullptr, 0);
+  ar.take<float>(rows * c);
+  ar.take<float>(rows * c * nm);
+  ar.take<float>(rows * c * nm);
+  ar.take<float>(rows * c);
+  return ar.used;
+}
+
+template <class T>
+static int transition_t(const pf_transition_params* p, const T* x, int64_t xs, T* out, int64_t os,
+                        int64_t rows, int c, int nm, int acc, Arena& ar, cudaStream_t st) {
+  float* y = ar.take<float>(rows * c);
+  float* a = ar.take<float>(rows * c * nm);
+  float* b = ar.take<float>(rows * c * nm);
+  float* o = ar.take<float>(rows * c);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "transition workspace too small");
+  const int hc = c * nm;
+  PF_TRY((ln_view<T, float>(x, xs, 0, rows, 1, c, p->ln_w, p->ln_b, 1e-5f, y, c, st)));
+  PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_a, 0, c, a, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_b, 0, c, b, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
+  k_swiglu<<<nblk(rows * hc, 256), 256, 0, st>>>(a, b, rows * hc);
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(b, 0, hc, (const T*)p->w_o, 0, hc, o, 0, c, 1, 1, rows, c, hc, 1.f, 0, st)));
+  k_combine_view<T><<<nblk(rows * c, 256), 256, 0, st>>>(out, os, 0, rows, 1, c, o, nullptr, acc);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int transition(const pf_transition_params* p, const void* x, int64_t xs, void* out, int64_t os,
+               int64_t rows, int c, int nm, int acc, int dtype, void* ws, size_t ws_bytes,
+               cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return transition_t<float>(p, (const float*)x, xs, (float*)out, os, rows, c, nm, acc, ar, st);
+  return transition_t<__nv_bfloat16>(p, (const __nv_bfloat16*)x, xs, (__nv_bfloat16*)out, os, rows,
+                                     c, nm, acc, ar, st);
+}
+
+// ---------------------------------------------------------------- AttentionPairBias
+size_t apb_pair_bias_ws_bytes(int64_t P, int c_z, int H) {
+  return align_up((size_t)P * c_z * 4, 256) + align_up((size_t)P * H * 4, 256);
+}
+
+int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                  float* bias, int64_t hs, int64_t rs, int c_z, int H, int dtype, void* ws,
+                  size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  int64_t P = n_rows * n_cols;
+  float* x = ar.take<float>(P * c_z);
+  float* bb = ar.take<float>(P * H);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "apb_pair_bias workspace too small");
+  if (dtype == PF_F32) {
+    PF_TRY((ln_view<float, float>((const float*)z.ptr, z.row_stride, z.col_stride, n_rows, n_cols,
+                                  c_z, p->ln_z_w, p->ln_z_b, 1e-5f, x, c_z, st)));
+    PF_TRY((gemm<float, float>(x, 0, c_z, (const float*)p->w_z, 0, c_z, bb, 0, H, 1, 1, P, H, c_z, 1.f, 0, st)));
+  } else {
+    PF_TRY((ln_view<__nv_bfloat16, float>((const __nv_bfloat16*)z.ptr, z.row_stride, z.col_stride,
+                                          n_rows, n_cols, c_z, p->ln_z_w, p->ln_z_b, 1e-5f, x, c_z, st)));
+    PF_TRY((gemm<float, __nv_bfloat16>(x, 0, c_z, (const __nv_bfloat16*)p->w_z, 0, c_z, bb, 0, H, 1,
+                                       1, P, H, c_z, 1.f, 0, st)));
+  }
+  k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, bias, hs, rs, 1.f);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+size_t apb_ws_bytes(int64_t n, int c_s, int H) {
+  Arena ar(nullptr, 0);
+  ar.take<float>(n * c_s);        // a
+  ar.take<float>(n * c_s * 4);    // q k v g
+  ar.take<float>(n * c_s);        // o
+  ar.take<float>(n * c_s);        // y
+  ar.take<float>((int64_t)H * n * n);  // own bias
+  return ar.used;
+}
+
+template <class T>
+static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* bias, int64_t n,
+                 int c_s, int H, int acc, Arena& ar, cudaStream_t st) {
+  float* a = ar.take<float>(n * c_s);
+  float* qkvg = ar.take<float>(n * c_s * 4);
+  float* o = ar.take<float>(n * c_s);
+  float* y = ar.take<float>(n * c_s);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "apb workspace too small");
+  float *q = qkvg, *k = qkvg + n * c_s, *v = qkvg + 2 * n * c_s, *g = qkvg + 3 * n * c_s;
+  const int d = c_s / H;
+  PF_TRY((ln_view<T, float>(s_in, c_s, 0, n, 1, c_s, p->ln_a_w, p->ln_a_b, 1e-5f, a, c_s, st)));
+  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_q, 0, c_s, q, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  if (p->b_q) {
+    k_add_bias<<<nblk(n * c_s, 256), 256, 0, st>>>(q, p->b_q, n, c_s);
+    PF_CHECK_LAUNCH();
+  }
+  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_k, 0, c_s, k, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_v, 0, c_s, v, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_g, 0, c_s, g, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  pf_mask_view nomask{nullptr, 0, 0};
+  // one "row" (i = 0) of n queries over n keys; bias(h, j, k) = bias[h*n*n + j*n + k]
+  PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, n * n, n, 1.0f, nomask, 0.f,
+                                1, n, H, n, o, 0, c_s, st)));
+  k_gate_inplace<<<nblk(n * c_s, 256), 256, 0, st>>>(o, g, n * c_s);
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(o, 0, c_s, (const T*)p->w_o, 0, c_s, y, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  k_combine_view<T><<<nblk(n * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, n, 1, c_s, y, nullptr, acc);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int apb(const pf_apb_params* p, const void* s_in, void* s_out, pf_pair_view z, const float* bias,
+        int64_t n, int c_s, int c_z, int H, int acc, int dtype, void* ws, size_t ws_bytes,
+        cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (bias == nullptr) {
+    float* own = ar.take<float>((int64_t)H * n * n);
+    if (!ar.ok()) return fail(PF_EWORKSPACE, "apb workspace too small");
+    // the pair-bias pass needs its own scratch: reuse the tail of the workspace
+    size_t tail_off = align_up(ar.used, 256);
+    size_t need = apb_pair_bias_ws_bytes(n * n, c_z, H);
+    size_t after = tail_off + need;
+    if (!ar.counting && after > ar.cap) {
+      // the pair-bias scratch is only needed before the single-attention pass: place it
+      // after the bias buffer, the attention buffers reuse the same region afterwards
+      return fail(PF_EWORKSPACE, "apb workspace too small for the pair-bias pass");
+    }
+    PF_TRY(apb_pair_bias(p, z, n, n, own, n * n, n, c_z, H, dtype, ar.base + tail_off, need, st));
+    bias = own;
+  }
+  if (dtype == PF_F32)
+    return apb_t<float>(p, (const float*)s_in, (float*)s_out, bias, n, c_s, H, acc, ar, st);
+  return apb_t<__nv_bfloat16>(p, (const __nv_bfloat16*)s_in, (__nv_bfloat16*)s_out, bias, n, c_s,
+                              H, acc, ar, st);
+}
+
+size_t apb_ws_bytes_full(int64_t n, int c_s, int c_z, int H) {
+  size_t own = align_up((size_t)H * n * n * 4, 256);
+  size_t pb = apb_pair_bias_ws_bytes(n * n, c_z, H);
+  size_t att = apb_ws_bytes(n, c_s, H) - align_up((size_t)H * n * n * 4, 256);
+  return own + (pb > att ? pb : att) + 1024;
+}
+
+}  // namespace simt
+}  // namespace pf

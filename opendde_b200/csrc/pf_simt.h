@@ -1,0 +1,42 @@
+// pf_simt.h -- generic SIMT path (fp32 arithmetic), see pf_simt.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include "../../include/pairformer_b200.h"
+
+namespace pf {
+namespace simt {
+
+int layernorm(const void* x, void* y, const float* g, const float* b, int64_t rows, int c,
+              float eps, int dtype, cudaStream_t st);
+
+size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
+int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
+           int c_h, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+
+size_t triatt_ws_bytes(int64_t n_rows, int64_t n_keys, int64_t n_q, int c, int H, int d);
+int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias,
+           int64_t b_hs, int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys,
+           int64_t n_valid, int64_t q_col0, int64_t n_q, int c, int H, int d, float inf, int acc,
+           int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t triatt_bias_ws_bytes(int64_t n_rows, int64_t n_cols, int c, int H);
+int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                void* bias, int64_t hs, int64_t rs, int c, int H, int dtype, void* ws,
+                size_t ws_bytes, cudaStream_t st);
+
+size_t transition_ws_bytes(int64_t rows, int c, int nm);
+int transition(const pf_transition_params* p, const void* x, int64_t xs, void* out, int64_t os,
+               int64_t rows, int c, int nm, int acc, int dtype, void* ws, size_t ws_bytes,
+               cudaStream_t st);
+
+size_t apb_pair_bias_ws_bytes(int64_t P, int c_z, int H);
+int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                  float* bias, int64_t hs, int64_t rs, int c_z, int H, int dtype, void* ws,
+                  size_t ws_bytes, cudaStream_t st);
+size_t apb_ws_bytes_full(int64_t n, int c_s, int c_z, int H);
+int apb(const pf_apb_params* p, const void* s_in, void* s_out, pf_pair_view z, const float* bias,
+        int64_t n, int c_s, int c_z, int H, int acc, int dtype, void* ws, size_t ws_bytes,
+        cudaStream_t st);
+
+}  // namespace simt
+}  // namespace pf

@@ -1,0 +1,35 @@
+// pf_tc.h -- tcgen05 / TMA (sm_100a) kernels of the bf16 path. Each *_supported() says
+// whether the shape is covered; the API layer routes everything else to the SIMT path.
+#pragma once
+#include <cuda_runtime.h>
+#include "../../include/pairformer_b200.h"
+
+namespace pf {
+namespace tc {
+
+bool layernorm_supported(int c, const void* x, const void* y);
+int layernorm_bf16(const void* x, void* y, const float* g, const float* b, int64_t rows, int c,
+                   float eps, cudaStream_t st);
+
+bool trimul_supported(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
+size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
+int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
+           int c_h, int acc, void* ws, size_t ws_bytes, cudaStream_t st);
+
+bool triatt_bias_supported(int c, int H);
+int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
+                void* bias, int64_t hs, int64_t rs, int c, int H, cudaStream_t st);
+bool triatt_supported(int c, int H, int d);
+size_t triatt_ws_bytes(int64_t n_rows, int64_t n_keys, int64_t n_q, int c, int H, int d);
+int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias,
+           int64_t b_hs, int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys,
+           int64_t n_valid, int64_t q_col0, int64_t n_q, int c, int H, int d, float inf, int acc,
+           void* ws, size_t ws_bytes, cudaStream_t st);
+
+bool transition_supported(int c, int nm);
+int transition(const pf_transition_params* p, const void* x, int64_t xs, void* out, int64_t os,
+               int64_t rows, int c, int nm, int acc, cudaStream_t st);
+
+}  // namespace tc
+}  // namespace pf

@@ -1,0 +1,210 @@
+"""Torch-facing wrappers over the C ABI: validation, pair views, weight packs, workspaces.
+
+Every function here launches CUDA work through ``libpairformer_b200.so`` on
+``torch.cuda.current_stream()``. CPU tensors are rejected (there is no CPU fallback).
+The compute mode follows the pair tensor's dtype: float32 -> PF_F32 (SIMT fp32),
+bfloat16 -> PF_BF16 (tcgen05 tensor cores where the shape is covered).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Dict, Optional
+
+import torch
+
+from . import _abi
+from ._abi import ApbParams, MaskView, PairView, TransitionParams, TriattParams, TrimulParams, check
+
+_DTYPES = {torch.float32: _abi.PF_F32, torch.bfloat16: _abi.PF_BF16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"opendde_b200 supports float32 and bfloat16 pair tensors, got {t.dtype}") from None
+
+
+def require_cuda(*ts: Optional[torch.Tensor]) -> None:
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("opendde_b200 kernels need CUDA tensors; there is no CPU fallback "
+                               "(use the reference modules for CPU execution)")
+
+
+def stream_ptr() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def pair_view(t: torch.Tensor) -> PairView:
+    """[R, C, ch] tensor (any row/col strides, contiguous channels) -> PairView."""
+    if t.dim() != 3:
+        raise ValueError(f"pair tensor must be [R, C, ch], got shape {tuple(t.shape)}")
+    if t.stride(2) != 1 and t.shape[2] > 1:
+        raise ValueError("pair tensor channel dim must be contiguous")
+    return PairView(t.data_ptr(), t.stride(0), t.stride(1))
+
+
+def mask_view(m: Optional[torch.Tensor]) -> MaskView:
+    if m is None:
+        return MaskView(None, 0, 0)
+    if m.dtype != torch.float32:
+        raise TypeError("mask views are float32")
+    return MaskView(m.data_ptr(), m.stride(0), m.stride(1))
+
+
+def prepare_mask(mask: Optional[torch.Tensor], n_rows: int, n_cols: int, device) -> torch.Tensor:
+    """Float32 CUDA mask of shape [n_rows, n_cols] (ones when None)."""
+    if mask is None:
+        return torch.ones((n_rows, n_cols), device=device, dtype=torch.float32)
+    return mask.to(device=device, dtype=torch.float32)
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty((max(int(nbytes), 1),), dtype=torch.uint8, device=device)
+
+
+def _ptr(t: Optional[torch.Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+# ------------------------------------------------------------------------------ weight packs
+
+class WeightPack:
+    """Weights converted once to the compute dtype (LayerNorm parameters stay fp32).
+
+    Built from a module's parameters; rebuilt when any parameter's storage or version
+    counter changes (e.g. after ``load_state_dict``).
+    """
+
+    def __init__(self, key, tensors: Dict[str, torch.Tensor], struct):
+        self.key = key
+        self.tensors = tensors  # keeps the converted storage alive
+        self.struct = struct
+
+
+def pack_key(params, dtype, device):
+    return (dtype, str(device)) + tuple((p.data_ptr(), p._version) for p in params)
+
+
+def _conv(p: Optional[torch.Tensor], dtype, device) -> Optional[torch.Tensor]:
+    if p is None:
+        return None
+    return p.detach().to(device=device, dtype=dtype).contiguous()
+
+
+def make_pack(struct_cls, spec: Dict[str, Optional[torch.Tensor]], f32_names, dtype, device, key):
+    tensors = {}
+    for name, p in spec.items():
+        tensors[name] = _conv(p, torch.float32 if name in f32_names else dtype, device)
+    struct = struct_cls(**{n: _ptr(t) for n, t in tensors.items()})
+    return WeightPack(key, tensors, struct)
+
+
+# ------------------------------------------------------------------------------ ops
+
+def layernorm(x: torch.Tensor, weight: Optional[torch.Tensor], bias: Optional[torch.Tensor],
+              eps: float = 1e-5) -> torch.Tensor:
+    require_cuda(x)
+    code = dtype_code(x)
+    x = x.contiguous()
+    y = torch.empty_like(x)
+    c = x.shape[-1]
+    w = None if weight is None else weight.detach().float().contiguous()
+    b = None if bias is None else bias.detach().float().contiguous()
+    check(_abi.load().pf_layernorm_fwd(x.data_ptr(), y.data_ptr(), _ptr(w), _ptr(b),
+                                       x.numel() // c, c, eps, code, stream_ptr()))
+    return y
+
+
+def trimul(pack: WeightPack, za: torch.Tensor, zb: torch.Tensor, ma: torch.Tensor,
+           mb: torch.Tensor, zg: torch.Tensor, zo: torch.Tensor, c_h: int, accumulate: bool) -> None:
+    """zo (+)= TriangleMultiplicativeUpdate on views (see pf_trimul_fwd); gate source zg."""
+    require_cuda(za, zb, zg, zo, ma, mb)
+    code = dtype_code(zo)
+    n_i, n_k, c_z = za.shape
+    n_j = zb.shape[0]
+    if zb.shape[1] != n_k or zo.shape[:2] != (n_i, n_j) or zg.shape[:2] != (n_i, n_j):
+        raise ValueError(f"trimul view shapes disagree: za {tuple(za.shape)} zb {tuple(zb.shape)} zo {tuple(zo.shape)}")
+    nbytes = _abi.workspace_bytes("pf_trimul_workspace_size", n_i, n_j, n_k, c_z, c_h, code)
+    ws = workspace(nbytes, zo.device)
+    check(_abi.load().pf_trimul_fwd(ctypes.byref(pack.struct), pair_view(za), pair_view(zb),
+                                    mask_view(ma), mask_view(mb), pair_view(zg), pair_view(zo),
+                                    n_i, n_j, n_k,
+                                    c_z, c_h, int(accumulate), code, ws.data_ptr(), ws.numel(),
+                                    stream_ptr()))
+
+
+def triatt_bias(pack: WeightPack, z: torch.Tensor, heads: int, out: torch.Tensor) -> None:
+    """out[h, r, s] = triangle bias of z(r, s) (fp32 natural units, or bf16 x log2(e))."""
+    require_cuda(z, out)
+    code = dtype_code(z)
+    n_r, n_c, c = z.shape
+    nbytes = _abi.workspace_bytes("pf_triatt_bias_workspace_size", n_r, n_c, c, heads, code)
+    ws = workspace(nbytes, z.device)
+    check(_abi.load().pf_triatt_bias(ctypes.byref(pack.struct), pair_view(z), n_r, n_c,
+                                     out.data_ptr(), out.stride(0), out.stride(1), c, heads, code,
+                                     ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def triatt(pack: WeightPack, zs: torch.Tensor, m: torch.Tensor, zo: torch.Tensor, heads: int,
+           head_dim: int, inf: float, accumulate: bool, bias: Optional[torch.Tensor] = None,
+           q_col0: int = 0, n_q: Optional[int] = None, n_valid_keys: Optional[int] = None) -> None:
+    """zo (+)= starting-node triangle attention of slab zs (see pf_triatt_fwd)."""
+    require_cuda(zs, zo, m, bias)
+    code = dtype_code(zs)
+    n_rows, n_keys, c = zs.shape
+    n_q = n_keys if n_q is None else n_q
+    n_valid = n_keys if n_valid_keys is None else n_valid_keys
+    nbytes = _abi.workspace_bytes("pf_triatt_workspace_size", n_rows, n_keys, n_q, c, heads, head_dim, code)
+    ws = workspace(nbytes, zs.device)
+    b_ptr, b_hs, b_rs = (None, 0, 0) if bias is None else (bias.data_ptr(), bias.stride(0), bias.stride(1))
+    check(_abi.load().pf_triatt_fwd(ctypes.byref(pack.struct), pair_view(zs), mask_view(m), b_ptr,
+                                    b_hs, b_rs, pair_view(zo), n_rows, n_keys, n_valid, q_col0, n_q,
+                                    c, heads, head_dim, inf, int(accumulate), code, ws.data_ptr(),
+                                    ws.numel(), stream_ptr()))
+
+
+def transition(pack: WeightPack, x2d: torch.Tensor, out2d: torch.Tensor, n_mult: int,
+               accumulate: bool) -> None:
+    """out (+)= Transition(x) over rows of 2-D views (row strides allowed, contiguous channels)."""
+    require_cuda(x2d, out2d)
+    code = dtype_code(x2d)
+    rows, c = x2d.shape
+    if x2d.stride(1) != 1 or out2d.stride(1) != 1:
+        raise ValueError("transition rows must have contiguous channels")
+    nbytes = _abi.workspace_bytes("pf_transition_workspace_size", rows, c, n_mult, code)
+    ws = workspace(nbytes, x2d.device)
+    check(_abi.load().pf_transition_fwd(ctypes.byref(pack.struct), x2d.data_ptr(), x2d.stride(0),
+                                        out2d.data_ptr(), out2d.stride(0), rows, c, n_mult,
+                                        int(accumulate), code, ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def apb_pair_bias(pack: WeightPack, z: torch.Tensor, heads: int, out: torch.Tensor) -> None:
+    """out[h, r, s] (fp32) = linear_nobias_z(layernorm_z(z(r, s)))."""
+    require_cuda(z, out)
+    code = dtype_code(z)
+    n_r, n_c, c_z = z.shape
+    nbytes = _abi.workspace_bytes("pf_apb_pair_bias_workspace_size", n_r, n_c, c_z, heads, code)
+    ws = workspace(nbytes, z.device)
+    check(_abi.load().pf_apb_pair_bias(ctypes.byref(pack.struct), pair_view(z), n_r, n_c,
+                                       out.data_ptr(), out.stride(0), out.stride(1), c_z, heads,
+                                       code, ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def apb(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, z: Optional[torch.Tensor],
+        bias: Optional[torch.Tensor], heads: int, accumulate: bool) -> None:
+    """s_out (+)= AttentionPairBias(s_in, z) (bias from z when ``bias`` is None)."""
+    require_cuda(s_in, s_out, z, bias)
+    code = dtype_code(s_in)
+    n, c_s = s_in.shape
+    c_z = z.shape[-1] if z is not None else 0
+    if bias is not None and (bias.dtype != torch.float32 or not bias.is_contiguous()):
+        raise ValueError("apb bias must be a contiguous float32 [H, N, N] tensor")
+    nbytes = _abi.workspace_bytes("pf_apb_workspace_size", n, c_s, c_z, heads, code)
+    ws = workspace(nbytes, s_in.device)
+    zv = pair_view(z) if z is not None else PairView(None, 0, 0)
+    check(_abi.load().pf_apb_fwd(ctypes.byref(pack.struct), s_in.data_ptr(), s_out.data_ptr(), zv,
+                                 _ptr(bias), n, c_s, c_z, heads, int(accumulate), code,
+                                 ws.data_ptr(), ws.numel(), stream_ptr()))

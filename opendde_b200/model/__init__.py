@@ -1,0 +1,12 @@
+"""Module mirror of opendde.model (Pairformer pair stack only)."""
+from .pairformer import PairformerBlock, PairformerStack  # noqa: F401
+from .primitives import Linear, LinearNoBias, Transition  # noqa: F401
+from .transformer import AttentionPairBias  # noqa: F401
+from .triangular import (  # noqa: F401
+    LayerNorm,
+    OpenfoldLinear,
+    TriangleAttention,
+    TriangleMultiplicationIncoming,
+    TriangleMultiplicationOutgoing,
+    TriangleMultiplicativeUpdate,
+)

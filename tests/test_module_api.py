@@ -1,0 +1,43 @@
+"""Host-side behaviour of the drop-in modules (no GPU): names, errors, no CPU fallback."""
+import numpy as np
+import pytest
+import torch
+
+from golden_cases import GOLDEN_DIR, module_for
+from opendde_b200.model import PairformerBlock, PairformerStack, TriangleAttention, TriangleMultiplicationOutgoing
+
+
+@pytest.mark.parametrize("kind,fname", [("block", "block_n16.npz"), ("trimul_out", "trimul_out_n13.npz"),
+                                        ("triatt_start", "triatt_start_n13.npz"), ("apb", "apb_n13.npz")])
+def test_parameter_names_match_reference(kind, fname):
+    rec = np.load(f"{GOLDEN_DIR}/{fname}")
+    names = sorted(n for n, _ in module_for(kind).named_parameters())
+    assert names == list(rec["param_names"])
+
+
+def test_stack_state_dict_keys():
+    st = PairformerStack(n_blocks=2)
+    keys = set(st.state_dict())
+    assert "blocks.1.tri_att_end.mha.linear_g.weight" in keys
+    assert "blocks.0.attention_pair_bias.attention.linear_q.bias" in keys
+
+
+def test_invalid_kernel_strings_raise_reference_errors():
+    tm = TriangleMultiplicationOutgoing(c_z=16, c_hidden=16)
+    with pytest.raises(ValueError, match="triangle_multiplicative must be 'cuequivariance' or 'torch'"):
+        tm(torch.zeros(4, 4, 16), triangle_multiplicative="triton")
+    ta = TriangleAttention(16, 8, 2)
+    with pytest.raises(ValueError, match="Invalid triangle_attention"):
+        ta(torch.zeros(4, 4, 16), triangle_attention="bogus")
+    blk = PairformerBlock(c_z=32, c_s=0, c_hidden_mul=32, no_heads_pair=1)
+    with pytest.raises(ValueError):
+        blk(None, torch.zeros(4, 4, 32), torch.ones(4, 4), triangle_attention="x")
+
+
+def test_cpu_tensors_are_rejected_no_fallback():
+    tm = TriangleMultiplicationOutgoing(c_z=16, c_hidden=16)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        tm(torch.zeros(4, 4, 16))
+    blk = PairformerBlock(c_z=32, c_s=0, c_hidden_mul=32, no_heads_pair=1)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        blk(None, torch.zeros(4, 4, 32), torch.ones(4, 4))
