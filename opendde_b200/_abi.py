@@ -36,7 +36,7 @@ _STATUS_NAMES = {
 
 # Every symbol the header declares (checked by tests/test_abi_symbols.py).
 EXPORTED = (
-    "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path",
+    "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path", "pf_device_status",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
     "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
@@ -98,6 +98,7 @@ def load(path: str = LIB_PATH):
         "pf_last_error_string": ([], c_char_p),
         "pf_last_path": ([], c_char_p),
         "pf_set_option": ([c_int, c_int64], c_int),
+        "pf_device_status": ([POINTER(c_int), c_int], c_int),
         "pf_layernorm_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p], c_int),
         "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
@@ -139,6 +140,13 @@ def last_path() -> str:
 
 def set_force_simt(flag: bool) -> None:
     check(load().pf_set_option(PF_OPT_FORCE_SIMT, 1 if flag else 0))
+
+
+def device_status(clear: bool = False) -> int:
+    """Read (and optionally clear) the device status word; synchronises the device."""
+    v = c_int(0)
+    check(load().pf_device_status(ctypes.byref(v), 1 if clear else 0))
+    return int(v.value)
 
 
 def workspace_bytes(fn_name: str, *args) -> int:

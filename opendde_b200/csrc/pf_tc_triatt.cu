@@ -1,0 +1,794 @@
+// pf_tc_triatt.cu -- triangle attention (starting node; the ending node is the same code on
+// transposed views) on tcgen05 tensor cores. c = 128, H = 4, d = 32.
+//
+// Kernels (intermediates in the caller's workspace):
+//   k_triatt_maskprep : per row i, the log2-domain key bias inf*(m-1)*log2(e) (or -inf for keys
+//                       that do not exist), and a per-128-key-tile flag: no bias add needed /
+//                       add per element / skip the tile (every key masked while the row has a
+//                       fully valid key, so exp() underflows to exactly 0 in the reference too).
+//   k_triatt_proj     : TMA tile of 128 positions -> LayerNorm in place -> one UMMA chain into
+//                       512 TMEM columns: [q | k] (N=256) and [v | bias] (N=144). q is stored
+//                       pre-scaled by log2(e)/sqrt(d); v transposed (keys contiguous, f16) so the
+//                       P.V MMA reads it K-major; the triangle bias in log2 units.
+//   k_triatt_core     : one CTA per (row i, head h, 128 queries). Per 128-key tile: S = Q K^T
+//                       (UMMA, TMEM), softmax in registers (one thread per query, exp2), P in f16
+//                       to shared memory, then [o | l] = P [V^T ; 1]^T in one UMMA (the ones row
+//                       gives the row sum of exactly the f16 P used for o).
+//   k_triatt_out      : LN(z) -> gate logits (UMMA), o * sigmoid(gate) -> W_o (UMMA) -> residual.
+// Reference: opendde/model/triangular/triangular.py:648-706, layers.py:302-424.
+
+#include "pf_common.cuh"
+#include "pf_sm100.cuh"
+#include "pf_tc.h"
+#include "pf_tmap.h"
+
+namespace pf {
+namespace tc {
+using namespace sm100;
+
+namespace {
+
+constexpr int CH = 128, H = 4, D = 32, HD = 128, TILE = 128;
+constexpr float LOG2E = 1.4426950408889634f;
+
+enum TileFlag : uint8_t { TF_NOADD = 0, TF_ADD = 1, TF_SKIP = 2 };
+
+// ------------------------------------------------------------------ mask prep
+__global__ void k_triatt_maskprep(pf_mask_view m, int64_t n_keys, int64_t n_valid, float inf,
+                                  float* __restrict__ mb, int64_t ld_mb, uint8_t* __restrict__ flags,
+                                  int n_tiles) {
+  const int64_t i = blockIdx.x;
+  const int tid = threadIdx.x;  // 128 threads
+  __shared__ int s_any_full;
+  if (tid == 0) s_any_full = 0;
+  __syncthreads();
+  int any_full = 0;
+  for (int64_t k = tid; k < n_valid; k += 128) {
+    const float mv = m.ptr ? m.ptr[i * m.row_stride + k * m.col_stride] : 1.0f;
+    any_full |= (mv == 1.0f);
+  }
+  if (any_full) atomicOr(&s_any_full, 1);
+  __syncthreads();
+  const bool row_full = s_any_full != 0;
+  for (int kt = 0; kt < n_tiles; ++kt) {
+    const int64_t k = (int64_t)kt * 128 + tid;
+    float mv = 0.f;
+    bool exists = k < n_valid;
+    if (exists) mv = m.ptr ? m.ptr[i * m.row_stride + k * m.col_stride] : 1.0f;
+    mb[i * ld_mb + k] = exists ? inf * (mv - 1.0f) * LOG2E : -INFINITY;
+    const int all_one = __syncthreads_and(exists && mv == 1.0f);
+    const int all_zero = __syncthreads_and(!exists || mv == 0.0f);
+    if (tid == 0) flags[i * n_tiles + kt] = (all_zero && row_full) ? TF_SKIP : (all_one ? TF_NOADD : TF_ADD);
+  }
+}
+
+// LayerNorm of one row of a SW128 two-atom tile, in place (same as the trimul path).
+__device__ __forceinline__ void ln_row_inplace(uint8_t* tile, int row, const float* __restrict__ g,
+                                               const float* __restrict__ b) {
+  float v[CH];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 q = *reinterpret_cast<const uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7));
+    v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
+    v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
+    v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
+    v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) s += v[c];
+  const float mean = s * (1.0f / CH);
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const float d = v[c] - mean;
+    sq += d * d;
+  }
+  const float rstd = rsqrtf(sq * (1.0f / CH) + 1e-5f);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = j * 8 + e;
+      y[e] = (v[c] - mean) * rstd * __ldg(g + c) + __ldg(b + c);
+    }
+    uint4 q;
+    q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
+    q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
+    *reinterpret_cast<uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7)) = q;
+  }
+}
+
+// D (+)= A[128 x K=128] * B[n x 128]^T, SW128 two-atom operands.
+__device__ __forceinline__ void umma_k128(uint32_t d_tmem, uint32_t sA, uint32_t sB,
+                                          uint32_t b_atom_bytes, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
+    umma_f16(d_tmem, sdesc(sA + atom * 16384 + within, 1024, SWZ_128B),
+             sdesc(sB + atom * b_atom_bytes + within, 1024, SWZ_128B), idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// ------------------------------------------------------------------ projection
+struct ProjArgs {
+  int64_t n_rows, n_keys, tiles_per_row;
+  int64_t q_col0, n_q;
+  int want_qkv, want_bias;
+  __nv_bfloat16* q;   // [(i*H+h)*n_q + j][D]
+  __nv_bfloat16* k;   // [(i*H+h)*ld_keys + key][D]
+  __half* vt;         // [((i*H+h)*D + dd)*ld_keys + key]
+  __nv_bfloat16* bias;  // bias + h*b_hs + r*b_rs + s (log2 units)
+  int64_t ld_keys, b_hs, b_rs;
+  const float *ln_w, *ln_b;
+  float q_scale;
+  unsigned int* status;
+};
+
+constexpr uint32_t PB_ATOM = 400 * 128;               // 400 weight rows x 128 B
+constexpr uint32_t PROJ_SMEM = 32768 + 2 * PB_ATOM + 64;
+
+__global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUtensorMap tz,
+                                                     const __grid_constant__ CUtensorMap twq,
+                                                     const __grid_constant__ CUtensorMap twk,
+                                                     const __grid_constant__ CUtensorMap twv,
+                                                     const __grid_constant__ CUtensorMap twb,
+                                                     const ProjArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t sA = base, sB = base + 32768;
+  const uint32_t bar_load = base + 32768 + 2 * PB_ATOM, bar_mma = bar_load + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 32768 + 2 * PB_ATOM + 16);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t t = blockIdx.x;
+  const int64_t r = t / a.tiles_per_row;
+  const int64_t c0 = (t % a.tiles_per_row) * TILE;
+
+  if (tid == 0) {
+    mbar_init(bar_load, 1);
+    mbar_init(bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_load, 32768 + 2 * PB_ATOM);
+    tma_load_3d(sA, &tz, bar_load, 0, (int)c0, (int)r);
+    tma_load_3d(sA + 16384, &tz, bar_load, 64, (int)c0, (int)r);
+#pragma unroll
+    for (int at = 0; at < 2; ++at) {
+      const uint32_t b0 = sB + at * PB_ATOM;
+      tma_load_2d(b0, &twq, bar_load, at * 64, 0);
+      tma_load_2d(b0 + 128 * 128, &twk, bar_load, at * 64, 0);
+      tma_load_2d(b0 + 256 * 128, &twv, bar_load, at * 64, 0);
+      tma_load_2d(b0 + 384 * 128, &twb, bar_load, at * 64, 0);  // 16 rows, rows >= H read 0
+    }
+  }
+  mbar_wait(bar_load, 0, a.status);
+  ln_row_inplace(g, tid, a.ln_w, a.ln_b);
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem, sA, sB, PB_ATOM, idesc_f16(128, 256, true));                      // q | k
+    umma_k128(tmem + 256, sA, sB + 256 * 128, PB_ATOM, idesc_f16(128, 144, true));    // v | bias
+    umma_commit(bar_mma);
+  }
+  mbar_wait(bar_mma, 0, a.status);
+  tc_fence_after();
+
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const int64_t col = c0 + tid;
+  const bool valid = col < a.n_keys;
+  // q, k: 32 contiguous values per (head, position)
+#pragma unroll 1
+  for (int h = 0; h < H; ++h) {
+    uint32_t qv[32], kv[32];
+    tmem_ld32(tmem + lane_base + h * D, qv);
+    tmem_ld32(tmem + lane_base + 128 + h * D, kv);
+    tmem_ld_wait();
+    if (valid && a.want_qkv) {
+      const int64_t jq = col - a.q_col0;
+      if (jq >= 0 && jq < a.n_q) {
+        uint4* dq = reinterpret_cast<uint4*>(a.q + (((int64_t)r * H + h) * a.n_q + jq) * D);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          uint4 w;
+          w.x = pack_bf16(__uint_as_float(qv[e * 8 + 0]) * a.q_scale, __uint_as_float(qv[e * 8 + 1]) * a.q_scale);
+          w.y = pack_bf16(__uint_as_float(qv[e * 8 + 2]) * a.q_scale, __uint_as_float(qv[e * 8 + 3]) * a.q_scale);
+          w.z = pack_bf16(__uint_as_float(qv[e * 8 + 4]) * a.q_scale, __uint_as_float(qv[e * 8 + 5]) * a.q_scale);
+          w.w = pack_bf16(__uint_as_float(qv[e * 8 + 6]) * a.q_scale, __uint_as_float(qv[e * 8 + 7]) * a.q_scale);
+          dq[e] = w;
+        }
+      }
+      uint4* dk = reinterpret_cast<uint4*>(a.k + (((int64_t)r * H + h) * a.ld_keys + col) * D);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint4 w;
+        w.x = pack_bf16(__uint_as_float(kv[e * 8 + 0]), __uint_as_float(kv[e * 8 + 1]));
+        w.y = pack_bf16(__uint_as_float(kv[e * 8 + 2]), __uint_as_float(kv[e * 8 + 3]));
+        w.z = pack_bf16(__uint_as_float(kv[e * 8 + 4]), __uint_as_float(kv[e * 8 + 5]));
+        w.w = pack_bf16(__uint_as_float(kv[e * 8 + 6]), __uint_as_float(kv[e * 8 + 7]));
+        dk[e] = w;
+      }
+    }
+  }
+  // v transposed: vt[(i,h,dd)][key], 2-byte stores coalesced across the warp
+#pragma unroll 1
+  for (int h = 0; h < H; ++h) {
+    uint32_t vv[32];
+    tmem_ld32(tmem + lane_base + 256 + h * D, vv);
+    tmem_ld_wait();
+    if (valid && a.want_qkv) {
+      __half* dv = a.vt + (((int64_t)r * H + h) * D) * a.ld_keys + col;
+#pragma unroll
+      for (int dd = 0; dd < D; ++dd) dv[(int64_t)dd * a.ld_keys] = __float2half_rn(__uint_as_float(vv[dd]));
+    }
+  }
+  {
+    uint32_t bv[16];
+    tmem_ld16(tmem + lane_base + 384, bv);
+    tmem_ld_wait();
+    if (valid && a.want_bias) {
+#pragma unroll
+      for (int h = 0; h < H; ++h)
+        a.bias[h * a.b_hs + r * a.b_rs + col] = __float2bfloat16_rn(__uint_as_float(bv[h]) * LOG2E);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ core
+struct CoreArgs {
+  int64_t n_rows, n_q, n_tiles_k;
+  const float* mb;        // [n_rows][ld_mb] (log2 units)
+  int64_t ld_mb;
+  const uint8_t* flags;   // [n_rows][n_tiles_k]
+  __nv_bfloat16* o;       // [(i*n_q + j)][HD]
+  unsigned int* status;
+};
+
+// shared-memory map (offsets from the 1024-aligned base)
+constexpr uint32_t C_Q = 0;                 // 128 x 64 B (SW64)          8 KB
+constexpr uint32_t C_K = 8192;              // 128 x 64 B (SW64)          8 KB
+constexpr uint32_t C_VT = 16384;            // 2 atoms x 48 rows x 128 B  12 KB (rows 32..47 = [1;0])
+constexpr uint32_t C_VT_ATOM = 48 * 128;
+constexpr uint32_t C_BIAS = 16384 + 12288;  // 2 atoms x 128 rows x 128 B 32 KB   (offset 28672)
+constexpr uint32_t C_P = C_BIAS + 32768;    // 2 atoms x 128 rows x 128 B 32 KB   (offset 61440)
+constexpr uint32_t C_MB = C_P + 32768;      // 128 fp32                    512 B (offset 94208)
+constexpr uint32_t C_BAR = C_MB + 512;
+constexpr uint32_t CORE_SMEM = C_BAR + 64;
+static_assert(C_BIAS % 1024 == 0 && C_P % 1024 == 0 && C_VT_ATOM % 1024 == 0, "swizzle atoms need 1 KB alignment");
+
+__global__ void __launch_bounds__(160, 2) k_triatt_core(const __grid_constant__ CUtensorMap tq,
+                                                        const __grid_constant__ CUtensorMap tk,
+                                                        const __grid_constant__ CUtensorMap tvt,
+                                                        const __grid_constant__ CUtensorMap tb,
+                                                        const __grid_constant__ CUtensorMap tmb,
+                                                        const CoreArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t bar_q = base + C_BAR, bar_kv = bar_q + 8, bar_s = bar_q + 16, bar_p = bar_q + 24,
+                 bar_o = bar_q + 32;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + C_BAR + 48);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int64_t jt = blockIdx.x;                // query tile
+  const int h = blockIdx.y;
+  const int64_t i = blockIdx.z;
+  const int64_t j0 = jt * TILE;
+  const int ih = (int)(i * H + h);
+  const uint8_t* flags = a.flags + i * a.n_tiles_k;
+
+  if (tid == 128) {
+    mbar_init(bar_q, 1);
+    mbar_init(bar_kv, 1);
+    mbar_init(bar_s, 1);
+    mbar_init(bar_p, 4);
+    mbar_init(bar_o, 1);
+    fence_barrier_init();
+  }
+  if (warp == 4) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  if (tid < 128) {
+    // constant augmentation rows of the V^T operand: row 32 = 1.0 (f16), rows 33..47 = 0
+    for (int idx = tid; idx < 2 * 16 * 8; idx += 128) {
+      const int atom = idx >> 7, rr = 32 + ((idx >> 3) & 15), ch = idx & 7;
+      const uint32_t one2 = (rr == 32) ? 0x3C003C00u : 0u;
+      *reinterpret_cast<uint4*>(g + C_VT + atom * C_VT_ATOM + sw128_off(rr, ch)) =
+          make_uint4(one2, one2, one2, one2);
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_o = tmem + 128;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      // producer + MMA issuer (single thread, serialised per key tile)
+      mbar_arrive_expect_tx(bar_q, 128 * 64);
+      tma_load_3d(base + C_Q, &tq, bar_q, 0, (int)j0, ih);
+      bool ok = mbar_wait(bar_q, 0, a.status);
+      uint32_t it = 0;
+      for (int64_t kt = 0; kt < a.n_tiles_k && ok; ++kt) {
+        if (flags[kt] == TF_SKIP) continue;
+        const int k0 = (int)(kt * TILE);
+        mbar_arrive_expect_tx(bar_kv, 8192 + 2 * 4096 + 32768 + 512);
+        tma_load_3d(base + C_K, &tk, bar_kv, 0, k0, ih);
+        tma_load_3d(base + C_VT, &tvt, bar_kv, k0, 0, ih);
+        tma_load_3d(base + C_VT + C_VT_ATOM, &tvt, bar_kv, k0 + 64, 0, ih);
+        tma_load_3d(base + C_BIAS, &tb, bar_kv, k0, (int)j0, h);
+        tma_load_3d(base + C_BIAS + 16384, &tb, bar_kv, k0 + 64, (int)j0, h);
+        tma_load_2d(base + C_MB, &tmb, bar_kv, k0, (int)i);
+        ok = mbar_wait(bar_kv, it & 1, a.status);
+        tc_fence_after();
+        // S = Q K^T : M=128, N=128, K=32 (two K=16 steps inside the 64 B swizzle row)
+        constexpr uint32_t id_s = idesc_f16(128, 128, true);
+        umma_f16(t_s, sdesc(base + C_Q, 512, SWZ_64B), sdesc(base + C_K, 512, SWZ_64B), id_s, 0u);
+        umma_f16(t_s, sdesc(base + C_Q + 32, 512, SWZ_64B), sdesc(base + C_K + 32, 512, SWZ_64B), id_s, 1u);
+        umma_commit(bar_s);
+        ok = ok && mbar_wait(bar_p, it & 1, a.status);
+        tc_fence_after();
+        // [o | l] = P [V^T ; 1]^T : M=128, N=48, K=128 (f16 operands)
+        constexpr uint32_t id_o = idesc_f16(128, 48, false);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
+          umma_f16(t_o, sdesc(base + C_P + atom * 16384 + within, 1024, SWZ_128B),
+                   sdesc(base + C_VT + atom * C_VT_ATOM + within, 1024, SWZ_128B), id_o, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_o);
+        ok = ok && mbar_wait(bar_o, it & 1, a.status);
+        ++it;
+      }
+    }
+  } else {
+    // softmax warps: thread = query row j0 + tid, TMEM lane quarter = warp
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    float m_run = -INFINITY, l_run = 0.f;
+    float acc[D];
+#pragma unroll
+    for (int e = 0; e < D; ++e) acc[e] = 0.f;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int64_t kt = 0; kt < a.n_tiles_k && ok; ++kt) {
+      const uint8_t fl = flags[kt];
+      if (fl == TF_SKIP) continue;
+      ok = mbar_wait(bar_s, it & 1, a.status);
+      tc_fence_after();
+      float s[TILE];
+#pragma unroll
+      for (int cc = 0; cc < TILE; cc += 32) {
+        uint32_t v[32];
+        tmem_ld32(t_s + lane_base + cc, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) s[cc + e] = __uint_as_float(v[e]);
+      }
+      // + triangle bias (bf16, log2 units), + mask bias where needed
+      const float* mbs = reinterpret_cast<const float*>(g + C_MB);
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const uint4 q = *reinterpret_cast<const uint4*>(g + C_BIAS + (ch >> 3) * 16384 + sw128_off(tid, ch & 7));
+        const int c = ch * 8;
+        s[c + 0] += bf16lo(q.x); s[c + 1] += bf16hi(q.x);
+        s[c + 2] += bf16lo(q.y); s[c + 3] += bf16hi(q.y);
+        s[c + 4] += bf16lo(q.z); s[c + 5] += bf16hi(q.z);
+        s[c + 6] += bf16lo(q.w); s[c + 7] += bf16hi(q.w);
+      }
+      if (fl == TF_ADD) {
+#pragma unroll
+        for (int c = 0; c < TILE; ++c) s[c] += mbs[c];
+      }
+#pragma unroll
+      for (int c = 0; c < TILE; ++c) tmax = fmaxf(tmax, s[c]);
+      const float m_new = fmaxf(m_run, tmax);
+      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+      const float alpha = ex2_approx(m_run - m_use);
+      // P = exp2(s - m) in f16, K-major SW128 rows of the A operand
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        const int c = ch * 8;
+        uint4 w;
+        w.x = pack_f16(ex2_approx(s[c + 0] - m_use), ex2_approx(s[c + 1] - m_use));
+        w.y = pack_f16(ex2_approx(s[c + 2] - m_use), ex2_approx(s[c + 3] - m_use));
+        w.z = pack_f16(ex2_approx(s[c + 4] - m_use), ex2_approx(s[c + 5] - m_use));
+        w.w = pack_f16(ex2_approx(s[c + 6] - m_use), ex2_approx(s[c + 7] - m_use));
+        *reinterpret_cast<uint4*>(g + C_P + (ch >> 3) * 16384 + sw128_off(tid, ch & 7)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_p);
+      ok = ok && mbar_wait(bar_o, it & 1, a.status);
+      tc_fence_after();
+      uint32_t ov[32], lv[16];
+      tmem_ld32(t_o + lane_base, ov);
+      tmem_ld16(t_o + lane_base + 32, lv);
+      tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < D; ++e) acc[e] = acc[e] * alpha + __uint_as_float(ov[e]);
+      l_run = l_run * alpha + __uint_as_float(lv[0]);
+      m_run = m_new;
+      ++it;
+    }
+    const int64_t j = j0 + tid;
+    if (j < a.n_q) {
+      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(a.o + ((int64_t)i * a.n_q + j) * HD + h * D);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        uint4 w;
+        w.x = pack_bf16(acc[e * 8 + 0] * inv, acc[e * 8 + 1] * inv);
+        w.y = pack_bf16(acc[e * 8 + 2] * inv, acc[e * 8 + 3] * inv);
+        w.z = pack_bf16(acc[e * 8 + 4] * inv, acc[e * 8 + 5] * inv);
+        w.w = pack_bf16(acc[e * 8 + 6] * inv, acc[e * 8 + 7] * inv);
+        dst[e] = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ output
+struct OutArgs {
+  int64_t n_rows, n_q, tiles_per_row, q_col0;
+  __nv_bfloat16* zo;
+  int64_t zo_rs, zo_cs;
+  const float *ln_w, *ln_b;
+  int accumulate;
+  unsigned int* status;
+};
+constexpr uint32_t OUT_SMEM = 4 * 32768 + 64;
+
+__global__ void __launch_bounds__(128) k_triatt_out(const __grid_constant__ CUtensorMap tz,
+                                                    const __grid_constant__ CUtensorMap to,
+                                                    const __grid_constant__ CUtensorMap twg,
+                                                    const __grid_constant__ CUtensorMap two,
+                                                    const OutArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t sZ = base, sO = base + 32768, sBG = base + 65536, sBO = base + 98304;
+  const uint32_t bar_load = base + 131072, bar_m1 = bar_load + 8, bar_m2 = bar_load + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 131072 + 32);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t t = blockIdx.x;
+  const int64_t i = t / a.tiles_per_row;
+  const int64_t j0 = (t % a.tiles_per_row) * TILE;
+  const int64_t j = j0 + tid;
+  const bool valid = j < a.n_q;
+
+  if (tid == 0) {
+    mbar_init(bar_load, 1);
+    mbar_init(bar_m1, 1);
+    mbar_init(bar_m2, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_load, 4 * 32768);
+    tma_load_3d(sZ, &tz, bar_load, 0, (int)(a.q_col0 + j0), (int)i);
+    tma_load_3d(sZ + 16384, &tz, bar_load, 64, (int)(a.q_col0 + j0), (int)i);
+    tma_load_3d(sO, &to, bar_load, 0, (int)j0, (int)i);
+    tma_load_3d(sO + 16384, &to, bar_load, 64, (int)j0, (int)i);
+    tma_load_2d(sBG, &twg, bar_load, 0, 0);
+    tma_load_2d(sBG + 16384, &twg, bar_load, 64, 0);
+    tma_load_2d(sBO, &two, bar_load, 0, 0);
+    tma_load_2d(sBO + 16384, &two, bar_load, 64, 0);
+  }
+  mbar_wait(bar_load, 0, a.status);
+  ln_row_inplace(g, tid, a.ln_w, a.ln_b);
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem + 128, sZ, sBG, 16384, idesc_f16(128, 128, true));
+    umma_commit(bar_m1);
+  }
+  mbar_wait(bar_m1, 0, a.status);
+  tc_fence_after();
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  // o * sigmoid(gate), in place in the o tile (row tid)
+#pragma unroll 1
+  for (int cc = 0; cc < HD; cc += 32) {
+    uint32_t gv[32];
+    tmem_ld32(tmem + lane_base + 128 + cc, gv);
+    tmem_ld_wait();
+#pragma unroll
+    for (int q4 = 0; q4 < 4; ++q4) {
+      const int ch = (cc >> 3) + q4;  // 16-byte chunk index 0..15
+      uint4* p = reinterpret_cast<uint4*>(g + 32768 + (ch >> 3) * 16384 + sw128_off(tid, ch & 7));
+      uint4 v = *p;
+      const float* gg = reinterpret_cast<const float*>(gv) + q4 * 8;
+      v.x = pack_bf16(bf16lo(v.x) * fast_sigmoid(gg[0]), bf16hi(v.x) * fast_sigmoid(gg[1]));
+      v.y = pack_bf16(bf16lo(v.y) * fast_sigmoid(gg[2]), bf16hi(v.y) * fast_sigmoid(gg[3]));
+      v.z = pack_bf16(bf16lo(v.z) * fast_sigmoid(gg[4]), bf16hi(v.z) * fast_sigmoid(gg[5]));
+      v.w = pack_bf16(bf16lo(v.w) * fast_sigmoid(gg[6]), bf16hi(v.w) * fast_sigmoid(gg[7]));
+      *p = v;
+    }
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem, sO, sBO, 16384, idesc_f16(128, 128, true));
+    umma_commit(bar_m2);
+  }
+  mbar_wait(bar_m2, 0, a.status);
+  tc_fence_after();
+  __nv_bfloat16* zp = a.zo + i * a.zo_rs + (valid ? j : 0) * a.zo_cs;
+#pragma unroll 1
+  for (int cc = 0; cc < CH; cc += 32) {
+    uint32_t ov[32];
+    tmem_ld32(tmem + lane_base + cc, ov);
+    tmem_ld_wait();
+    if (valid) {
+      uint4* dst = reinterpret_cast<uint4*>(zp + cc);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) u[k] = __uint_as_float(ov[e * 8 + k]);
+        if (a.accumulate) {
+          const uint4 old = dst[e];
+          u[0] += bf16lo(old.x); u[1] += bf16hi(old.x); u[2] += bf16lo(old.y); u[3] += bf16hi(old.y);
+          u[4] += bf16lo(old.z); u[5] += bf16hi(old.z); u[6] += bf16lo(old.w); u[7] += bf16hi(old.w);
+        }
+        uint4 w;
+        w.x = pack_bf16(u[0], u[1]); w.y = pack_bf16(u[2], u[3]);
+        w.z = pack_bf16(u[4], u[5]); w.w = pack_bf16(u[6], u[7]);
+        dst[e] = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ host
+int pair_tmap(CUtensorMap* m, const void* ptr, int64_t rs, int64_t cs, int64_t n_rows, int64_t n_cols) {
+  if (rs % 8 || cs % 8)
+    return fail(PF_EINVAL_SHAPE, "bf16 pair views need row/col strides that are multiples of 8 elements");
+  const uint64_t dims[3] = {(uint64_t)CH, (uint64_t)n_cols, (uint64_t)n_rows};
+  const uint64_t str[2] = {(uint64_t)cs * 2, (uint64_t)rs * 2};
+  const uint32_t box[3] = {64, (uint32_t)TILE, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, ptr, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int weight_tmap(CUtensorMap* m, const void* w, int rows, int cols, int box_rows) {
+  const uint64_t dims[2] = {(uint64_t)cols, (uint64_t)rows};
+  const uint64_t str[1] = {(uint64_t)cols * 2};
+  const uint32_t box[2] = {64, (uint32_t)box_rows};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <class K>
+int set_smem(K kernel, uint32_t bytes) {
+  PF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return PF_OK;
+}
+
+int ensure_attrs() {
+  static bool done = false;
+  if (!done) {
+    PF_TRY(set_smem(k_triatt_proj, PROJ_SMEM + 1024));
+    PF_TRY(set_smem(k_triatt_core, CORE_SMEM + 1024));
+    PF_TRY(set_smem(k_triatt_out, OUT_SMEM + 1024));
+    done = true;
+  }
+  return PF_OK;
+}
+
+struct TriattWs {
+  __nv_bfloat16 *q, *k, *bias, *o;
+  __half* vt;
+  float* mb;
+  uint8_t* flags;
+  int64_t ld_keys, ld_mb, n_tiles_k;
+};
+
+void triatt_plan(Arena& ar, int64_t n_rows, int64_t n_keys, int64_t n_q, bool own_bias, TriattWs& w) {
+  w.ld_keys = (n_keys + 7) / 8 * 8;
+  w.n_tiles_k = (n_keys + TILE - 1) / TILE;
+  w.ld_mb = w.n_tiles_k * TILE;
+  w.q = ar.take<__nv_bfloat16>((size_t)n_rows * H * n_q * D);
+  w.k = ar.take<__nv_bfloat16>((size_t)n_rows * H * w.ld_keys * D);
+  w.vt = ar.take<__half>((size_t)n_rows * H * D * w.ld_keys);
+  w.bias = own_bias ? ar.take<__nv_bfloat16>((size_t)H * n_q * w.ld_keys) : nullptr;
+  w.o = ar.take<__nv_bfloat16>((size_t)n_rows * n_q * HD);
+  w.mb = ar.take<float>((size_t)n_rows * w.ld_mb);
+  w.flags = ar.take<uint8_t>((size_t)n_rows * w.n_tiles_k);
+}
+
+int launch_proj(const pf_triatt_params* p, const void* zptr, int64_t rs, int64_t cs, int64_t n_rows,
+                int64_t n_cols, ProjArgs pa, cudaStream_t st) {
+  CUtensorMap tz, twq, twk, twv, twb;
+  PF_TRY(pair_tmap(&tz, zptr, rs, cs, n_rows, n_cols));
+  PF_TRY(weight_tmap(&twq, p->w_q, HD, CH, 128));
+  PF_TRY(weight_tmap(&twk, p->w_k, HD, CH, 128));
+  PF_TRY(weight_tmap(&twv, p->w_v, HD, CH, 128));
+  PF_TRY(weight_tmap(&twb, p->w_bias, H, CH, 16));
+  pa.tiles_per_row = (n_cols + TILE - 1) / TILE;
+  const int64_t nt = n_rows * pa.tiles_per_row;
+  if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "triatt projection grid too large");
+  k_triatt_proj<<<(unsigned)nt, 128, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, pa);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+}  // namespace
+
+bool triatt_bias_supported(int c, int heads) { return c == CH && heads == H; }
+bool triatt_supported(int c, int heads, int d) { return c == CH && heads == H && d == D; }
+
+size_t triatt_ws_bytes(int64_t n_rows, int64_t n_keys, int64_t n_q, int, int, int) {
+  Arena ar(nullptr, 0);
+  TriattWs w;
+  triatt_plan(ar, n_rows, n_keys, n_q, true, w);
+  return ar.used;
+}
+
+int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols, void* bias,
+                int64_t hs, int64_t rs, int, int, cudaStream_t st) {
+  PF_TRY(ensure_attrs());
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  ProjArgs pa{};
+  pa.n_rows = n_rows;
+  pa.n_keys = n_cols;
+  pa.q_col0 = 0;
+  pa.n_q = 0;
+  pa.want_qkv = 0;
+  pa.want_bias = 1;
+  pa.bias = (__nv_bfloat16*)bias;
+  pa.b_hs = hs;
+  pa.b_rs = rs;
+  pa.ln_w = p->ln_w;
+  pa.ln_b = p->ln_b;
+  pa.status = status;
+  return launch_proj(p, z.ptr, z.row_stride, z.col_stride, n_rows, n_cols, pa, st);
+}
+
+int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias, int64_t b_hs,
+           int64_t b_rs, pf_pair_view zo, int64_t n_rows, int64_t n_keys, int64_t n_valid, int64_t q_col0,
+           int64_t n_q, int, int, int, float inf, int acc, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  TriattWs w;
+  triatt_plan(ar, n_rows, n_keys, n_q, bias == nullptr, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "triatt workspace too small");
+  if (zo.row_stride % 8 || zo.col_stride % 8 || ((uintptr_t)zo.ptr) % 16)
+    return fail(PF_EINVAL_SHAPE, "bf16 output view must be 16-byte aligned with strides multiple of 8");
+  if (bias != nullptr && (b_hs % 8 || b_rs % 8 || ((uintptr_t)bias) % 16))
+    return fail(PF_EINVAL_SHAPE, "bias buffer must be 16-byte aligned with strides multiple of 8");
+  if (n_rows * H > 0x7fffffffll || w.n_tiles_k > 0x7fffffffll)
+    return fail(PF_EUNSUPPORTED, "triatt problem too large");
+  PF_TRY(ensure_attrs());
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  // 0. mask bias + tile flags
+  k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags,
+                                                      (int)w.n_tiles_k);
+  PF_CHECK_LAUNCH();
+  // 1. projections (+ own bias in the square single-device case)
+  ProjArgs pa{};
+  pa.n_rows = n_rows;
+  pa.n_keys = n_keys;
+  pa.q_col0 = q_col0;
+  pa.n_q = n_q;
+  pa.want_qkv = 1;
+  pa.want_bias = bias == nullptr;
+  pa.q = w.q;
+  pa.k = w.k;
+  pa.vt = w.vt;
+  pa.bias = w.bias;
+  pa.ld_keys = w.ld_keys;
+  pa.b_hs = (int64_t)n_q * w.ld_keys;
+  pa.b_rs = w.ld_keys;
+  pa.ln_w = p->ln_w;
+  pa.ln_b = p->ln_b;
+  pa.q_scale = LOG2E / sqrtf((float)D);
+  pa.status = status;
+  PF_TRY(launch_proj(p, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys, pa, st));
+  // 2. attention core
+  const void* bptr = bias ? bias : (const void*)w.bias;
+  const int64_t bhs = bias ? b_hs : pa.b_hs, brs = bias ? b_rs : pa.b_rs;
+  CUtensorMap tq, tk, tvt, tb, tmb;
+  {
+    const uint64_t dq[3] = {(uint64_t)D, (uint64_t)n_q, (uint64_t)(n_rows * H)};
+    const uint64_t sq[2] = {(uint64_t)D * 2, (uint64_t)n_q * D * 2};
+    const uint32_t bq[3] = {D, TILE, 1};
+    PF_TRY(make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_64B));
+    const uint64_t dk[3] = {(uint64_t)D, (uint64_t)n_keys, (uint64_t)(n_rows * H)};
+    const uint64_t sk[2] = {(uint64_t)D * 2, (uint64_t)w.ld_keys * D * 2};
+    PF_TRY(make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.k, dk, sk, bq, CU_TENSOR_MAP_SWIZZLE_64B));
+    const uint64_t dv[3] = {(uint64_t)n_keys, (uint64_t)D, (uint64_t)(n_rows * H)};
+    const uint64_t sv[2] = {(uint64_t)w.ld_keys * 2, (uint64_t)D * w.ld_keys * 2};
+    const uint32_t bv[3] = {64, D, 1};
+    PF_TRY(make_tmap(&tvt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.vt, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t db[3] = {(uint64_t)n_keys, (uint64_t)n_q, (uint64_t)H};
+    const uint64_t sb[2] = {(uint64_t)brs * 2, (uint64_t)bhs * 2};
+    const uint32_t bb[3] = {64, TILE, 1};
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bptr, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t dm[2] = {(uint64_t)w.ld_mb, (uint64_t)n_rows};
+    const uint64_t sm[1] = {(uint64_t)w.ld_mb * 4};
+    const uint32_t bm[2] = {TILE, 1};
+    PF_TRY(make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w.mb, dm, sm, bm, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
+  CoreArgs ca{n_rows, n_q, w.n_tiles_k, w.mb, w.ld_mb, w.flags, w.o, status};
+  dim3 grid((unsigned)((n_q + TILE - 1) / TILE), H, (unsigned)n_rows);
+  if (n_rows > 65535) return fail(PF_EUNSUPPORTED, "triatt: more than 65535 rows per call");
+  k_triatt_core<<<grid, 160, CORE_SMEM + 1024, st>>>(tq, tk, tvt, tb, tmb, ca);
+  PF_CHECK_LAUNCH();
+  // 3. gate, output projection, residual
+  CUtensorMap tz, to, twg, two;
+  PF_TRY(pair_tmap(&tz, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys));
+  {
+    const uint64_t d3[3] = {(uint64_t)HD, (uint64_t)n_q, (uint64_t)n_rows};
+    const uint64_t s3[2] = {(uint64_t)HD * 2, (uint64_t)n_q * HD * 2};
+    const uint32_t b3[3] = {64, TILE, 1};
+    PF_TRY(make_tmap(&to, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.o, d3, s3, b3, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  PF_TRY(weight_tmap(&twg, p->w_g, HD, CH, 128));
+  PF_TRY(weight_tmap(&two, p->w_o, CH, HD, 128));
+  OutArgs oa{};
+  oa.n_rows = n_rows;
+  oa.n_q = n_q;
+  oa.tiles_per_row = (n_q + TILE - 1) / TILE;
+  oa.q_col0 = q_col0;
+  oa.zo = (__nv_bfloat16*)zo.ptr;
+  oa.zo_rs = zo.row_stride;
+  oa.zo_cs = zo.col_stride;
+  oa.ln_w = p->ln_w;
+  oa.ln_b = p->ln_b;
+  oa.accumulate = acc;
+  oa.status = status;
+  const int64_t nto = n_rows * oa.tiles_per_row;
+  k_triatt_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tz, to, twg, two, oa);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+}  // namespace tc
+}  // namespace pf

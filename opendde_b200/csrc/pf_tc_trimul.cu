@@ -1,0 +1,588 @@
+// pf_tc_trimul.cu -- triangle multiplicative update on tcgen05 tensor cores (bf16 in,
+// fp32 accumulate), c_z = c_h = 128.
+//
+// Three kernels, intermediates in the caller's workspace (bf16):
+//   1. k_trimul_proj : a 128-position tile of a view is TMA-loaded (128B swizzle), LayerNorm'd
+//      in place in shared memory, multiplied by [W_p; W_g] (one 128x256x128 UMMA chain into
+//      TMEM) and written channel-major as a(ch, r, k) = mask * sigmoid(g) * p. Channel-major
+//      rows are exactly the K-major operands of the contraction, so neither the incoming
+//      direction nor the ending node needs a physical transpose.
+//   2. k_trimul_bgemm: x[ch] = a[ch] * b[ch]^T for every channel: 128x256 output tiles, a
+//      4-stage TMA -> UMMA pipeline (one producer thread, one MMA thread, 4 epilogue warps
+//      reading the TMEM accumulator), bf16 output x[ch][i][j].
+//   3. k_trimul_out  : per 128 output positions, LN_out over the 128 channels of x (read
+//      channel-major, coalesced), LN_in of the gate source tile, two chained 128x128x128 UMMAs
+//      (W_g then W_z, sharing one A buffer), epilogue zo (+)= (W_z x) * sigmoid(W_g z).
+// Reference: opendde/model/triangular/triangular.py:530-567 (maths), :112-139 (orientation).
+
+#include "pf_common.cuh"
+#include "pf_sm100.cuh"
+#include "pf_tc.h"
+#include "pf_tmap.h"
+
+namespace pf {
+namespace tc {
+using namespace sm100;
+
+namespace {
+
+constexpr int CH = 128;    // c_z == c_h on this path
+constexpr int TILE = 128;  // positions per projection / output CTA
+
+// LayerNorm of row `row` of a K-major SW128 tile holding 128 bf16 channels (two 64-channel
+// atoms of 16 KB), in place. Stats in fp32 (two-pass, biased variance, eps inside sqrt).
+__device__ __forceinline__ void ln_row_inplace_sw128(uint8_t* tile, int row, const float* __restrict__ g,
+                                                     const float* __restrict__ b, float eps) {
+  float v[CH];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const uint4 q = *reinterpret_cast<const uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7));
+    v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
+    v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
+    v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
+    v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) s += v[c];
+  const float mean = s * (1.0f / CH);
+  float sq = 0.f;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const float d = v[c] - mean;
+    sq += d * d;
+  }
+  const float rstd = rsqrtf(sq * (1.0f / CH) + eps);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int c = j * 8 + e;
+      y[e] = (v[c] - mean) * rstd * __ldg(g + c) + __ldg(b + c);
+    }
+    uint4 q;
+    q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
+    q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
+    *reinterpret_cast<uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7)) = q;
+  }
+}
+
+// Issue the 8 K-steps (K = 128) of D = A[128 x 128] * B[n x 128]^T with SW128 K-major tiles
+// stored as two 64-channel atoms (A atom stride 16 KB, B atom stride b_atom_bytes).
+__device__ __forceinline__ void umma_k128(uint32_t d_tmem, uint32_t sA, uint32_t sB,
+                                          uint32_t b_atom_bytes, uint32_t idesc) {
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
+    const uint64_t ad = sdesc(sA + atom * 16384 + within, 1024, SWZ_128B);
+    const uint64_t bd = sdesc(sB + atom * b_atom_bytes + within, 1024, SWZ_128B);
+    umma_f16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
+  }
+}
+
+// ------------------------------------------------------------------ kernel 1: projections
+struct ProjSide {
+  int64_t n_rows, n_cols;
+  pf_mask_view mask;
+  __nv_bfloat16* out;  // channel-major [CH][n_rows][ld]
+  int64_t ch_stride;
+  int64_t tiles_per_row;
+  int64_t ntiles;
+};
+struct ProjArgs {
+  ProjSide side[2];
+  int64_t ld;
+  const float* ln_w;
+  const float* ln_b;
+  unsigned int* status;
+};
+
+constexpr uint32_t PROJ_SMEM = 32768 + 65536 + 64;
+
+__global__ void __launch_bounds__(128) k_trimul_proj(const __grid_constant__ CUtensorMap tz0,
+                                                     const __grid_constant__ CUtensorMap tz1,
+                                                     const __grid_constant__ CUtensorMap tw0p,
+                                                     const __grid_constant__ CUtensorMap tw0g,
+                                                     const __grid_constant__ CUtensorMap tw1p,
+                                                     const __grid_constant__ CUtensorMap tw1g,
+                                                     const ProjArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const int which = blockIdx.x & 1;
+  const int64_t t = blockIdx.x >> 1;
+  const ProjSide& sd = args.side[which];
+  if (t >= sd.ntiles) return;
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t sA = base, sB = base + 32768;
+  const uint32_t bar_load = base + 98304, bar_mma = bar_load + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 98304 + 16);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t r = t / sd.tiles_per_row;
+  const int64_t c0 = (t % sd.tiles_per_row) * TILE;
+  const CUtensorMap* tz = which ? &tz1 : &tz0;
+  const CUtensorMap* twp = which ? &tw1p : &tw0p;
+  const CUtensorMap* twg = which ? &tw1g : &tw0g;
+
+  if (tid == 0) {
+    mbar_init(bar_load, 1);
+    mbar_init(bar_mma, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_load, 32768 + 65536);
+    tma_load_3d(sA, tz, bar_load, 0, (int)c0, (int)r);
+    tma_load_3d(sA + 16384, tz, bar_load, 64, (int)c0, (int)r);
+    tma_load_2d(sB, twp, bar_load, 0, 0);              // atom 0: rows 0..127 = W_p
+    tma_load_2d(sB + 16384, twg, bar_load, 0, 0);      //         rows 128..255 = W_g
+    tma_load_2d(sB + 32768, twp, bar_load, 64, 0);     // atom 1
+    tma_load_2d(sB + 49152, twg, bar_load, 64, 0);
+  }
+  mbar_wait(bar_load, 0, args.status);
+  ln_row_inplace_sw128(g, tid, args.ln_w, args.ln_b, 1e-5f);
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem, sA, sB, 32768, idesc_f16(128, 256, true));
+    umma_commit(bar_mma);
+  }
+  mbar_wait(bar_mma, 0, args.status);
+  tc_fence_after();
+
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  const int64_t col = c0 + tid;
+  const bool valid = col < sd.n_cols;
+  float m = 0.f;
+  if (valid) m = sd.mask.ptr ? sd.mask.ptr[r * sd.mask.row_stride + col * sd.mask.col_stride] : 1.f;
+  __nv_bfloat16* outp = sd.out + r * args.ld + col;
+#pragma unroll 1
+  for (int cc = 0; cc < CH; cc += 32) {
+    uint32_t pv[32], gv[32];
+    tmem_ld32(tmem + lane_base + cc, pv);
+    tmem_ld32(tmem + lane_base + 128 + cc, gv);
+    tmem_ld_wait();
+    if (valid) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        // reference order: mask * sigmoid(g) * p  (triangular.py:539-544)
+        const float v = m * fast_sigmoid(__uint_as_float(gv[e])) * __uint_as_float(pv[e]);
+        outp[(int64_t)(cc + e) * sd.ch_stride] = __float2bfloat16_rn(v);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ kernel 2: contraction
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr uint32_t A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t GEMM_SMEM = STAGES * STAGE_BYTES + 256;
+
+struct GemmArgs {
+  int M, N, K;
+  __nv_bfloat16* out;
+  int64_t ldo;
+  int64_t out_bstride;
+  unsigned int* status;
+};
+
+__global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__ CUtensorMap ta,
+                                                         const __grid_constant__ CUtensorMap tb,
+                                                         const GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t bars = base + STAGES * STAGE_BYTES;
+  // full[s] at bars + 8s, empty[s] at bars + 64 + 8s, tmem_full at bars + 128
+  const uint32_t bar_tmem_full = bars + 128;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + STAGES * STAGE_BYTES + 192);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
+  const int nk = (args.K + BK - 1) / BK;
+
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bars + 8 * s, 1);
+      mbar_init(bars + 64 + 8 * s, 1);
+    }
+    mbar_init(bar_tmem_full, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&ta);
+    tma_prefetch_desc(&tb);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0 && lane == 0) {
+    // TMA producer
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES, u = kb / STAGES;
+      if (u > 0) mbar_wait(bars + 64 + 8 * s, (u - 1) & 1, args.status);
+      const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
+      mbar_arrive_expect_tx(bars + 8 * s, STAGE_BYTES);
+      tma_load_3d(sa, &ta, bars + 8 * s, kb * BK, m0, bz);
+      tma_load_3d(sb, &tb, bars + 8 * s, kb * BK, n0, bz);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // MMA issuer
+    constexpr uint32_t idesc = idesc_f16(BM, BN, true);
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % STAGES, u = kb / STAGES;
+      mbar_wait(bars + 8 * s, u & 1, args.status);
+      tc_fence_after();
+      const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+      for (int kk = 0; kk < BK / 16; ++kk) {
+        const uint64_t ad = sdesc(sa + kk * 32, 1024, SWZ_128B);
+        const uint64_t bd = sdesc(sb + kk * 32, 1024, SWZ_128B);
+        umma_f16(tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(bars + 64 + 8 * s);  // frees the stage when these MMAs finish
+    }
+    umma_commit(bar_tmem_full);
+  } else if (warp >= 2) {
+    // epilogue: TMEM -> bf16 -> global
+    mbar_wait(bar_tmem_full, 0, args.status);
+    tc_fence_after();
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const int gm = m0 + row;
+    __nv_bfloat16* orow = args.out + (int64_t)bz * args.out_bstride + (int64_t)gm * args.ldo;
+#pragma unroll 1
+    for (int cc = 0; cc < BN; cc += 32) {
+      uint32_t v[32];
+      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cc, v);
+      tmem_ld_wait();
+      const int gn = n0 + cc;
+      if (gm < args.M && gn < args.N) {
+        if (gn + 32 <= args.N) {
+          uint4* dst = reinterpret_cast<uint4*>(orow + gn);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(v[e * 8 + 0]), __uint_as_float(v[e * 8 + 1]));
+            w.y = pack_bf16(__uint_as_float(v[e * 8 + 2]), __uint_as_float(v[e * 8 + 3]));
+            w.z = pack_bf16(__uint_as_float(v[e * 8 + 4]), __uint_as_float(v[e * 8 + 5]));
+            w.w = pack_bf16(__uint_as_float(v[e * 8 + 6]), __uint_as_float(v[e * 8 + 7]));
+            dst[e] = w;
+          }
+        } else {
+          for (int e = 0; e < 32 && gn + e < args.N; ++e) orow[gn + e] = __float2bfloat16_rn(__uint_as_float(v[e]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ kernel 3: output
+struct OutArgs {
+  const __nv_bfloat16* x;  // [CH][n_i][ldx]
+  int64_t ldx, x_ch_stride;
+  __nv_bfloat16* zo;
+  int64_t zo_rs, zo_cs;
+  int64_t n_i, n_j, tiles_per_row;
+  const float *ln_in_w, *ln_in_b, *ln_out_w, *ln_out_b;
+  int accumulate;
+  unsigned int* status;
+};
+
+constexpr uint32_t OUT_SMEM = 3 * 32768 + 64;
+
+__global__ void __launch_bounds__(128) k_trimul_out(const __grid_constant__ CUtensorMap tzg,
+                                                    const __grid_constant__ CUtensorMap twz,
+                                                    const __grid_constant__ CUtensorMap twg,
+                                                    const OutArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* g = smem_raw + (base - raw);
+  const uint32_t sA = base, sBG = base + 32768, sBZ = base + 65536;
+  const uint32_t bar_load = base + 98304, bar_m1 = bar_load + 8, bar_m2 = bar_load + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 98304 + 32);
+  const int tid = threadIdx.x, warp = tid >> 5;
+  const int64_t t = blockIdx.x;
+  const int64_t i = t / args.tiles_per_row;
+  const int64_t j0 = (t % args.tiles_per_row) * TILE;
+  const int64_t j = j0 + tid;
+  const bool valid = j < args.n_j;
+
+  if (tid == 0) {
+    mbar_init(bar_load, 1);
+    mbar_init(bar_m1, 1);
+    mbar_init(bar_m2, 1);
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    mbar_arrive_expect_tx(bar_load, 3 * 32768);
+    tma_load_3d(sA, &tzg, bar_load, 0, (int)j0, (int)i);
+    tma_load_3d(sA + 16384, &tzg, bar_load, 64, (int)j0, (int)i);
+    tma_load_2d(sBG, &twg, bar_load, 0, 0);
+    tma_load_2d(sBG + 16384, &twg, bar_load, 64, 0);
+    tma_load_2d(sBZ, &twz, bar_load, 0, 0);
+    tma_load_2d(sBZ + 16384, &twz, bar_load, 64, 0);
+  }
+
+  // LN_out over the channels of x(i, j): channel-major reads, coalesced across the warp
+  uint32_t hv[CH / 2];
+  {
+    float v[CH];
+    const __nv_bfloat16* xp = args.x + i * args.ldx + (valid ? j : 0);
+#pragma unroll
+    for (int c = 0; c < CH; ++c) v[c] = valid ? __bfloat162float(xp[(int64_t)c * args.x_ch_stride]) : 0.f;
+    float s = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) s += v[c];
+    const float mean = s * (1.0f / CH);
+    float sq = 0.f;
+#pragma unroll
+    for (int c = 0; c < CH; ++c) {
+      const float d = v[c] - mean;
+      sq += d * d;
+    }
+    const float rstd = rsqrtf(sq * (1.0f / CH) + 1e-5f);
+#pragma unroll
+    for (int c = 0; c < CH; c += 2) {
+      const float y0 = (v[c] - mean) * rstd * __ldg(args.ln_out_w + c) + __ldg(args.ln_out_b + c);
+      const float y1 = (v[c + 1] - mean) * rstd * __ldg(args.ln_out_w + c + 1) + __ldg(args.ln_out_b + c + 1);
+      hv[c / 2] = pack_bf16(y0, y1);
+    }
+  }
+
+  mbar_wait(bar_load, 0, args.status);
+  ln_row_inplace_sw128(g, tid, args.ln_in_w, args.ln_in_b, 1e-5f);
+  fence_proxy_async_smem();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem + 128, sA, sBG, 16384, idesc_f16(128, 128, true));  // gate logits
+    umma_commit(bar_m1);
+  }
+  mbar_wait(bar_m1, 0, args.status);  // A is free again
+  tc_fence_after();
+#pragma unroll
+  for (int jj = 0; jj < 16; ++jj) {
+    uint4 q;
+    q.x = hv[jj * 4 + 0]; q.y = hv[jj * 4 + 1]; q.z = hv[jj * 4 + 2]; q.w = hv[jj * 4 + 3];
+    *reinterpret_cast<uint4*>(g + (jj >> 3) * 16384 + sw128_off(tid, jj & 7)) = q;
+  }
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  if (tid == 0) {
+    tc_fence_after();
+    umma_k128(tmem, sA, sBZ, 16384, idesc_f16(128, 128, true));  // W_z . LN_out(x)
+    umma_commit(bar_m2);
+  }
+  mbar_wait(bar_m2, 0, args.status);
+  tc_fence_after();
+
+  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+  __nv_bfloat16* zp = args.zo + i * args.zo_rs + (valid ? j : 0) * args.zo_cs;
+#pragma unroll 1
+  for (int cc = 0; cc < CH; cc += 32) {
+    uint32_t zv[32], gv[32];
+    tmem_ld32(tmem + lane_base + cc, zv);
+    tmem_ld32(tmem + lane_base + 128 + cc, gv);
+    tmem_ld_wait();
+    if (valid) {
+      uint4* dst = reinterpret_cast<uint4*>(zp + cc);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float u[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          u[k] = __uint_as_float(zv[e * 8 + k]) * fast_sigmoid(__uint_as_float(gv[e * 8 + k]));
+        if (args.accumulate) {
+          const uint4 old = dst[e];
+          u[0] += bf16lo(old.x); u[1] += bf16hi(old.x); u[2] += bf16lo(old.y); u[3] += bf16hi(old.y);
+          u[4] += bf16lo(old.z); u[5] += bf16hi(old.z); u[6] += bf16lo(old.w); u[7] += bf16hi(old.w);
+        }
+        uint4 w;
+        w.x = pack_bf16(u[0], u[1]); w.y = pack_bf16(u[2], u[3]);
+        w.z = pack_bf16(u[4], u[5]); w.w = pack_bf16(u[6], u[7]);
+        dst[e] = w;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ------------------------------------------------------------------ host helpers
+int pair_tmap(CUtensorMap* m, const pf_pair_view& v, int64_t n_rows, int64_t n_cols) {
+  if (v.row_stride % 8 || v.col_stride % 8)
+    return fail(PF_EINVAL_SHAPE, "bf16 pair views need row/col strides that are multiples of 8 elements");
+  const uint64_t dims[3] = {(uint64_t)CH, (uint64_t)n_cols, (uint64_t)n_rows};
+  const uint64_t str[2] = {(uint64_t)v.col_stride * 2, (uint64_t)v.row_stride * 2};
+  const uint32_t box[3] = {64, (uint32_t)TILE, 1};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, v.ptr, dims, str, box,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int weight_tmap(CUtensorMap* m, const void* w, int rows, int cols, int box_rows) {
+  const uint64_t dims[2] = {(uint64_t)cols, (uint64_t)rows};
+  const uint64_t str[1] = {(uint64_t)cols * 2};
+  const uint32_t box[2] = {64, (uint32_t)box_rows};
+  return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <class K>
+int set_smem(K kernel, uint32_t bytes) {
+  PF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return PF_OK;
+}
+
+struct TrimulWs {
+  __nv_bfloat16 *a, *b, *x;
+  int64_t ld_k, ld_j;
+};
+
+void trimul_plan(Arena& ar, int64_t n_i, int64_t n_j, int64_t n_k, TrimulWs& w) {
+  w.ld_k = (n_k + 7) / 8 * 8;
+  w.ld_j = (n_j + 7) / 8 * 8;
+  w.a = ar.take<__nv_bfloat16>((size_t)CH * n_i * w.ld_k);
+  w.b = ar.take<__nv_bfloat16>((size_t)CH * n_j * w.ld_k);
+  w.x = ar.take<__nv_bfloat16>((size_t)CH * n_i * w.ld_j);
+}
+
+}  // namespace
+
+bool trimul_supported(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h) {
+  return c_z == CH && c_h == CH && n_i >= 1 && n_j >= 1 && n_k >= 1 && n_i < (1ll << 31) &&
+         n_j < (1ll << 31) && n_k < (1ll << 31);
+}
+
+size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int, int) {
+  Arena ar(nullptr, 0);
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, w);
+  return ar.used;
+}
+
+int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+           int, int, int acc, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small");
+  if (zo.row_stride % 8 || zo.col_stride % 8 || ((uintptr_t)zo.ptr) % 16)
+    return fail(PF_EINVAL_SHAPE, "bf16 output view must be 16-byte aligned with strides multiple of 8");
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  static bool attrs = false;
+  if (!attrs) {
+    PF_TRY(set_smem(k_trimul_proj, PROJ_SMEM + 1024));
+    PF_TRY(set_smem(k_trimul_bgemm, GEMM_SMEM + 1024));
+    PF_TRY(set_smem(k_trimul_out, OUT_SMEM + 1024));
+    attrs = true;
+  }
+  // 1. projections
+  CUtensorMap tz0, tz1, tw0p, tw0g, tw1p, tw1g;
+  PF_TRY(pair_tmap(&tz0, za, n_i, n_k));
+  PF_TRY(pair_tmap(&tz1, zb, n_j, n_k));
+  PF_TRY(weight_tmap(&tw0p, p->w_ap, CH, CH, 128));
+  PF_TRY(weight_tmap(&tw0g, p->w_ag, CH, CH, 128));
+  PF_TRY(weight_tmap(&tw1p, p->w_bp, CH, CH, 128));
+  PF_TRY(weight_tmap(&tw1g, p->w_bg, CH, CH, 128));
+  ProjArgs pa;
+  const int64_t tpr_k = (n_k + TILE - 1) / TILE;
+  pa.side[0] = ProjSide{n_i, n_k, ma, w.a, (int64_t)n_i * w.ld_k, tpr_k, n_i * tpr_k};
+  pa.side[1] = ProjSide{n_j, n_k, mb, w.b, (int64_t)n_j * w.ld_k, tpr_k, n_j * tpr_k};
+  pa.ld = w.ld_k;
+  pa.ln_w = p->ln_in_w;
+  pa.ln_b = p->ln_in_b;
+  pa.status = status;
+  const int64_t nt = pa.side[0].ntiles > pa.side[1].ntiles ? pa.side[0].ntiles : pa.side[1].ntiles;
+  if (2 * nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "trimul projection grid too large");
+  k_trimul_proj<<<(unsigned)(2 * nt), 128, PROJ_SMEM + 1024, st>>>(tz0, tz1, tw0p, tw0g, tw1p, tw1g, pa);
+  PF_CHECK_LAUNCH();
+  // 2. contraction x[ch] = a[ch] b[ch]^T
+  CUtensorMap ta, tb;
+  {
+    const uint64_t da[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)CH};
+    const uint64_t sa[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_i * w.ld_k * 2};
+    const uint32_t ba[3] = {BK, BM, 1};
+    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t db[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)CH};
+    const uint64_t sb[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_j * w.ld_k * 2};
+    const uint32_t bb[3] = {BK, BN, 1};
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  GemmArgs ga{(int)n_i, (int)n_j, (int)n_k, w.x, w.ld_j, (int64_t)n_i * w.ld_j, status};
+  dim3 grid((unsigned)((n_j + BN - 1) / BN), (unsigned)((n_i + BM - 1) / BM), CH);
+  if (grid.y > 65535) return fail(PF_EUNSUPPORTED, "trimul contraction grid too large");
+  k_trimul_bgemm<<<grid, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
+  PF_CHECK_LAUNCH();
+  // 3. LN_out, W_z, gate, residual
+  CUtensorMap tzg, twz, twg;
+  PF_TRY(pair_tmap(&tzg, zg, n_i, n_j));
+  PF_TRY(weight_tmap(&twz, p->w_z, CH, CH, 128));
+  PF_TRY(weight_tmap(&twg, p->w_g, CH, CH, 128));
+  OutArgs oa;
+  oa.x = w.x;
+  oa.ldx = w.ld_j;
+  oa.x_ch_stride = (int64_t)n_i * w.ld_j;
+  oa.zo = (__nv_bfloat16*)zo.ptr;
+  oa.zo_rs = zo.row_stride;
+  oa.zo_cs = zo.col_stride;
+  oa.n_i = n_i;
+  oa.n_j = n_j;
+  oa.tiles_per_row = (n_j + TILE - 1) / TILE;
+  oa.ln_in_w = p->ln_in_w;
+  oa.ln_in_b = p->ln_in_b;
+  oa.ln_out_w = p->ln_out_w;
+  oa.ln_out_b = p->ln_out_b;
+  oa.accumulate = acc;
+  oa.status = status;
+  const int64_t nto = n_i * oa.tiles_per_row;
+  k_trimul_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tzg, twz, twg, oa);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+}  // namespace tc
+}  // namespace pf

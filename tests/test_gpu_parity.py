@@ -92,3 +92,22 @@ def test_block_bf16_vs_fp32_oracle(cuda_device):
             s.to(cuda_device, torch.bfloat16), z.to(cuda_device, torch.bfloat16), mask.to(cuda_device))
     assert rel_l2(z_out, z_ref) <= BF16_TOL
     assert rel_l2(s_out, s_ref) <= BF16_TOL
+
+
+@pytest.mark.parametrize("kind", ["trimul_out", "trimul_in", "triatt_start", "triatt_end", "transition"])
+@pytest.mark.parametrize("n", [300])
+def test_bf16_tensor_core_path_vs_simt_path(kind, n, cuda_device):
+    """The tcgen05 kernels and the SIMT kernels agree on one bf16 problem with partial tiles."""
+    mod, params, s, z, mask = _case(kind, n, ragged=True, full_rows=[5])
+    mod = cuda_module(mod, params, cuda_device)
+    got_tc = cuda_op(kind, mod, s, z, mask, cuda_device, torch.bfloat16)
+    path = _abi.last_path()
+    _abi.set_force_simt(True)
+    try:
+        got_simt = cuda_op(kind, mod, s, z, mask, cuda_device, torch.bfloat16)
+    finally:
+        _abi.set_force_simt(False)
+    assert path == "tc", f"{kind} dispatched to {path}"
+    assert _abi.device_status(clear=True) == 0
+    err = rel_l2(got_tc, got_simt)
+    assert err <= 1e-2, f"{kind}: tc vs simt rel-L2 {err:.3e}"
