@@ -1,0 +1,422 @@
+"""Benchmark: ms per Pairformer block at N_token=1536, bf16, B200.
+
+A step is one forward of the 48-block Pairformer trunk (PairformerStack, c_z=128, c_s=384,
+4x32 triangle heads, c_hidden=128, transition x4, 16 single heads) over one synthetic
+input (z, s ~ N(0,1), all-ones mask, seed-0 random weights: the reference's default init
+zeroes every output projection). ``value`` = device time per step / 48 with inputs resident
+in HBM; ``e2e`` = the same through the public API with the step's inputs copied from
+pinned host memory and the outputs copied back inside the timed region. The pair tensor
+(604 MB) is larger than L2, so no separate flush is needed.
+
+--impl reference times the reference algorithm's CPU path (the oracle restatement of the
+reference PyTorch modules; the reference itself is not installed on the GPU box) on the
+host cores for a bounded row sample of the same workload, extrapolated to ms per block.
+
+N > 1 GPUs: Fold-CP 2D pair sharding (1x2, 2x2, 2x4 grids) of the same trunk; total work
+fixed ("strong" scaling); time = max over ranks.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+N_TOKEN = 1536
+C_Z, C_S, HEADS_PAIR, HEAD_DIM, C_H, N_SINGLE_HEADS = 128, 384, 4, 32, 128, 16
+METRIC = "ms per Pairformer block at N_token=1536, 1/2/4/8 B200; tri-attn/tri-mul % peak"
+GRIDS = {1: (1, 1), 2: (1, 2), 4: (2, 2), 8: (2, 4)}
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ------------------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason sampling while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sm.append(float(parts[1]))
+                    mx = float(parts[2])
+                except ValueError:
+                    continue
+                for nm, v in zip(names, parts[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(nm)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ------------------------------------------------------------------------------ CPU sample
+def cpu_block_sample_ms(n: int, rows: int, threads: int) -> float:
+    """The reference algorithm on the host (oracle restatement, fp32 torch CPU), one block.
+
+    Every op of the block is row-separable: rows [0, rows) of each op's output are computed
+    with everything they need (the O(N^2) projections for those rows, and the full-K
+    contraction / full-key attention for them), and the time is scaled by n / rows.
+    """
+    from oracle import pairformer_oracle as O
+    from opendde_b200.utils import seeded_params
+    from opendde_b200.model import PairformerBlock
+
+    torch.set_num_threads(threads)
+    blk = PairformerBlock(n_heads=N_SINGLE_HEADS, c_z=C_Z, c_s=C_S)
+    p = seeded_params([(k, tuple(v.shape)) for k, v in blk.named_parameters()], seed=0)
+    sub = lambda pre: {k[len(pre) + 1:]: v for k, v in p.items() if k.startswith(pre + ".")}  # noqa: E731
+    g = torch.Generator().manual_seed(1)
+    zr = torch.randn((rows, n, C_Z), generator=g)
+    bfull = torch.empty((C_H, n, n)).uniform_(-1, 1, generator=g)  # stands in for the projected b
+    bias = torch.empty((HEADS_PAIR, n, n)).uniform_(-1, 1, generator=g)
+    s = torch.randn((n, C_S), generator=g)
+    mask = torch.ones((rows, n))
+    scale = n / rows
+    t = 0.0
+    with torch.no_grad():
+        for pre in ("tri_mul_out", "tri_mul_in"):
+            q = sub(pre)
+            t0 = time.perf_counter()
+            zn = O.layer_norm(zr, q["layer_norm_in.weight"], q["layer_norm_in.bias"])
+            a = mask[..., None] * torch.sigmoid(O.linear(zn, q["linear_a_g.weight"])) * O.linear(zn, q["linear_a_p.weight"])
+            b = mask[..., None] * torch.sigmoid(O.linear(zn, q["linear_b_g.weight"])) * O.linear(zn, q["linear_b_p.weight"])
+            x = torch.matmul(a.permute(2, 0, 1), bfull.transpose(-1, -2)).permute(1, 2, 0)
+            x = O.layer_norm(x, q["layer_norm_out.weight"], q["layer_norm_out.bias"])
+            x = O.linear(x, q["linear_z.weight"]) * torch.sigmoid(O.linear(zn, q["linear_g.weight"]))
+            t += (time.perf_counter() - t0) * scale
+            del a, b, x
+        for pre in ("tri_att_start", "tri_att_end"):
+            q = sub(pre)
+            t0 = time.perf_counter()
+            x = O.layer_norm(zr, q["layer_norm.weight"], q["layer_norm.bias"])
+            _ = O.linear(x, q["linear.weight"])  # the bias rows these output rows contribute
+            d = HEAD_DIM
+            qq = O.linear(x, q["mha.linear_q.weight"]).view(rows, n, HEADS_PAIR, d).transpose(1, 2) / math.sqrt(d)
+            kk = O.linear(x, q["mha.linear_k.weight"]).view(rows, n, HEADS_PAIR, d).transpose(1, 2)
+            vv = O.linear(x, q["mha.linear_v.weight"]).view(rows, n, HEADS_PAIR, d).transpose(1, 2)
+            for r0 in range(0, rows, 8):
+                lg = torch.matmul(qq[r0:r0 + 8], kk[r0:r0 + 8].transpose(-1, -2))
+                lg = lg + (1e9 * (mask[r0:r0 + 8] - 1))[:, None, None, :] + bias[None]
+                o = torch.matmul(torch.softmax(lg, -1), vv[r0:r0 + 8]).transpose(1, 2)
+                gg = torch.sigmoid(O.linear(x[r0:r0 + 8], q["mha.linear_g.weight"])).view(o.shape)
+                O.linear((o * gg).reshape(o.shape[0], n, -1), q["mha.linear_o.weight"])
+            t += (time.perf_counter() - t0) * scale
+        t0 = time.perf_counter()
+        O.transition(zr, sub("pair_transition"))
+        t += (time.perf_counter() - t0) * scale
+        t0 = time.perf_counter()
+        apb = sub("attention_pair_bias")
+        O.pair_bias(zr, apb)  # pair-bias rows for these output rows (scaled)
+        t += (time.perf_counter() - t0) * scale
+        t0 = time.perf_counter()
+        a = O.layer_norm(s, apb["layernorm_a.weight"], apb["layernorm_a.bias"])
+        dd = C_S // N_SINGLE_HEADS
+        qs = (O.linear(a, apb["attention.linear_q.weight"], apb["attention.linear_q.bias"]).view(n, N_SINGLE_HEADS, dd).transpose(0, 1) / math.sqrt(dd))
+        ks = O.linear(a, apb["attention.linear_k.weight"]).view(n, N_SINGLE_HEADS, dd).transpose(0, 1)
+        vs = O.linear(a, apb["attention.linear_v.weight"]).view(n, N_SINGLE_HEADS, dd).transpose(0, 1)
+        pb = torch.empty((N_SINGLE_HEADS, n, n)).uniform_(-1, 1, generator=g)
+        o = torch.matmul(torch.softmax(torch.matmul(qs, ks.transpose(-1, -2)) + pb, -1), vs)
+        O.transition(s, sub("single_transition"))
+        t += time.perf_counter() - t0
+    return t * 1e3
+
+
+# ------------------------------------------------------------------------------ work model
+def kernel_work(name: str, n: int):
+    """Algorithmic work of one launch at the bench workload: (bound, amount, unit)."""
+    n3 = float(n) ** 3
+    n2 = float(n) ** 2
+    table = {
+        "k_triatt_core": ("tensor", 4 * HEADS_PAIR * HEAD_DIM * n3, "flop"),
+        "k_trimul_bgemm": ("tensor", 2 * C_H * n3, "flop"),
+        "k_trimul_proj": ("hbm", n2 * (2 * C_Z + 2 * C_H) * 2, "byte"),   # read z once per side, write a/b
+        "k_trimul_out": ("hbm", n2 * (C_H + C_Z + 2 * C_Z) * 2, "byte"),   # read x, z(gate), z r+w
+        "k_triatt_proj": ("hbm", n2 * (C_Z + 3 * HEADS_PAIR * HEAD_DIM + HEADS_PAIR) * 2, "byte"),
+        "k_triatt_out": ("hbm", n2 * (C_Z + HEADS_PAIR * HEAD_DIM + 2 * C_Z) * 2, "byte"),
+        "k_transition": ("tensor", 3 * 2 * C_Z * 4 * C_Z * n2, "flop"),
+    }
+    return table.get(name)
+
+
+def read_traffic(kernel: str):
+    """DRAM bytes per launch for `kernel` from the committed ncu summary, if any."""
+    p = os.path.join(ROOT, "profiles", "dram_traffic_per_launch.txt")
+    if not os.path.exists(p):
+        return None
+    with open(p) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) >= 2 and parts[0] == kernel:
+                try:
+                    return float(parts[1])
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------------------------ main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=N_TOKEN)
+    ap.add_argument("--blocks", type=int, default=48)
+    ap.add_argument("--cpu-rows", type=int, default=32)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    cores = os.cpu_count() or 1
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        rows = max(8, min(args.cpu_rows, args.n))
+        for _ in range(args.warmup):
+            cpu_block_sample_ms(args.n, rows, cores)
+        vals = [cpu_block_sample_ms(args.n, rows, cores) for _ in range(args.steps)]
+        v = statistics.median(vals)
+        sample = (f"rows 0..{rows - 1} of every op of one block at N={args.n} (row-separable; the rows' "
+                  f"projections, full-K contractions and full-key attention), scaled x{args.n}/{rows}; "
+                  f"fp32 torch CPU restatement of the reference modules")
+        print(json.dumps({
+            "metric": METRIC, "value": v, "unit": "ms/block", "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v * args.blocks,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": f"pairformer_trunk_{args.blocks}blk_N{args.n}", "n_token": args.n,
+                       "c_z": C_Z, "c_s": C_S, "blocks": args.blocks},
+            "cpu_baseline": {"value": v, "unit": "ms/block", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "ms/block", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    from opendde_b200 import _abi
+    from opendde_b200.model import PairformerStack
+    from opendde_b200.utils import make_inputs, seeded_init_
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    distributed = world > 1
+    if distributed:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        os.environ["OPENDDE_FOLDCP_MODE"] = "distributed"
+        os.environ["OPENDDE_FOLDCP_SIZE_CP"] = str(world)
+        os.environ["OPENDDE_FOLDCP_SIZE_DP"] = "1"
+        r_, c_ = GRIDS[world]
+        os.environ["OPENDDE_FOLDCP_MESH"] = f"{r_}x{c_}"
+
+    stack = PairformerStack(n_blocks=args.blocks, n_heads=N_SINGLE_HEADS, c_z=C_Z, c_s=C_S)
+    seeded_init_(stack, seed=0)
+    stack = stack.to(dev)
+    s0, z0, m0 = make_inputs(args.n, c_z=C_Z, c_s=C_S, seed=1)
+    z_dev = z0.to(dev, torch.bfloat16)
+    s_dev = s0.to(dev, torch.bfloat16)
+    m_dev = m0.to(dev)
+    z_host = z0.to(torch.bfloat16).pin_memory()
+    s_host = s0.to(torch.bfloat16).pin_memory()
+    m_host = m0.pin_memory()
+    z_out_host = torch.empty_like(z_host).pin_memory()
+    s_out_host = torch.empty_like(s_host).pin_memory()
+
+    def barrier():
+        if distributed:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    def step_resident():
+        with torch.no_grad():
+            return stack(s_dev, z_dev, m_dev)
+
+    def step_e2e():
+        with torch.no_grad():
+            zz = z_host.to(dev, non_blocking=True)
+            ss = s_host.to(dev, non_blocking=True)
+            mm = m_host.to(dev, non_blocking=True)
+            so, zo = stack(ss, zz, mm)
+            z_out_host.copy_(zo, non_blocking=True)
+            s_out_host.copy_(so, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step_resident()
+    step_e2e()
+    barrier()
+
+    # ---- timed: resident inputs (value) with per-kernel events (roofline)
+    st = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _abi.profile_enable(True)
+    _abi.profile_report()  # clear
+    launches0 = _abi.launch_count()
+    with ClockSampler(local_rank) as clk:
+        barrier()
+        ev0.record(st)
+        for _ in range(args.steps):
+            step_resident()
+        ev1.record(st)
+        barrier()
+    launches = _abi.launch_count() - launches0
+    _abi.profile_enable(False)
+    prof = _abi.profile_report()
+    ms_step = ev0.elapsed_time(ev1) / args.steps
+
+    # ---- timed: end to end through the public API with host buffers
+    barrier()
+    ev0.record(st)
+    for _ in range(args.steps):
+        step_e2e()
+    ev1.record(st)
+    barrier()
+    ms_e2e = ev0.elapsed_time(ev1) / args.steps
+    assert _abi.device_status() == 0, "a device-side bounded wait timed out"
+
+    if distributed:
+        t = torch.tensor([ms_step, ms_e2e], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_step, ms_e2e = t.tolist()
+
+    peaks = load_peaks()
+    clocks = clk.summary()
+    # dominant kernel and its roofline
+    kernels = {k: {"launches": v[0], "total_ms": v[1], "share": None} for k, v in prof.items()}
+    tot = sum(v[1] for v in prof.values()) or 1.0
+    for k in kernels:
+        kernels[k]["share"] = kernels[k]["total_ms"] / tot
+    dom = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
+    roofline = None
+    fracs = {}
+    for name in ("k_triatt_core", "k_trimul_bgemm", dom):
+        if name is None or name not in prof:
+            continue
+        w = kernel_work(name, args.n)
+        if w is None:
+            continue
+        bound, amount, unit = w
+        avg_s = prof[name][1] / prof[name][0] / 1e3
+        if bound == "tensor":
+            ach = amount / avg_s / 1e12
+            peak = peaks["bf16_tflops_sustained"]
+            entry = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                     "traffic": read_traffic(name), "kernel": name,
+                     "peak_kind": f"bf16 dense sustained ({peaks['source']})",
+                     "work_per_launch": amount, "avg_launch_ms": avg_s * 1e3}
+        else:
+            ach = amount / avg_s / 1e9
+            peak = peaks["hbm_gbs"]
+            entry = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "traffic": read_traffic(name), "kernel": name, "peak_kind": f"HBM copy ({peaks['source']})",
+                     "work_per_launch": amount, "avg_launch_ms": avg_s * 1e3}
+        fracs[name] = entry
+        if name == dom:
+            roofline = entry
+
+    cpu_baseline = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows = max(8, min(args.cpu_rows, args.n))
+        v = cpu_block_sample_ms(args.n, rows, cores)
+        cpu_baseline = {"value": v, "unit": "ms/block", "cores": cores, "kind": "port",
+                        "sample": f"rows 0..{rows - 1} of every op of one block at N={args.n}, scaled x{args.n}/{rows}; "
+                                  "fp32 torch CPU restatement of the reference modules"}
+
+    z_bytes = z_host.numel() * 2
+    h2d = z_bytes + s_host.numel() * 2 + m_host.numel() * 4
+    d2h = z_bytes + s_host.numel() * 2
+    if rank == 0:
+        grid = GRIDS.get(world, (1, world))
+        out = {
+            "metric": METRIC,
+            "value": ms_step / args.blocks,
+            "unit": "ms/block",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": False,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: z,s ~ N(0,1), all-ones mask, seed-0 N(0,1/fan_in) weights",
+            "config": {"workload": f"pairformer_trunk_{args.blocks}blk_N{args.n}_bf16", "n_token": args.n,
+                       "c_z": C_Z, "c_s": C_S, "blocks": args.blocks, "grid": f"{grid[0]}x{grid[1]}",
+                       "l2": "inputs larger than L2 (pair tensor 604 MB)"},
+            "e2e": {"value": ms_e2e / args.blocks, "unit": "ms/block", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "roofline": roofline,
+            "tri_attn": fracs.get("k_triatt_core"),
+            "tri_mul": fracs.get("k_trimul_bgemm"),
+            "kernels": kernels,
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "cpu_baseline": cpu_baseline,
+        }
+        print(json.dumps(out), flush=True)
+    if distributed:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -77,6 +77,15 @@ PF_API const char* pf_last_path(void);
  * device (it copies the word to the host); clear != 0 resets it. No reference counterpart
  * (the reference has no device-side waits). */
 PF_API int pf_device_status(int* status_out, int clear);
+/* Measurement hooks (no reference counterpart; the reference times whole stages with
+ * host wall clocks, opendde/distributed/foldcp/metrics.py:136-234):
+ * pf_launch_count  -- number of kernels this library has launched in the process;
+ * pf_profile_enable -- when on, every launch is bracketed by a CUDA event pair on its stream;
+ * pf_profile_report -- resolves the pairs into JSON {"kernel": [launches, total_ms], ...}
+ *                      (waits for the last recorded event) and clears them. */
+PF_API long long pf_launch_count(void);
+PF_API int pf_profile_enable(int on);
+PF_API int pf_profile_report(char* buf, size_t len);
 
 /* ---- LayerNorm ------------------------------------------------------------------------
  * y[r, :] = (x[r, :] - mean) / sqrt(var + eps) * gamma + beta over the last dim c.

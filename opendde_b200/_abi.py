@@ -37,6 +37,7 @@ _STATUS_NAMES = {
 # Every symbol the header declares (checked by tests/test_abi_symbols.py).
 EXPORTED = (
     "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path", "pf_device_status",
+    "pf_launch_count", "pf_profile_enable", "pf_profile_report",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
     "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
@@ -99,6 +100,9 @@ def load(path: str = LIB_PATH):
         "pf_last_path": ([], c_char_p),
         "pf_set_option": ([c_int, c_int64], c_int),
         "pf_device_status": ([POINTER(c_int), c_int], c_int),
+        "pf_launch_count": ([], ctypes.c_longlong),
+        "pf_profile_enable": ([c_int], c_int),
+        "pf_profile_report": ([ctypes.c_char_p, c_size_t], c_int),
         "pf_layernorm_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p], c_int),
         "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
@@ -147,6 +151,22 @@ def device_status(clear: bool = False) -> int:
     v = c_int(0)
     check(load().pf_device_status(ctypes.byref(v), 1 if clear else 0))
     return int(v.value)
+
+
+def launch_count() -> int:
+    return int(load().pf_launch_count())
+
+
+def profile_enable(on: bool) -> None:
+    check(load().pf_profile_enable(1 if on else 0))
+
+
+def profile_report() -> dict:
+    """Per-kernel {name: (launches, total_ms)} since the last report (synchronises)."""
+    import json
+    buf = ctypes.create_string_buffer(1 << 16)
+    check(load().pf_profile_report(buf, len(buf)))
+    return {k: (int(v[0]), float(v[1])) for k, v in json.loads(buf.value.decode()).items()}
 
 
 def workspace_bytes(fn_name: str, *args) -> int:

@@ -13,6 +13,7 @@
 #include <cmath>
 
 #include "pf_common.cuh"
+#include "pf_prof.h"
 #include "pf_simt.h"
 
 namespace pf {
@@ -313,7 +314,10 @@ static int ln_view(const T* x, int64_t rs, int64_t cs, int64_t n_rows, int64_t n
   if (c > 1024) return fail(PF_EUNSUPPORTED, "LayerNorm channel count %d > 1024", c);
   int64_t P = n_rows * n_cols;
   if (P == 0) return PF_OK;
-  k_ln_view<T, TO><<<nblk(P, 8), 256, 0, st>>>(x, rs, cs, n_rows, n_cols, c, g, b, eps, out, ops);
+  {
+    PF_LAUNCH_SCOPE(0, "k_ln_view");
+    k_ln_view<T, TO><<<nblk(P, 8), 256, 0, st>>>(x, rs, cs, n_rows, n_cols, c, g, b, eps, out, ops);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -327,8 +331,11 @@ static int gemm(const TA* A, int64_t sAb, int64_t sAm, const TB* B, int64_t sBb,
     return fail(PF_EUNSUPPORTED, "SIMT GEMM grid too large (batch %lld, M %lld)",
                 (long long)batch, (long long)M);
   dim3 grid(nblk(N, 64), nblk(M, 64), (unsigned)batch);
-  k_gemm_nt<TA, TB><<<grid, 256, 0, st>>>(A, sAb, sAm, B, sBb, sBn, C, sCb, sCm, sCn, M, N, K,
-                                          alpha, acc);
+  {
+    PF_LAUNCH_SCOPE(st, "k_gemm_nt");
+    k_gemm_nt<TA, TB><<<grid, 256, 0, st>>>(A, sAb, sAm, B, sBb, sBn, C, sCb, sCm, sCn, M, N, K,
+                                            alpha, acc);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -385,20 +392,29 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
                             p->ln_in_w, p->ln_in_b, eps, w.xa, c_z, st)));
   PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ap, 0, c_z, w.pa, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ag, 0, c_z, w.pg, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
-  k_gate_to_cmajor<<<nblk(Pa * c_h, 256), 256, 0, st>>>(w.pa, w.pg, ma, n_i, n_k, c_h, w.a);
+  {
+    PF_LAUNCH_SCOPE(0, "k_gate_to_cmajor");
+    k_gate_to_cmajor<<<nblk(Pa * c_h, 256), 256, 0, st>>>(w.pa, w.pg, ma, n_i, n_k, c_h, w.a);
+  }
   PF_CHECK_LAUNCH();
   // b
   PF_TRY((ln_view<T, float>((const T*)zb.ptr, zb.row_stride, zb.col_stride, n_j, n_k, c_z,
                             p->ln_in_w, p->ln_in_b, eps, w.xb, c_z, st)));
   PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bp, 0, c_z, w.pa, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bg, 0, c_z, w.pg, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
-  k_gate_to_cmajor<<<nblk(Pb * c_h, 256), 256, 0, st>>>(w.pa, w.pg, mb, n_j, n_k, c_h, w.b);
+  {
+    PF_LAUNCH_SCOPE(0, "k_gate_to_cmajor");
+    k_gate_to_cmajor<<<nblk(Pb * c_h, 256), 256, 0, st>>>(w.pa, w.pg, mb, n_j, n_k, c_h, w.b);
+  }
   PF_CHECK_LAUNCH();
   // x[ch] = a[ch] b[ch]^T  (batched over channels)
   PF_TRY((gemm<float, float>(w.a, Pa, n_k, w.b, Pb, n_k, w.p, Po, n_j, 1, c_h, n_i, n_j, n_k,
                              1.f, 0, st)));
   // LN_out, linear_z
-  k_ln_cmajor<<<nblk(Po, 8), 256, 0, st>>>(w.p, Po, c_h, p->ln_out_w, p->ln_out_b, eps, w.xn);
+  {
+    PF_LAUNCH_SCOPE(0, "k_ln_cmajor");
+    k_ln_cmajor<<<nblk(Po, 8), 256, 0, st>>>(w.p, Po, c_h, p->ln_out_w, p->ln_out_b, eps, w.xn);
+  }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(w.xn, 0, c_h, (const T*)p->w_z, 0, c_h, w.y, 0, c_z, 1, 1, Po, c_z, c_h,
                          1.f, 0, st)));
@@ -407,8 +423,11 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
                             p->ln_in_w, p->ln_in_b, eps, w.xo, c_z, st)));
   PF_TRY((gemm<float, T>(w.xo, 0, c_z, (const T*)p->w_g, 0, c_z, w.gg, 0, c_z, 1, 1, Po, c_z, c_z,
                          1.f, 0, st)));
-  k_combine_view<T><<<nblk(Po * c_z, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
-                                                         n_i, n_j, c_z, w.y, w.gg, acc);
+  {
+    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    k_combine_view<T><<<nblk(Po * c_z, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
+                                                           n_i, n_j, c_z, w.y, w.gg, acc);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -462,6 +481,7 @@ static int launch_attn(int d, const float* q, int64_t q_rs, int64_t q_ps, int64_
                                              b_hs, b_rs, bias_scale, m, inf, n_q, n_valid, sd, \
                                              o, o_rs, o_ps);                                   \
     break;
+  PF_LAUNCH_SCOPE(st, "k_attn_simt");
   switch (d) {
     PF_ATTN_CASE(8)
     PF_ATTN_CASE(16)
@@ -523,11 +543,17 @@ static int triatt_t(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, 
   // gate from LN'd query input, then output projection
   PF_TRY((gemm<float, T>(w.x + q_col0 * c, n_keys * c, c, (const T*)p->w_g, 0, c, w.g, n_q * hd,
                          hd, 1, n_rows, n_q, hd, c, 1.f, 0, st)));
-  k_gate_inplace<<<nblk(Pq * hd, 256), 256, 0, st>>>(w.o, w.g, Pq * hd);
+  {
+    PF_LAUNCH_SCOPE(0, "k_gate_inplace");
+    k_gate_inplace<<<nblk(Pq * hd, 256), 256, 0, st>>>(w.o, w.g, Pq * hd);
+  }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(w.o, 0, hd, (const T*)p->w_o, 0, hd, w.y, 0, c, 1, 1, Pq, c, hd, 1.f, 0, st)));
-  k_combine_view<T><<<nblk(Pq * c, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
-                                                       n_rows, n_q, c, w.y, nullptr, acc);
+  {
+    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    k_combine_view<T><<<nblk(Pq * c, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
+                                                         n_rows, n_q, c, w.y, nullptr, acc);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -571,13 +597,19 @@ int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64
   if (dtype == PF_F32) {
     PF_TRY(triatt_bias_t<float>(p, z, n_rows, n_cols, bias, hs, rs, c, H, 1.f, x, st));
     PF_TRY((gemm<float, float>(x, 0, c, (const float*)p->w_bias, 0, c, bb, 0, H, 1, 1, P, H, c, 1.f, 0, st)));
-    k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, (float*)bias, hs, rs, 1.f);
+    {
+      PF_LAUNCH_SCOPE(0, "k_bias_store");
+      k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, (float*)bias, hs, rs, 1.f);
+    }
   } else {
     PF_TRY(triatt_bias_t<__nv_bfloat16>(p, z, n_rows, n_cols, bias, hs, rs, c, H, 1.f, x, st));
     PF_TRY((gemm<float, __nv_bfloat16>(x, 0, c, (const __nv_bfloat16*)p->w_bias, 0, c, bb, 0, H, 1, 1,
                                        P, H, c, 1.f, 0, st)));
-    k_bias_store<__nv_bfloat16><<<nblk(P * H, 256), 256, 0, st>>>(
-        bb, n_rows, n_cols, H, (__nv_bfloat16*)bias, hs, rs, 1.4426950408889634f);
+    {
+      PF_LAUNCH_SCOPE(0, "k_bias_store");
+      k_bias_store<__nv_bfloat16><<<nblk(P * H, 256), 256, 0, st>>>(
+          bb, n_rows, n_cols, H, (__nv_bfloat16*)bias, hs, rs, 1.4426950408889634f);
+    }
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
@@ -605,10 +637,16 @@ static int transition_t(const pf_transition_params* p, const T* x, int64_t xs, T
   PF_TRY((ln_view<T, float>(x, xs, 0, rows, 1, c, p->ln_w, p->ln_b, 1e-5f, y, c, st)));
   PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_a, 0, c, a, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_b, 0, c, b, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
-  k_swiglu<<<nblk(rows * hc, 256), 256, 0, st>>>(a, b, rows * hc);
+  {
+    PF_LAUNCH_SCOPE(0, "k_swiglu");
+    k_swiglu<<<nblk(rows * hc, 256), 256, 0, st>>>(a, b, rows * hc);
+  }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(b, 0, hc, (const T*)p->w_o, 0, hc, o, 0, c, 1, 1, rows, c, hc, 1.f, 0, st)));
-  k_combine_view<T><<<nblk(rows * c, 256), 256, 0, st>>>(out, os, 0, rows, 1, c, o, nullptr, acc);
+  {
+    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    k_combine_view<T><<<nblk(rows * c, 256), 256, 0, st>>>(out, os, 0, rows, 1, c, o, nullptr, acc);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -646,7 +684,10 @@ int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_
     PF_TRY((gemm<float, __nv_bfloat16>(x, 0, c_z, (const __nv_bfloat16*)p->w_z, 0, c_z, bb, 0, H, 1,
                                        1, P, H, c_z, 1.f, 0, st)));
   }
-  k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, bias, hs, rs, 1.f);
+  {
+    PF_LAUNCH_SCOPE(0, "k_bias_store");
+    k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, bias, hs, rs, 1.f);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -674,7 +715,10 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   PF_TRY((ln_view<T, float>(s_in, c_s, 0, n, 1, c_s, p->ln_a_w, p->ln_a_b, 1e-5f, a, c_s, st)));
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_q, 0, c_s, q, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   if (p->b_q) {
-    k_add_bias<<<nblk(n * c_s, 256), 256, 0, st>>>(q, p->b_q, n, c_s);
+    {
+      PF_LAUNCH_SCOPE(0, "k_add_bias");
+      k_add_bias<<<nblk(n * c_s, 256), 256, 0, st>>>(q, p->b_q, n, c_s);
+    }
     PF_CHECK_LAUNCH();
   }
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_k, 0, c_s, k, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
@@ -684,10 +728,16 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   // one "row" (i = 0) of n queries over n keys; bias(h, j, k) = bias[h*n*n + j*n + k]
   PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, n * n, n, 1.0f, nomask, 0.f,
                                 1, n, H, n, o, 0, c_s, st)));
-  k_gate_inplace<<<nblk(n * c_s, 256), 256, 0, st>>>(o, g, n * c_s);
+  {
+    PF_LAUNCH_SCOPE(0, "k_gate_inplace");
+    k_gate_inplace<<<nblk(n * c_s, 256), 256, 0, st>>>(o, g, n * c_s);
+  }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(o, 0, c_s, (const T*)p->w_o, 0, c_s, y, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
-  k_combine_view<T><<<nblk(n * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, n, 1, c_s, y, nullptr, acc);
+  {
+    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    k_combine_view<T><<<nblk(n * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, n, 1, c_s, y, nullptr, acc);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }

@@ -18,6 +18,7 @@
 // Reference: opendde/model/triangular/triangular.py:648-706, layers.py:302-424.
 
 #include "pf_common.cuh"
+#include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
 #include "pf_tmap.h"
@@ -653,7 +654,10 @@ int launch_proj(const pf_triatt_params* p, const void* zptr, int64_t rs, int64_t
   pa.tiles_per_row = (n_cols + TILE - 1) / TILE;
   const int64_t nt = n_rows * pa.tiles_per_row;
   if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "triatt projection grid too large");
-  k_triatt_proj<<<(unsigned)nt, 128, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, pa);
+  {
+    PF_LAUNCH_SCOPE(st, "k_triatt_proj");
+    k_triatt_proj<<<(unsigned)nt, 128, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, pa);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
@@ -708,8 +712,11 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   unsigned int* status;
   PF_TRY(device_status_ptr(&status));
   // 0. mask bias + tile flags
-  k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags,
-                                                      (int)w.n_tiles_k);
+  {
+    PF_LAUNCH_SCOPE(st, "k_triatt_maskprep");
+    k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags,
+                                                        (int)w.n_tiles_k);
+  }
   PF_CHECK_LAUNCH();
   // 1. projections (+ own bias in the square single-device case)
   ProjArgs pa{};
@@ -759,7 +766,10 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   CoreArgs ca{n_rows, n_q, w.n_tiles_k, w.mb, w.ld_mb, w.flags, w.o, status};
   dim3 grid((unsigned)((n_q + TILE - 1) / TILE), H, (unsigned)n_rows);
   if (n_rows > 65535) return fail(PF_EUNSUPPORTED, "triatt: more than 65535 rows per call");
-  k_triatt_core<<<grid, 160, CORE_SMEM + 1024, st>>>(tq, tk, tvt, tb, tmb, ca);
+  {
+    PF_LAUNCH_SCOPE(st, "k_triatt_core");
+    k_triatt_core<<<grid, 160, CORE_SMEM + 1024, st>>>(tq, tk, tvt, tb, tmb, ca);
+  }
   PF_CHECK_LAUNCH();
   // 3. gate, output projection, residual
   CUtensorMap tz, to, twg, two;
@@ -785,7 +795,10 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   oa.accumulate = acc;
   oa.status = status;
   const int64_t nto = n_rows * oa.tiles_per_row;
-  k_triatt_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tz, to, twg, two, oa);
+  {
+    PF_LAUNCH_SCOPE(st, "k_triatt_out");
+    k_triatt_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tz, to, twg, two, oa);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }

@@ -16,6 +16,7 @@
 // Reference: opendde/model/triangular/triangular.py:530-567 (maths), :112-139 (orientation).
 
 #include "pf_common.cuh"
+#include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
 #include "pf_tmap.h"
@@ -538,7 +539,10 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   pa.status = status;
   const int64_t nt = pa.side[0].ntiles > pa.side[1].ntiles ? pa.side[0].ntiles : pa.side[1].ntiles;
   if (2 * nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "trimul projection grid too large");
-  k_trimul_proj<<<(unsigned)(2 * nt), 128, PROJ_SMEM + 1024, st>>>(tz0, tz1, tw0p, tw0g, tw1p, tw1g, pa);
+  {
+    PF_LAUNCH_SCOPE(st, "k_trimul_proj");
+    k_trimul_proj<<<(unsigned)(2 * nt), 128, PROJ_SMEM + 1024, st>>>(tz0, tz1, tw0p, tw0g, tw1p, tw1g, pa);
+  }
   PF_CHECK_LAUNCH();
   // 2. contraction x[ch] = a[ch] b[ch]^T
   CUtensorMap ta, tb;
@@ -555,7 +559,10 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   GemmArgs ga{(int)n_i, (int)n_j, (int)n_k, w.x, w.ld_j, (int64_t)n_i * w.ld_j, status};
   dim3 grid((unsigned)((n_j + BN - 1) / BN), (unsigned)((n_i + BM - 1) / BM), CH);
   if (grid.y > 65535) return fail(PF_EUNSUPPORTED, "trimul contraction grid too large");
-  k_trimul_bgemm<<<grid, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
+  {
+    PF_LAUNCH_SCOPE(st, "k_trimul_bgemm");
+    k_trimul_bgemm<<<grid, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
+  }
   PF_CHECK_LAUNCH();
   // 3. LN_out, W_z, gate, residual
   CUtensorMap tzg, twz, twg;
@@ -579,7 +586,10 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   oa.accumulate = acc;
   oa.status = status;
   const int64_t nto = n_i * oa.tiles_per_row;
-  k_trimul_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tzg, twz, twg, oa);
+  {
+    PF_LAUNCH_SCOPE(st, "k_trimul_out");
+    k_trimul_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tzg, twz, twg, oa);
+  }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
