@@ -127,6 +127,23 @@ PF_API int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_vie
                   int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* Allocation-free variant of pf_trimul_fwd (no counterpart in the reference). For callers
+ * that cannot allocate device memory or pass a workspace (a plugin inside a runtime that owns
+ * every allocation, a foreign-language binding that only holds its input/output pointers):
+ * the scratch comes from a fixed array of PF_STATIC_SCRATCH_BYTES compiled into the library,
+ * reserved on every GPU that loads it until the process exits (48 MiB: a square bf16 problem
+ * up to n = 256 with c_z = c_h = 128). Larger requests return PF_EINVAL_SHAPE with a message
+ * naming the limit. The first call on a device looks up the array's device address (make it
+ * before any stream capture begins); no call allocates or frees memory. Calls share the
+ * array: calls whose GPU work overlaps race and must be serialised by the caller. */
+#define PF_STATIC_SCRATCH_BYTES (48u * 1024u * 1024u)
+PF_API size_t pf_static_scratch_bytes(void);
+PF_API int pf_trimul_fwd_static_scratch(const pf_trimul_params* w, pf_pair_view za, pf_pair_view zb,
+                                        pf_mask_view ma, pf_mask_view mb, pf_pair_view zg,
+                                        pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+                                        int32_t c_z, int32_t c_h, int32_t accumulate, int32_t dtype,
+                                        void* stream);
+
 /* ---- Triangle attention (starting node; ending node = transposed views) ------------------
  * Replaces TriangleAttention.forward (opendde/model/triangular/triangular.py:648-706) with
  * Attention._prep_qkv/_attention/_wrap_up (opendde/model/triangular/layers.py:302-424), and

@@ -40,6 +40,7 @@ EXPORTED = (
     "pf_launch_count", "pf_profile_enable", "pf_profile_report",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
+    "pf_static_scratch_bytes", "pf_trimul_fwd_static_scratch",
     "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
     "pf_transition_workspace_size", "pf_transition_fwd",
     "pf_apb_pair_bias_workspace_size", "pf_apb_pair_bias", "pf_apb_workspace_size", "pf_apb_fwd",
@@ -107,6 +108,10 @@ def load(path: str = LIB_PATH):
         "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
                            c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_static_scratch_bytes": ([], c_size_t),
+        "pf_trimul_fwd_static_scratch": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView,
+                                          PairView, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,
+                                          c_void_p], c_int),
         "pf_triatt_bias_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_triatt_bias": ([POINTER(TriattParams), PairView, c_int64, c_int64, c_void_p, c_int64, c_int64,
                             c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
