@@ -315,7 +315,7 @@ static int ln_view(const T* x, int64_t rs, int64_t cs, int64_t n_rows, int64_t n
   int64_t P = n_rows * n_cols;
   if (P == 0) return PF_OK;
   {
-    PF_LAUNCH_SCOPE(0, "k_ln_view");
+    PF_LAUNCH_SCOPE(st, "k_ln_view");
     k_ln_view<T, TO><<<nblk(P, 8), 256, 0, st>>>(x, rs, cs, n_rows, n_cols, c, g, b, eps, out, ops);
   }
   PF_CHECK_LAUNCH();
@@ -393,7 +393,7 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
   PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ap, 0, c_z, w.pa, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ag, 0, c_z, w.pg, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_gate_to_cmajor");
+    PF_LAUNCH_SCOPE(st, "k_gate_to_cmajor");
     k_gate_to_cmajor<<<nblk(Pa * c_h, 256), 256, 0, st>>>(w.pa, w.pg, ma, n_i, n_k, c_h, w.a);
   }
   PF_CHECK_LAUNCH();
@@ -403,7 +403,7 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
   PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bp, 0, c_z, w.pa, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bg, 0, c_z, w.pg, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_gate_to_cmajor");
+    PF_LAUNCH_SCOPE(st, "k_gate_to_cmajor");
     k_gate_to_cmajor<<<nblk(Pb * c_h, 256), 256, 0, st>>>(w.pa, w.pg, mb, n_j, n_k, c_h, w.b);
   }
   PF_CHECK_LAUNCH();
@@ -412,7 +412,7 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
                              1.f, 0, st)));
   // LN_out, linear_z
   {
-    PF_LAUNCH_SCOPE(0, "k_ln_cmajor");
+    PF_LAUNCH_SCOPE(st, "k_ln_cmajor");
     k_ln_cmajor<<<nblk(Po, 8), 256, 0, st>>>(w.p, Po, c_h, p->ln_out_w, p->ln_out_b, eps, w.xn);
   }
   PF_CHECK_LAUNCH();
@@ -424,7 +424,7 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
   PF_TRY((gemm<float, T>(w.xo, 0, c_z, (const T*)p->w_g, 0, c_z, w.gg, 0, c_z, 1, 1, Po, c_z, c_z,
                          1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    PF_LAUNCH_SCOPE(st, "k_combine_view");
     k_combine_view<T><<<nblk(Po * c_z, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
                                                            n_i, n_j, c_z, w.y, w.gg, acc);
   }
@@ -534,9 +534,9 @@ static int triatt_t(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, 
                                   (const float*)bias, b_hs, b_rs, 1.0f, m, inf, n_rows, n_q, H,
                                   n_valid, w.o, n_q * hd, hd, st)));
   } else {
-    // bf16 bias buffers hold log2-scaled values (the tensor-core path's format)
-    PF_TRY((launch_attn<T, __nv_bfloat16>(d, w.q, n_keys * hd, hd, q_col0, w.k, w.v, n_keys * hd,
-                                          hd, (const __nv_bfloat16*)bias, b_hs, b_rs,
+    // bf16-mode bias buffers hold f16 log2-scaled values (the tensor-core path's format)
+    PF_TRY((launch_attn<T, __half>(d, w.q, n_keys * hd, hd, q_col0, w.k, w.v, n_keys * hd,
+                                          hd, (const __half*)bias, b_hs, b_rs,
                                           0.69314718055994531f, m, inf, n_rows, n_q, H, n_valid,
                                           w.o, n_q * hd, hd, st)));
   }
@@ -544,13 +544,13 @@ static int triatt_t(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, 
   PF_TRY((gemm<float, T>(w.x + q_col0 * c, n_keys * c, c, (const T*)p->w_g, 0, c, w.g, n_q * hd,
                          hd, 1, n_rows, n_q, hd, c, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_gate_inplace");
+    PF_LAUNCH_SCOPE(st, "k_gate_inplace");
     k_gate_inplace<<<nblk(Pq * hd, 256), 256, 0, st>>>(w.o, w.g, Pq * hd);
   }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(w.o, 0, hd, (const T*)p->w_o, 0, hd, w.y, 0, c, 1, 1, Pq, c, hd, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    PF_LAUNCH_SCOPE(st, "k_combine_view");
     k_combine_view<T><<<nblk(Pq * c, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride,
                                                          n_rows, n_q, c, w.y, nullptr, acc);
   }
@@ -598,7 +598,7 @@ int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64
     PF_TRY(triatt_bias_t<float>(p, z, n_rows, n_cols, bias, hs, rs, c, H, 1.f, x, st));
     PF_TRY((gemm<float, float>(x, 0, c, (const float*)p->w_bias, 0, c, bb, 0, H, 1, 1, P, H, c, 1.f, 0, st)));
     {
-      PF_LAUNCH_SCOPE(0, "k_bias_store");
+      PF_LAUNCH_SCOPE(st, "k_bias_store");
       k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, (float*)bias, hs, rs, 1.f);
     }
   } else {
@@ -606,9 +606,9 @@ int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64
     PF_TRY((gemm<float, __nv_bfloat16>(x, 0, c, (const __nv_bfloat16*)p->w_bias, 0, c, bb, 0, H, 1, 1,
                                        P, H, c, 1.f, 0, st)));
     {
-      PF_LAUNCH_SCOPE(0, "k_bias_store");
-      k_bias_store<__nv_bfloat16><<<nblk(P * H, 256), 256, 0, st>>>(
-          bb, n_rows, n_cols, H, (__nv_bfloat16*)bias, hs, rs, 1.4426950408889634f);
+      PF_LAUNCH_SCOPE(st, "k_bias_store");
+      k_bias_store<__half><<<nblk(P * H, 256), 256, 0, st>>>(
+          bb, n_rows, n_cols, H, (__half*)bias, hs, rs, 1.4426950408889634f);
     }
   }
   PF_CHECK_LAUNCH();
@@ -638,13 +638,13 @@ static int transition_t(const pf_transition_params* p, const T* x, int64_t xs, T
   PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_a, 0, c, a, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(y, 0, c, (const T*)p->w_b, 0, c, b, 0, hc, 1, 1, rows, hc, c, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_swiglu");
+    PF_LAUNCH_SCOPE(st, "k_swiglu");
     k_swiglu<<<nblk(rows * hc, 256), 256, 0, st>>>(a, b, rows * hc);
   }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(b, 0, hc, (const T*)p->w_o, 0, hc, o, 0, c, 1, 1, rows, c, hc, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    PF_LAUNCH_SCOPE(st, "k_combine_view");
     k_combine_view<T><<<nblk(rows * c, 256), 256, 0, st>>>(out, os, 0, rows, 1, c, o, nullptr, acc);
   }
   PF_CHECK_LAUNCH();
@@ -685,7 +685,7 @@ int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_
                                        1, P, H, c_z, 1.f, 0, st)));
   }
   {
-    PF_LAUNCH_SCOPE(0, "k_bias_store");
+    PF_LAUNCH_SCOPE(st, "k_bias_store");
     k_bias_store<float><<<nblk(P * H, 256), 256, 0, st>>>(bb, n_rows, n_cols, H, bias, hs, rs, 1.f);
   }
   PF_CHECK_LAUNCH();
@@ -716,7 +716,7 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_q, 0, c_s, q, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   if (p->b_q) {
     {
-      PF_LAUNCH_SCOPE(0, "k_add_bias");
+      PF_LAUNCH_SCOPE(st, "k_add_bias");
       k_add_bias<<<nblk(n * c_s, 256), 256, 0, st>>>(q, p->b_q, n, c_s);
     }
     PF_CHECK_LAUNCH();
@@ -729,13 +729,13 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, n * n, n, 1.0f, nomask, 0.f,
                                 1, n, H, n, o, 0, c_s, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_gate_inplace");
+    PF_LAUNCH_SCOPE(st, "k_gate_inplace");
     k_gate_inplace<<<nblk(n * c_s, 256), 256, 0, st>>>(o, g, n * c_s);
   }
   PF_CHECK_LAUNCH();
   PF_TRY((gemm<float, T>(o, 0, c_s, (const T*)p->w_o, 0, c_s, y, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   {
-    PF_LAUNCH_SCOPE(0, "k_combine_view");
+    PF_LAUNCH_SCOPE(st, "k_combine_view");
     k_combine_view<T><<<nblk(n * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, n, 1, c_s, y, nullptr, acc);
   }
   PF_CHECK_LAUNCH();

@@ -35,9 +35,14 @@ constexpr float LOG2E = 1.4426950408889634f;
 enum TileFlag : uint8_t { TF_NOADD = 0, TF_ADD = 1, TF_SKIP = 2 };
 
 // ------------------------------------------------------------------ mask prep
+// Key bias per row in f16 log2 units: 0 for a key with mask >= 1, -inf for a masked key (the
+// reference's inf*(m-1) with inf = 1e9 sends it to exactly zero weight next to any valid key)
+// and for keys that do not exist. A row with no key of mask 1 is a "uniform" row: the
+// reference's logits are all ~ -1e9 there and its softmax is the uniform average over the
+// keys, so its bias is 0 on existing keys and the core ignores the logits (rowflags bit 0).
 __global__ void k_triatt_maskprep(pf_mask_view m, int64_t n_keys, int64_t n_valid, float inf,
-                                  float* __restrict__ mb, int64_t ld_mb, uint8_t* __restrict__ flags,
-                                  int n_tiles) {
+                                  __half* __restrict__ mb, int64_t ld_mb, uint8_t* __restrict__ flags,
+                                  uint8_t* __restrict__ rowflags, int n_tiles) {
   const int64_t i = blockIdx.x;
   const int tid = threadIdx.x;  // 128 threads
   __shared__ int s_any_full;
@@ -46,20 +51,22 @@ __global__ void k_triatt_maskprep(pf_mask_view m, int64_t n_keys, int64_t n_vali
   int any_full = 0;
   for (int64_t k = tid; k < n_valid; k += 128) {
     const float mv = m.ptr ? m.ptr[i * m.row_stride + k * m.col_stride] : 1.0f;
-    any_full |= (mv == 1.0f);
+    any_full |= (mv >= 1.0f);
   }
   if (any_full) atomicOr(&s_any_full, 1);
   __syncthreads();
   const bool row_full = s_any_full != 0;
+  if (tid == 0) rowflags[i] = row_full ? 0 : 1;
   for (int kt = 0; kt < n_tiles; ++kt) {
     const int64_t k = (int64_t)kt * 128 + tid;
     float mv = 0.f;
-    bool exists = k < n_valid;
+    const bool exists = k < n_valid;
     if (exists) mv = m.ptr ? m.ptr[i * m.row_stride + k * m.col_stride] : 1.0f;
-    mb[i * ld_mb + k] = exists ? inf * (mv - 1.0f) * LOG2E : -INFINITY;
-    const int all_one = __syncthreads_and(exists && mv == 1.0f);
-    const int all_zero = __syncthreads_and(!exists || mv == 0.0f);
-    if (tid == 0) flags[i * n_tiles + kt] = (all_zero && row_full) ? TF_SKIP : (all_one ? TF_NOADD : TF_ADD);
+    const bool live = exists && (mv >= 1.0f || !row_full);
+    mb[i * ld_mb + k] = live ? __float2half_rn(0.f) : __float2half_rn(-INFINITY);
+    const int all_live = __syncthreads_and(live);
+    const int all_dead = __syncthreads_and(!live);
+    if (tid == 0) flags[i * n_tiles + kt] = all_dead ? TF_SKIP : (all_live ? TF_NOADD : TF_ADD);
   }
 }
 
@@ -117,10 +124,10 @@ struct ProjArgs {
   int64_t n_rows, n_keys, tiles_per_row;
   int64_t q_col0, n_q;
   int want_qkv, want_bias;
-  __nv_bfloat16* q;   // [(i*H+h)*n_q + j][D]
-  __nv_bfloat16* k;   // [(i*H+h)*ld_keys + key][D]
+  __half* q;          // [(i*H+h)*n_q + j][D]     f16, x log2(e)/sqrt(d)
+  __half* k;          // [(i*H+h)*ld_keys + key][D] f16
   __half* vt;         // [((i*H+h)*D + dd)*ld_keys + key]
-  __nv_bfloat16* bias;  // bias + h*b_hs + r*b_rs + s (log2 units)
+  __half* bias;        // bias + h*b_hs + r*b_rs + s (f16, log2 units)
   int64_t ld_keys, b_hs, b_rs;
   const float *ln_w, *ln_b;
   float q_scale;
@@ -205,10 +212,10 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           uint4 w;
-          w.x = pack_bf16(__uint_as_float(qv[e * 8 + 0]) * a.q_scale, __uint_as_float(qv[e * 8 + 1]) * a.q_scale);
-          w.y = pack_bf16(__uint_as_float(qv[e * 8 + 2]) * a.q_scale, __uint_as_float(qv[e * 8 + 3]) * a.q_scale);
-          w.z = pack_bf16(__uint_as_float(qv[e * 8 + 4]) * a.q_scale, __uint_as_float(qv[e * 8 + 5]) * a.q_scale);
-          w.w = pack_bf16(__uint_as_float(qv[e * 8 + 6]) * a.q_scale, __uint_as_float(qv[e * 8 + 7]) * a.q_scale);
+          w.x = pack_f16(__uint_as_float(qv[e * 8 + 0]) * a.q_scale, __uint_as_float(qv[e * 8 + 1]) * a.q_scale);
+          w.y = pack_f16(__uint_as_float(qv[e * 8 + 2]) * a.q_scale, __uint_as_float(qv[e * 8 + 3]) * a.q_scale);
+          w.z = pack_f16(__uint_as_float(qv[e * 8 + 4]) * a.q_scale, __uint_as_float(qv[e * 8 + 5]) * a.q_scale);
+          w.w = pack_f16(__uint_as_float(qv[e * 8 + 6]) * a.q_scale, __uint_as_float(qv[e * 8 + 7]) * a.q_scale);
           dq[e] = w;
         }
       }
@@ -216,10 +223,10 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         uint4 w;
-        w.x = pack_bf16(__uint_as_float(kv[e * 8 + 0]), __uint_as_float(kv[e * 8 + 1]));
-        w.y = pack_bf16(__uint_as_float(kv[e * 8 + 2]), __uint_as_float(kv[e * 8 + 3]));
-        w.z = pack_bf16(__uint_as_float(kv[e * 8 + 4]), __uint_as_float(kv[e * 8 + 5]));
-        w.w = pack_bf16(__uint_as_float(kv[e * 8 + 6]), __uint_as_float(kv[e * 8 + 7]));
+        w.x = pack_f16(__uint_as_float(kv[e * 8 + 0]), __uint_as_float(kv[e * 8 + 1]));
+        w.y = pack_f16(__uint_as_float(kv[e * 8 + 2]), __uint_as_float(kv[e * 8 + 3]));
+        w.z = pack_f16(__uint_as_float(kv[e * 8 + 4]), __uint_as_float(kv[e * 8 + 5]));
+        w.w = pack_f16(__uint_as_float(kv[e * 8 + 6]), __uint_as_float(kv[e * 8 + 7]));
         dk[e] = w;
       }
     }
@@ -243,7 +250,7 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
     if (valid && a.want_bias) {
 #pragma unroll
       for (int h = 0; h < H; ++h)
-        a.bias[h * a.b_hs + r * a.b_rs + col] = __float2bfloat16_rn(__uint_as_float(bv[h]) * LOG2E);
+        a.bias[h * a.b_hs + r * a.b_rs + col] = __float2half_rn(__uint_as_float(bv[h]) * LOG2E);
     }
   }
   tc_fence_before();
@@ -255,209 +262,7 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
 }
 
 // ------------------------------------------------------------------ core
-struct CoreArgs {
-  int64_t n_rows, n_q, n_tiles_k;
-  const float* mb;        // [n_rows][ld_mb] (log2 units)
-  int64_t ld_mb;
-  const uint8_t* flags;   // [n_rows][n_tiles_k]
-  __nv_bfloat16* o;       // [(i*n_q + j)][HD]
-  unsigned int* status;
-};
-
-// shared-memory map (offsets from the 1024-aligned base)
-constexpr uint32_t C_Q = 0;                 // 128 x 64 B (SW64)          8 KB
-constexpr uint32_t C_K = 8192;              // 128 x 64 B (SW64)          8 KB
-constexpr uint32_t C_VT = 16384;            // 2 atoms x 48 rows x 128 B  12 KB (rows 32..47 = [1;0])
-constexpr uint32_t C_VT_ATOM = 48 * 128;
-constexpr uint32_t C_BIAS = 16384 + 12288;  // 2 atoms x 128 rows x 128 B 32 KB   (offset 28672)
-constexpr uint32_t C_P = C_BIAS + 32768;    // 2 atoms x 128 rows x 128 B 32 KB   (offset 61440)
-constexpr uint32_t C_MB = C_P + 32768;      // 128 fp32                    512 B (offset 94208)
-constexpr uint32_t C_BAR = C_MB + 512;
-constexpr uint32_t CORE_SMEM = C_BAR + 64;
-static_assert(C_BIAS % 1024 == 0 && C_P % 1024 == 0 && C_VT_ATOM % 1024 == 0, "swizzle atoms need 1 KB alignment");
-
-__global__ void __launch_bounds__(160, 2) k_triatt_core(const __grid_constant__ CUtensorMap tq,
-                                                        const __grid_constant__ CUtensorMap tk,
-                                                        const __grid_constant__ CUtensorMap tvt,
-                                                        const __grid_constant__ CUtensorMap tb,
-                                                        const __grid_constant__ CUtensorMap tmb,
-                                                        const CoreArgs a) {
-  extern __shared__ uint8_t smem_raw[];
-  const uint32_t raw = smem_u32(smem_raw);
-  const uint32_t base = (raw + 1023u) & ~1023u;
-  uint8_t* g = smem_raw + (base - raw);
-  const uint32_t bar_q = base + C_BAR, bar_kv = bar_q + 8, bar_s = bar_q + 16, bar_p = bar_q + 24,
-                 bar_o = bar_q + 32;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + C_BAR + 48);
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t jt = blockIdx.x;                // query tile
-  const int h = blockIdx.y;
-  const int64_t i = blockIdx.z;
-  const int64_t j0 = jt * TILE;
-  const int ih = (int)(i * H + h);
-  const uint8_t* flags = a.flags + i * a.n_tiles_k;
-
-  if (tid == 128) {
-    mbar_init(bar_q, 1);
-    mbar_init(bar_kv, 1);
-    mbar_init(bar_s, 1);
-    mbar_init(bar_p, 4);
-    mbar_init(bar_o, 1);
-    fence_barrier_init();
-  }
-  if (warp == 4) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
-    tmem_relinquish();
-  }
-  if (tid < 128) {
-    // constant augmentation rows of the V^T operand: row 32 = 1.0 (f16), rows 33..47 = 0
-    for (int idx = tid; idx < 2 * 16 * 8; idx += 128) {
-      const int atom = idx >> 7, rr = 32 + ((idx >> 3) & 15), ch = idx & 7;
-      const uint32_t one2 = (rr == 32) ? 0x3C003C00u : 0u;
-      *reinterpret_cast<uint4*>(g + C_VT + atom * C_VT_ATOM + sw128_off(rr, ch)) =
-          make_uint4(one2, one2, one2, one2);
-    }
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t t_s = tmem, t_o = tmem + 128;
-
-  if (warp == 4) {
-    if (lane == 0) {
-      // producer + MMA issuer (single thread, serialised per key tile)
-      mbar_arrive_expect_tx(bar_q, 128 * 64);
-      tma_load_3d(base + C_Q, &tq, bar_q, 0, (int)j0, ih);
-      bool ok = mbar_wait(bar_q, 0, a.status);
-      uint32_t it = 0;
-      for (int64_t kt = 0; kt < a.n_tiles_k && ok; ++kt) {
-        if (flags[kt] == TF_SKIP) continue;
-        const int k0 = (int)(kt * TILE);
-        mbar_arrive_expect_tx(bar_kv, 8192 + 2 * 4096 + 32768 + 512);
-        tma_load_3d(base + C_K, &tk, bar_kv, 0, k0, ih);
-        tma_load_3d(base + C_VT, &tvt, bar_kv, k0, 0, ih);
-        tma_load_3d(base + C_VT + C_VT_ATOM, &tvt, bar_kv, k0 + 64, 0, ih);
-        tma_load_3d(base + C_BIAS, &tb, bar_kv, k0, (int)j0, h);
-        tma_load_3d(base + C_BIAS + 16384, &tb, bar_kv, k0 + 64, (int)j0, h);
-        tma_load_2d(base + C_MB, &tmb, bar_kv, k0, (int)i);
-        ok = mbar_wait(bar_kv, it & 1, a.status);
-        tc_fence_after();
-        // S = Q K^T : M=128, N=128, K=32 (two K=16 steps inside the 64 B swizzle row)
-        constexpr uint32_t id_s = idesc_f16(128, 128, true);
-        umma_f16(t_s, sdesc(base + C_Q, 512, SWZ_64B), sdesc(base + C_K, 512, SWZ_64B), id_s, 0u);
-        umma_f16(t_s, sdesc(base + C_Q + 32, 512, SWZ_64B), sdesc(base + C_K + 32, 512, SWZ_64B), id_s, 1u);
-        umma_commit(bar_s);
-        ok = ok && mbar_wait(bar_p, it & 1, a.status);
-        tc_fence_after();
-        // [o | l] = P [V^T ; 1]^T : M=128, N=48, K=128 (f16 operands)
-        constexpr uint32_t id_o = idesc_f16(128, 48, false);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
-          umma_f16(t_o, sdesc(base + C_P + atom * 16384 + within, 1024, SWZ_128B),
-                   sdesc(base + C_VT + atom * C_VT_ATOM + within, 1024, SWZ_128B), id_o, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(bar_o);
-        ok = ok && mbar_wait(bar_o, it & 1, a.status);
-        ++it;
-      }
-    }
-  } else {
-    // softmax warps: thread = query row j0 + tid, TMEM lane quarter = warp
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    float m_run = -INFINITY, l_run = 0.f;
-    float acc[D];
-#pragma unroll
-    for (int e = 0; e < D; ++e) acc[e] = 0.f;
-    uint32_t it = 0;
-    bool ok = true;
-    for (int64_t kt = 0; kt < a.n_tiles_k && ok; ++kt) {
-      const uint8_t fl = flags[kt];
-      if (fl == TF_SKIP) continue;
-      ok = mbar_wait(bar_s, it & 1, a.status);
-      tc_fence_after();
-      float s[TILE];
-#pragma unroll
-      for (int cc = 0; cc < TILE; cc += 32) {
-        uint32_t v[32];
-        tmem_ld32(t_s + lane_base + cc, v);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[cc + e] = __uint_as_float(v[e]);
-      }
-      // + triangle bias (bf16, log2 units), + mask bias where needed
-      const float* mbs = reinterpret_cast<const float*>(g + C_MB);
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const uint4 q = *reinterpret_cast<const uint4*>(g + C_BIAS + (ch >> 3) * 16384 + sw128_off(tid, ch & 7));
-        const int c = ch * 8;
-        s[c + 0] += bf16lo(q.x); s[c + 1] += bf16hi(q.x);
-        s[c + 2] += bf16lo(q.y); s[c + 3] += bf16hi(q.y);
-        s[c + 4] += bf16lo(q.z); s[c + 5] += bf16hi(q.z);
-        s[c + 6] += bf16lo(q.w); s[c + 7] += bf16hi(q.w);
-      }
-      if (fl == TF_ADD) {
-#pragma unroll
-        for (int c = 0; c < TILE; ++c) s[c] += mbs[c];
-      }
-#pragma unroll
-      for (int c = 0; c < TILE; ++c) tmax = fmaxf(tmax, s[c]);
-      const float m_new = fmaxf(m_run, tmax);
-      const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-      const float alpha = ex2_approx(m_run - m_use);
-      // P = exp2(s - m) in f16, K-major SW128 rows of the A operand
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        const int c = ch * 8;
-        uint4 w;
-        w.x = pack_f16(ex2_approx(s[c + 0] - m_use), ex2_approx(s[c + 1] - m_use));
-        w.y = pack_f16(ex2_approx(s[c + 2] - m_use), ex2_approx(s[c + 3] - m_use));
-        w.z = pack_f16(ex2_approx(s[c + 4] - m_use), ex2_approx(s[c + 5] - m_use));
-        w.w = pack_f16(ex2_approx(s[c + 6] - m_use), ex2_approx(s[c + 7] - m_use));
-        *reinterpret_cast<uint4*>(g + C_P + (ch >> 3) * 16384 + sw128_off(tid, ch & 7)) = w;
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(bar_p);
-      ok = ok && mbar_wait(bar_o, it & 1, a.status);
-      tc_fence_after();
-      uint32_t ov[32], lv[16];
-      tmem_ld32(t_o + lane_base, ov);
-      tmem_ld16(t_o + lane_base + 32, lv);
-      tmem_ld_wait();
-#pragma unroll
-      for (int e = 0; e < D; ++e) acc[e] = acc[e] * alpha + __uint_as_float(ov[e]);
-      l_run = l_run * alpha + __uint_as_float(lv[0]);
-      m_run = m_new;
-      ++it;
-    }
-    const int64_t j = j0 + tid;
-    if (j < a.n_q) {
-      const float inv = l_run > 0.f ? 1.0f / l_run : 0.f;
-      uint4* dst = reinterpret_cast<uint4*>(a.o + ((int64_t)i * a.n_q + j) * HD + h * D);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        uint4 w;
-        w.x = pack_bf16(acc[e * 8 + 0] * inv, acc[e * 8 + 1] * inv);
-        w.y = pack_bf16(acc[e * 8 + 2] * inv, acc[e * 8 + 3] * inv);
-        w.z = pack_bf16(acc[e * 8 + 4] * inv, acc[e * 8 + 5] * inv);
-        w.w = pack_bf16(acc[e * 8 + 6] * inv, acc[e * 8 + 7] * inv);
-        dst[e] = w;
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 4) {
-    __syncwarp();
-    tc_fence_after();
-    tmem_dealloc(tmem, 256);
-  }
-}
+#include "pf_triatt_core.cuh"
 
 // ------------------------------------------------------------------ output
 struct OutArgs {
@@ -605,6 +410,17 @@ int weight_tmap(CUtensorMap* m, const void* w, int rows, int cols, int box_rows)
   return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+int64_t num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <class K>
 int set_smem(K kernel, uint32_t bytes) {
   PF_CUDA_TRY(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
@@ -615,7 +431,7 @@ int ensure_attrs() {
   static bool done = false;
   if (!done) {
     PF_TRY(set_smem(k_triatt_proj, PROJ_SMEM + 1024));
-    PF_TRY(set_smem(k_triatt_core, CORE_SMEM + 1024));
+    PF_TRY(set_smem(k_triatt_core, CORE3_SMEM + 1024));
     PF_TRY(set_smem(k_triatt_out, OUT_SMEM + 1024));
     done = true;
   }
@@ -623,10 +439,10 @@ int ensure_attrs() {
 }
 
 struct TriattWs {
-  __nv_bfloat16 *q, *k, *bias, *o;
-  __half* vt;
-  float* mb;
-  uint8_t* flags;
+  __half *q, *k;
+  __nv_bfloat16* o;
+  __half *vt, *bias, *mb;
+  uint8_t *flags, *rowflags;
   int64_t ld_keys, ld_mb, n_tiles_k;
 };
 
@@ -634,13 +450,14 @@ void triatt_plan(Arena& ar, int64_t n_rows, int64_t n_keys, int64_t n_q, bool ow
   w.ld_keys = (n_keys + 7) / 8 * 8;
   w.n_tiles_k = (n_keys + TILE - 1) / TILE;
   w.ld_mb = w.n_tiles_k * TILE;
-  w.q = ar.take<__nv_bfloat16>((size_t)n_rows * H * n_q * D);
-  w.k = ar.take<__nv_bfloat16>((size_t)n_rows * H * w.ld_keys * D);
+  w.q = ar.take<__half>((size_t)n_rows * H * n_q * D);
+  w.k = ar.take<__half>((size_t)n_rows * H * w.ld_keys * D);
   w.vt = ar.take<__half>((size_t)n_rows * H * D * w.ld_keys);
-  w.bias = own_bias ? ar.take<__nv_bfloat16>((size_t)H * n_q * w.ld_keys) : nullptr;
+  w.bias = own_bias ? ar.take<__half>((size_t)H * n_q * w.ld_keys) : nullptr;
   w.o = ar.take<__nv_bfloat16>((size_t)n_rows * n_q * HD);
-  w.mb = ar.take<float>((size_t)n_rows * w.ld_mb);
+  w.mb = ar.take<__half>((size_t)n_rows * w.ld_mb);
   w.flags = ar.take<uint8_t>((size_t)n_rows * w.n_tiles_k);
+  w.rowflags = ar.take<uint8_t>((size_t)n_rows);
 }
 
 int launch_proj(const pf_triatt_params* p, const void* zptr, int64_t rs, int64_t cs, int64_t n_rows,
@@ -686,7 +503,7 @@ int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64
   pa.n_q = 0;
   pa.want_qkv = 0;
   pa.want_bias = 1;
-  pa.bias = (__nv_bfloat16*)bias;
+  pa.bias = (__half*)bias;
   pa.b_hs = hs;
   pa.b_rs = rs;
   pa.ln_w = p->ln_w;
@@ -714,7 +531,7 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   // 0. mask bias + tile flags
   {
     PF_LAUNCH_SCOPE(st, "k_triatt_maskprep");
-    k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags,
+    k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags, w.rowflags,
                                                         (int)w.n_tiles_k);
   }
   PF_CHECK_LAUNCH();
@@ -741,15 +558,12 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   // 2. attention core
   const void* bptr = bias ? bias : (const void*)w.bias;
   const int64_t bhs = bias ? b_hs : pa.b_hs, brs = bias ? b_rs : pa.b_rs;
-  CUtensorMap tq, tk, tvt, tb, tmb;
+  CUtensorMap tk, tvt, tb, tmb;
   {
-    const uint64_t dq[3] = {(uint64_t)D, (uint64_t)n_q, (uint64_t)(n_rows * H)};
-    const uint64_t sq[2] = {(uint64_t)D * 2, (uint64_t)n_q * D * 2};
     const uint32_t bq[3] = {D, TILE, 1};
-    PF_TRY(make_tmap(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.q, dq, sq, bq, CU_TENSOR_MAP_SWIZZLE_64B));
     const uint64_t dk[3] = {(uint64_t)D, (uint64_t)n_keys, (uint64_t)(n_rows * H)};
     const uint64_t sk[2] = {(uint64_t)D * 2, (uint64_t)w.ld_keys * D * 2};
-    PF_TRY(make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.k, dk, sk, bq, CU_TENSOR_MAP_SWIZZLE_64B));
+    PF_TRY(make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.k, dk, sk, bq, CU_TENSOR_MAP_SWIZZLE_64B));
     const uint64_t dv[3] = {(uint64_t)n_keys, (uint64_t)D, (uint64_t)(n_rows * H)};
     const uint64_t sv[2] = {(uint64_t)w.ld_keys * 2, (uint64_t)D * w.ld_keys * 2};
     const uint32_t bv[3] = {64, D, 1};
@@ -757,18 +571,30 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
     const uint64_t db[3] = {(uint64_t)n_keys, (uint64_t)n_q, (uint64_t)H};
     const uint64_t sb[2] = {(uint64_t)brs * 2, (uint64_t)bhs * 2};
     const uint32_t bb[3] = {64, TILE, 1};
-    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, bptr, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, bptr, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
     const uint64_t dm[2] = {(uint64_t)w.ld_mb, (uint64_t)n_rows};
-    const uint64_t sm[1] = {(uint64_t)w.ld_mb * 4};
+    const uint64_t sm[1] = {(uint64_t)w.ld_mb * 2};
     const uint32_t bm[2] = {TILE, 1};
-    PF_TRY(make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, w.mb, dm, sm, bm, CU_TENSOR_MAP_SWIZZLE_NONE));
+    PF_TRY(make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.mb, dm, sm, bm, CU_TENSOR_MAP_SWIZZLE_NONE));
   }
-  CoreArgs ca{n_rows, n_q, w.n_tiles_k, w.mb, w.ld_mb, w.flags, w.o, status};
-  dim3 grid((unsigned)((n_q + TILE - 1) / TILE), H, (unsigned)n_rows);
-  if (n_rows > 65535) return fail(PF_EUNSUPPORTED, "triatt: more than 65535 rows per call");
-  {
+  if (n_valid == 0) {
+    // no key exists: every attention output is zero
+    PF_CUDA_TRY(cudaMemsetAsync(w.o, 0, (size_t)n_rows * n_q * HD * sizeof(__nv_bfloat16), st));
+  } else {
+    CoreArgs ca{};
+    ca.n_rows = n_rows;
+    ca.n_q = n_q;
+    ca.n_tiles_k = w.n_tiles_k;
+    ca.n_qt = (n_q + TILE - 1) / TILE;
+    ca.n_items = ((n_rows + 1) / 2) * H * ca.n_qt;
+    ca.flags = w.flags;
+    ca.rowflags = w.rowflags;
+    ca.q = w.q;
+    ca.o = w.o;
+    ca.status = status;
+    const int64_t grid = ca.n_items < num_sms() ? ca.n_items : num_sms();
     PF_LAUNCH_SCOPE(st, "k_triatt_core");
-    k_triatt_core<<<grid, 160, CORE_SMEM + 1024, st>>>(tq, tk, tvt, tb, tmb, ca);
+    k_triatt_core<<<(unsigned)grid, 320, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
   }
   PF_CHECK_LAUNCH();
   // 3. gate, output projection, residual
