@@ -139,6 +139,23 @@ __device__ __forceinline__ uint32_t tile_logits(uint32_t t_s, const uint8_t* bro
   return mx;
 }
 
+// Softmax thread: fetch its query row (32 f16) of item `it`, row r, into registers.
+__device__ __forceinline__ void fetch_q_row(const CoreArgs& a, const Item& it, int r, int row_tid,
+                                            uint32_t (&qv)[16]) {
+  const int64_t j = (int64_t)it.jt * TILE + row_tid;
+  if (j < a.n_q) {
+    const uint4* src = reinterpret_cast<const uint4*>(a.q + (((it.i0 + r) * H + it.h) * a.n_q + j) * D);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const uint4 u = src[e];
+      qv[e * 4 + 0] = u.x; qv[e * 4 + 1] = u.y; qv[e * 4 + 2] = u.z; qv[e * 4 + 3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) qv[e] = 0u;
+  }
+}
+
 // Softmax thread: copy its query row (32 f16) of item `it`, row r, into TMEM Q slot `slot`.
 __device__ __forceinline__ void load_q_row(const CoreArgs& a, const Item& it, int r, int row_tid,
                                            uint32_t tmem_row, int slot, uint32_t lane_base) {
@@ -355,18 +372,18 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_q0);
       }
+      // Q of this row's next item, one item ahead, into the other slot: fetched from global
+      // memory now, written to TMEM after this item's first tile so the fetch latency is hidden.
+      // Slot (n+1)&1 was last read by the S MMAs of item n-1, all complete by now.
+      uint32_t qnext[16];
+      bool q_pending = false;
       {
-        // Q of this row's next item, one item ahead, into the other slot. Slot (n+1)&1 was last
-        // read by the S MMAs of item n-1, all complete since this group finished item n-1.
         const int64_t wn = w + gridDim.x;
         if (wn < a.n_items) {
           const Item itn = decode_item(a, wn);
           if (r == 0 || itn.has_b) {
-            load_q_row(a, itn, r, row_tid, tb_r, (n + 1) & 1, lane_base);
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar_q0 + 8 * ((n + 1) & 1));
+            fetch_q_row(a, itn, r, row_tid, qnext);
+            q_pending = true;
           }
         }
       }
@@ -434,6 +451,14 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_p);
+        if (q_pending) {  // warp-uniform
+          tmem_st16(tb_r + lane_base + T_Q + 16 * ((n + 1) & 1), qnext);
+          tmem_st_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar_q0 + 8 * ((n + 1) & 1));
+          q_pending = false;
+        }
       }
       // item epilogue: o = O / l
       ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (t - 1) & 1, a.status)) && ok;

@@ -94,7 +94,7 @@ def test_block_bf16_vs_fp32_oracle(cuda_device):
     assert rel_l2(s_out, s_ref) <= BF16_TOL
 
 
-@pytest.mark.parametrize("kind", ["trimul_out", "trimul_in", "triatt_start", "triatt_end"])
+@pytest.mark.parametrize("kind", ["trimul_out", "trimul_in", "triatt_start", "triatt_end", "transition"])
 @pytest.mark.parametrize("n", [300])
 def test_bf16_tensor_core_path_vs_simt_path(kind, n, cuda_device):
     """The tcgen05 kernels and the SIMT kernels agree on one bf16 problem with partial tiles."""
