@@ -246,11 +246,15 @@ int pf_transition_fwd(const pf_transition_params* w, const void* x, int64_t x_st
 }
 
 // ------------------------------------------------------------------ AttentionPairBias
+static bool apb_bias_tc(int c_z, int heads, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::apb_pair_bias_supported(c_z, heads);
+}
+
 int pf_apb_pair_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t heads,
                                     int32_t dtype, size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = simt::apb_pair_bias_ws_bytes(n_rows * n_cols, c_z, heads);
+  *bytes = apb_bias_tc(c_z, heads, dtype) ? 0 : simt::apb_pair_bias_ws_bytes(n_rows * n_cols, c_z, heads);
   return PF_OK;
 }
 
@@ -265,16 +269,26 @@ int pf_apb_pair_bias(const pf_apb_params* w, pf_pair_view z, int64_t n_rows, int
   size_t need;
   PF_TRY(pf_apb_pair_bias_workspace_size(n_rows, n_cols, c_z, heads, dtype, &need));
   PF_TRY(check_ws(workspace, workspace_bytes, need, "apb_pair_bias"));
+  if (apb_bias_tc(c_z, heads, dtype)) {
+    set_path("tc");
+    return tc::apb_pair_bias(w, z, n_rows, n_cols, bias, hs, rs, (cudaStream_t)stream);
+  }
   set_path("simt");
   return simt::apb_pair_bias(w, z, n_rows, n_cols, bias, hs, rs, c_z, heads, dtype, workspace,
                              workspace_bytes, (cudaStream_t)stream);
 }
 
+// workspace of pf_apb_fwd: [own pair bias (only when bias == NULL)] [pair-bias scratch | attention]
+static size_t apb_own_bias_bytes(int64_t n, int heads) { return align_up((size_t)heads * n * n * 4, 256); }
+
 int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, int32_t dtype,
                           size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = simt::apb_ws_bytes_full(n, c_s, c_z, heads);
+  size_t pb = 0;
+  PF_TRY(pf_apb_pair_bias_workspace_size(n, n, c_z > 0 ? c_z : 1, heads, dtype, &pb));
+  const size_t att = simt::apb_attn_ws_bytes(n, c_s);
+  *bytes = apb_own_bias_bytes(n, heads) + (pb > att ? pb : att);
   return PF_OK;
 }
 
@@ -292,9 +306,21 @@ int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_pair_vi
   size_t need;
   PF_TRY(pf_apb_workspace_size(n, c_s, c_z, heads, dtype, &need));
   PF_TRY(check_ws(workspace, workspace_bytes, need, "apb"));
-  set_path("simt");
-  return simt::apb(w, s_in, s_out, z, bias, n, c_s, c_z, heads, accumulate, dtype, workspace,
-                   workspace_bytes, (cudaStream_t)stream);
+  char* ws = (char*)workspace;
+  const size_t own = apb_own_bias_bytes(n, heads);
+  bool bias_tc = false;
+  if (bias == nullptr) {
+    float* own_bias = (float*)ws;
+    PF_TRY(pf_apb_pair_bias(w, z, n, n, own_bias, n * n, n, c_z, heads, dtype, ws + own,
+                            workspace_bytes - own, stream));
+    bias = own_bias;
+    bias_tc = apb_bias_tc(c_z, heads, dtype);
+  }
+  // The pair bias (one pass over the N x N x c_z pair tensor) dominates; the single-row
+  // attention over N tokens is SIMT in both modes.
+  set_path(bias_tc ? "tc+simt" : "simt");
+  return simt::apb(w, s_in, s_out, z, bias, n, c_s, c_z, heads, accumulate, dtype, ws + own,
+                   workspace_bytes - own, (cudaStream_t)stream);
 }
 
 }  // extern "C"

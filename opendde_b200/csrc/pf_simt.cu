@@ -774,5 +774,15 @@ size_t apb_ws_bytes_full(int64_t n, int c_s, int c_z, int H) {
   return own + (pb > att ? pb : att) + 1024;
 }
 
+// the attention part of apb() alone (bias supplied by the caller)
+size_t apb_attn_ws_bytes(int64_t n, int c_s) {
+  Arena ar(nullptr, 0);
+  ar.take<float>(n * c_s);
+  ar.take<float>(n * c_s * 4);
+  ar.take<float>(n * c_s);
+  ar.take<float>(n * c_s);
+  return ar.used + 1024;
+}
+
 }  // namespace simt
 }  // namespace pf

@@ -27,6 +27,10 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
            int64_t n_valid, int64_t q_col0, int64_t n_q, int c, int H, int d, float inf, int acc,
            void* ws, size_t ws_bytes, cudaStream_t st);
 
+bool apb_pair_bias_supported(int c_z, int heads);
+int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols, float* bias,
+                  int64_t hs, int64_t rs, cudaStream_t st);
+
 bool transition_supported(int c, int nm);
 int transition(const pf_transition_params* p, const void* x, int64_t xs, void* out, int64_t os,
                int64_t rows, int c, int nm, int acc, cudaStream_t st);

@@ -94,7 +94,7 @@ def test_block_bf16_vs_fp32_oracle(cuda_device):
     assert rel_l2(s_out, s_ref) <= BF16_TOL
 
 
-@pytest.mark.parametrize("kind", ["trimul_out", "trimul_in", "triatt_start", "triatt_end", "transition"])
+@pytest.mark.parametrize("kind", ["trimul_out", "trimul_in", "triatt_start", "triatt_end", "transition", "apb"])
 @pytest.mark.parametrize("n", [300])
 def test_bf16_tensor_core_path_vs_simt_path(kind, n, cuda_device):
     """The tcgen05 kernels and the SIMT kernels agree on one bf16 problem with partial tiles."""
@@ -107,7 +107,8 @@ def test_bf16_tensor_core_path_vs_simt_path(kind, n, cuda_device):
         got_simt = cuda_op(kind, mod, s, z, mask, cuda_device, torch.bfloat16)
     finally:
         _abi.set_force_simt(False)
-    assert path == "tc", f"{kind} dispatched to {path}"
+    # apb: the pair bias runs on the tensor cores, the N-token single attention on SIMT.
+    assert path == ("tc+simt" if kind == "apb" else "tc"), f"{kind} dispatched to {path}"
     assert _abi.device_status(clear=True) == 0
     err = rel_l2(got_tc, got_simt)
     assert err <= 1e-2, f"{kind}: tc vs simt rel-L2 {err:.3e}"
