@@ -186,10 +186,10 @@ def kernel_work(name: str, n: int):
     table = {
         "k_triatt_core": ("tensor", 4 * HEADS_PAIR * HEAD_DIM * n3, "flop"),
         "k_trimul_bgemm": ("tensor", 2 * C_H * n3, "flop"),
-        "k_trimul_proj": ("hbm", n2 * (2 * C_Z + 2 * C_H) * 2, "byte"),   # read z once per side, write a/b
-        "k_trimul_out": ("hbm", n2 * (C_H + C_Z + 2 * C_Z) * 2, "byte"),   # read x, z(gate), z r+w
+        "k_trimul_proj": ("hbm", n2 * (C_Z + 2 * C_H) * 2, "byte"),       # read z, write a and b
+        "k_trimul_out": ("hbm", n2 * (C_H + 2 * C_Z) * 2, "byte"),        # read x and z (gate + residual), write z
         "k_triatt_proj": ("hbm", n2 * (C_Z + 3 * HEADS_PAIR * HEAD_DIM + HEADS_PAIR) * 2, "byte"),
-        "k_triatt_out": ("hbm", n2 * (C_Z + HEADS_PAIR * HEAD_DIM + 2 * C_Z) * 2, "byte"),
+        "k_triatt_out": ("hbm", n2 * (HEADS_PAIR * HEAD_DIM + 2 * C_Z) * 2, "byte"),  # read o and z, write z
         "k_transition": ("tensor", 3 * 2 * C_Z * 4 * C_Z * n2, "flop"),
     }
     return table.get(name)

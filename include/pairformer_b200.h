@@ -233,6 +233,18 @@ PF_API int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_
                int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
                void* stream);
 
+/* pf_apb_rows_fwd: the query rows [q_row0, q_row0 + n_q) of pf_apb_fwd, as the Fold-CP single
+ * bridge runs them on one rank (real_pairformer.py:1714-1810, _single_update_rank_range):
+ * keys and values come from all n rows of s_in; s_out holds n_q rows (row r = query
+ * q_row0 + r, row stride c_s); bias(h, r, k) = bias[h*head_stride + r*row_stride + k] (fp32)
+ * for local query r and key k < n. s_out = (accumulate ? s_out : 0) + APB rows. */
+PF_API int pf_apb_rows_workspace_size(int64_t n, int64_t n_q, int32_t c_s, int32_t heads, int32_t dtype,
+                                      size_t* bytes);
+PF_API int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out, const float* bias,
+                           int64_t head_stride, int64_t row_stride, int64_t n, int64_t q_row0,
+                           int64_t n_q, int32_t c_s, int32_t heads, int32_t accumulate, int32_t dtype,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

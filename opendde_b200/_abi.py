@@ -44,6 +44,7 @@ EXPORTED = (
     "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
     "pf_transition_workspace_size", "pf_transition_fwd",
     "pf_apb_pair_bias_workspace_size", "pf_apb_pair_bias", "pf_apb_workspace_size", "pf_apb_fwd",
+    "pf_apb_rows_workspace_size", "pf_apb_rows_fwd",
 )
 
 
@@ -128,6 +129,9 @@ def load(path: str = LIB_PATH):
         "pf_apb_workspace_size": ([c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
         "pf_apb_fwd": ([POINTER(ApbParams), c_void_p, c_void_p, PairView, c_void_p, c_int64, c_int32, c_int32,
                         c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_apb_rows_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_apb_rows_fwd": ([POINTER(ApbParams), c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                             c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

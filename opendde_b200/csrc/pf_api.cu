@@ -287,7 +287,7 @@ int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, in
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   size_t pb = 0;
   PF_TRY(pf_apb_pair_bias_workspace_size(n, n, c_z > 0 ? c_z : 1, heads, dtype, &pb));
-  const size_t att = simt::apb_attn_ws_bytes(n, c_s);
+  const size_t att = simt::apb_rows_ws_bytes(n, n, c_s);
   *bytes = apb_own_bias_bytes(n, heads) + (pb > att ? pb : att);
   return PF_OK;
 }
@@ -319,8 +319,37 @@ int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_pair_vi
   // The pair bias (one pass over the N x N x c_z pair tensor) dominates; the single-row
   // attention over N tokens is SIMT in both modes.
   set_path(bias_tc ? "tc+simt" : "simt");
-  return simt::apb(w, s_in, s_out, z, bias, n, c_s, c_z, heads, accumulate, dtype, ws + own,
-                   workspace_bytes - own, (cudaStream_t)stream);
+  return simt::apb_rows(w, s_in, s_out, bias, n * n, n, n, 0, n, c_s, heads, accumulate, dtype, ws + own,
+                        workspace_bytes - own, (cudaStream_t)stream);
+}
+
+int pf_apb_rows_workspace_size(int64_t n, int64_t n_q, int32_t c_s, int32_t heads, int32_t dtype,
+                               size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  (void)heads;
+  *bytes = simt::apb_rows_ws_bytes(n, n_q, c_s);
+  return PF_OK;
+}
+
+int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out, const float* bias,
+                    int64_t head_stride, int64_t row_stride, int64_t n, int64_t q_row0, int64_t n_q,
+                    int32_t c_s, int32_t heads, int32_t accumulate, int32_t dtype, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_q || !w->w_k || !w->w_v || !w->w_g || !w->w_o || !s_in || !s_out || !bias)
+    return fail(PF_EINVAL_ARG, "apb_rows: null pointer");
+  if (n < 0 || n_q < 0 || q_row0 < 0 || q_row0 + n_q > n || c_s <= 0 || c_s > 1024 || heads <= 0 ||
+      c_s % heads != 0)
+    return fail(PF_EINVAL_SHAPE, "apb_rows: bad sizes n=%lld q_row0=%lld n_q=%lld c_s=%d heads=%d",
+                (long long)n, (long long)q_row0, (long long)n_q, c_s, heads);
+  if (n_q == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_apb_rows_workspace_size(n, n_q, c_s, heads, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "apb_rows"));
+  set_path("simt");
+  return simt::apb_rows(w, s_in, s_out, bias, head_stride, row_stride, n, q_row0, n_q, c_s, heads,
+                        accumulate, dtype, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 }  // extern "C"

@@ -692,96 +692,69 @@ int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_
   return PF_OK;
 }
 
-size_t apb_ws_bytes(int64_t n, int c_s, int H) {
-  Arena ar(nullptr, 0);
-  ar.take<float>(n * c_s);        // a
-  ar.take<float>(n * c_s * 4);    // q k v g
-  ar.take<float>(n * c_s);        // o
-  ar.take<float>(n * c_s);        // y
-  ar.take<float>((int64_t)H * n * n);  // own bias
-  return ar.used;
-}
-
 template <class T>
-static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* bias, int64_t n,
-                 int c_s, int H, int acc, Arena& ar, cudaStream_t st) {
+static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* bias, int64_t b_hs,
+                 int64_t b_rs, int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, Arena& ar,
+                 cudaStream_t st) {
+  // keys/values need LN(s) of all n rows; queries, gate and output only rows [q0, q0 + nq)
   float* a = ar.take<float>(n * c_s);
-  float* qkvg = ar.take<float>(n * c_s * 4);
-  float* o = ar.take<float>(n * c_s);
-  float* y = ar.take<float>(n * c_s);
+  float* kv = ar.take<float>(n * c_s * 2);
+  float* qg = ar.take<float>(nq * c_s * 2);
+  float* o = ar.take<float>(nq * c_s);
+  float* y = ar.take<float>(nq * c_s);
   if (!ar.ok()) return fail(PF_EWORKSPACE, "apb workspace too small");
-  float *q = qkvg, *k = qkvg + n * c_s, *v = qkvg + 2 * n * c_s, *g = qkvg + 3 * n * c_s;
+  float *k = kv, *v = kv + n * c_s, *q = qg, *g = qg + nq * c_s;
+  const float* aq = a + q0 * c_s;
   const int d = c_s / H;
   PF_TRY((ln_view<T, float>(s_in, c_s, 0, n, 1, c_s, p->ln_a_w, p->ln_a_b, 1e-5f, a, c_s, st)));
-  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_q, 0, c_s, q, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(aq, 0, c_s, (const T*)p->w_q, 0, c_s, q, 0, c_s, 1, 1, nq, c_s, c_s, 1.f, 0, st)));
   if (p->b_q) {
     {
       PF_LAUNCH_SCOPE(st, "k_add_bias");
-      k_add_bias<<<nblk(n * c_s, 256), 256, 0, st>>>(q, p->b_q, n, c_s);
+      k_add_bias<<<nblk(nq * c_s, 256), 256, 0, st>>>(q, p->b_q, nq, c_s);
     }
     PF_CHECK_LAUNCH();
   }
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_k, 0, c_s, k, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_v, 0, c_s, v, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
-  PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_g, 0, c_s, g, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(aq, 0, c_s, (const T*)p->w_g, 0, c_s, g, 0, c_s, 1, 1, nq, c_s, c_s, 1.f, 0, st)));
   pf_mask_view nomask{nullptr, 0, 0};
-  // one "row" (i = 0) of n queries over n keys; bias(h, j, k) = bias[h*n*n + j*n + k]
-  PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, n * n, n, 1.0f, nomask, 0.f,
-                                1, n, H, n, o, 0, c_s, st)));
+  // one "row" (i = 0) of nq queries over n keys; bias(h, j, k) = bias[h*b_hs + j*b_rs + k]
+  PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, b_hs, b_rs, 1.0f, nomask, 0.f,
+                                1, nq, H, n, o, 0, c_s, st)));
   {
     PF_LAUNCH_SCOPE(st, "k_gate_inplace");
-    k_gate_inplace<<<nblk(n * c_s, 256), 256, 0, st>>>(o, g, n * c_s);
+    k_gate_inplace<<<nblk(nq * c_s, 256), 256, 0, st>>>(o, g, nq * c_s);
   }
   PF_CHECK_LAUNCH();
-  PF_TRY((gemm<float, T>(o, 0, c_s, (const T*)p->w_o, 0, c_s, y, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(o, 0, c_s, (const T*)p->w_o, 0, c_s, y, 0, c_s, 1, 1, nq, c_s, c_s, 1.f, 0, st)));
   {
     PF_LAUNCH_SCOPE(st, "k_combine_view");
-    k_combine_view<T><<<nblk(n * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, n, 1, c_s, y, nullptr, acc);
+    k_combine_view<T><<<nblk(nq * c_s, 256), 256, 0, st>>>(s_out, c_s, 0, nq, 1, c_s, y, nullptr, acc);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
 
-int apb(const pf_apb_params* p, const void* s_in, void* s_out, pf_pair_view z, const float* bias,
-        int64_t n, int c_s, int c_z, int H, int acc, int dtype, void* ws, size_t ws_bytes,
-        cudaStream_t st) {
-  Arena ar(ws, ws_bytes);
-  if (bias == nullptr) {
-    float* own = ar.take<float>((int64_t)H * n * n);
-    if (!ar.ok()) return fail(PF_EWORKSPACE, "apb workspace too small");
-    // the pair-bias pass needs its own scratch: reuse the tail of the workspace
-    size_t tail_off = align_up(ar.used, 256);
-    size_t need = apb_pair_bias_ws_bytes(n * n, c_z, H);
-    size_t after = tail_off + need;
-    if (!ar.counting && after > ar.cap) {
-      // the pair-bias scratch is only needed before the single-attention pass: place it
-      // after the bias buffer, the attention buffers reuse the same region afterwards
-      return fail(PF_EWORKSPACE, "apb workspace too small for the pair-bias pass");
-    }
-    PF_TRY(apb_pair_bias(p, z, n, n, own, n * n, n, c_z, H, dtype, ar.base + tail_off, need, st));
-    bias = own;
-  }
-  if (dtype == PF_F32)
-    return apb_t<float>(p, (const float*)s_in, (float*)s_out, bias, n, c_s, H, acc, ar, st);
-  return apb_t<__nv_bfloat16>(p, (const __nv_bfloat16*)s_in, (__nv_bfloat16*)s_out, bias, n, c_s,
-                              H, acc, ar, st);
-}
-
-size_t apb_ws_bytes_full(int64_t n, int c_s, int c_z, int H) {
-  size_t own = align_up((size_t)H * n * n * 4, 256);
-  size_t pb = apb_pair_bias_ws_bytes(n * n, c_z, H);
-  size_t att = apb_ws_bytes(n, c_s, H) - align_up((size_t)H * n * n * 4, 256);
-  return own + (pb > att ? pb : att) + 1024;
-}
-
-// the attention part of apb() alone (bias supplied by the caller)
-size_t apb_attn_ws_bytes(int64_t n, int c_s) {
+size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s) {
   Arena ar(nullptr, 0);
   ar.take<float>(n * c_s);
-  ar.take<float>(n * c_s * 4);
-  ar.take<float>(n * c_s);
-  ar.take<float>(n * c_s);
+  ar.take<float>(n * c_s * 2);
+  ar.take<float>(nq * c_s * 2);
+  ar.take<float>(nq * c_s);
+  ar.take<float>(nq * c_s);
   return ar.used + 1024;
+}
+
+int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float* bias, int64_t b_hs,
+             int64_t b_rs, int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, int dtype, void* ws,
+             size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return apb_t<float>(p, (const float*)s_in, (float*)s_out, bias, b_hs, b_rs, n, q0, nq, c_s, H, acc,
+                        ar, st);
+  return apb_t<__nv_bfloat16>(p, (const __nv_bfloat16*)s_in, (__nv_bfloat16*)s_out, bias, b_hs, b_rs, n,
+                              q0, nq, c_s, H, acc, ar, st);
 }
 
 }  // namespace simt

@@ -33,11 +33,10 @@ size_t apb_pair_bias_ws_bytes(int64_t P, int c_z, int H);
 int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
                   float* bias, int64_t hs, int64_t rs, int c_z, int H, int dtype, void* ws,
                   size_t ws_bytes, cudaStream_t st);
-size_t apb_ws_bytes_full(int64_t n, int c_s, int c_z, int H);
-size_t apb_attn_ws_bytes(int64_t n, int c_s);
-int apb(const pf_apb_params* p, const void* s_in, void* s_out, pf_pair_view z, const float* bias,
-        int64_t n, int c_s, int c_z, int H, int acc, int dtype, void* ws, size_t ws_bytes,
-        cudaStream_t st);
+size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s);
+int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float* bias, int64_t b_hs,
+             int64_t b_rs, int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, int dtype, void* ws,
+             size_t ws_bytes, cudaStream_t st);
 
 }  // namespace simt
 }  // namespace pf

@@ -208,3 +208,25 @@ def apb(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, z: Optional[t
     check(_abi.load().pf_apb_fwd(ctypes.byref(pack.struct), s_in.data_ptr(), s_out.data_ptr(), zv,
                                  _ptr(bias), n, c_s, c_z, heads, int(accumulate), code,
                                  ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def apb_rows(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, bias: torch.Tensor, q_row0: int,
+             heads: int, accumulate: bool) -> None:
+    """s_out (+)= AttentionPairBias query rows [q_row0, q_row0 + len(s_out)) of s_in.
+
+    ``bias`` is the fp32 pair bias of those query rows over all keys, [H, n_q, n] with a
+    contiguous key dimension (any head/row strides).
+    """
+    require_cuda(s_in, s_out, bias)
+    code = dtype_code(s_in)
+    n, c_s = s_in.shape
+    n_q = s_out.shape[0]
+    if not s_out.is_contiguous() or s_out.shape[1] != c_s or s_out.dtype != s_in.dtype:
+        raise ValueError("apb_rows output must be a contiguous [n_q, c_s] tensor of the input dtype")
+    if bias.dtype != torch.float32 or bias.dim() != 3 or bias.shape[1] < n_q or bias.shape[2] < n or bias.stride(2) != 1:
+        raise ValueError("apb_rows bias must be float32 [H, n_q, n] with contiguous keys")
+    nbytes = _abi.workspace_bytes("pf_apb_rows_workspace_size", n, n_q, c_s, heads, code)
+    ws = workspace(nbytes, s_in.device)
+    check(_abi.load().pf_apb_rows_fwd(ctypes.byref(pack.struct), s_in.data_ptr(), s_out.data_ptr(),
+                                      bias.data_ptr(), bias.stride(0), bias.stride(1), n, q_row0, n_q, c_s,
+                                      heads, int(accumulate), code, ws.data_ptr(), ws.numel(), stream_ptr()))
