@@ -262,7 +262,7 @@ def main():
     if distributed:
         import torch.distributed as dist
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
         os.environ["OPENDDE_FOLDCP_MODE"] = "distributed"
         os.environ["OPENDDE_FOLDCP_SIZE_CP"] = str(world)
         os.environ["OPENDDE_FOLDCP_SIZE_DP"] = "1"

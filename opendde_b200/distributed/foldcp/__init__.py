@@ -1,0 +1,38 @@
+"""Fold-CP: 2D context parallelism of the Pairformer pair stack over an R x C GPU mesh
+(drop-in for opendde/distributed/foldcp; square meshes generalised to R x C)."""
+
+from .config import FOLDCP_ENVIRONMENT_KEYS, FOLDCP_MESH_KEY, FoldCPConfig, apply_foldcp_config
+from .layout import FoldCP2DLayout
+from .mesh import FoldCPProcessMesh, clear_mesh_cache
+from .pair_sharding import (
+    FoldCPPairShardSpec,
+    gather_pair_tensor,
+    gather_pair_tensor_like,
+    gather_pair_tensor_like_to_rank,
+    infer_pair_dims,
+    make_pair_shard_spec,
+    shard_pair_feature_dict,
+    shard_pair_tensor,
+)
+from .real_pairformer import (
+    FoldCPPairContext,
+    distributed_attention_pair_bias_update,
+    distributed_pair_transition_update,
+    distributed_pairformer_block_pair_update,
+    distributed_pairformer_stack_pair_update,
+    distributed_pairformer_stack_single_bridge_update,
+    distributed_triangle_attention_update,
+    distributed_triangle_multiplication_update,
+    make_context,
+)
+
+__all__ = [
+    "FOLDCP_ENVIRONMENT_KEYS", "FOLDCP_MESH_KEY", "FoldCPConfig", "apply_foldcp_config", "FoldCP2DLayout",
+    "FoldCPProcessMesh", "clear_mesh_cache", "FoldCPPairShardSpec", "gather_pair_tensor",
+    "gather_pair_tensor_like", "gather_pair_tensor_like_to_rank", "infer_pair_dims", "make_pair_shard_spec",
+    "shard_pair_feature_dict", "shard_pair_tensor", "FoldCPPairContext", "make_context",
+    "distributed_attention_pair_bias_update", "distributed_pair_transition_update",
+    "distributed_pairformer_block_pair_update", "distributed_pairformer_stack_pair_update",
+    "distributed_pairformer_stack_single_bridge_update", "distributed_triangle_attention_update",
+    "distributed_triangle_multiplication_update",
+]

@@ -1,0 +1,80 @@
+"""Fold-CP on one B200: every rank of an R x C mesh emulated as a thread on cuda:0, running
+the real drivers and the real kernels (bands, bias planes, query offsets, transposed views).
+
+bf16: the CP stack equals the single-device stack (same kernels, same full-K contractions
+and full-key softmax per output) up to bf16 rounding of the exchanged tiles; fp32: equals
+the CPU oracle at the fp32 bar.
+"""
+import pytest
+import torch
+
+from foldcp_support import ThreadMesh
+from gpu_helpers import max_abs, rel_l2
+from oracle import pairformer_oracle as O
+from opendde_b200 import _abi
+from opendde_b200.distributed.foldcp import real_pairformer as RP
+from opendde_b200.distributed.foldcp.ops import KernelOps
+from opendde_b200.distributed.foldcp.pair_sharding import _spec_for, shard_with_spec
+from opendde_b200.model import PairformerStack
+from opendde_b200.utils import ragged_pair_mask, seeded_params
+
+pytestmark = pytest.mark.gpu
+
+
+def _stack(n_blocks, dev, **kw):
+    st = PairformerStack(n_blocks=n_blocks, **kw)
+    p = seeded_params([(k, tuple(v.shape)) for k, v in st.named_parameters()], seed=0, perturb_1d=True)
+    with torch.no_grad():
+        for k, v in st.named_parameters():
+            v.copy_(p[k])
+    return st.to(dev), p
+
+
+def _cp(shape, stack, s, z, mask):
+    mesh = ThreadMesh(shape)
+
+    def rank_fn(ex, rank):
+        spec = _spec_for(tuple(z.shape), shape, ex.coord, (0, 1))
+        z_local = shard_with_spec(z, spec)
+        ctx = RP.make_context(None, z_local, spec, mask_full=mask, exchange=ex)
+        return RP.distributed_pairformer_stack_single_bridge_update(
+            stack, s.clone(), z_local, None, z_spec=spec, ops=KernelOps(), context=ctx)
+
+    with torch.no_grad():
+        out = mesh.run(rank_fn)
+    torch.cuda.synchronize()
+    return out
+
+
+@pytest.mark.parametrize("shape", [(1, 2), (2, 2), (2, 4)])
+def test_cp_bf16_matches_single_device(shape, cuda_device):
+    n = 300   # not a multiple of the tiles: exercises padding and partial MMA tiles
+    stack, _ = _stack(1, cuda_device)
+    g = torch.Generator().manual_seed(1)
+    z = torch.randn((n, n, 128), generator=g).to(cuda_device, torch.bfloat16)
+    s = torch.randn((n, 384), generator=g).to(cuda_device, torch.bfloat16)
+    mask = ragged_pair_mask(n, seed=3, drop=0.2, full_rows=[5]).to(cuda_device)
+    with torch.no_grad():
+        s1, z1 = stack(s, z, mask)
+    outs = _cp(shape, stack, s, z, mask)
+    assert _abi.device_status(clear=True) == 0
+    for s2, z2 in outs:
+        assert rel_l2(z2, z1) <= 5e-3
+        assert rel_l2(s2, s1) <= 5e-3
+
+
+@pytest.mark.parametrize("shape", [(1, 2), (2, 4)])
+def test_cp_fp32_matches_oracle(shape, cuda_device):
+    n = 37
+    stack, p = _stack(1, cuda_device, n_heads=16, c_z=128, c_s=384)
+    g = torch.Generator().manual_seed(2)
+    z = torch.randn((n, n, 128), generator=g)
+    s = torch.randn((n, 384), generator=g)
+    mask = ragged_pair_mask(n, seed=4, drop=0.2, full_rows=[0])
+    torch.set_num_threads(8)
+    with torch.no_grad():
+        s_ref, z_ref = O.pairformer_stack(s, z, mask, p, 1)
+    outs = _cp(shape, stack, s.to(cuda_device), z.to(cuda_device), mask.to(cuda_device))
+    for s2, z2 in outs:
+        assert max_abs(z2, z_ref) <= 1e-4
+        assert max_abs(s2, s_ref) <= 1e-4
