@@ -410,16 +410,7 @@ int weight_tmap(CUtensorMap* m, const void* w, int rows, int cols, int box_rows)
   return make_tmap(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, w, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-int64_t num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
-  }
-  return n;
-}
+int64_t num_sms() { return sm_count(); }
 
 template <class K>
 int set_smem(K kernel, uint32_t bytes) {

@@ -19,6 +19,7 @@
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
 namespace pf {
@@ -306,149 +307,212 @@ __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__
 }
 
 // ------------------------------------------------------------------ kernel 3: output
+// Persistent: one CTA per SM walks the output tiles (tile k of the CTA goes to compute
+// warpgroup k & 1, which owns shared-memory stage k & 1 and TMEM columns [256 w, 256 w + 256)).
+//   warp 0      TMA producer: W_g, W_z once; per tile the z tile (K-major SW128) and the x tile
+//               (channel-major box, 128 channels x 128 positions) into the warpgroup's stage
+//   warp 1      MMA issuer: gate = W_g LN_in(z) into cols +128, acc = W_z LN_out(x) into cols +0
+//   warps 2-9   two warpgroups; thread = position. x column -> registers -> LN_out(x) written
+//               K-major into the x buffer; LN_in(z) in place in the z buffer; epilogue
+//               acc * sigmoid(gate) (+ residual read back from global, an L2 hit) written into
+//               the z buffer, which is then TMA-stored.
 struct OutArgs {
-  const __nv_bfloat16* x;  // [CH][n_i][ldx]
-  int64_t ldx, x_ch_stride;
-  __nv_bfloat16* zo;
-  int64_t zo_rs, zo_cs;
-  int64_t n_i, n_j, tiles_per_row;
+  int64_t n_i, n_j, tiles_per_row, n_tiles;
   const float *ln_in_w, *ln_in_b, *ln_out_w, *ln_out_b;
-  int accumulate;
+  int resid;                     // 0: none (zo = update), else zo += update
+  const __nv_bfloat16* zo;
+  int64_t zo_rs, zo_cs;
   unsigned int* status;
 };
 
-constexpr uint32_t OUT_SMEM = 3 * 32768 + 64;
+constexpr uint32_t O_WG = 0, O_WZ = 32768, O_STAGE = 65536, O_STAGE_BYTES = 65536;
+constexpr uint32_t O_LN = O_STAGE + 2 * O_STAGE_BYTES;  // 4 x 128 fp32 LayerNorm parameters
+constexpr uint32_t O_BAR = O_LN + 2048;
+constexpr uint32_t OUT_SMEM = O_BAR + 256;
 
-__global__ void __launch_bounds__(128) k_trimul_out(const __grid_constant__ CUtensorMap tzg,
-                                                    const __grid_constant__ CUtensorMap twz,
-                                                    const __grid_constant__ CUtensorMap twg,
-                                                    const OutArgs args) {
+__global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ CUtensorMap tzg,
+                                                       const __grid_constant__ CUtensorMap tx,
+                                                       const __grid_constant__ CUtensorMap tzo,
+                                                       const __grid_constant__ CUtensorMap twz,
+                                                       const __grid_constant__ CUtensorMap twg,
+                                                       const OutArgs args) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
-  const uint32_t sA = base, sBG = base + 32768, sBZ = base + 65536;
-  const uint32_t bar_load = base + 98304, bar_m1 = bar_load + 8, bar_m2 = bar_load + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 98304 + 32);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t t = blockIdx.x;
-  const int64_t i = t / args.tiles_per_row;
-  const int64_t j0 = (t % args.tiles_per_row) * TILE;
-  const int64_t j = j0 + tid;
-  const bool valid = j < args.n_j;
+  const uint32_t bars = base + O_BAR;
+  const uint32_t wbar = bars;
+  auto full = [&](int w) { return bars + 8 + 8 * w; };
+  auto empty = [&](int w) { return bars + 24 + 8 * w; };
+  auto ready = [&](int w) { return bars + 40 + 8 * w; };
+  auto done = [&](int w) { return bars + 56 + 8 * w; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + O_BAR + 128);
+  float* lnp = reinterpret_cast<float*>(g + O_LN);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_m1, 1);
-    mbar_init(bar_m2, 1);
+    mbar_init(wbar, 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(full(w), 1);
+      mbar_init(empty(w), 1);
+      mbar_init(ready(w), 1);
+      mbar_init(done(w), 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  for (int c = tid; c < 128; c += blockDim.x) {
+    lnp[c] = args.ln_in_w[c];
+    lnp[128 + c] = args.ln_in_b[c];
+    lnp[256 + c] = args.ln_out_w[c];
+    lnp[384 + c] = args.ln_out_b[c];
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int64_t G = gridDim.x;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_load, 3 * 32768);
-    tma_load_3d(sA, &tzg, bar_load, 0, (int)j0, (int)i);
-    tma_load_3d(sA + 16384, &tzg, bar_load, 64, (int)j0, (int)i);
-    tma_load_2d(sBG, &twg, bar_load, 0, 0);
-    tma_load_2d(sBG + 16384, &twg, bar_load, 64, 0);
-    tma_load_2d(sBZ, &twz, bar_load, 0, 0);
-    tma_load_2d(sBZ + 16384, &twz, bar_load, 64, 0);
-  }
-
-  // LN_out over the channels of x(i, j): channel-major reads, coalesced across the warp
-  uint32_t hv[CH / 2];
-  {
-    float v[CH];
-    const __nv_bfloat16* xp = args.x + i * args.ldx + (valid ? j : 0);
-#pragma unroll
-    for (int c = 0; c < CH; ++c) v[c] = valid ? __bfloat162float(xp[(int64_t)c * args.x_ch_stride]) : 0.f;
-    float s = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) s += v[c];
-    const float mean = s * (1.0f / CH);
-    float sq = 0.f;
-#pragma unroll
-    for (int c = 0; c < CH; ++c) {
-      const float d = v[c] - mean;
-      sq += d * d;
-    }
-    const float rstd = rsqrtf(sq * (1.0f / CH) + 1e-5f);
-#pragma unroll
-    for (int c = 0; c < CH; c += 2) {
-      const float y0 = (v[c] - mean) * rstd * __ldg(args.ln_out_w + c) + __ldg(args.ln_out_b + c);
-      const float y1 = (v[c + 1] - mean) * rstd * __ldg(args.ln_out_w + c + 1) + __ldg(args.ln_out_b + c + 1);
-      hv[c / 2] = pack_bf16(y0, y1);
-    }
-  }
-
-  mbar_wait(bar_load, 0, args.status);
-  ln_row_inplace_sw128(g, tid, args.ln_in_w, args.ln_in_b, 1e-5f);
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem + 128, sA, sBG, 16384, idesc_f16(128, 128, true));  // gate logits
-    umma_commit(bar_m1);
-  }
-  mbar_wait(bar_m1, 0, args.status);  // A is free again
-  tc_fence_after();
-#pragma unroll
-  for (int jj = 0; jj < 16; ++jj) {
-    uint4 q;
-    q.x = hv[jj * 4 + 0]; q.y = hv[jj * 4 + 1]; q.z = hv[jj * 4 + 2]; q.w = hv[jj * 4 + 3];
-    *reinterpret_cast<uint4*>(g + (jj >> 3) * 16384 + sw128_off(tid, jj & 7)) = q;
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem, sA, sBZ, 16384, idesc_f16(128, 128, true));  // W_z . LN_out(x)
-    umma_commit(bar_m2);
-  }
-  mbar_wait(bar_m2, 0, args.status);
-  tc_fence_after();
-
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  __nv_bfloat16* zp = args.zo + i * args.zo_rs + (valid ? j : 0) * args.zo_cs;
-#pragma unroll 1
-  for (int cc = 0; cc < CH; cc += 32) {
-    uint32_t zv[32], gv[32];
-    tmem_ld32(tmem + lane_base + cc, zv);
-    tmem_ld32(tmem + lane_base + 128 + cc, gv);
-    tmem_ld_wait();
-    if (valid) {
-      uint4* dst = reinterpret_cast<uint4*>(zp + cc);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float u[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          u[k] = __uint_as_float(zv[e * 8 + k]) * fast_sigmoid(__uint_as_float(gv[e * 8 + k]));
-        if (args.accumulate) {
-          const uint4 old = dst[e];
-          u[0] += bf16lo(old.x); u[1] += bf16hi(old.x); u[2] += bf16lo(old.y); u[3] += bf16hi(old.y);
-          u[4] += bf16lo(old.z); u[5] += bf16hi(old.z); u[6] += bf16lo(old.w); u[7] += bf16hi(old.w);
-        }
-        uint4 w;
-        w.x = pack_bf16(u[0], u[1]); w.y = pack_bf16(u[2], u[3]);
-        w.z = pack_bf16(u[4], u[5]); w.w = pack_bf16(u[6], u[7]);
-        dst[e] = w;
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tzg);
+      tma_prefetch_desc(&tx);
+      mbar_arrive_expect_tx(wbar, 65536);
+      tma_load_2d(base + O_WG, &twg, wbar, 0, 0);
+      tma_load_2d(base + O_WG + 16384, &twg, wbar, 64, 0);
+      tma_load_2d(base + O_WZ, &twz, wbar, 0, 0);
+      tma_load_2d(base + O_WZ + 16384, &twz, wbar, 64, 0);
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= args.n_tiles) break;
+        const int w = (int)(k & 1);
+        const int64_t n = k >> 1;
+        if (n > 0) mbar_wait(empty(w), (uint32_t)((n - 1) & 1), args.status);
+        const int i = (int)(t / args.tiles_per_row);
+        const int j0 = (int)((t % args.tiles_per_row) * TILE);
+        const uint32_t st = base + O_STAGE + w * O_STAGE_BYTES;
+        mbar_arrive_expect_tx(full(w), 65536);
+        tma_load_3d(st, &tzg, full(w), 0, j0, i);
+        tma_load_3d(st + 16384, &tzg, full(w), 64, j0, i);
+        tma_load_3d(st + 32768, &tx, full(w), j0, i, 0);
       }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      mbar_wait(wbar, 0, args.status);
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= args.n_tiles) break;
+        const int w = (int)(k & 1);
+        const uint32_t par = (uint32_t)((k >> 1) & 1);
+        const uint32_t sZ = base + O_STAGE + w * O_STAGE_BYTES, sX = sZ + 32768;
+        mbar_wait(ready(w), par, args.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256 + 128, sZ, base + O_WG, 16384, idesc_f16(128, 128, true));
+        tile::umma_k128(tmem + w * 256, sX, base + O_WZ, 16384, idesc_f16(128, 128, true));
+        umma_commit(done(w));
+      }
+    }
+  } else {
+    const int wg = (warp - 2) >> 2;
+    const int q = warp & 3;             // TMEM lane quarter this warp may access
+    const int row = q * 32 + lane;      // position within the tile
+    const bool leader = (warp == 2 + 4 * wg) && lane == 0;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* zt = g + O_STAGE + wg * O_STAGE_BYTES;
+    uint8_t* xt = zt + 32768;
+    const uint32_t st = base + O_STAGE + wg * O_STAGE_BYTES;
+    for (int64_t k = wg;; k += 2) {
+      const int64_t t = blockIdx.x + k * G;
+      if (t >= args.n_tiles) break;
+      const uint32_t par = (uint32_t)((k >> 1) & 1);
+      const int i = (int)(t / args.tiles_per_row);
+      const int j0 = (int)((t % args.tiles_per_row) * TILE);
+      mbar_wait(full(wg), par, args.status);
+      // x(i, j0 + row, :) from the channel-major tile
+      uint32_t xr[64];
+      {
+        const uint16_t* xs = reinterpret_cast<const uint16_t*>(xt);
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          xr[c] = (uint32_t)xs[(2 * c) * TILE + row] | ((uint32_t)xs[(2 * c + 1) * TILE + row] << 16);
+      }
+      named_bar_sync(1 + wg, 128);   // every x column is in registers
+      {
+        float m, r;
+        tile::row_stats(xr, 1e-5f, m, r);
+        tile::store_norm_row(xt, row, xr, m, r, lnp + 256, lnp + 384);
+      }
+      asm volatile("" ::: "memory");  // keep the two row passes apart (register pressure)
+      {
+        uint32_t zr[64];
+        float m, r;
+        tile::load_row(zt, row, zr);
+        tile::row_stats(zr, 1e-5f, m, r);
+        tile::store_norm_row(zt, row, zr, m, r, lnp, lnp + 128);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(ready(wg));
+      // residual row, fetched while the GEMMs run (zo's old values; an L2 hit when zo is zg)
+      const int64_t j = (int64_t)j0 + row;
+      const bool valid = j < args.n_j;
+      const bool rd = args.resid && valid;
+      const uint4* zp = reinterpret_cast<const uint4*>(args.zo + (int64_t)i * args.zo_rs + (valid ? j : 0) * args.zo_cs);
+      uint4 old[16];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) old[c] = rd ? __ldg(zp + c) : make_uint4(0, 0, 0, 0);
+      mbar_wait(done(wg), par, args.status);
+      tc_fence_after();
+#pragma unroll
+      for (int c = 8; c < 16; ++c) old[c] = rd ? __ldg(zp + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int cc = 0; cc < CH; cc += 16) {
+        uint32_t av[16], gv[16];
+        tmem_ld16(tmem + lane_base + wg * 256 + cc, av);
+        tmem_ld16(tmem + lane_base + wg * 256 + 128 + cc, gv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int chunk = (cc >> 3) + e;
+          uint4* dst = reinterpret_cast<uint4*>(zt + tile::chunk_off(row, chunk));
+          float u[8];
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk)
+            u[kk] = __uint_as_float(av[e * 8 + kk]) * fast_sigmoid(__uint_as_float(gv[e * 8 + kk]));
+          {
+            const uint4 o = old[chunk];
+            u[0] += bf16lo(o.x); u[1] += bf16hi(o.x); u[2] += bf16lo(o.y); u[3] += bf16hi(o.y);
+            u[4] += bf16lo(o.z); u[5] += bf16hi(o.z); u[6] += bf16lo(o.w); u[7] += bf16hi(o.w);
+          }
+          uint4 wv;
+          wv.x = pack_bf16(u[0], u[1]); wv.y = pack_bf16(u[2], u[3]);
+          wv.z = pack_bf16(u[4], u[5]); wv.w = pack_bf16(u[6], u[7]);
+          *dst = wv;
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_bar_sync(1 + wg, 128);
+      if (leader) {
+        tma_store_3d(&tzo, st, 0, j0, i);
+        tma_store_3d(&tzo, st + 16384, 64, j0, i);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        mbar_arrive(empty(wg));
+      }
+    }
+    if (leader) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -564,31 +628,36 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     k_trimul_bgemm<<<grid, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
   }
   PF_CHECK_LAUNCH();
-  // 3. LN_out, W_z, gate, residual
-  CUtensorMap tzg, twz, twg;
+  // 3. LN_out, W_z, gate, residual (persistent, one CTA per SM)
+  CUtensorMap tzg, tzo, txm, twz, twg;
   PF_TRY(pair_tmap(&tzg, zg, n_i, n_j));
+  PF_TRY(pair_tmap(&tzo, zo, n_i, n_j));
   PF_TRY(weight_tmap(&twz, p->w_z, CH, CH, 128));
   PF_TRY(weight_tmap(&twg, p->w_g, CH, CH, 128));
+  {
+    const uint64_t dx[3] = {(uint64_t)n_j, (uint64_t)n_i, (uint64_t)CH};
+    const uint64_t sx[2] = {(uint64_t)w.ld_j * 2, (uint64_t)n_i * w.ld_j * 2};
+    const uint32_t bx[3] = {(uint32_t)TILE, 1, (uint32_t)CH};
+    PF_TRY(make_tmap(&txm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
   OutArgs oa;
-  oa.x = w.x;
-  oa.ldx = w.ld_j;
-  oa.x_ch_stride = (int64_t)n_i * w.ld_j;
-  oa.zo = (__nv_bfloat16*)zo.ptr;
-  oa.zo_rs = zo.row_stride;
-  oa.zo_cs = zo.col_stride;
   oa.n_i = n_i;
   oa.n_j = n_j;
   oa.tiles_per_row = (n_j + TILE - 1) / TILE;
+  oa.n_tiles = n_i * oa.tiles_per_row;
   oa.ln_in_w = p->ln_in_w;
   oa.ln_in_b = p->ln_in_b;
   oa.ln_out_w = p->ln_out_w;
   oa.ln_out_b = p->ln_out_b;
-  oa.accumulate = acc;
+  oa.resid = acc ? 1 : 0;
+  oa.zo = (const __nv_bfloat16*)zo.ptr;
+  oa.zo_rs = zo.row_stride;
+  oa.zo_cs = zo.col_stride;
   oa.status = status;
-  const int64_t nto = n_i * oa.tiles_per_row;
+  const int64_t grid_o = oa.n_tiles < sm_count() ? oa.n_tiles : sm_count();
   {
     PF_LAUNCH_SCOPE(st, "k_trimul_out");
-    k_trimul_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tzg, twz, twg, oa);
+    k_trimul_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tzg, txm, tzo, twz, twg, oa);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;

@@ -49,6 +49,19 @@ int device_status_ptr(unsigned int** out) {
   return PF_OK;
 }
 
+int64_t sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (n[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
+  }
+  return n[dev];
+}
+
 }  // namespace pf
 
 extern "C" PF_API int pf_device_status(int* status_out, int clear) {

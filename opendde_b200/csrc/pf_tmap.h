@@ -18,4 +18,7 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* ba
 // in a static __device__ variable of the current device; returns its device address.
 int device_status_ptr(unsigned int** out);
 
+// Number of SMs of the current device (persistent grids are sized by it).
+int64_t sm_count();
+
 }  // namespace pf
