@@ -14,13 +14,15 @@
 //                       (UMMA, TMEM), softmax in registers (one thread per query, exp2), P in f16
 //                       to shared memory, then [o | l] = P [V^T ; 1]^T in one UMMA (the ones row
 //                       gives the row sum of exactly the f16 P used for o).
-//   k_triatt_out      : LN(z) -> gate logits (UMMA), o * sigmoid(gate) -> W_o (UMMA) -> residual.
+//   k_triatt_out      : persistent; LN(z) -> gate logits (UMMA), o * sigmoid(gate) -> W_o (UMMA)
+//                       -> residual, TMA-stored.
 // Reference: opendde/model/triangular/triangular.py:648-706, layers.py:302-424.
 
 #include "pf_common.cuh"
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
 namespace pf {
@@ -265,131 +267,213 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
 #include "pf_triatt_core.cuh"
 
 // ------------------------------------------------------------------ output
+// Persistent, one CTA per SM; tile k of a CTA goes to compute warpgroup k & 1, which owns
+// shared-memory stage k & 1 (z tile + o tile) and TMEM columns [256 w, 256 w + 256).
+//   warp 0     TMA producer (W_g, W_o once; z and o tiles per tile)
+//   warp 1     MMA issuer: gate = W_g LN(z) (cols +128), then y = W_o (o * sigmoid(gate)) (cols +0)
+//   warps 2-9  LN(z) in place; o * sigmoid(gate) in place; y (+ residual read from zo, fetched
+//              while the W_o GEMM runs) written into the z buffer and TMA-stored to zo.
 struct OutArgs {
-  int64_t n_rows, n_q, tiles_per_row, q_col0;
-  __nv_bfloat16* zo;
+  int64_t n_rows, n_q, tiles_per_row, n_tiles, q_col0;
+  const __nv_bfloat16* zo;
   int64_t zo_rs, zo_cs;
   const float *ln_w, *ln_b;
   int accumulate;
   unsigned int* status;
 };
-constexpr uint32_t OUT_SMEM = 4 * 32768 + 64;
+constexpr uint32_t O_WG = 0, O_WO = 32768, O_STAGE = 65536, O_STAGE_BYTES = 65536;
+constexpr uint32_t O_LN = O_STAGE + 2 * O_STAGE_BYTES, O_BAR = O_LN + 1024;
+constexpr uint32_t OUT_SMEM = O_BAR + 256;
 
-__global__ void __launch_bounds__(128) k_triatt_out(const __grid_constant__ CUtensorMap tz,
-                                                    const __grid_constant__ CUtensorMap to,
-                                                    const __grid_constant__ CUtensorMap twg,
-                                                    const __grid_constant__ CUtensorMap two,
-                                                    const OutArgs a) {
+__global__ void __launch_bounds__(320, 1) k_triatt_out(const __grid_constant__ CUtensorMap tz,
+                                                       const __grid_constant__ CUtensorMap to,
+                                                       const __grid_constant__ CUtensorMap tzo,
+                                                       const __grid_constant__ CUtensorMap twg,
+                                                       const __grid_constant__ CUtensorMap two,
+                                                       const OutArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
-  const uint32_t sZ = base, sO = base + 32768, sBG = base + 65536, sBO = base + 98304;
-  const uint32_t bar_load = base + 131072, bar_m1 = bar_load + 8, bar_m2 = bar_load + 16;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 131072 + 32);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t t = blockIdx.x;
-  const int64_t i = t / a.tiles_per_row;
-  const int64_t j0 = (t % a.tiles_per_row) * TILE;
-  const int64_t j = j0 + tid;
-  const bool valid = j < a.n_q;
-
+  const uint32_t bars = base + O_BAR, wbar = bars;
+  auto full = [&](int w) { return bars + 8 + 8 * w; };
+  auto empty = [&](int w) { return bars + 24 + 8 * w; };
+  auto rg = [&](int w) { return bars + 40 + 8 * w; };
+  auto ro = [&](int w) { return bars + 56 + 8 * w; };
+  auto mg = [&](int w) { return bars + 72 + 8 * w; };
+  auto mo = [&](int w) { return bars + 88 + 8 * w; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + O_BAR + 128);
+  float* lnp = reinterpret_cast<float*>(g + O_LN);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_m1, 1);
-    mbar_init(bar_m2, 1);
+    mbar_init(wbar, 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(full(w), 1);
+      mbar_init(empty(w), 1);
+      mbar_init(rg(w), 1);
+      mbar_init(ro(w), 1);
+      mbar_init(mg(w), 1);
+      mbar_init(mo(w), 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  for (int c = tid; c < CH; c += blockDim.x) {
+    lnp[c] = a.ln_w[c];
+    lnp[CH + c] = a.ln_b[c];
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_load, 4 * 32768);
-    tma_load_3d(sZ, &tz, bar_load, 0, (int)(a.q_col0 + j0), (int)i);
-    tma_load_3d(sZ + 16384, &tz, bar_load, 64, (int)(a.q_col0 + j0), (int)i);
-    tma_load_3d(sO, &to, bar_load, 0, (int)j0, (int)i);
-    tma_load_3d(sO + 16384, &to, bar_load, 64, (int)j0, (int)i);
-    tma_load_2d(sBG, &twg, bar_load, 0, 0);
-    tma_load_2d(sBG + 16384, &twg, bar_load, 64, 0);
-    tma_load_2d(sBO, &two, bar_load, 0, 0);
-    tma_load_2d(sBO + 16384, &two, bar_load, 64, 0);
-  }
-  mbar_wait(bar_load, 0, a.status);
-  ln_row_inplace(g, tid, a.ln_w, a.ln_b);
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem + 128, sZ, sBG, 16384, idesc_f16(128, 128, true));
-    umma_commit(bar_m1);
-  }
-  mbar_wait(bar_m1, 0, a.status);
-  tc_fence_after();
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  // o * sigmoid(gate), in place in the o tile (row tid)
-#pragma unroll 1
-  for (int cc = 0; cc < HD; cc += 32) {
-    uint32_t gv[32];
-    tmem_ld32(tmem + lane_base + 128 + cc, gv);
-    tmem_ld_wait();
-#pragma unroll
-    for (int q4 = 0; q4 < 4; ++q4) {
-      const int ch = (cc >> 3) + q4;  // 16-byte chunk index 0..15
-      uint4* p = reinterpret_cast<uint4*>(g + 32768 + (ch >> 3) * 16384 + sw128_off(tid, ch & 7));
-      uint4 v = *p;
-      const float* gg = reinterpret_cast<const float*>(gv) + q4 * 8;
-      v.x = pack_bf16(bf16lo(v.x) * fast_sigmoid(gg[0]), bf16hi(v.x) * fast_sigmoid(gg[1]));
-      v.y = pack_bf16(bf16lo(v.y) * fast_sigmoid(gg[2]), bf16hi(v.y) * fast_sigmoid(gg[3]));
-      v.z = pack_bf16(bf16lo(v.z) * fast_sigmoid(gg[4]), bf16hi(v.z) * fast_sigmoid(gg[5]));
-      v.w = pack_bf16(bf16lo(v.w) * fast_sigmoid(gg[6]), bf16hi(v.w) * fast_sigmoid(gg[7]));
-      *p = v;
-    }
-  }
-  fence_proxy_async_smem();
-  tc_fence_before();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem, sO, sBO, 16384, idesc_f16(128, 128, true));
-    umma_commit(bar_m2);
-  }
-  mbar_wait(bar_m2, 0, a.status);
-  tc_fence_after();
-  __nv_bfloat16* zp = a.zo + i * a.zo_rs + (valid ? j : 0) * a.zo_cs;
-#pragma unroll 1
-  for (int cc = 0; cc < CH; cc += 32) {
-    uint32_t ov[32];
-    tmem_ld32(tmem + lane_base + cc, ov);
-    tmem_ld_wait();
-    if (valid) {
-      uint4* dst = reinterpret_cast<uint4*>(zp + cc);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float u[8];
-#pragma unroll
-        for (int k = 0; k < 8; ++k) u[k] = __uint_as_float(ov[e * 8 + k]);
-        if (a.accumulate) {
-          const uint4 old = dst[e];
-          u[0] += bf16lo(old.x); u[1] += bf16hi(old.x); u[2] += bf16lo(old.y); u[3] += bf16hi(old.y);
-          u[4] += bf16lo(old.z); u[5] += bf16hi(old.z); u[6] += bf16lo(old.w); u[7] += bf16hi(old.w);
-        }
-        uint4 w;
-        w.x = pack_bf16(u[0], u[1]); w.y = pack_bf16(u[2], u[3]);
-        w.z = pack_bf16(u[4], u[5]); w.w = pack_bf16(u[6], u[7]);
-        dst[e] = w;
+  const int64_t G = gridDim.x;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tz);
+      tma_prefetch_desc(&to);
+      mbar_arrive_expect_tx(wbar, 65536);
+      tma_load_2d(base + O_WG, &twg, wbar, 0, 0);
+      tma_load_2d(base + O_WG + 16384, &twg, wbar, 64, 0);
+      tma_load_2d(base + O_WO, &two, wbar, 0, 0);
+      tma_load_2d(base + O_WO + 16384, &two, wbar, 64, 0);
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= a.n_tiles) break;
+        const int w = (int)(k & 1);
+        const int64_t n = k >> 1;
+        if (n > 0) mbar_wait(empty(w), (uint32_t)((n - 1) & 1), a.status);
+        const int i = (int)(t / a.tiles_per_row);
+        const int j0 = (int)((t % a.tiles_per_row) * TILE);
+        const uint32_t st = base + O_STAGE + w * O_STAGE_BYTES;
+        mbar_arrive_expect_tx(full(w), 65536);
+        tma_load_3d(st, &tz, full(w), 0, (int)(a.q_col0 + j0), i);
+        tma_load_3d(st + 16384, &tz, full(w), 64, (int)(a.q_col0 + j0), i);
+        tma_load_3d(st + 32768, &to, full(w), 0, j0, i);
+        tma_load_3d(st + 49152, &to, full(w), 64, j0, i);
       }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      mbar_wait(wbar, 0, a.status);
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= a.n_tiles) break;
+        const int w = (int)(k & 1);
+        const uint32_t par = (uint32_t)((k >> 1) & 1);
+        const uint32_t sZ = base + O_STAGE + w * O_STAGE_BYTES, sO = sZ + 32768;
+        mbar_wait(rg(w), par, a.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256 + 128, sZ, base + O_WG, 16384, idesc_f16(128, 128, true));
+        umma_commit(mg(w));
+        mbar_wait(ro(w), par, a.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256, sO, base + O_WO, 16384, idesc_f16(128, 128, true));
+        umma_commit(mo(w));
+      }
+    }
+  } else {
+    const int wg = (warp - 2) >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool leader = (warp == 2 + 4 * wg) && lane == 0;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* zt = g + O_STAGE + wg * O_STAGE_BYTES;
+    uint8_t* ot = zt + 32768;
+    const uint32_t st = base + O_STAGE + wg * O_STAGE_BYTES;
+    for (int64_t k = wg;; k += 2) {
+      const int64_t t = blockIdx.x + k * G;
+      if (t >= a.n_tiles) break;
+      const uint32_t par = (uint32_t)((k >> 1) & 1);
+      const int i = (int)(t / a.tiles_per_row);
+      const int j0 = (int)((t % a.tiles_per_row) * TILE);
+      mbar_wait(full(wg), par, a.status);
+      {
+        uint32_t zr[64];
+        float m, r;
+        tile::load_row(zt, row, zr);
+        tile::row_stats(zr, 1e-5f, m, r);
+        tile::store_norm_row(zt, row, zr, m, r, lnp, lnp + CH);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(rg(wg));
+      mbar_wait(mg(wg), par, a.status);
+      tc_fence_after();
+      // o * sigmoid(gate), in place in the o tile
+#pragma unroll
+      for (int cc = 0; cc < HD; cc += 16) {
+        uint32_t gv[16];
+        tmem_ld16(tmem + lane_base + wg * 256 + 128 + cc, gv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          uint4* p = reinterpret_cast<uint4*>(ot + tile::chunk_off(row, (cc >> 3) + e));
+          uint4 v = *p;
+          const float* gg = reinterpret_cast<const float*>(gv) + e * 8;
+          v.x = pack_bf16(bf16lo(v.x) * fast_sigmoid(gg[0]), bf16hi(v.x) * fast_sigmoid(gg[1]));
+          v.y = pack_bf16(bf16lo(v.y) * fast_sigmoid(gg[2]), bf16hi(v.y) * fast_sigmoid(gg[3]));
+          v.z = pack_bf16(bf16lo(v.z) * fast_sigmoid(gg[4]), bf16hi(v.z) * fast_sigmoid(gg[5]));
+          v.w = pack_bf16(bf16lo(v.w) * fast_sigmoid(gg[6]), bf16hi(v.w) * fast_sigmoid(gg[7]));
+          *p = v;
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(ro(wg));
+      const int64_t j = (int64_t)j0 + row;
+      const bool rd = a.accumulate && j < a.n_q;
+      const uint4* zp = reinterpret_cast<const uint4*>(a.zo + (int64_t)i * a.zo_rs + (rd ? j : 0) * a.zo_cs);
+      uint4 old[16];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) old[c] = rd ? __ldg(zp + c) : make_uint4(0, 0, 0, 0);
+      mbar_wait(mo(wg), par, a.status);
+      tc_fence_after();
+#pragma unroll
+      for (int c = 8; c < 16; ++c) old[c] = rd ? __ldg(zp + c) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int cc = 0; cc < CH; cc += 16) {
+        uint32_t ov[16];
+        tmem_ld16(tmem + lane_base + wg * 256 + cc, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int chunk = (cc >> 3) + e;
+          const uint4 o = old[chunk];
+          float u[8];
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) u[kk] = __uint_as_float(ov[e * 8 + kk]);
+          u[0] += bf16lo(o.x); u[1] += bf16hi(o.x); u[2] += bf16lo(o.y); u[3] += bf16hi(o.y);
+          u[4] += bf16lo(o.z); u[5] += bf16hi(o.z); u[6] += bf16lo(o.w); u[7] += bf16hi(o.w);
+          uint4 wv;
+          wv.x = pack_bf16(u[0], u[1]); wv.y = pack_bf16(u[2], u[3]);
+          wv.z = pack_bf16(u[4], u[5]); wv.w = pack_bf16(u[6], u[7]);
+          *reinterpret_cast<uint4*>(zt + tile::chunk_off(row, chunk)) = wv;
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_bar_sync(1 + wg, 128);
+      if (leader) {
+        tma_store_3d(&tzo, st, 0, j0, i);
+        tma_store_3d(&tzo, st + 16384, 64, j0, i);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        mbar_arrive(empty(wg));
+      }
+    }
+    if (leader) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -599,22 +683,25 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   }
   PF_TRY(weight_tmap(&twg, p->w_g, HD, CH, 128));
   PF_TRY(weight_tmap(&two, p->w_o, CH, HD, 128));
+  CUtensorMap tzo;
+  PF_TRY(pair_tmap(&tzo, zo.ptr, zo.row_stride, zo.col_stride, n_rows, n_q));
   OutArgs oa{};
   oa.n_rows = n_rows;
   oa.n_q = n_q;
   oa.tiles_per_row = (n_q + TILE - 1) / TILE;
+  oa.n_tiles = n_rows * oa.tiles_per_row;
   oa.q_col0 = q_col0;
-  oa.zo = (__nv_bfloat16*)zo.ptr;
+  oa.zo = (const __nv_bfloat16*)zo.ptr;
   oa.zo_rs = zo.row_stride;
   oa.zo_cs = zo.col_stride;
   oa.ln_w = p->ln_w;
   oa.ln_b = p->ln_b;
   oa.accumulate = acc;
   oa.status = status;
-  const int64_t nto = n_rows * oa.tiles_per_row;
   {
+    const int64_t grid_o = oa.n_tiles < num_sms() ? oa.n_tiles : num_sms();
     PF_LAUNCH_SCOPE(st, "k_triatt_out");
-    k_triatt_out<<<(unsigned)nto, 128, OUT_SMEM + 1024, st>>>(tz, to, twg, two, oa);
+    k_triatt_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tz, to, tzo, twg, two, oa);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;

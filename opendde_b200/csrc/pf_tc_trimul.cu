@@ -2,17 +2,18 @@
 // fp32 accumulate), c_z = c_h = 128.
 //
 // Three kernels, intermediates in the caller's workspace (bf16):
-//   1. k_trimul_proj : a 128-position tile of a view is TMA-loaded (128B swizzle), LayerNorm'd
-//      in place in shared memory, multiplied by [W_p; W_g] (one 128x256x128 UMMA chain into
-//      TMEM) and written channel-major as a(ch, r, k) = mask * sigmoid(g) * p. Channel-major
-//      rows are exactly the K-major operands of the contraction, so neither the incoming
-//      direction nor the ending node needs a physical transpose.
+//   1. k_trimul_proj : persistent; per (128-position tile, side) the z tile is TMA-loaded
+//      (128B swizzle), LayerNorm'd in place, multiplied by [W_p; W_g] (one 128x256x128 UMMA
+//      chain into TMEM) and a(ch, r, k) = mask * sigmoid(g) * p is transposed in shared memory
+//      and TMA-stored channel-major. Channel-major rows are exactly the K-major operands of
+//      the contraction, so neither the incoming direction nor the ending node needs a
+//      physical transpose.
 //   2. k_trimul_bgemm: x[ch] = a[ch] * b[ch]^T for every channel: 128x256 output tiles, a
 //      4-stage TMA -> UMMA pipeline (one producer thread, one MMA thread, 4 epilogue warps
 //      reading the TMEM accumulator), bf16 output x[ch][i][j].
-//   3. k_trimul_out  : per 128 output positions, LN_out over the 128 channels of x (read
-//      channel-major, coalesced), LN_in of the gate source tile, two chained 128x128x128 UMMAs
-//      (W_g then W_z, sharing one A buffer), epilogue zo (+)= (W_z x) * sigmoid(W_g z).
+//   3. k_trimul_out  : persistent; per 128 output positions, the channel-major x tile and the
+//      gate-source z tile by TMA, LN_out(x) and LN_in(z) into UMMA operands, two 128x128x128
+//      UMMAs (W_g, W_z), epilogue zo (+)= (W_z x) * sigmoid(W_g z), TMA-stored.
 // Reference: opendde/model/triangular/triangular.py:530-567 (maths), :112-139 (orientation).
 
 #include "pf_common.cuh"
@@ -31,163 +32,204 @@ namespace {
 constexpr int CH = 128;    // c_z == c_h on this path
 constexpr int TILE = 128;  // positions per projection / output CTA
 
-// LayerNorm of row `row` of a K-major SW128 tile holding 128 bf16 channels (two 64-channel
-// atoms of 16 KB), in place. Stats in fp32 (two-pass, biased variance, eps inside sqrt).
-__device__ __forceinline__ void ln_row_inplace_sw128(uint8_t* tile, int row, const float* __restrict__ g,
-                                                     const float* __restrict__ b, float eps) {
-  float v[CH];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint4 q = *reinterpret_cast<const uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7));
-    v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
-    v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
-    v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
-    v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) s += v[c];
-  const float mean = s * (1.0f / CH);
-  float sq = 0.f;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const float d = v[c] - mean;
-    sq += d * d;
-  }
-  const float rstd = rsqrtf(sq * (1.0f / CH) + eps);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float y[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int c = j * 8 + e;
-      y[e] = (v[c] - mean) * rstd * __ldg(g + c) + __ldg(b + c);
-    }
-    uint4 q;
-    q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
-    q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
-    *reinterpret_cast<uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7)) = q;
-  }
-}
-
-// Issue the 8 K-steps (K = 128) of D = A[128 x 128] * B[n x 128]^T with SW128 K-major tiles
-// stored as two 64-channel atoms (A atom stride 16 KB, B atom stride b_atom_bytes).
-__device__ __forceinline__ void umma_k128(uint32_t d_tmem, uint32_t sA, uint32_t sB,
-                                          uint32_t b_atom_bytes, uint32_t idesc) {
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
-    const uint64_t ad = sdesc(sA + atom * 16384 + within, 1024, SWZ_128B);
-    const uint64_t bd = sdesc(sB + atom * b_atom_bytes + within, 1024, SWZ_128B);
-    umma_f16(d_tmem, ad, bd, idesc, kk > 0 ? 1u : 0u);
-  }
-}
-
 // ------------------------------------------------------------------ kernel 1: projections
+// Persistent, one CTA per SM. Work item = (tile of 128 positions, side a or b), items of the
+// two sides interleaved so a z tile shared by both sides is read from DRAM once. Item k of a
+// CTA goes to compute warpgroup k & 1 (its own stage and 256 TMEM columns).
+//   warp 0     TMA producer: both sides' [W_p ; W_g] once, then z tiles
+//   warp 1     MMA issuer: [p | g] = [W_p ; W_g] LN(z)   (N = 256)
+//   warps 2-9  LN in place; epilogue mask * sigmoid(g) * p (reference order,
+//              triangular.py:539-544) transposed into the stage as [channel][position] and
+//              TMA-stored into the channel-major operand a[c][row][k] (or b).
 struct ProjSide {
   int64_t n_rows, n_cols;
   pf_mask_view mask;
-  __nv_bfloat16* out;  // channel-major [CH][n_rows][ld]
-  int64_t ch_stride;
   int64_t tiles_per_row;
   int64_t ntiles;
 };
 struct ProjArgs {
   ProjSide side[2];
-  int64_t ld;
+  int64_t n_items;
   const float* ln_w;
   const float* ln_b;
   unsigned int* status;
 };
 
-constexpr uint32_t PROJ_SMEM = 32768 + 65536 + 64;
+constexpr uint32_t P_W = 0, P_WSIDE = 65536, P_STAGE = 131072, P_STAGE_BYTES = 32768;
+constexpr uint32_t P_LN = P_STAGE + 2 * P_STAGE_BYTES, P_BAR = P_LN + 1024;
+constexpr uint32_t PROJ_SMEM = P_BAR + 256;
 
-__global__ void __launch_bounds__(128) k_trimul_proj(const __grid_constant__ CUtensorMap tz0,
-                                                     const __grid_constant__ CUtensorMap tz1,
-                                                     const __grid_constant__ CUtensorMap tw0p,
-                                                     const __grid_constant__ CUtensorMap tw0g,
-                                                     const __grid_constant__ CUtensorMap tw1p,
-                                                     const __grid_constant__ CUtensorMap tw1g,
-                                                     const ProjArgs args) {
+__global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ CUtensorMap tz0,
+                                                        const __grid_constant__ CUtensorMap tz1,
+                                                        const __grid_constant__ CUtensorMap to0,
+                                                        const __grid_constant__ CUtensorMap to1,
+                                                        const __grid_constant__ CUtensorMap tw0p,
+                                                        const __grid_constant__ CUtensorMap tw0g,
+                                                        const __grid_constant__ CUtensorMap tw1p,
+                                                        const __grid_constant__ CUtensorMap tw1g,
+                                                        const ProjArgs args) {
   extern __shared__ uint8_t smem_raw[];
-  const int which = blockIdx.x & 1;
-  const int64_t t = blockIdx.x >> 1;
-  const ProjSide& sd = args.side[which];
-  if (t >= sd.ntiles) return;
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
-  const uint32_t sA = base, sB = base + 32768;
-  const uint32_t bar_load = base + 98304, bar_mma = bar_load + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 98304 + 16);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t r = t / sd.tiles_per_row;
-  const int64_t c0 = (t % sd.tiles_per_row) * TILE;
-  const CUtensorMap* tz = which ? &tz1 : &tz0;
-  const CUtensorMap* twp = which ? &tw1p : &tw0p;
-  const CUtensorMap* twg = which ? &tw1g : &tw0g;
-
+  const uint32_t bars = base + P_BAR, wbar = bars;
+  auto full = [&](int w) { return bars + 8 + 8 * w; };
+  auto empty = [&](int w) { return bars + 24 + 8 * w; };
+  auto ready = [&](int w) { return bars + 40 + 8 * w; };
+  auto done = [&](int w) { return bars + 56 + 8 * w; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + P_BAR + 128);
+  float* lnp = reinterpret_cast<float*>(g + P_LN);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_mma, 1);
+    mbar_init(wbar, 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(full(w), 1);
+      mbar_init(empty(w), 1);
+      mbar_init(ready(w), 1);
+      mbar_init(done(w), 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+  for (int c = tid; c < CH; c += blockDim.x) {
+    lnp[c] = args.ln_w[c];
+    lnp[CH + c] = args.ln_b[c];
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int64_t G = gridDim.x;
+  // item -> (side, tile); false when that side has fewer tiles
+  auto decode = [&](int64_t item, int& side, int64_t& t) {
+    side = (int)(item & 1);
+    t = item >> 1;
+    return t < args.side[side].ntiles;
+  };
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_load, 32768 + 65536);
-    tma_load_3d(sA, tz, bar_load, 0, (int)c0, (int)r);
-    tma_load_3d(sA + 16384, tz, bar_load, 64, (int)c0, (int)r);
-    tma_load_2d(sB, twp, bar_load, 0, 0);              // atom 0: rows 0..127 = W_p
-    tma_load_2d(sB + 16384, twg, bar_load, 0, 0);      //         rows 128..255 = W_g
-    tma_load_2d(sB + 32768, twp, bar_load, 64, 0);     // atom 1
-    tma_load_2d(sB + 49152, twg, bar_load, 64, 0);
-  }
-  mbar_wait(bar_load, 0, args.status);
-  ln_row_inplace_sw128(g, tid, args.ln_w, args.ln_b, 1e-5f);
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem, sA, sB, 32768, idesc_f16(128, 256, true));
-    umma_commit(bar_mma);
-  }
-  mbar_wait(bar_mma, 0, args.status);
-  tc_fence_after();
-
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const int64_t col = c0 + tid;
-  const bool valid = col < sd.n_cols;
-  float m = 0.f;
-  if (valid) m = sd.mask.ptr ? sd.mask.ptr[r * sd.mask.row_stride + col * sd.mask.col_stride] : 1.f;
-  __nv_bfloat16* outp = sd.out + r * args.ld + col;
-#pragma unroll 1
-  for (int cc = 0; cc < CH; cc += 32) {
-    uint32_t pv[32], gv[32];
-    tmem_ld32(tmem + lane_base + cc, pv);
-    tmem_ld32(tmem + lane_base + 128 + cc, gv);
-    tmem_ld_wait();
-    if (valid) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        // reference order: mask * sigmoid(g) * p  (triangular.py:539-544)
-        const float v = m * fast_sigmoid(__uint_as_float(gv[e])) * __uint_as_float(pv[e]);
-        outp[(int64_t)(cc + e) * sd.ch_stride] = __float2bfloat16_rn(v);
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tz0);
+      tma_prefetch_desc(&tz1);
+      mbar_arrive_expect_tx(wbar, 131072);
+      // per side: atom 0 = [W_p ; W_g] channels 0..63 (32 KB), atom 1 = channels 64..127
+      tma_load_2d(base + P_W, &tw0p, wbar, 0, 0);
+      tma_load_2d(base + P_W + 16384, &tw0g, wbar, 0, 0);
+      tma_load_2d(base + P_W + 32768, &tw0p, wbar, 64, 0);
+      tma_load_2d(base + P_W + 49152, &tw0g, wbar, 64, 0);
+      tma_load_2d(base + P_W + P_WSIDE, &tw1p, wbar, 0, 0);
+      tma_load_2d(base + P_W + P_WSIDE + 16384, &tw1g, wbar, 0, 0);
+      tma_load_2d(base + P_W + P_WSIDE + 32768, &tw1p, wbar, 64, 0);
+      tma_load_2d(base + P_W + P_WSIDE + 49152, &tw1g, wbar, 64, 0);
+      int64_t k = 0;
+      for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
+        int side;
+        int64_t t;
+        if (!decode(item, side, t)) continue;
+        const int w = (int)(k & 1);
+        const int64_t n = k >> 1;
+        ++k;
+        if (n > 0) mbar_wait(empty(w), (uint32_t)((n - 1) & 1), args.status);
+        const ProjSide& sd = args.side[side];
+        const int r = (int)(t / sd.tiles_per_row);
+        const int c0 = (int)((t % sd.tiles_per_row) * TILE);
+        const uint32_t st = base + P_STAGE + w * P_STAGE_BYTES;
+        const CUtensorMap* tz = side ? &tz1 : &tz0;
+        mbar_arrive_expect_tx(full(w), 32768);
+        tma_load_3d(st, tz, full(w), 0, c0, r);
+        tma_load_3d(st + 16384, tz, full(w), 64, c0, r);
       }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      mbar_wait(wbar, 0, args.status);
+      int64_t k = 0;
+      for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
+        int side;
+        int64_t t;
+        if (!decode(item, side, t)) continue;
+        const int w = (int)(k & 1);
+        const uint32_t par = (uint32_t)((k >> 1) & 1);
+        ++k;
+        mbar_wait(ready(w), par, args.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256, base + P_STAGE + w * P_STAGE_BYTES, base + P_W + side * P_WSIDE, 32768,
+                        idesc_f16(128, 256, true));
+        umma_commit(done(w));
+      }
+    }
+  } else {
+    const int wg = (warp - 2) >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool leader = (warp == 2 + 4 * wg) && lane == 0;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* zt = g + P_STAGE + wg * P_STAGE_BYTES;
+    const uint32_t st = base + P_STAGE + wg * P_STAGE_BYTES;
+    int64_t k = 0;
+    for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
+      int side;
+      int64_t t;
+      if (!decode(item, side, t)) continue;
+      const int w = (int)(k & 1);
+      const uint32_t par = (uint32_t)((k >> 1) & 1);
+      ++k;
+      if (w != wg) continue;
+      const ProjSide& sd = args.side[side];
+      const int r = (int)(t / sd.tiles_per_row);
+      const int c0 = (int)((t % sd.tiles_per_row) * TILE);
+      mbar_wait(full(wg), par, args.status);
+      {
+        uint32_t zr[64];
+        float m, rs;
+        tile::load_row(zt, row, zr);
+        tile::row_stats(zr, 1e-5f, m, rs);
+        tile::store_norm_row(zt, row, zr, m, rs, lnp, lnp + CH);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(ready(wg));
+      const int64_t col = (int64_t)c0 + row;
+      float mk = 0.f;
+      if (col < sd.n_cols)
+        mk = sd.mask.ptr ? sd.mask.ptr[(int64_t)r * sd.mask.row_stride + col * sd.mask.col_stride] : 1.f;
+      mbar_wait(done(wg), par, args.status);
+      tc_fence_after();
+      // [channel][position] bf16 tile over the (consumed) z tile: 256 B per channel
+      unsigned short* ot = reinterpret_cast<unsigned short*>(zt);
+#pragma unroll
+      for (int cc = 0; cc < CH; cc += 16) {
+        uint32_t pv[16], gv[16];
+        tmem_ld16(tmem + lane_base + wg * 256 + cc, pv);
+        tmem_ld16(tmem + lane_base + wg * 256 + 128 + cc, gv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const float v = mk * fast_sigmoid(__uint_as_float(gv[e])) * __uint_as_float(pv[e]);
+          ot[(cc + e) * TILE + row] = __bfloat16_as_ushort(__float2bfloat16_rn(v));
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_bar_sync(1 + wg, 128);
+      if (leader) {
+        tma_store_3d(side ? &to1 : &to0, st, c0, r, 0);
+        bulk_commit_group();
+        bulk_wait_group_read0();
+        mbar_arrive(empty(wg));
+      }
+    }
+    if (leader) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -585,27 +627,36 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     PF_TRY(set_smem(k_trimul_out, OUT_SMEM + 1024));
     attrs = true;
   }
-  // 1. projections
-  CUtensorMap tz0, tz1, tw0p, tw0g, tw1p, tw1g;
+  // 1. projections (persistent)
+  CUtensorMap tz0, tz1, to0, to1, tw0p, tw0g, tw1p, tw1g;
   PF_TRY(pair_tmap(&tz0, za, n_i, n_k));
   PF_TRY(pair_tmap(&tz1, zb, n_j, n_k));
   PF_TRY(weight_tmap(&tw0p, p->w_ap, CH, CH, 128));
   PF_TRY(weight_tmap(&tw0g, p->w_ag, CH, CH, 128));
   PF_TRY(weight_tmap(&tw1p, p->w_bp, CH, CH, 128));
   PF_TRY(weight_tmap(&tw1g, p->w_bg, CH, CH, 128));
+  {
+    const uint32_t bo[3] = {(uint32_t)TILE, 1, (uint32_t)CH};
+    const uint64_t d0[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)CH};
+    const uint64_t s0[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_i * w.ld_k * 2};
+    PF_TRY(make_tmap(&to0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.a, d0, s0, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
+    const uint64_t d1[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)CH};
+    const uint64_t s1[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_j * w.ld_k * 2};
+    PF_TRY(make_tmap(&to1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.b, d1, s1, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
   ProjArgs pa;
   const int64_t tpr_k = (n_k + TILE - 1) / TILE;
-  pa.side[0] = ProjSide{n_i, n_k, ma, w.a, (int64_t)n_i * w.ld_k, tpr_k, n_i * tpr_k};
-  pa.side[1] = ProjSide{n_j, n_k, mb, w.b, (int64_t)n_j * w.ld_k, tpr_k, n_j * tpr_k};
-  pa.ld = w.ld_k;
+  pa.side[0] = ProjSide{n_i, n_k, ma, tpr_k, n_i * tpr_k};
+  pa.side[1] = ProjSide{n_j, n_k, mb, tpr_k, n_j * tpr_k};
+  const int64_t nt = pa.side[0].ntiles > pa.side[1].ntiles ? pa.side[0].ntiles : pa.side[1].ntiles;
+  pa.n_items = 2 * nt;
   pa.ln_w = p->ln_in_w;
   pa.ln_b = p->ln_in_b;
   pa.status = status;
-  const int64_t nt = pa.side[0].ntiles > pa.side[1].ntiles ? pa.side[0].ntiles : pa.side[1].ntiles;
-  if (2 * nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "trimul projection grid too large");
   {
+    const int64_t grid_p = pa.n_items < sm_count() ? pa.n_items : sm_count();
     PF_LAUNCH_SCOPE(st, "k_trimul_proj");
-    k_trimul_proj<<<(unsigned)(2 * nt), 128, PROJ_SMEM + 1024, st>>>(tz0, tz1, tw0p, tw0g, tw1p, tw1g, pa);
+    k_trimul_proj<<<(unsigned)grid_p, 320, PROJ_SMEM + 1024, st>>>(tz0, tz1, to0, to1, tw0p, tw0g, tw1p, tw1g, pa);
   }
   PF_CHECK_LAUNCH();
   // 2. contraction x[ch] = a[ch] b[ch]^T
