@@ -72,97 +72,68 @@ __global__ void k_triatt_maskprep(pf_mask_view m, int64_t n_keys, int64_t n_vali
   }
 }
 
-// LayerNorm of one row of a SW128 two-atom tile, in place (same as the trimul path).
-__device__ __forceinline__ void ln_row_inplace(uint8_t* tile, int row, const float* __restrict__ g,
-                                               const float* __restrict__ b) {
-  float v[CH];
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const uint4 q = *reinterpret_cast<const uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7));
-    v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
-    v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
-    v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
-    v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) s += v[c];
-  const float mean = s * (1.0f / CH);
-  float sq = 0.f;
-#pragma unroll
-  for (int c = 0; c < CH; ++c) {
-    const float d = v[c] - mean;
-    sq += d * d;
-  }
-  const float rstd = rsqrtf(sq * (1.0f / CH) + 1e-5f);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float y[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int c = j * 8 + e;
-      y[e] = (v[c] - mean) * rstd * __ldg(g + c) + __ldg(b + c);
-    }
-    uint4 q;
-    q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
-    q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
-    *reinterpret_cast<uint4*>(tile + (j >> 3) * 16384 + sw128_off(row, j & 7)) = q;
-  }
-}
-
-// D (+)= A[128 x K=128] * B[n x 128]^T, SW128 two-atom operands.
-__device__ __forceinline__ void umma_k128(uint32_t d_tmem, uint32_t sA, uint32_t sB,
-                                          uint32_t b_atom_bytes, uint32_t idesc) {
-#pragma unroll
-  for (int kk = 0; kk < 8; ++kk) {
-    const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
-    umma_f16(d_tmem, sdesc(sA + atom * 16384 + within, 1024, SWZ_128B),
-             sdesc(sB + atom * b_atom_bytes + within, 1024, SWZ_128B), idesc, kk > 0 ? 1u : 0u);
-  }
-}
-
 // ------------------------------------------------------------------ projection
+// Persistent, one CTA per SM; tile k of a CTA goes to compute warpgroup k & 1 (its own z
+// stage and 256 TMEM columns). Per tile: LN(z) in place, then two UMMA chains into the same
+// columns: [q | k] (N = 256), and after the warpgroup has read them, [v | bias] (N = 144).
+// q, k (f16, 64 B per head and position) and the bias are stored directly; v^T is transposed
+// into the stage as [(h, d)][key] and TMA-stored.
 struct ProjArgs {
-  int64_t n_rows, n_keys, tiles_per_row;
+  int64_t n_rows, n_keys, tiles_per_row, n_tiles;
   int64_t q_col0, n_q;
   int want_qkv, want_bias;
   __half* q;          // [(i*H+h)*n_q + j][D]     f16, x log2(e)/sqrt(d)
   __half* k;          // [(i*H+h)*ld_keys + key][D] f16
-  __half* vt;         // [((i*H+h)*D + dd)*ld_keys + key]
-  __half* bias;        // bias + h*b_hs + r*b_rs + s (f16, log2 units)
+  __half* bias;       // bias + h*b_hs + r*b_rs + s (f16, log2 units)
   int64_t ld_keys, b_hs, b_rs;
   const float *ln_w, *ln_b;
   float q_scale;
   unsigned int* status;
 };
 
-constexpr uint32_t PB_ATOM = 400 * 128;               // 400 weight rows x 128 B
-constexpr uint32_t PROJ_SMEM = 32768 + 2 * PB_ATOM + 64;
+constexpr uint32_t PB_ATOM = 400 * 128;               // 400 weight rows x 128 B per K atom
+constexpr uint32_t PJ_STAGE = 2 * PB_ATOM, PJ_STAGE_BYTES = 32768;
+constexpr uint32_t PJ_LN = PJ_STAGE + 2 * PJ_STAGE_BYTES, PJ_BAR = PJ_LN + 1024;
+constexpr uint32_t PROJ_SMEM = PJ_BAR + 256;
 
-__global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUtensorMap tz,
-                                                     const __grid_constant__ CUtensorMap twq,
-                                                     const __grid_constant__ CUtensorMap twk,
-                                                     const __grid_constant__ CUtensorMap twv,
-                                                     const __grid_constant__ CUtensorMap twb,
-                                                     const ProjArgs a) {
+__global__ void __launch_bounds__(320, 1) k_triatt_proj(const __grid_constant__ CUtensorMap tz,
+                                                        const __grid_constant__ CUtensorMap twq,
+                                                        const __grid_constant__ CUtensorMap twk,
+                                                        const __grid_constant__ CUtensorMap twv,
+                                                        const __grid_constant__ CUtensorMap twb,
+                                                        const __grid_constant__ CUtensorMap tvt,
+                                                        const ProjArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
-  const uint32_t sA = base, sB = base + 32768;
-  const uint32_t bar_load = base + 32768 + 2 * PB_ATOM, bar_mma = bar_load + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 32768 + 2 * PB_ATOM + 16);
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int64_t t = blockIdx.x;
-  const int64_t r = t / a.tiles_per_row;
-  const int64_t c0 = (t % a.tiles_per_row) * TILE;
-
+  const uint32_t bars = base + PJ_BAR, wbar = bars;
+  auto full = [&](int w) { return bars + 8 + 8 * w; };
+  auto empty = [&](int w) { return bars + 24 + 8 * w; };
+  auto ready = [&](int w) { return bars + 40 + 8 * w; };
+  auto done_a = [&](int w) { return bars + 56 + 8 * w; };
+  auto tfree = [&](int w) { return bars + 72 + 8 * w; };
+  auto done_b = [&](int w) { return bars + 88 + 8 * w; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + PJ_BAR + 128);
+  float* lnp = reinterpret_cast<float*>(g + PJ_LN);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
-    mbar_init(bar_load, 1);
-    mbar_init(bar_mma, 1);
+    mbar_init(wbar, 1);
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(full(w), 1);
+      mbar_init(empty(w), 1);
+      mbar_init(ready(w), 1);
+      mbar_init(done_a(w), 1);
+      mbar_init(tfree(w), 1);
+      mbar_init(done_b(w), 1);
+    }
     fence_barrier_init();
   }
-  if (warp == 0) {
+  for (int c = tid; c < CH; c += blockDim.x) {
+    lnp[c] = a.ln_w[c];
+    lnp[CH + c] = a.ln_b[c];
+  }
+  if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
@@ -170,94 +141,159 @@ __global__ void __launch_bounds__(128) k_triatt_proj(const __grid_constant__ CUt
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int64_t G = gridDim.x;
 
-  if (tid == 0) {
-    mbar_arrive_expect_tx(bar_load, 32768 + 2 * PB_ATOM);
-    tma_load_3d(sA, &tz, bar_load, 0, (int)c0, (int)r);
-    tma_load_3d(sA + 16384, &tz, bar_load, 64, (int)c0, (int)r);
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tz);
+      mbar_arrive_expect_tx(wbar, 2 * PB_ATOM);
 #pragma unroll
-    for (int at = 0; at < 2; ++at) {
-      const uint32_t b0 = sB + at * PB_ATOM;
-      tma_load_2d(b0, &twq, bar_load, at * 64, 0);
-      tma_load_2d(b0 + 128 * 128, &twk, bar_load, at * 64, 0);
-      tma_load_2d(b0 + 256 * 128, &twv, bar_load, at * 64, 0);
-      tma_load_2d(b0 + 384 * 128, &twb, bar_load, at * 64, 0);  // 16 rows, rows >= H read 0
+      for (int at = 0; at < 2; ++at) {
+        const uint32_t b0 = base + at * PB_ATOM;
+        tma_load_2d(b0, &twq, wbar, at * 64, 0);
+        tma_load_2d(b0 + 128 * 128, &twk, wbar, at * 64, 0);
+        tma_load_2d(b0 + 256 * 128, &twv, wbar, at * 64, 0);
+        tma_load_2d(b0 + 384 * 128, &twb, wbar, at * 64, 0);  // 16 rows, rows >= H read 0
+      }
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= a.n_tiles) break;
+        const int w = (int)(k & 1);
+        const int64_t n = k >> 1;
+        if (n > 0) mbar_wait(empty(w), (uint32_t)((n - 1) & 1), a.status);
+        const int r = (int)(t / a.tiles_per_row);
+        const int c0 = (int)((t % a.tiles_per_row) * TILE);
+        const uint32_t st = base + PJ_STAGE + w * PJ_STAGE_BYTES;
+        mbar_arrive_expect_tx(full(w), 32768);
+        tma_load_3d(st, &tz, full(w), 0, c0, r);
+        tma_load_3d(st + 16384, &tz, full(w), 64, c0, r);
+      }
     }
-  }
-  mbar_wait(bar_load, 0, a.status);
-  ln_row_inplace(g, tid, a.ln_w, a.ln_b);
-  fence_proxy_async_smem();
-  __syncthreads();
-  if (tid == 0) {
-    tc_fence_after();
-    umma_k128(tmem, sA, sB, PB_ATOM, idesc_f16(128, 256, true));                      // q | k
-    umma_k128(tmem + 256, sA, sB + 256 * 128, PB_ATOM, idesc_f16(128, 144, true));    // v | bias
-    umma_commit(bar_mma);
-  }
-  mbar_wait(bar_mma, 0, a.status);
-  tc_fence_after();
-
-  const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-  const int64_t col = c0 + tid;
-  const bool valid = col < a.n_keys;
-  // q, k: 32 contiguous values per (head, position)
-#pragma unroll 1
-  for (int h = 0; h < H; ++h) {
-    uint32_t qv[32], kv[32];
-    tmem_ld32(tmem + lane_base + h * D, qv);
-    tmem_ld32(tmem + lane_base + 128 + h * D, kv);
-    tmem_ld_wait();
-    if (valid && a.want_qkv) {
+  } else if (warp == 1) {
+    if (lane == 0) {
+      mbar_wait(wbar, 0, a.status);
+      for (int64_t k = 0;; ++k) {
+        const int64_t t = blockIdx.x + k * G;
+        if (t >= a.n_tiles) break;
+        const int w = (int)(k & 1);
+        const uint32_t par = (uint32_t)((k >> 1) & 1);
+        const uint32_t sA = base + PJ_STAGE + w * PJ_STAGE_BYTES;
+        mbar_wait(ready(w), par, a.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256, sA, base, PB_ATOM, idesc_f16(128, 256, true));              // q | k
+        umma_commit(done_a(w));
+        mbar_wait(tfree(w), par, a.status);
+        tc_fence_after();
+        tile::umma_k128(tmem + w * 256, sA, base + 256 * 128, PB_ATOM, idesc_f16(128, 144, true));  // v | bias
+        umma_commit(done_b(w));
+      }
+    }
+  } else {
+    const int wg = (warp - 2) >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const bool leader = (warp == 2 + 4 * wg) && lane == 0;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* zt = g + PJ_STAGE + wg * PJ_STAGE_BYTES;
+    const uint32_t st = base + PJ_STAGE + wg * PJ_STAGE_BYTES;
+    const uint32_t tm = tmem + lane_base + wg * 256;
+    for (int64_t k = wg;; k += 2) {
+      const int64_t t = blockIdx.x + k * G;
+      if (t >= a.n_tiles) break;
+      const uint32_t par = (uint32_t)((k >> 1) & 1);
+      const int r = (int)(t / a.tiles_per_row);
+      const int c0 = (int)((t % a.tiles_per_row) * TILE);
+      mbar_wait(full(wg), par, a.status);
+      {
+        uint32_t zr[64];
+        float m, rs;
+        tile::load_row(zt, row, zr);
+        tile::row_stats(zr, 1e-5f, m, rs);
+        tile::store_norm_row(zt, row, zr, m, rs, lnp, lnp + CH);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(ready(wg));
+      const int64_t col = (int64_t)c0 + row;
+      const bool valid = col < a.n_keys && a.want_qkv;
       const int64_t jq = col - a.q_col0;
-      if (jq >= 0 && jq < a.n_q) {
-        uint4* dq = reinterpret_cast<uint4*>(a.q + (((int64_t)r * H + h) * a.n_q + jq) * D);
+      const bool qvalid = valid && jq >= 0 && jq < a.n_q;
+      mbar_wait(done_a(wg), par, a.status);
+      tc_fence_after();
+#pragma unroll 1
+      for (int h = 0; h < H; ++h) {
+        uint32_t qv[32], kv[32];
+        tmem_ld32(tm + h * D, qv);
+        tmem_ld32(tm + 128 + h * D, kv);
+        tmem_ld_wait();
+        if (qvalid) {
+          uint4* dq = reinterpret_cast<uint4*>(a.q + (((int64_t)r * H + h) * a.n_q + jq) * D);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          uint4 w;
-          w.x = pack_f16(__uint_as_float(qv[e * 8 + 0]) * a.q_scale, __uint_as_float(qv[e * 8 + 1]) * a.q_scale);
-          w.y = pack_f16(__uint_as_float(qv[e * 8 + 2]) * a.q_scale, __uint_as_float(qv[e * 8 + 3]) * a.q_scale);
-          w.z = pack_f16(__uint_as_float(qv[e * 8 + 4]) * a.q_scale, __uint_as_float(qv[e * 8 + 5]) * a.q_scale);
-          w.w = pack_f16(__uint_as_float(qv[e * 8 + 6]) * a.q_scale, __uint_as_float(qv[e * 8 + 7]) * a.q_scale);
-          dq[e] = w;
+          for (int e = 0; e < 4; ++e) {
+            uint4 w4;
+            w4.x = pack_f16(__uint_as_float(qv[e * 8 + 0]) * a.q_scale, __uint_as_float(qv[e * 8 + 1]) * a.q_scale);
+            w4.y = pack_f16(__uint_as_float(qv[e * 8 + 2]) * a.q_scale, __uint_as_float(qv[e * 8 + 3]) * a.q_scale);
+            w4.z = pack_f16(__uint_as_float(qv[e * 8 + 4]) * a.q_scale, __uint_as_float(qv[e * 8 + 5]) * a.q_scale);
+            w4.w = pack_f16(__uint_as_float(qv[e * 8 + 6]) * a.q_scale, __uint_as_float(qv[e * 8 + 7]) * a.q_scale);
+            dq[e] = w4;
+          }
+        }
+        if (valid) {
+          uint4* dk = reinterpret_cast<uint4*>(a.k + (((int64_t)r * H + h) * a.ld_keys + col) * D);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            uint4 w4;
+            w4.x = pack_f16(__uint_as_float(kv[e * 8 + 0]), __uint_as_float(kv[e * 8 + 1]));
+            w4.y = pack_f16(__uint_as_float(kv[e * 8 + 2]), __uint_as_float(kv[e * 8 + 3]));
+            w4.z = pack_f16(__uint_as_float(kv[e * 8 + 4]), __uint_as_float(kv[e * 8 + 5]));
+            w4.w = pack_f16(__uint_as_float(kv[e * 8 + 6]), __uint_as_float(kv[e * 8 + 7]));
+            dk[e] = w4;
+          }
         }
       }
-      uint4* dk = reinterpret_cast<uint4*>(a.k + (((int64_t)r * H + h) * a.ld_keys + col) * D);
+      tc_fence_before();
+      named_bar_sync(1 + wg, 128);
+      if (leader) mbar_arrive(tfree(wg));
+      mbar_wait(done_b(wg), par, a.status);
+      tc_fence_after();
+      // v^T staged as [(h, d)][key] over the consumed z tile
+      unsigned short* vs = reinterpret_cast<unsigned short*>(zt);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        uint4 w;
-        w.x = pack_f16(__uint_as_float(kv[e * 8 + 0]), __uint_as_float(kv[e * 8 + 1]));
-        w.y = pack_f16(__uint_as_float(kv[e * 8 + 2]), __uint_as_float(kv[e * 8 + 3]));
-        w.z = pack_f16(__uint_as_float(kv[e * 8 + 4]), __uint_as_float(kv[e * 8 + 5]));
-        w.w = pack_f16(__uint_as_float(kv[e * 8 + 6]), __uint_as_float(kv[e * 8 + 7]));
-        dk[e] = w;
+      for (int cc = 0; cc < HD; cc += 16) {
+        uint32_t vv[16];
+        tmem_ld16(tm + cc, vv);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vs[(cc + e) * TILE + row] = __half_as_ushort(__float2half_rn(__uint_as_float(vv[e])));
+      }
+      {
+        uint32_t bv[16];
+        tmem_ld16(tm + HD, bv);
+        tmem_ld_wait();
+        if (a.want_bias && col < a.n_keys) {
+#pragma unroll
+          for (int h = 0; h < H; ++h)
+            a.bias[h * a.b_hs + (int64_t)r * a.b_rs + col] = __float2half_rn(__uint_as_float(bv[h]) * LOG2E);
+        }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_bar_sync(1 + wg, 128);
+      if (leader) {
+        if (a.want_qkv) {
+          tma_store_2d(&tvt, st, c0, r * HD);
+          bulk_commit_group();
+          bulk_wait_group_read0();
+        }
+        mbar_arrive(empty(wg));
       }
     }
-  }
-  // v transposed: vt[(i,h,dd)][key], 2-byte stores coalesced across the warp
-#pragma unroll 1
-  for (int h = 0; h < H; ++h) {
-    uint32_t vv[32];
-    tmem_ld32(tmem + lane_base + 256 + h * D, vv);
-    tmem_ld_wait();
-    if (valid && a.want_qkv) {
-      __half* dv = a.vt + (((int64_t)r * H + h) * D) * a.ld_keys + col;
-#pragma unroll
-      for (int dd = 0; dd < D; ++dd) dv[(int64_t)dd * a.ld_keys] = __float2half_rn(__uint_as_float(vv[dd]));
-    }
-  }
-  {
-    uint32_t bv[16];
-    tmem_ld16(tmem + lane_base + 384, bv);
-    tmem_ld_wait();
-    if (valid && a.want_bias) {
-#pragma unroll
-      for (int h = 0; h < H; ++h)
-        a.bias[h * a.b_hs + r * a.b_rs + col] = __float2half_rn(__uint_as_float(bv[h]) * LOG2E);
-    }
+    if (leader) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -536,19 +572,27 @@ void triatt_plan(Arena& ar, int64_t n_rows, int64_t n_keys, int64_t n_q, bool ow
 }
 
 int launch_proj(const pf_triatt_params* p, const void* zptr, int64_t rs, int64_t cs, int64_t n_rows,
-                int64_t n_cols, ProjArgs pa, cudaStream_t st) {
-  CUtensorMap tz, twq, twk, twv, twb;
+                int64_t n_cols, ProjArgs pa, __half* vt, cudaStream_t st) {
+  CUtensorMap tz, twq, twk, twv, twb, tvt;
   PF_TRY(pair_tmap(&tz, zptr, rs, cs, n_rows, n_cols));
   PF_TRY(weight_tmap(&twq, p->w_q, HD, CH, 128));
   PF_TRY(weight_tmap(&twk, p->w_k, HD, CH, 128));
   PF_TRY(weight_tmap(&twv, p->w_v, HD, CH, 128));
   PF_TRY(weight_tmap(&twb, p->w_bias, H, CH, 16));
+  if (vt) {
+    const uint64_t dv[2] = {(uint64_t)n_cols, (uint64_t)n_rows * HD};
+    const uint64_t sv[1] = {(uint64_t)pa.ld_keys * 2};
+    const uint32_t bv[2] = {(uint32_t)TILE, (uint32_t)HD};
+    PF_TRY(make_tmap(&tvt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vt, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_NONE));
+  } else {
+    tvt = tz;  // unused (no q/k/v wanted)
+  }
   pa.tiles_per_row = (n_cols + TILE - 1) / TILE;
-  const int64_t nt = n_rows * pa.tiles_per_row;
-  if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "triatt projection grid too large");
+  pa.n_tiles = n_rows * pa.tiles_per_row;
   {
+    const int64_t grid_p = pa.n_tiles < num_sms() ? pa.n_tiles : num_sms();
     PF_LAUNCH_SCOPE(st, "k_triatt_proj");
-    k_triatt_proj<<<(unsigned)nt, 128, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, pa);
+    k_triatt_proj<<<(unsigned)grid_p, 320, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, tvt, pa);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
@@ -584,7 +628,7 @@ int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64
   pa.ln_w = p->ln_w;
   pa.ln_b = p->ln_b;
   pa.status = status;
-  return launch_proj(p, z.ptr, z.row_stride, z.col_stride, n_rows, n_cols, pa, st);
+  return launch_proj(p, z.ptr, z.row_stride, z.col_stride, n_rows, n_cols, pa, nullptr, st);
 }
 
 int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias, int64_t b_hs,
@@ -620,7 +664,6 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   pa.want_bias = bias == nullptr;
   pa.q = w.q;
   pa.k = w.k;
-  pa.vt = w.vt;
   pa.bias = w.bias;
   pa.ld_keys = w.ld_keys;
   pa.b_hs = (int64_t)n_q * w.ld_keys;
@@ -629,7 +672,7 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   pa.ln_b = p->ln_b;
   pa.q_scale = LOG2E / sqrtf((float)D);
   pa.status = status;
-  PF_TRY(launch_proj(p, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys, pa, st));
+  PF_TRY(launch_proj(p, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys, pa, w.vt, st));
   // 2. attention core
   const void* bptr = bias ? bias : (const void*)w.bias;
   const int64_t bhs = bias ? b_hs : pa.b_hs, brs = bias ? b_rs : pa.b_rs;
