@@ -127,6 +127,7 @@ __global__ void __launch_bounds__(320, 1) k_triatt_proj(const __grid_constant__ 
       mbar_init(tfree(w), 1);
       mbar_init(done_b(w), 1);
     }
+    mbar_init(bars + 104, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < CH; c += blockDim.x) {
@@ -187,6 +188,8 @@ __global__ void __launch_bounds__(320, 1) k_triatt_proj(const __grid_constant__ 
         tile::umma_k128(tmem + w * 256, sA, base + 256 * 128, PB_ATOM, idesc_f16(128, 144, true));  // v | bias
         umma_commit(done_b(w));
       }
+      umma_commit(bars + 104);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 104, 0);
     }
   } else {
     const int wg = (warp - 2) >> 2;
@@ -351,6 +354,7 @@ __global__ void __launch_bounds__(320, 1) k_triatt_out(const __grid_constant__ C
       mbar_init(mg(w), 1);
       mbar_init(mo(w), 1);
     }
+    mbar_init(bars + 104, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < CH; c += blockDim.x) {
@@ -410,6 +414,8 @@ __global__ void __launch_bounds__(320, 1) k_triatt_out(const __grid_constant__ C
         tile::umma_k128(tmem + w * 256, sO, base + O_WO, 16384, idesc_f16(128, 128, true));
         umma_commit(mo(w));
       }
+      umma_commit(bars + 104);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 104, 0);
     }
   } else {
     const int wg = (warp - 2) >> 2;

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
       mbar_init(ready(w), 1);
       mbar_init(done(w), 1);
     }
+    mbar_init(bars + 72, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < CH; c += blockDim.x) {
@@ -160,6 +161,8 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
                         idesc_f16(128, 256, true));
         umma_commit(done(w));
       }
+      umma_commit(bars + 72);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 72, 0);
     }
   } else {
     const int wg = (warp - 2) >> 2;
@@ -400,6 +403,7 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
       mbar_init(ready(w), 1);
       mbar_init(done(w), 1);
     }
+    mbar_init(bars + 72, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < 128; c += blockDim.x) {
@@ -457,6 +461,8 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
         tile::umma_k128(tmem + w * 256, sX, base + O_WZ, 16384, idesc_f16(128, 128, true));
         umma_commit(done(w));
       }
+      umma_commit(bars + 72);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 72, 0);
     }
   } else {
     const int wg = (warp - 2) >> 2;

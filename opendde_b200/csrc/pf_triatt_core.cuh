@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
   const uint32_t bars = base + CC_BAR;
   // barriers: full[3] @0, empty[3] @24, then per row r: s @48+8r, p @64+8r, o @80+8r,
   // q[slot] @96+16r+8slot (one per TMEM Q slot, so a slot's barrier is never two phases
-  // ahead of its waiter), ofree @128+8r; TMEM slot @200
+  // ahead of its waiter), ofree @128+8r; drain @176; TMEM slot @200
   const uint32_t bar_full0 = bars, bar_empty0 = bars + 24;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + CC_BAR + 200);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
       mbar_init(bars + 96 + 16 * r + 8, 4);  // Q rows written into slot 1
       mbar_init(bars + 128 + 8 * r, 4);      // O/L read out, free for the next item
     }
+    mbar_init(bars + 176, 1);                // drain
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -350,6 +351,8 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         first = first2;
         ++step;
       }
+      umma_commit(bars + 176);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 176, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax (row r)
