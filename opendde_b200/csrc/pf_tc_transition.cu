@@ -1,19 +1,23 @@
 // pf_tc_transition.cu -- pair Transition (LN -> SiLU(W_a y) * (W_b y) -> W_out, + residual) on
 // tcgen05 tensor cores, c = 128, hidden = 4c = 512, bf16 in / fp32 accumulate.
 //
-// One CTA = 128 rows. The 512-wide hidden layer never leaves the SM: it is produced and consumed
-// in 8 chunks of 64:
-//   [a | b](chunk)  = LN(x) [W_a(chunk); W_b(chunk)]^T     UMMA 128x128x128 -> TMEM (2 slots)
-//   h(chunk)        = silu(a) * b  -> bf16 -> shared memory (2 slots, SW128 K-major)
+// One CTA = two 128-row tiles (A and B). The 512-wide hidden layer never leaves the SM: it is
+// produced and consumed in 8 chunks of 64, and every weight chunk brought in by TMA serves
+// both tiles (half the L2 weight traffic of one tile per CTA):
+//   [a | b](chunk)  = LN(x) [W_a(chunk); W_b(chunk)]^T     UMMA 128x128x128 -> TMEM
+//   h(chunk)        = silu(a) * b  -> bf16 -> shared memory (SW128 K-major)
 //   out            += h(chunk) W_o(:, chunk)^T             UMMA 128x128x64  -> TMEM
-// Warps 0-3: LayerNorm prologue, silu epilogue per chunk, final residual epilogue (thread = row).
-// Warp 4: MMA issuer. Warp 5: TMA producer for the x tile and the weight-chunk ring (2 slots).
+// Warps 0-3 / 4-7: tile A / tile B (thread = row): LayerNorm prologue, silu per chunk, final
+// residual epilogue (TMA store). Warp 8: TMA producer (x tiles, weight-chunk ring of 2 slots).
+// Warp 9: MMA issuer. While one warpgroup turns a chunk into h, the tensor core works on the
+// other tile, so the SiLU and the MMAs overlap.
 // Reference: opendde/model/modules/primitives.py:182-217.
 
 #include "pf_common.cuh"
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
 namespace pf {
@@ -25,16 +29,17 @@ namespace {
 constexpr int C = 128, HID = 512, CHUNK = 64, NCHUNK = HID / CHUNK, TILE = 128;
 
 // shared memory (offsets from the 1 KB aligned base)
-constexpr uint32_t S_A = 0;                 // LN(x): 2 atoms x 128 rows x 128 B = 32 KB
-constexpr uint32_t S_W = 32768;             // 2 slots x 48 KB: [W_a;W_b] 2 atoms x 128 rows (32 KB) + W_o 128 rows x 128 B (16 KB)
+constexpr uint32_t S_X = 0;                   // 2 tiles x 32 KB: x, LN(x) in place, then the output tile
+constexpr uint32_t S_W = 65536;               // 2 slots x 48 KB: [W_a;W_b] 2 atoms x 128 rows (32 KB) + W_o 128 rows x 128 B (16 KB)
 constexpr uint32_t S_W_SLOT = 49152;
-constexpr uint32_t S_H = S_W + 2 * S_W_SLOT;  // 2 slots x 16 KB: h 128 rows x 64 (128 B)
-constexpr uint32_t S_BAR = S_H + 2 * 16384;
+constexpr uint32_t S_H = S_W + 2 * S_W_SLOT;  // 2 tiles x 16 KB: h 128 rows x 64 (128 B)
+constexpr uint32_t S_LN = S_H + 2 * 16384;    // LayerNorm weight and bias (fp32)
+constexpr uint32_t S_BAR = S_LN + 1024;
 constexpr uint32_t TR_SMEM = S_BAR + 256;
 
 struct TrArgs {
   int64_t rows;
-  __nv_bfloat16* out;
+  const __nv_bfloat16* out;  // residual source (the output rows' old values)
   int64_t out_stride;
   const float *ln_w, *ln_b;
   int accumulate;
@@ -48,7 +53,8 @@ __device__ __forceinline__ float silu_fast(float a) {
   return a * fmaf(0.5f, t, 0.5f);
 }
 
-__global__ void __launch_bounds__(192, 1) k_transition(const __grid_constant__ CUtensorMap tx,
+__global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ CUtensorMap tx,
+                                                       const __grid_constant__ CUtensorMap tout,
                                                        const __grid_constant__ CUtensorMap twa,
                                                        const __grid_constant__ CUtensorMap twb,
                                                        const __grid_constant__ CUtensorMap two,
@@ -58,205 +64,202 @@ __global__ void __launch_bounds__(192, 1) k_transition(const __grid_constant__ C
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
   const uint32_t bars = base + S_BAR;
-  // barriers: x_full @0, a_ready @8, w_full[2] @16, w_empty[2] @32, ab_full[2] @48,
-  // ab_empty[2] @64, h_full[2] @80, h_empty[2] @96, out_full @112; TMEM slot @128
-  const uint32_t b_x = bars, b_a = bars + 8, b_wf = bars + 16, b_we = bars + 32, b_abf = bars + 48,
-                 b_abe = bars + 64, b_hf = bars + 80, b_he = bars + 96, b_out = bars + 112;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + S_BAR + 128);
+  // barriers (per tile t = 0, 1 at +8t): x_full @0, ln_ready @16, ab_full @32, ab_empty @48,
+  // h_full @64, h_empty @80, out_full @96; weight slots s: w_full @112+8s, w_empty @128+8s;
+  // drain @144; TMEM slot @192
+  auto b_x = [&](int t) { return bars + 8 * t; };
+  auto b_ln = [&](int t) { return bars + 16 + 8 * t; };
+  auto b_abf = [&](int t) { return bars + 32 + 8 * t; };
+  auto b_abe = [&](int t) { return bars + 48 + 8 * t; };
+  auto b_hf = [&](int t) { return bars + 64 + 8 * t; };
+  auto b_he = [&](int t) { return bars + 80 + 8 * t; };
+  auto b_out = [&](int t) { return bars + 96 + 8 * t; };
+  auto b_wf = [&](int s) { return bars + 112 + 8 * s; };
+  auto b_we = [&](int s) { return bars + 128 + 8 * s; };
+  const uint32_t b_drain = bars + 144;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + S_BAR + 192);
+  float* lnp = reinterpret_cast<float*>(g + S_LN);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int64_t r0 = (int64_t)blockIdx.x * TILE;
+  const int64_t r0 = (int64_t)blockIdx.x * (2 * TILE);
+  const bool has_b = r0 + TILE < a.rows;  // tile B holds at least one row
+  const int ntile = has_b ? 2 : 1;
 
   if (tid == 0) {
-    mbar_init(b_x, 1);
-    mbar_init(b_a, 4);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(b_wf + 8 * s, 1);
-      mbar_init(b_we + 8 * s, 1);
-      mbar_init(b_abf + 8 * s, 1);
-      mbar_init(b_abe + 8 * s, 4);
-      mbar_init(b_hf + 8 * s, 4);
-      mbar_init(b_he + 8 * s, 1);
+    for (int t = 0; t < 2; ++t) {
+      mbar_init(b_x(t), 1);
+      mbar_init(b_ln(t), 4);
+      mbar_init(b_abf(t), 1);
+      mbar_init(b_abe(t), 4);
+      mbar_init(b_hf(t), 4);
+      mbar_init(b_he(t), 1);
+      mbar_init(b_out(t), 1);
+      mbar_init(b_wf(t), 1);
+      mbar_init(b_we(t), 1);
     }
-    mbar_init(b_out, 1);
+    mbar_init(b_drain, 1);
     fence_barrier_init();
   }
-  if (warp == 4) {
+  for (int c = tid; c < C; c += blockDim.x) {
+    lnp[c] = a.ln_w[c];
+    lnp[C + c] = a.ln_b[c];
+  }
+  if (warp == 9) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tmem = *tmem_slot;  // D_ab slots at 0 / 128, D_out at 256
+  const uint32_t tmem = *tmem_slot;  // tile t: D_ab at 256 t, D_out at 256 t + 128
 
-  if (warp == 5) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
-      mbar_arrive_expect_tx(b_x, 32768);
-      tma_load_2d(base + S_A, &tx, b_x, 0, (int)r0);
-      tma_load_2d(base + S_A + 16384, &tx, b_x, 64, (int)r0);
+      for (int t = 0; t < ntile; ++t) {
+        mbar_arrive_expect_tx(b_x(t), 32768);
+        tma_load_2d(base + S_X + t * 32768, &tx, b_x(t), 0, (int)(r0 + t * TILE));
+        tma_load_2d(base + S_X + t * 32768 + 16384, &tx, b_x(t), 64, (int)(r0 + t * TILE));
+      }
       for (int hc = 0; hc < NCHUNK; ++hc) {
         const int s = hc & 1;
-        if (hc >= 2 && !mbar_wait(b_we + 8 * s, ((hc - 2) >> 1) & 1, a.status)) break;
-        const uint32_t w = base + S_W + s * S_W_SLOT, full = b_wf + 8 * s;
-        mbar_arrive_expect_tx(full, S_W_SLOT);
+        if (hc >= 2 && !mbar_wait(b_we(s), ((hc - 2) >> 1) & 1, a.status)) break;
+        const uint32_t w = base + S_W + s * S_W_SLOT;
+        mbar_arrive_expect_tx(b_wf(s), S_W_SLOT);
         // atom k (K 64k..64k+63): rows 0..63 = W_a chunk, rows 64..127 = W_b chunk
-        tma_load_2d(w, &twa, full, 0, hc * CHUNK);
-        tma_load_2d(w + 8192, &twb, full, 0, hc * CHUNK);
-        tma_load_2d(w + 16384, &twa, full, 64, hc * CHUNK);
-        tma_load_2d(w + 16384 + 8192, &twb, full, 64, hc * CHUNK);
-        tma_load_2d(w + 32768, &two, full, hc * CHUNK, 0);  // W_o[:, chunk] 128 rows x 64
+        tma_load_2d(w, &twa, b_wf(s), 0, hc * CHUNK);
+        tma_load_2d(w + 8192, &twb, b_wf(s), 0, hc * CHUNK);
+        tma_load_2d(w + 16384, &twa, b_wf(s), 64, hc * CHUNK);
+        tma_load_2d(w + 16384 + 8192, &twb, b_wf(s), 64, hc * CHUNK);
+        tma_load_2d(w + 32768, &two, b_wf(s), hc * CHUNK, 0);  // W_o[:, chunk] 128 rows x 64
       }
     }
-  } else if (warp == 4) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
+    // Order per chunk hc: ab(t, hc) for each tile, then out(t, hc) for each tile, so one
+    // tile's ab MMAs run while the other tile's warpgroup is busy with its silu.
     if (lane == 0) {
       constexpr uint32_t id_ab = idesc_f16(128, 128, true);
       constexpr uint32_t id_o = idesc_f16(128, 128, true);
-      bool ok = mbar_wait(b_a, 0, a.status);  // LN(x) in smem
-      auto mma_ab = [&](int hc) {
+      bool ok = true;
+      for (int t = 0; t < ntile; ++t) ok = mbar_wait(b_ln(t), 0, a.status) && ok;  // LN(x) in smem
+      for (int hc = 0; hc < NCHUNK; ++hc) {
         const int s = hc & 1;
         const uint32_t w = base + S_W + s * S_W_SLOT;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t atom = kk >> 2, within = (kk & 3) * 32;
-          umma_f16(tmem + 128 * s, sdesc(base + S_A + atom * 16384 + within, 1024, SWZ_128B),
-                   sdesc(w + atom * 16384 + within, 1024, SWZ_128B), id_ab, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(b_abf + 8 * s);
-      };
-      for (int hc = 0; hc < 2 && ok; ++hc) {
-        ok = mbar_wait(b_wf + 8 * hc, 0, a.status);
-        tc_fence_after();
-        mma_ab(hc);
-      }
-      for (int hc = 0; hc < NCHUNK && ok; ++hc) {
-        const int s = hc & 1;
-        ok = mbar_wait(b_hf + 8 * s, (hc >> 1) & 1, a.status);
-        tc_fence_after();
-        const uint32_t hb = base + S_H + s * 16384, w = base + S_W + s * S_W_SLOT + 32768;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          umma_f16(tmem + 256, sdesc(hb + kk * 32, 1024, SWZ_128B), sdesc(w + kk * 32, 1024, SWZ_128B), id_o,
-                   (hc > 0 || kk > 0) ? 1u : 0u);
-        }
-        umma_commit(b_he + 8 * s);  // h slot s free when this MMA finishes
-        umma_commit(b_we + 8 * s);  // weight slot s free (its ab and out MMAs are done)
-        if (hc + 2 < NCHUNK) {
-          ok = ok && mbar_wait(b_wf + 8 * s, ((hc + 2) >> 1) & 1, a.status);
-          ok = ok && mbar_wait(b_abe + 8 * s, (hc >> 1) & 1, a.status);  // D_ab slot read out
+        ok = mbar_wait(b_wf(s), (hc >> 1) & 1, a.status) && ok;
+        for (int t = 0; t < ntile; ++t) {
+          if (hc > 0) ok = mbar_wait(b_abe(t), (hc - 1) & 1, a.status) && ok;  // D_ab read out
           tc_fence_after();
-          mma_ab(hc + 2);
+          tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, w, 16384, id_ab);
+          umma_commit(b_abf(t));
         }
+        for (int t = 0; t < ntile; ++t) {
+          ok = mbar_wait(b_hf(t), hc & 1, a.status) && ok;
+          tc_fence_after();
+          const uint32_t hb = base + S_H + t * 16384, wo = w + 32768;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_f16(tmem + 256 * t + 128, sdesc(hb + kk * 32, 1024, SWZ_128B), sdesc(wo + kk * 32, 1024, SWZ_128B),
+                     id_o, (hc > 0 || kk > 0) ? 1u : 0u);
+          umma_commit(b_he(t));  // h buffer of tile t free when this MMA finishes
+        }
+        umma_commit(b_we(s));  // weight slot s free (its ab and out MMAs are done)
       }
-      umma_commit(b_out);
+      for (int t = 0; t < ntile; ++t) umma_commit(b_out(t));
+      umma_commit(b_drain);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(b_drain, 0);
     }
   } else {
-    // ---------------------------------------------------------------- compute warps (thread = row)
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-    mbar_wait(b_x, 0, a.status);
-    {
-      // LayerNorm in place (two 64-channel SW128 atoms)
-      float v[C];
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        const uint4 q = *reinterpret_cast<const uint4*>(g + S_A + (j >> 3) * 16384 + sw128_off(tid, j & 7));
-        v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
-        v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
-        v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
-        v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
+    // ---------------------------------------------------------------- compute warpgroups
+    const int t = warp >> 2;
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+    uint8_t* xt = g + S_X + t * 32768;
+    const int64_t grow = r0 + t * TILE + row;
+    if (t < ntile) {
+      mbar_wait(b_x(t), 0, a.status);
+      {
+        uint32_t xr[64];
+        float m, rs;
+        tile::load_row(xt, row, xr);
+        tile::row_stats(xr, 1e-5f, m, rs);
+        tile::store_norm_row(xt, row, xr, m, rs, lnp, lnp + C);
       }
-      float sm = 0.f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) sm += v[c];
-      const float mean = sm * (1.0f / C);
-      float sq = 0.f;
-#pragma unroll
-      for (int c = 0; c < C; ++c) {
-        const float d = v[c] - mean;
-        sq += d * d;
-      }
-      const float rstd = rsqrtf(sq * (1.0f / C) + 1e-5f);
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float y[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int c = j * 8 + e;
-          y[e] = (v[c] - mean) * rstd * __ldg(a.ln_w + c) + __ldg(a.ln_b + c);
-        }
-        uint4 q;
-        q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
-        q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
-        *reinterpret_cast<uint4*>(g + S_A + (j >> 3) * 16384 + sw128_off(tid, j & 7)) = q;
-      }
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) mbar_arrive(b_a);
-    for (int hc = 0; hc < NCHUNK; ++hc) {
-      const int s = hc & 1;
-      mbar_wait(b_abf + 8 * s, (hc >> 1) & 1, a.status);
-      tc_fence_after();
-      uint32_t av[32], bv[32];
-      uint32_t hv[32];  // 64 bf16 of h for this row
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        tmem_ld32(tmem + 128 * s + lane_base + half * 32, av);
-        tmem_ld32(tmem + 128 * s + lane_base + 64 + half * 32, bv);
-        tmem_ld_wait();
-#pragma unroll
-        for (int e = 0; e < 16; ++e)
-          hv[half * 16 + e] = pack_bf16(silu_fast(__uint_as_float(av[2 * e])) * __uint_as_float(bv[2 * e]),
-                                        silu_fast(__uint_as_float(av[2 * e + 1])) * __uint_as_float(bv[2 * e + 1]));
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(b_abe + 8 * s);  // D_ab slot may be overwritten
-      if (hc >= 2) mbar_wait(b_he + 8 * s, ((hc - 2) >> 1) & 1, a.status);
-      uint8_t* hb = g + S_H + s * 16384;
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch)
-        *reinterpret_cast<uint4*>(hb + sw128_off(tid, ch)) =
-            make_uint4(hv[ch * 4 + 0], hv[ch * 4 + 1], hv[ch * 4 + 2], hv[ch * 4 + 3]);
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(b_hf + 8 * s);
-    }
-    // residual epilogue
-    mbar_wait(b_out, 0, a.status);
-    tc_fence_after();
-    const int64_t row = r0 + tid;
-    const bool valid = row < a.rows;
-    __nv_bfloat16* op = a.out + (valid ? row : 0) * a.out_stride;
-#pragma unroll 1
-    for (int cc = 0; cc < C; cc += 32) {
-      uint32_t ov[32];
-      tmem_ld32(tmem + 256 + lane_base + cc, ov);
-      tmem_ld_wait();
-      if (valid) {
-        uint4* dst = reinterpret_cast<uint4*>(op + cc);
+      if (lane == 0) mbar_arrive(b_ln(t));
+      const uint32_t tab = tmem + 256 * t + lane_base;
+      uint8_t* hb = g + S_H + t * 16384;
+      for (int hc = 0; hc < NCHUNK; ++hc) {
+        mbar_wait(b_abf(t), hc & 1, a.status);
+        tc_fence_after();
+        uint32_t hv[32];  // 64 bf16 of h for this row
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
+        for (int half = 0; half < 2; ++half) {
+          uint32_t av[32], bv[32];
+          tmem_ld32(tab + half * 32, av);
+          tmem_ld32(tab + 64 + half * 32, bv);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            hv[half * 16 + e] = pack_bf16(silu_fast(__uint_as_float(av[2 * e])) * __uint_as_float(bv[2 * e]),
+                                          silu_fast(__uint_as_float(av[2 * e + 1])) * __uint_as_float(bv[2 * e + 1]));
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_abe(t));  // D_ab may be overwritten
+        if (hc > 0) mbar_wait(b_he(t), (hc - 1) & 1, a.status);
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch)
+          *reinterpret_cast<uint4*>(hb + sw128_off(row, ch)) =
+              make_uint4(hv[ch * 4 + 0], hv[ch * 4 + 1], hv[ch * 4 + 2], hv[ch * 4 + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(b_hf(t));
+      }
+      // residual epilogue: out (+ old rows, an L2 hit) written over the x tile and TMA-stored
+      const bool valid = grow < a.rows;
+      const bool rd = a.accumulate && valid;
+      const uint4* op = reinterpret_cast<const uint4*>(a.out + (valid ? grow : 0) * a.out_stride);
+      uint4 old[16];
+#pragma unroll
+      for (int c = 0; c < 16; ++c) old[c] = rd ? __ldg(op + c) : make_uint4(0, 0, 0, 0);
+      mbar_wait(b_out(t), 0, a.status);
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < C; cc += 16) {
+        uint32_t ov[16];
+        tmem_ld16(tmem + 256 * t + 128 + lane_base + cc, ov);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int chunk = (cc >> 3) + e;
+          const uint4 o = old[chunk];
           float u[8];
 #pragma unroll
           for (int k = 0; k < 8; ++k) u[k] = __uint_as_float(ov[e * 8 + k]);
-          if (a.accumulate) {
-            const uint4 old = dst[e];
-            u[0] += bf16lo(old.x); u[1] += bf16hi(old.x); u[2] += bf16lo(old.y); u[3] += bf16hi(old.y);
-            u[4] += bf16lo(old.z); u[5] += bf16hi(old.z); u[6] += bf16lo(old.w); u[7] += bf16hi(old.w);
-          }
-          uint4 w;
-          w.x = pack_bf16(u[0], u[1]); w.y = pack_bf16(u[2], u[3]);
-          w.z = pack_bf16(u[4], u[5]); w.w = pack_bf16(u[6], u[7]);
-          dst[e] = w;
+          u[0] += bf16lo(o.x); u[1] += bf16hi(o.x); u[2] += bf16lo(o.y); u[3] += bf16hi(o.y);
+          u[4] += bf16lo(o.z); u[5] += bf16hi(o.z); u[6] += bf16lo(o.w); u[7] += bf16hi(o.w);
+          uint4 wv;
+          wv.x = pack_bf16(u[0], u[1]); wv.y = pack_bf16(u[2], u[3]);
+          wv.z = pack_bf16(u[4], u[5]); wv.w = pack_bf16(u[6], u[7]);
+          *reinterpret_cast<uint4*>(xt + tile::chunk_off(row, chunk)) = wv;
         }
+      }
+      tc_fence_before();
+      fence_proxy_async_smem();
+      named_bar_sync(1 + t, 128);
+      if (warp == 4 * t && lane == 0) {
+        tma_store_2d(&tout, base + S_X + t * 32768, 0, (int)(r0 + t * TILE));
+        tma_store_2d(&tout, base + S_X + t * 32768 + 16384, 64, (int)(r0 + t * TILE));
+        bulk_commit_group();
+        bulk_wait_group0();
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == 9) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, 512);
@@ -295,12 +298,19 @@ int transition(const pf_transition_params* p, const void* x, int64_t xs, void* o
   PF_TRY(wmap(&twa, p->w_a, HID, C, 64, CHUNK));
   PF_TRY(wmap(&twb, p->w_b, HID, C, 64, CHUNK));
   PF_TRY(wmap(&two, p->w_o, C, HID, 64, C));
-  TrArgs a{rows, (__nv_bfloat16*)out, os, p->ln_w, p->ln_b, acc, status};
-  const int64_t nt = (rows + TILE - 1) / TILE;
+  CUtensorMap tout;
+  {
+    const uint64_t dims[2] = {(uint64_t)C, (uint64_t)rows};
+    const uint64_t str[1] = {(uint64_t)os * 2};
+    const uint32_t box[2] = {64, TILE};
+    PF_TRY(make_tmap(&tout, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  TrArgs a{rows, (const __nv_bfloat16*)out, os, p->ln_w, p->ln_b, acc, status};
+  const int64_t nt = (rows + 2 * TILE - 1) / (2 * TILE);
   if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "transition grid too large");
   {
     PF_LAUNCH_SCOPE(st, "k_transition");
-    k_transition<<<(unsigned)nt, 192, TR_SMEM + 1024, st>>>(tx, twa, twb, two, a);
+    k_transition<<<(unsigned)nt, 320, TR_SMEM + 1024, st>>>(tx, tout, twa, twb, two, a);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
