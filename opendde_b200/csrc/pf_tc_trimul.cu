@@ -243,12 +243,19 @@ constexpr uint32_t GEMM_SMEM = STAGES * STAGE_BYTES + 256;
 
 struct GemmArgs {
   int M, N, K;
+  int m_tiles, n_tiles;
+  int64_t n_work;           // channels * m_tiles * n_tiles
   __nv_bfloat16* out;
   int64_t ldo;
   int64_t out_bstride;
   unsigned int* status;
 };
 
+// Persistent: one CTA per SM walks the (channel, m tile, n tile) work list (n fastest, so the
+// CTAs running at one time share a channel's a and b in L2). The TMA ring runs across tiles;
+// two TMEM accumulators (2 x 256 columns) let the epilogue of one tile overlap the MMAs of
+// the next. Warp 0: TMA producer. Warp 1: MMA issuer. Warps 2-5: epilogue (TMEM -> bf16 ->
+// global, one output row per thread).
 __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__ CUtensorMap ta,
                                                          const __grid_constant__ CUtensorMap tb,
                                                          const GemmArgs args) {
@@ -257,25 +264,39 @@ __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
   const uint32_t bars = base + STAGES * STAGE_BYTES;
-  // full[s] at bars + 8s, empty[s] at bars + 64 + 8s, tmem_full at bars + 128
-  const uint32_t bar_tmem_full = bars + 128;
+  // full[s] @8s, empty[s] @64+8s, acc_full[b] @128+8b, acc_empty[b] @144+8b, drain @160;
+  // TMEM slot @192
+  auto acc_full = [&](int b) { return bars + 128 + 8 * b; };
+  auto acc_empty = [&](int b) { return bars + 144 + 8 * b; };
+  const uint32_t bar_drain = bars + 160;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + STAGES * STAGE_BYTES + 192);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
   const int nk = (args.K + BK - 1) / BK;
+  const int64_t G = gridDim.x;
+  auto decode = [&](int64_t t, int& ch, int& m0, int& n0) {
+    const int nt = (int)(t % args.n_tiles);
+    const int64_t r = t / args.n_tiles;
+    m0 = (int)(r % args.m_tiles) * BM;
+    ch = (int)(r / args.m_tiles);
+    n0 = nt * BN;
+  };
 
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(bars + 8 * s, 1);
       mbar_init(bars + 64 + 8 * s, 1);
     }
-    mbar_init(bar_tmem_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full(b), 1);
+      mbar_init(acc_empty(b), 4);
+    }
+    mbar_init(bar_drain, 1);
     fence_barrier_init();
     tma_prefetch_desc(&ta);
     tma_prefetch_desc(&tb);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), 256);
+    tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -283,63 +304,93 @@ __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0 && lane == 0) {
-    // TMA producer
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES, u = kb / STAGES;
-      if (u > 0) mbar_wait(bars + 64 + 8 * s, (u - 1) & 1, args.status);
-      const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
-      mbar_arrive_expect_tx(bars + 8 * s, STAGE_BYTES);
-      tma_load_3d(sa, &ta, bars + 8 * s, kb * BK, m0, bz);
-      tma_load_3d(sb, &tb, bars + 8 * s, kb * BK, n0, bz);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // MMA issuer
-    constexpr uint32_t idesc = idesc_f16(BM, BN, true);
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % STAGES, u = kb / STAGES;
-      mbar_wait(bars + 8 * s, u & 1, args.status);
-      tc_fence_after();
-      const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
-#pragma unroll
-      for (int kk = 0; kk < BK / 16; ++kk) {
-        const uint64_t ad = sdesc(sa + kk * 32, 1024, SWZ_128B);
-        const uint64_t bd = sdesc(sb + kk * 32, 1024, SWZ_128B);
-        umma_f16(tmem, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
-      }
-      umma_commit(bars + 64 + 8 * s);  // frees the stage when these MMAs finish
-    }
-    umma_commit(bar_tmem_full);
-  } else if (warp >= 2) {
-    // epilogue: TMEM -> bf16 -> global
-    mbar_wait(bar_tmem_full, 0, args.status);
-    tc_fence_after();
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const int gm = m0 + row;
-    __nv_bfloat16* orow = args.out + (int64_t)bz * args.out_bstride + (int64_t)gm * args.ldo;
-#pragma unroll 1
-    for (int cc = 0; cc < BN; cc += 32) {
-      uint32_t v[32];
-      tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + cc, v);
-      tmem_ld_wait();
-      const int gn = n0 + cc;
-      if (gm < args.M && gn < args.N) {
-        if (gn + 32 <= args.N) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + gn);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            uint4 w;
-            w.x = pack_bf16(__uint_as_float(v[e * 8 + 0]), __uint_as_float(v[e * 8 + 1]));
-            w.y = pack_bf16(__uint_as_float(v[e * 8 + 2]), __uint_as_float(v[e * 8 + 3]));
-            w.z = pack_bf16(__uint_as_float(v[e * 8 + 4]), __uint_as_float(v[e * 8 + 5]));
-            w.w = pack_bf16(__uint_as_float(v[e * 8 + 6]), __uint_as_float(v[e * 8 + 7]));
-            dst[e] = w;
-          }
-        } else {
-          for (int e = 0; e < 32 && gn + e < args.N; ++e) orow[gn + e] = __float2bfloat16_rn(__uint_as_float(v[e]));
+  if (warp == 0) {
+    if (lane == 0) {
+      // TMA producer: one k-block counter across all tiles of this CTA
+      uint32_t cnt = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < args.n_work && ok; t += G) {
+        int ch, m0, n0;
+        decode(t, ch, m0, n0);
+        for (int kb = 0; kb < nk; ++kb, ++cnt) {
+          const uint32_t s = cnt % STAGES, u = cnt / STAGES;
+          if (u > 0) ok = mbar_wait(bars + 64 + 8 * s, (u - 1) & 1, args.status) && ok;
+          const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(bars + 8 * s, STAGE_BYTES);
+          tma_load_3d(sa, &ta, bars + 8 * s, kb * BK, m0, ch);
+          tma_load_3d(sb, &tb, bars + 8 * s, kb * BK, n0, ch);
         }
       }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_f16(BM, BN, true);
+      uint32_t cnt = 0, j = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < args.n_work && ok; t += G, ++j) {
+        const uint32_t b = j & 1;
+        if (j >= 2) ok = mbar_wait(acc_empty(b), ((j >> 1) - 1) & 1, args.status) && ok;  // epilogue drained it
+        tc_fence_after();
+        const uint32_t acc = tmem + 256 * b;
+        for (int kb = 0; kb < nk; ++kb, ++cnt) {
+          const uint32_t s = cnt % STAGES, u = cnt / STAGES;
+          ok = mbar_wait(bars + 8 * s, u & 1, args.status) && ok;
+          tc_fence_after();
+          const uint32_t sa = base + s * STAGE_BYTES, sb = sa + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            const uint64_t ad = sdesc(sa + kk * 32, 1024, SWZ_128B);
+            const uint64_t bd = sdesc(sb + kk * 32, 1024, SWZ_128B);
+            umma_f16(acc, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
+          }
+          umma_commit(bars + 64 + 8 * s);  // frees the stage when these MMAs finish
+        }
+        umma_commit(acc_full(b));
+      }
+      umma_commit(bar_drain);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bar_drain, 0);
+    }
+  } else {
+    // epilogue: TMEM -> bf16 -> global
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    uint32_t j = 0;
+    for (int64_t t = blockIdx.x; t < args.n_work; t += G, ++j) {
+      int ch, m0, n0;
+      decode(t, ch, m0, n0);
+      const uint32_t b = j & 1;
+      mbar_wait(acc_full(b), (j >> 1) & 1, args.status);
+      tc_fence_after();
+      const int gm = m0 + row;
+      __nv_bfloat16* orow = args.out + (int64_t)ch * args.out_bstride + (int64_t)gm * args.ldo;
+#pragma unroll 1
+      for (int cc = 0; cc < BN; cc += 32) {
+        uint32_t v[32];
+        tmem_ld32(tmem + 256 * b + ((uint32_t)(q * 32) << 16) + cc, v);
+        tmem_ld_wait();
+        const int gn = n0 + cc;
+        if (gm < args.M && gn < args.N) {
+          if (gn + 32 <= args.N) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + gn);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              uint4 w;
+              w.x = pack_bf16(__uint_as_float(v[e * 8 + 0]), __uint_as_float(v[e * 8 + 1]));
+              w.y = pack_bf16(__uint_as_float(v[e * 8 + 2]), __uint_as_float(v[e * 8 + 3]));
+              w.z = pack_bf16(__uint_as_float(v[e * 8 + 4]), __uint_as_float(v[e * 8 + 5]));
+              w.w = pack_bf16(__uint_as_float(v[e * 8 + 6]), __uint_as_float(v[e * 8 + 7]));
+              dst[e] = w;
+            }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e)
+              if (gn + e < args.N) orow[gn + e] = __float2bfloat16_rn(__uint_as_float(v[e]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty(b));
     }
   }
   tc_fence_before();
@@ -347,7 +398,7 @@ __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -677,12 +728,21 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     const uint32_t bb[3] = {BK, BN, 1};
     PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
   }
-  GemmArgs ga{(int)n_i, (int)n_j, (int)n_k, w.x, w.ld_j, (int64_t)n_i * w.ld_j, status};
-  dim3 grid((unsigned)((n_j + BN - 1) / BN), (unsigned)((n_i + BM - 1) / BM), CH);
-  if (grid.y > 65535) return fail(PF_EUNSUPPORTED, "trimul contraction grid too large");
+  GemmArgs ga;
+  ga.M = (int)n_i;
+  ga.N = (int)n_j;
+  ga.K = (int)n_k;
+  ga.m_tiles = (int)((n_i + BM - 1) / BM);
+  ga.n_tiles = (int)((n_j + BN - 1) / BN);
+  ga.n_work = (int64_t)CH * ga.m_tiles * ga.n_tiles;
+  ga.out = w.x;
+  ga.ldo = w.ld_j;
+  ga.out_bstride = (int64_t)n_i * w.ld_j;
+  ga.status = status;
   {
+    const int64_t grid_g = ga.n_work < sm_count() ? ga.n_work : sm_count();
     PF_LAUNCH_SCOPE(st, "k_trimul_bgemm");
-    k_trimul_bgemm<<<grid, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
+    k_trimul_bgemm<<<(unsigned)grid_g, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
   }
   PF_CHECK_LAUNCH();
   // 3. LN_out, W_z, gate, residual (persistent, one CTA per SM)
