@@ -8,7 +8,9 @@ square mesh: a band request works for any R x C grid, and the ending-node / inco
 read column bands through transposed views instead of transposing z across ranks.
 
 An exchange object carries the transport: ``DistExchange`` runs over torch.distributed
-(NCCL on GPUs, gloo on CPU). The drivers only call ``region`` and ``all_gather``.
+(NCCL on GPUs, gloo on CPU). The drivers only call ``region`` and ``all_gather``; the band of
+a rank's own mesh row (or column) is an all-gather over the row (column) group, the other
+bands are point-to-point batches.
 """
 
 from __future__ import annotations
@@ -125,3 +127,18 @@ def col_band(ex, local, spec: FoldCPPairShardSpec, cols_of: Callable[[Tuple[int,
     """All padded rows x columns ``cols_of(coord)``."""
     full = (0, spec.n_padded)
     return ex.region(local, spec, lambda c: (full, cols_of(c)))
+
+
+def own_row_band(ex, local: torch.Tensor) -> torch.Tensor:
+    """This rank's mesh-row band (rows R_r x all padded columns), gathered over the row group
+    (one all-gather of the tiles, then one reorder into row-major)."""
+    t = ex.all_gather(local, "row")                     # [C, Tr, Tc, ...] by mesh column
+    rest = tuple(range(3, t.dim()))
+    return t.permute(1, 0, 2, *rest).reshape((t.shape[1], t.shape[0] * t.shape[2]) + tuple(t.shape[3:]))
+
+
+def own_col_band(ex, local: torch.Tensor) -> torch.Tensor:
+    """This rank's mesh-column band (all padded rows x columns C_c): the column group's tiles
+    stacked by mesh row are already that band, so the all-gather output is used as is."""
+    t = ex.all_gather(local, "col")                     # [R, Tr, Tc, ...] by mesh row
+    return t.reshape((t.shape[0] * t.shape[1],) + tuple(t.shape[2:]))

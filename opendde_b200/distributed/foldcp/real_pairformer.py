@@ -35,7 +35,7 @@ from typing import Optional, Tuple
 import torch
 import torch.distributed as dist
 
-from .exchange import DistExchange, col_band, row_band
+from .exchange import DistExchange, col_band, own_col_band, own_row_band, row_band
 from .layout import FoldCP2DLayout
 from .mesh import FoldCPProcessMesh
 from .ops import KernelOps
@@ -174,12 +174,12 @@ def _trimul(module, z_local, ctx: FoldCPPairContext, ops) -> None:
     spec, ex, m = ctx.spec, ctx.exchange, ctx.mask
     (r0, r1), (c0, c1) = ctx.rows, ctx.cols
     if module._outgoing:
-        za = row_band(ex, z_local, spec, _row_of(spec))      # z rows R_r  [Tr, Np, C]
+        za = own_row_band(ex, z_local)                         # z rows R_r  [Tr, Np, C]
         zb = row_band(ex, z_local, spec, _col_of(spec))      # z rows C_c  [Tc, Np, C]
         ma, mb = m[r0:r1], m[c0:c1]
     else:
         za = col_band(ex, z_local, spec, _row_of(spec)).transpose(0, 1)  # z cols R_r, read (i, k) = z(k, i)
-        zb = col_band(ex, z_local, spec, _col_of(spec)).transpose(0, 1)  # z cols C_c
+        zb = own_col_band(ex, z_local).transpose(0, 1)       # z cols C_c
         ma, mb = m[:, r0:r1].t(), m[:, c0:c1].t()
     ops.trimul(module, za, zb, ma, mb, z_local, z_local)
 
@@ -190,10 +190,10 @@ def _triatt(module, z_local, ctx: FoldCPPairContext, ending: bool, ops) -> None:
     n_pad = ctx.n_pad
     plane = _triatt_bias_plane(module, z_local, ctx, ending, ops)
     if not ending:
-        zs = row_band(ex, z_local, spec, _row_of(spec))      # rows R_r, keys = all columns
+        zs = own_row_band(ex, z_local)                         # rows R_r, keys = all columns
         ops.triatt(module, zs, m[r0:r1], plane[:, c0:c1, :n_pad], z_local, q_col0=c0, n_q=c1 - c0, n_valid=ctx.n)
     else:
-        zs = col_band(ex, z_local, spec, _col_of(spec)).transpose(0, 1)  # x rows C_c, keys = all rows of z
+        zs = own_col_band(ex, z_local).transpose(0, 1)       # x rows C_c, keys = all rows of z
         ops.triatt(module, zs, m[:, c0:c1].t(), plane[:, r0:r1, :n_pad], z_local.transpose(0, 1),
                    q_col0=r0, n_q=r1 - r0, n_valid=ctx.n)
 
