@@ -414,7 +414,9 @@ def main():
         }
         print(json.dumps(out), flush=True)
     if distributed:
+        from opendde_b200.distributed.foldcp import clear_mesh_cache
         torch.distributed.barrier()
+        clear_mesh_cache()
         torch.distributed.destroy_process_group()
 
 

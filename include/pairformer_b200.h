@@ -3,8 +3,9 @@
  *
  * Plain C: device pointers, sizes, element strides, dtype enums and a cudaStream_t passed
  * as void*. Every entry point returns a pf_status code; a human-readable message for the
- * last failure on the calling thread is available from pf_last_error_string(). No entry
- * point allocates or frees device memory: the caller owns inputs, outputs and workspace
+ * last failure on the calling thread is available from pf_last_error_string(). No compute
+ * entry point allocates or frees device memory (only the peer-window calls of the Fold-CP
+ * exchange, whose purpose it is): the caller owns inputs, outputs and workspace
  * (size it with the matching *_workspace_size call). All work is enqueued on the stream
  * passed in; no entry point synchronises the host.
  *
@@ -244,6 +245,40 @@ PF_API int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out
                            int64_t head_stride, int64_t row_stride, int64_t n, int64_t q_row0,
                            int64_t n_q, int32_t c_s, int32_t heads, int32_t accumulate, int32_t dtype,
                            void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---- Fold-CP band exchange through peer memory ------------------------------------------
+ * Replace the reference's ring / transpose band exchanges over NCCL send/receive
+ * (opendde/distributed/foldcp/comm.py:26-184, used by real_pairformer.py:1226-1404 and
+ * :2633-2756) for ranks on one NVLink node: each rank publishes its pair tile into a window
+ * exported with a CUDA IPC handle; the peers open the handle once and, after a stream-ordered
+ * barrier, copy the rectangles their bands need straight out of the window.
+ *
+ * pf_peer_window_alloc is the one entry point that allocates device memory (cudaMalloc of
+ * `bytes` on the current device); it writes the window's pointer and its IPC handle
+ * (pf_peer_handle_bytes() bytes) for the peers. pf_peer_window_open maps a peer's handle into
+ * this process (not valid on the process that allocated it); pf_peer_window_close unmaps it;
+ * pf_peer_window_free releases an own window once no peer reads it any more. */
+PF_API size_t pf_peer_handle_bytes(void);
+PF_API int pf_peer_window_alloc(size_t bytes, void** ptr_out, void* handle_out);
+PF_API int pf_peer_window_free(void* ptr);
+PF_API int pf_peer_window_open(const void* handle, void** ptr_out);
+PF_API int pf_peer_window_close(void* ptr);
+
+/* One 2D byte rectangle: rows x row_bytes from src (row pitch src_pitch bytes) to dst (pitch
+ * dst_pitch). src may be a peer's window. */
+typedef struct {
+  const void* src;
+  void* dst;
+  int64_t rows;
+  int64_t row_bytes;
+  int64_t src_pitch;
+  int64_t dst_pitch;
+} pf_copy_region;
+#define PF_MAX_COPY_REGIONS 32
+/* Copies up to PF_MAX_COPY_REGIONS rectangles with one kernel launch on `stream` (16-byte
+ * vectors when every pointer, pitch and row length allows). The caller orders it after the
+ * peers' writes (the barrier) and before anything overwrites the sources. */
+PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_regions, void* stream);
 
 #ifdef __cplusplus
 }

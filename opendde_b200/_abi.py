@@ -45,6 +45,8 @@ EXPORTED = (
     "pf_transition_workspace_size", "pf_transition_fwd",
     "pf_apb_pair_bias_workspace_size", "pf_apb_pair_bias", "pf_apb_workspace_size", "pf_apb_fwd",
     "pf_apb_rows_workspace_size", "pf_apb_rows_fwd",
+    "pf_peer_handle_bytes", "pf_peer_window_alloc", "pf_peer_window_free", "pf_peer_window_open",
+    "pf_peer_window_close", "pf_copy_regions",
 )
 
 
@@ -75,6 +77,14 @@ class TriattParams(Structure):
 
 class TransitionParams(Structure):
     _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w_a", "w_b", "w_o")]
+
+
+class CopyRegion(Structure):
+    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("row_bytes", c_int64),
+                ("src_pitch", c_int64), ("dst_pitch", c_int64)]
+
+
+PF_MAX_COPY_REGIONS = 32
 
 
 class ApbParams(Structure):
@@ -132,6 +142,12 @@ def load(path: str = LIB_PATH):
         "pf_apb_rows_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_apb_rows_fwd": ([POINTER(ApbParams), c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                              c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_peer_handle_bytes": ([], c_size_t),
+        "pf_peer_window_alloc": ([c_size_t, POINTER(c_void_p), c_void_p], c_int),
+        "pf_peer_window_free": ([c_void_p], c_int),
+        "pf_peer_window_open": ([c_void_p, POINTER(c_void_p)], c_int),
+        "pf_peer_window_close": ([c_void_p], c_int),
+        "pf_copy_regions": ([POINTER(CopyRegion), c_int32, c_void_p], c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -142,3 +142,36 @@ def own_col_band(ex, local: torch.Tensor) -> torch.Tensor:
     stacked by mesh row are already that band, so the all-gather output is used as is."""
     t = ex.all_gather(local, "col")                     # [R, Tr, Tc, ...] by mesh row
     return t.reshape((t.shape[0] * t.shape[1],) + tuple(t.shape[2:]))
+
+
+def gather_bands(ex, local: torch.Tensor, spec: FoldCPPairShardSpec, requests) -> List[torch.Tensor]:
+    """The bands of ``requests`` from one state of ``local``, each request one of
+    ("own_rows",), ("own_cols",) (this rank's mesh row / column band), ("rows", rows_of) or
+    ("cols", cols_of). Transports with a ``bands`` method serve them all from one snapshot;
+    otherwise own bands are all-gathers over the row / column group and the others
+    point-to-point regions."""
+    full = (0, spec.n_padded)
+
+    def need_of(req):
+        kind = req[0]
+        if kind == "own_rows":
+            return lambda c: (spec.row_range_of(c[0]), full)
+        if kind == "own_cols":
+            return lambda c: (full, spec.col_range_of(c[1]))
+        if kind == "rows":
+            return lambda c, f=req[1]: (f(c), full)
+        if kind == "cols":
+            return lambda c, f=req[1]: (full, f(c))
+        raise ValueError(f"unknown band request {kind!r}")
+
+    if hasattr(ex, "bands"):
+        return ex.bands(local, spec, [need_of(r) for r in requests])
+    out = []
+    for req in requests:
+        if req[0] == "own_rows":
+            out.append(own_row_band(ex, local))
+        elif req[0] == "own_cols":
+            out.append(own_col_band(ex, local))
+        else:
+            out.append(ex.region(local, spec, need_of(req)))
+    return out

@@ -94,5 +94,8 @@ class FoldCPProcessMesh:
 
 
 def clear_mesh_cache() -> None:
-    """Forget cached meshes (call before ``destroy_process_group``)."""
+    """Release the peer windows (collective) and forget cached meshes (call on every rank
+    before ``destroy_process_group``)."""
+    from .peer import release_windows
+    release_windows()
     _CACHE.clear()

@@ -1,0 +1,183 @@
+"""Peer-memory transport of the Fold-CP band exchange (ranks on one NVLink / NVSwitch node).
+
+Every rank owns one window (a device buffer exported with a CUDA IPC handle, opened once by
+every peer) holding two tile-sized slots. An op that reads bands of the pair plane:
+
+  1. copies this rank's tile into slot k % 2 of its window (a snapshot, local HBM copy);
+  2. passes a barrier: an all-reduce of one element over the CP group, ordered on the stream
+     after the snapshot, so that no rank reads before every snapshot is complete;
+  3. assembles each requested band with one ``pf_copy_regions`` launch that loads the band's
+     rectangles straight out of the peers' windows over NVLink.
+
+One barrier per op is enough because the slots alternate: a rank overwrites slot k % 2 again at
+op k + 2, after the barrier of op k + 1, which no rank passes before it has finished the reads
+of op k (they precede that barrier on its stream). The tile itself is never read by peers, so
+the op may update it in place while peers still copy the snapshot.
+
+This replaces the point-to-point send/receive batches and the packing/unpacking copies of the
+NCCL transport (and the reference's ring exchanges, opendde/distributed/foldcp/comm.py:26-184).
+Select it with ``OPENDDE_B200_FOLDCP_TRANSPORT=peer`` (the default for NCCL meshes) or fall
+back to the NCCL transport with ``=nccl``.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Dict, List, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from ... import _abi, kernels
+from .exchange import DistExchange, Need, Region, intersect, tile_region
+from .pair_sharding import FoldCPPairShardSpec
+
+TRANSPORT_KEY = "OPENDDE_B200_FOLDCP_TRANSPORT"
+
+CopyRegion = Tuple[int, int, int, int, int, int]  # src, dst, rows, row_bytes, src_pitch, dst_pitch
+
+
+def transport_choice(backend: str) -> str:
+    """"peer" or "nccl" for a mesh whose CP group runs on ``backend``."""
+    v = os.environ.get(TRANSPORT_KEY, "").strip().lower()
+    if v not in ("", "peer", "nccl"):
+        raise ValueError(f"{TRANSPORT_KEY} must be 'peer' or 'nccl', got {v!r}")
+    if backend != "nccl":
+        return "dist"
+    return v or "peer"
+
+
+def _slot_bytes(tile_bytes: int) -> int:
+    return (tile_bytes + 255) // 256 * 256
+
+
+def band_copy_plan(spec: FoldCPPairShardSpec, layout, want: Region, slot_ptrs: Sequence[int], out_ptr: int,
+                   pos_bytes: int) -> List[CopyRegion]:
+    """Rectangles that assemble the band ``want`` (rows x columns of the padded plane, stored
+    row-major into ``out_ptr``) from every rank's tile snapshot (``slot_ptrs[q]``: rank q's
+    tile, [Tr, Tc] positions of ``pos_bytes`` bytes, row-major)."""
+    (nr0, nr1), (nc0, nc1) = want
+    out_pitch = (nc1 - nc0) * pos_bytes
+    plan: List[CopyRegion] = []
+    for q in range(layout.numel):
+        (tr0, tr1), (tc0, tc1) = tile_region(spec, layout.to_coord(q))
+        ir, ic = intersect((tr0, tr1), (nr0, nr1)), intersect((tc0, tc1), (nc0, nc1))
+        if ir is None or ic is None:
+            continue
+        src_pitch = (tc1 - tc0) * pos_bytes
+        src = slot_ptrs[q] + (ir[0] - tr0) * src_pitch + (ic[0] - tc0) * pos_bytes
+        dst = out_ptr + (ir[0] - nr0) * out_pitch + (ic[0] - nc0) * pos_bytes
+        plan.append((src, dst, ir[1] - ir[0], (ic[1] - ic[0]) * pos_bytes, src_pitch, out_pitch))
+    return plan
+
+
+class PeerWindows:
+    """This rank's IPC window and the peers' opened windows, for one CP group."""
+
+    def __init__(self, group, cp_rank: int, numel: int, slot_bytes: int, device: torch.device) -> None:
+        lib = _abi.load()
+        self.group, self.cp_rank, self.numel, self.slot_bytes = group, cp_rank, numel, slot_bytes
+        self.device = device
+        hb = int(lib.pf_peer_handle_bytes())
+        own = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(hb)
+        _abi.check(lib.pf_peer_window_alloc(2 * slot_bytes, ctypes.byref(own), handle))
+        self.own = int(own.value)
+        mine = torch.frombuffer(bytearray(handle.raw), dtype=torch.uint8).to(device)
+        every = torch.empty((numel, hb), dtype=torch.uint8, device=device)
+        dist.all_gather_into_tensor(every, mine, group=group)
+        every = every.cpu().numpy()
+        self.bases: List[int] = []
+        self.opened: List[int] = []
+        for q in range(numel):
+            if q == cp_rank:
+                self.bases.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            buf = ctypes.create_string_buffer(every[q].tobytes(), hb)
+            _abi.check(lib.pf_peer_window_open(buf, ctypes.byref(p)))
+            self.bases.append(int(p.value))
+            self.opened.append(int(p.value))
+        self.flag = torch.zeros(1, dtype=torch.int32, device=device)
+        self.slot = 0
+
+    def slot_ptrs(self, slot: int) -> List[int]:
+        return [b + slot * self.slot_bytes for b in self.bases]
+
+    def barrier(self) -> None:
+        """Stream-ordered: work enqueued after it runs once every rank has enqueued and
+        completed the work before its own barrier."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def release(self) -> None:
+        """Unmap the peers' windows and free this rank's (collective: no rank reads after)."""
+        lib = _abi.load()
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        for p in self.opened:
+            _abi.check(lib.pf_peer_window_close(ctypes.c_void_p(p)))
+        self.opened = []
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        _abi.check(lib.pf_peer_window_free(ctypes.c_void_p(self.own)))
+        self.own = 0
+
+
+_WINDOWS: Dict[int, PeerWindows] = {}
+
+
+def windows_for(mesh, tile_bytes: int, device: torch.device) -> PeerWindows:
+    """The mesh's cached windows, grown (collectively) when a larger tile arrives."""
+    need = _slot_bytes(tile_bytes)
+    w = _WINDOWS.get(id(mesh))
+    if w is not None and w.slot_bytes >= need and w.device == device:
+        return w
+    if w is not None:
+        w.release()
+    w = PeerWindows(mesh.group_2d, mesh.cp_rank, mesh.layout.numel, need, device)
+    _WINDOWS[id(mesh)] = w
+    return w
+
+
+def release_windows() -> None:
+    """Free every cached window (collective over each window's group)."""
+    for w in list(_WINDOWS.values()):
+        w.release()
+    _WINDOWS.clear()
+
+
+class PeerExchange(DistExchange):
+    """DistExchange whose band requests are served from the peers' windows; all-gathers
+    (bias planes, single rows) stay NCCL collectives."""
+
+    def __init__(self, mesh, windows_fn=windows_for) -> None:
+        super().__init__(mesh)
+        self._windows_fn = windows_fn
+
+    def bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, needs: Sequence[Need]) -> List[torch.Tensor]:
+        """Every rectangle ``need(coord)`` of ``needs``, from one snapshot of ``local``."""
+        if not local.is_contiguous():
+            raise ValueError("peer exchange publishes contiguous tiles")
+        pos_bytes = local.element_size() * (local[0, 0].numel() if local.dim() > 2 else 1)
+        tile_bytes = local.numel() * local.element_size()
+        w = self._windows_fn(self.mesh, tile_bytes, local.device)
+        slot = w.slot
+        w.slot ^= 1
+        ptrs = w.slot_ptrs(slot)
+        row_bytes = local.shape[1] * pos_bytes
+        kernels.copy_regions([(local.data_ptr(), ptrs[self.mesh.cp_rank], local.shape[0], row_bytes, row_bytes,
+                               row_bytes)])
+        w.barrier()
+        outs, plan = [], []
+        for need in needs:
+            want = need(self.coord)
+            (r0, r1), (c0, c1) = want
+            out = local.new_empty((r1 - r0, c1 - c0) + tuple(local.shape[2:]))
+            plan += band_copy_plan(spec, self.layout, want, ptrs, out.data_ptr(), pos_bytes)
+            outs.append(out)
+        kernels.copy_regions(plan)
+        return outs
+
+    def region(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need) -> torch.Tensor:
+        return self.bands(local, spec, [need])[0]

@@ -35,7 +35,7 @@ from typing import Optional, Tuple
 import torch
 import torch.distributed as dist
 
-from .exchange import DistExchange, col_band, own_col_band, own_row_band, row_band
+from .exchange import DistExchange, gather_bands
 from .layout import FoldCP2DLayout
 from .mesh import FoldCPProcessMesh
 from .ops import KernelOps
@@ -118,11 +118,20 @@ def _full_mask(ex, spec, mask_full: Optional[torch.Tensor], mask_local: Optional
     return out
 
 
+def default_exchange(mesh: FoldCPProcessMesh):
+    """Peer-memory transport on NCCL meshes (unless OPENDDE_B200_FOLDCP_TRANSPORT=nccl), the
+    torch.distributed transport otherwise."""
+    from .peer import PeerExchange, transport_choice
+    if transport_choice(dist.get_backend(mesh.group_2d)) == "peer":
+        return PeerExchange(mesh)
+    return DistExchange(mesh)
+
+
 def make_context(mesh: FoldCPProcessMesh, z_local: torch.Tensor, z_spec: Optional[FoldCPPairShardSpec] = None,
                  mask_local: Optional[torch.Tensor] = None, mask_full: Optional[torch.Tensor] = None,
                  exchange=None) -> FoldCPPairContext:
     """Context over ``mesh`` (or over a given transport ``exchange``)."""
-    ex = exchange if exchange is not None else DistExchange(mesh)
+    ex = exchange if exchange is not None else default_exchange(mesh)
     spec = z_spec if z_spec is not None else _spec_from_local(z_local, ex.layout, ex.coord)
     return FoldCPPairContext(ex, spec, _full_mask(ex, spec, mask_full, mask_local, z_local.device))
 
@@ -174,12 +183,13 @@ def _trimul(module, z_local, ctx: FoldCPPairContext, ops) -> None:
     spec, ex, m = ctx.spec, ctx.exchange, ctx.mask
     (r0, r1), (c0, c1) = ctx.rows, ctx.cols
     if module._outgoing:
-        za = own_row_band(ex, z_local)                         # z rows R_r  [Tr, Np, C]
-        zb = row_band(ex, z_local, spec, _col_of(spec))      # z rows C_c  [Tc, Np, C]
+        # z rows R_r [Tr, Np, C] and z rows C_c [Tc, Np, C]
+        za, zb = gather_bands(ex, z_local, spec, [("own_rows",), ("rows", _col_of(spec))])
         ma, mb = m[r0:r1], m[c0:c1]
     else:
-        za = col_band(ex, z_local, spec, _row_of(spec)).transpose(0, 1)  # z cols R_r, read (i, k) = z(k, i)
-        zb = own_col_band(ex, z_local).transpose(0, 1)       # z cols C_c
+        # z columns R_r and C_c, read transposed: (i, k) = z(k, i)
+        za, zb = gather_bands(ex, z_local, spec, [("cols", _row_of(spec)), ("own_cols",)])
+        za, zb = za.transpose(0, 1), zb.transpose(0, 1)
         ma, mb = m[:, r0:r1].t(), m[:, c0:c1].t()
     ops.trimul(module, za, zb, ma, mb, z_local, z_local)
 
@@ -190,10 +200,11 @@ def _triatt(module, z_local, ctx: FoldCPPairContext, ending: bool, ops) -> None:
     n_pad = ctx.n_pad
     plane = _triatt_bias_plane(module, z_local, ctx, ending, ops)
     if not ending:
-        zs = own_row_band(ex, z_local)                         # rows R_r, keys = all columns
+        zs, = gather_bands(ex, z_local, spec, [("own_rows",)])   # rows R_r, keys = all columns
         ops.triatt(module, zs, m[r0:r1], plane[:, c0:c1, :n_pad], z_local, q_col0=c0, n_q=c1 - c0, n_valid=ctx.n)
     else:
-        zs = own_col_band(ex, z_local).transpose(0, 1)       # x rows C_c, keys = all rows of z
+        zs, = gather_bands(ex, z_local, spec, [("own_cols",)])
+        zs = zs.transpose(0, 1)                                 # x rows C_c, keys = all rows of z
         ops.triatt(module, zs, m[:, c0:c1].t(), plane[:, r0:r1, :n_pad], z_local.transpose(0, 1),
                    q_col0=r0, n_q=r1 - r0, n_valid=ctx.n)
 

@@ -230,3 +230,15 @@ def apb_rows(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, bias: to
     check(_abi.load().pf_apb_rows_fwd(ctypes.byref(pack.struct), s_in.data_ptr(), s_out.data_ptr(),
                                       bias.data_ptr(), bias.stride(0), bias.stride(1), n, q_row0, n_q, c_s,
                                       heads, int(accumulate), code, ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def copy_regions(regions) -> None:
+    """Copy 2D byte rectangles ``(src_ptr, dst_ptr, rows, row_bytes, src_pitch, dst_pitch)``
+    on the current stream, one kernel launch per PF_MAX_COPY_REGIONS rectangles (sources
+    may be peers' windows)."""
+    lib = _abi.load()
+    step = _abi.PF_MAX_COPY_REGIONS
+    for i in range(0, len(regions), step):
+        chunk = regions[i:i + step]
+        arr = (_abi.CopyRegion * len(chunk))(*[_abi.CopyRegion(*r) for r in chunk])
+        check(lib.pf_copy_regions(arr, len(chunk), stream_ptr()))

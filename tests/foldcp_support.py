@@ -5,8 +5,9 @@ restated on the CPU oracle (fp32 torch), with the same semantics, so the exchang
 assembly logic runs on CPU process groups (gloo) and is checked against the serial oracle.
 
 ``ThreadMesh``: R x C ranks emulated as threads of one process sharing one device; its
-transport copies band intersections straight out of the peers' tiles. It runs the real
-drivers (and, on a GPU, the real kernels) for every rank of a mesh on a single device.
+transport copies band intersections straight out of the peers' tiles ("copy"), or, on a GPU,
+runs the peer-memory transport with in-process windows ("peer"). It runs the real drivers (and,
+on a GPU, the real kernels) for every rank of a mesh on a single device.
 """
 
 from __future__ import annotations
@@ -17,9 +18,12 @@ from typing import Callable, Dict, List, Optional, Tuple
 
 import torch
 
+from types import SimpleNamespace
+
 from oracle import pairformer_oracle as O
 from opendde_b200.distributed.foldcp.exchange import copy_intersection, tile_region
 from opendde_b200.distributed.foldcp.layout import FoldCP2DLayout
+from opendde_b200.distributed.foldcp.peer import PeerExchange
 
 
 def _params(module) -> Dict[str, torch.Tensor]:
@@ -131,25 +135,75 @@ class _ThreadExchange:
         return out
 
 
+class _ThreadWindows:
+    """One rank's view of a ThreadMesh's peer windows (device buffers of one process); the
+    barrier synchronises the device and then the threads."""
+
+    def __init__(self, mesh: "ThreadMesh") -> None:
+        self.m = mesh
+        self.slot = 0
+
+    @property
+    def slot_bytes(self) -> int:
+        return self.m.win_bytes
+
+    def slot_ptrs(self, slot: int) -> List[int]:
+        return [b.data_ptr() + slot * self.m.win_bytes for b in self.m.win_bufs]
+
+    def barrier(self) -> None:
+        torch.cuda.synchronize()
+        self.m.wait()
+
+
+class ThreadPeerExchange(PeerExchange):
+    """The peer-memory transport (snapshot, barrier, pf_copy_regions gather) on a ThreadMesh:
+    the windows are buffers of this process, the all-gathers those of _ThreadExchange."""
+
+    def __init__(self, mesh: "ThreadMesh", rank: int) -> None:
+        self._t = _ThreadExchange(mesh, rank)
+        fake = SimpleNamespace(layout=mesh.layout, coord=self._t.coord, cp_rank=rank)
+        super().__init__(fake, windows_fn=lambda _m, nbytes, dev: mesh.peer_windows(rank, nbytes, dev))
+
+    def all_gather(self, t, axis):
+        return self._t.all_gather(t, axis)
+
+
 class ThreadMesh:
     """Run ``fn(exchange, rank)`` for every rank of an R x C mesh as threads."""
 
-    def __init__(self, shape: Tuple[int, int], timeout: float = 300.0) -> None:
+    def __init__(self, shape: Tuple[int, int], timeout: float = 300.0, transport: str = "copy") -> None:
         self.layout = FoldCP2DLayout(shape)
         self.barrier = threading.Barrier(self.layout.numel, timeout=timeout)
         self.slots: List[Optional[torch.Tensor]] = [None] * self.layout.numel
+        self.transport = transport
+        self.lock = threading.Lock()
+        self.win_bytes = 0
+        self.win_bufs: List[torch.Tensor] = []
+        self.win_views = [_ThreadWindows(self) for _ in range(self.layout.numel)]
 
     def wait(self) -> None:
         self.barrier.wait()
+
+    def peer_windows(self, rank: int, nbytes: int, device) -> _ThreadWindows:
+        with self.lock:
+            need = (nbytes + 255) // 256 * 256
+            if self.win_bytes < need:
+                if self.win_bufs:
+                    raise RuntimeError("thread windows cannot grow once in use")
+                self.win_bufs = [torch.empty(2 * need, dtype=torch.uint8, device=device)
+                                 for _ in range(self.layout.numel)]
+                self.win_bytes = need
+        return self.win_views[rank]
 
     def run(self, fn: Callable) -> list:
         n = self.layout.numel
         results: list = [None] * n
         errors: list = []
+        make = ThreadPeerExchange if self.transport == "peer" else _ThreadExchange
 
         def body(rank):
             try:
-                results[rank] = fn(_ThreadExchange(self, rank), rank)
+                results[rank] = fn(make(self, rank), rank)
             except BaseException as e:  # noqa: BLE001 - re-raised below
                 errors.append(e)
                 self.barrier.abort()

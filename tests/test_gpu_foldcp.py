@@ -30,8 +30,8 @@ def _stack(n_blocks, dev, **kw):
     return st.to(dev), p
 
 
-def _cp(shape, stack, s, z, mask):
-    mesh = ThreadMesh(shape)
+def _cp(shape, stack, s, z, mask, transport="copy"):
+    mesh = ThreadMesh(shape, transport=transport)
 
     def rank_fn(ex, rank):
         spec = _spec_for(tuple(z.shape), shape, ex.coord, (0, 1))
@@ -46,8 +46,9 @@ def _cp(shape, stack, s, z, mask):
     return out
 
 
+@pytest.mark.parametrize("transport", ["copy", "peer"])
 @pytest.mark.parametrize("shape", [(1, 2), (2, 2), (2, 4)])
-def test_cp_bf16_matches_single_device(shape, cuda_device):
+def test_cp_bf16_matches_single_device(shape, transport, cuda_device):
     n = 300   # not a multiple of the tiles: exercises padding and partial MMA tiles
     stack, _ = _stack(1, cuda_device)
     g = torch.Generator().manual_seed(1)
@@ -56,15 +57,16 @@ def test_cp_bf16_matches_single_device(shape, cuda_device):
     mask = ragged_pair_mask(n, seed=3, drop=0.2, full_rows=[5]).to(cuda_device)
     with torch.no_grad():
         s1, z1 = stack(s, z, mask)
-    outs = _cp(shape, stack, s, z, mask)
+    outs = _cp(shape, stack, s, z, mask, transport)
     assert _abi.device_status(clear=True) == 0
     for s2, z2 in outs:
         assert rel_l2(z2, z1) <= 5e-3
         assert rel_l2(s2, s1) <= 5e-3
 
 
+@pytest.mark.parametrize("transport", ["copy", "peer"])
 @pytest.mark.parametrize("shape", [(1, 2), (2, 4)])
-def test_cp_fp32_matches_oracle(shape, cuda_device):
+def test_cp_fp32_matches_oracle(shape, transport, cuda_device):
     n = 37
     stack, p = _stack(1, cuda_device, n_heads=16, c_z=128, c_s=384)
     g = torch.Generator().manual_seed(2)
@@ -74,7 +76,33 @@ def test_cp_fp32_matches_oracle(shape, cuda_device):
     torch.set_num_threads(8)
     with torch.no_grad():
         s_ref, z_ref = O.pairformer_stack(s, z, mask, p, 1)
-    outs = _cp(shape, stack, s.to(cuda_device), z.to(cuda_device), mask.to(cuda_device))
+    outs = _cp(shape, stack, s.to(cuda_device), z.to(cuda_device), mask.to(cuda_device), transport)
     for s2, z2 in outs:
         assert max_abs(z2, z_ref) <= 1e-4
         assert max_abs(s2, s_ref) <= 1e-4
+
+
+@pytest.mark.parametrize("unit", [16, 8, 4, 1])
+def test_copy_regions_every_vector_width(unit, cuda_device):
+    """pf_copy_regions moves 2D rectangles at the widest common alignment (16/8/4/1 bytes)."""
+    from opendde_b200 import kernels
+    size = 4 << 20
+    g = torch.Generator().manual_seed(7)
+    src = torch.randint(0, 255, (size,), generator=g, dtype=torch.uint8).to(cuda_device)
+    dst = torch.zeros_like(src)
+    u = unit
+    #        offset  rows  row_bytes  src_pitch  dst_pitch   (odd multiples of u: alignment is u)
+    rects = [(u, 100, 37 * u, 103 * u, 70 * u),
+             (64 * u, 3, 4097 * u, 4099 * u, 4098 * u),
+             (2 * u, 1, 25000 * u, 25000 * u, 25000 * u)]
+    regions, want = [], dst.clone()
+    for i, (off, rows, row_bytes, sp, dp) in enumerate(rects):
+        s_off, d_off = off, off + (1 << 20) * i
+        assert s_off + (rows - 1) * sp + row_bytes <= size      # every access in bounds
+        assert d_off + (rows - 1) * dp + row_bytes <= size
+        regions.append((src.data_ptr() + s_off, dst.data_ptr() + d_off, rows, row_bytes, sp, dp))
+        for r in range(rows):
+            want[d_off + r * dp:d_off + r * dp + row_bytes] = src[s_off + r * sp:s_off + r * sp + row_bytes]
+    kernels.copy_regions(regions)
+    torch.cuda.synchronize()
+    assert torch.equal(dst, want)
