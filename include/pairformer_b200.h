@@ -128,6 +128,26 @@ PF_API int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_vie
                   int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* The same update in two stages, for callers that move the projections between them (the
+ * Fold-CP ring of real_pairformer.py:1226-1404 exchanges a_local / b_local, :1308-1384):
+ * pf_trimul_project: a(ch, r, s) and b(ch, r, s) of one pair view z (with mask m), r < n_rows,
+ *   s < n_cols, stored channel-major at a_out[(ch*n_rows + r)*ld + s] (same for b_out) in the
+ *   storage dtype (fp32 for PF_F32, bf16 for PF_BF16; bf16 needs 16-byte aligned outputs and
+ *   ld a multiple of 8);
+ * pf_trimul_combine: x(i, j) = LN_out(sum_{k<n_k} a(ch, i, k) b(ch, j, k)) from a [c_h][n_i][ld]
+ *   and b [c_h][n_j][ld] in that layout, then zo (+)= (W_z x) * sigmoid(W_g LN_in(zg)). */
+PF_API int pf_trimul_project_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t c_h,
+                                            int32_t dtype, size_t* bytes);
+PF_API int pf_trimul_project(const pf_trimul_params* w, pf_pair_view z, pf_mask_view m, int64_t n_rows,
+                             int64_t n_cols, int32_t c_z, int32_t c_h, int32_t dtype, void* a_out, void* b_out,
+                             int64_t ld, void* workspace, size_t workspace_bytes, void* stream);
+PF_API int pf_trimul_combine_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
+                                            int32_t dtype, size_t* bytes);
+PF_API int pf_trimul_combine(const pf_trimul_params* w, const void* a, const void* b, int64_t ld, int64_t n_i,
+                             int64_t n_j, int64_t n_k, pf_pair_view zg, pf_pair_view zo, int32_t c_z,
+                             int32_t c_h, int32_t accumulate, int32_t dtype, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of pf_trimul_fwd (no counterpart in the reference). For callers
  * that cannot allocate device memory or pass a workspace (a plugin inside a runtime that owns
  * every allocation, a foreign-language binding that only holds its input/output pointers):
@@ -264,20 +284,25 @@ PF_API int pf_peer_window_free(void* ptr);
 PF_API int pf_peer_window_open(const void* handle, void** ptr_out);
 PF_API int pf_peer_window_close(void* ptr);
 
-/* One 2D byte rectangle: rows x row_bytes from src (row pitch src_pitch bytes) to dst (pitch
- * dst_pitch). src may be a peer's window. */
+/* One 3D byte box: planes x rows x row_bytes from src (row pitch src_pitch, plane pitch
+ * src_plane_pitch bytes) to dst (dst_pitch, dst_plane_pitch). src may be a peer's window. A
+ * band of a pair tile is one plane; a band of a channel-major projection has one plane per
+ * channel. */
 typedef struct {
   const void* src;
   void* dst;
+  int64_t planes;
   int64_t rows;
   int64_t row_bytes;
   int64_t src_pitch;
   int64_t dst_pitch;
+  int64_t src_plane_pitch;
+  int64_t dst_plane_pitch;
 } pf_copy_region;
 #define PF_MAX_COPY_REGIONS 32
-/* Copies up to PF_MAX_COPY_REGIONS rectangles with one kernel launch on `stream` (16-byte
- * vectors when every pointer, pitch and row length allows). The caller orders it after the
- * peers' writes (the barrier) and before anything overwrites the sources. */
+/* Copies up to PF_MAX_COPY_REGIONS boxes with one kernel launch on `stream` (16-byte vectors
+ * when every pointer, pitch and row length allows). The caller orders it after the peers'
+ * writes (the barrier) and before anything overwrites the sources. */
 PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_regions, void* stream);
 
 #ifdef __cplusplus

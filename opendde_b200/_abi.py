@@ -40,6 +40,8 @@ EXPORTED = (
     "pf_launch_count", "pf_profile_enable", "pf_profile_report",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
+    "pf_trimul_project_workspace_size", "pf_trimul_project", "pf_trimul_combine_workspace_size",
+    "pf_trimul_combine",
     "pf_static_scratch_bytes", "pf_trimul_fwd_static_scratch",
     "pf_triatt_bias_workspace_size", "pf_triatt_bias", "pf_triatt_workspace_size", "pf_triatt_fwd",
     "pf_transition_workspace_size", "pf_transition_fwd",
@@ -80,8 +82,9 @@ class TransitionParams(Structure):
 
 
 class CopyRegion(Structure):
-    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("rows", c_int64), ("row_bytes", c_int64),
-                ("src_pitch", c_int64), ("dst_pitch", c_int64)]
+    _fields_ = [("src", c_void_p), ("dst", c_void_p), ("planes", c_int64), ("rows", c_int64),
+                ("row_bytes", c_int64), ("src_pitch", c_int64), ("dst_pitch", c_int64),
+                ("src_plane_pitch", c_int64), ("dst_plane_pitch", c_int64)]
 
 
 PF_MAX_COPY_REGIONS = 32
@@ -119,6 +122,13 @@ def load(path: str = LIB_PATH):
         "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
                            c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_trimul_project_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_trimul_project": ([POINTER(TrimulParams), PairView, MaskView, c_int64, c_int64, c_int32, c_int32,
+                               c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_trimul_combine_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_trimul_combine": ([POINTER(TrimulParams), c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                               PairView, PairView, c_int32, c_int32, c_int32, c_int32, c_void_p, c_size_t,
+                               c_void_p], c_int),
         "pf_static_scratch_bytes": ([], c_size_t),
         "pf_trimul_fwd_static_scratch": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView,
                                           PairView, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32,

@@ -130,6 +130,73 @@ int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_view zb, p
                       workspace_bytes, st);
 }
 
+// Split stages of the same computation (Fold-CP exchanges the projections between them).
+int pf_trimul_project_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t c_h, int32_t dtype,
+                                     size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_h <= 0) return fail(PF_EINVAL_SHAPE, "trimul project: bad sizes");
+  *bytes = trimul_tc(n_rows, n_rows, n_cols, c_z, c_h, dtype) ? 0
+                                                             : simt::trimul_project_ws_bytes(n_rows, n_cols, c_z, c_h);
+  return PF_OK;
+}
+
+int pf_trimul_project(const pf_trimul_params* w, pf_pair_view z, pf_mask_view m, int64_t n_rows, int64_t n_cols,
+                      int32_t c_z, int32_t c_h, int32_t dtype, void* a_out, void* b_out, int64_t ld,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_ap || !w->w_ag || !w->w_bp || !w->w_bg) return fail(PF_EINVAL_ARG, "trimul project: null weight");
+  if (!view_ok(z) || !a_out || !b_out) return fail(PF_EINVAL_ARG, "trimul project: bad view or output pointer");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_h <= 0 || c_z > 1024 || c_h > 1024 || ld < n_cols)
+    return fail(PF_EINVAL_SHAPE, "trimul project: bad sizes n_rows=%lld n_cols=%lld ld=%lld c_z=%d c_h=%d",
+                (long long)n_rows, (long long)n_cols, (long long)ld, c_z, c_h);
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_trimul_project_workspace_size(n_rows, n_cols, c_z, c_h, dtype, &need));
+  if (need) PF_TRY(check_ws(workspace, workspace_bytes, need, "trimul project"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (trimul_tc(n_rows, n_rows, n_cols, c_z, c_h, dtype)) {
+    set_path("tc");
+    return tc::trimul_project(w, z, m, n_rows, n_cols, a_out, b_out, ld, st);
+  }
+  set_path("simt");
+  return simt::trimul_project(w, z, m, n_rows, n_cols, c_z, c_h, dtype, a_out, b_out, ld, workspace,
+                              workspace_bytes, st);
+}
+
+int pf_trimul_combine_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
+                                     int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0) return fail(PF_EINVAL_SHAPE, "trimul combine: bad sizes");
+  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::trimul_combine_ws_bytes(n_i, n_j)
+                                                      : simt::trimul_combine_ws_bytes(n_i, n_j, c_z, c_h);
+  return PF_OK;
+}
+
+int pf_trimul_combine(const pf_trimul_params* w, const void* a, const void* b, int64_t ld, int64_t n_i,
+                      int64_t n_j, int64_t n_k, pf_pair_view zg, pf_pair_view zo, int32_t c_z, int32_t c_h,
+                      int32_t accumulate, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_z || !w->w_g) return fail(PF_EINVAL_ARG, "trimul combine: null weight pointer");
+  if (!view_ok(zg) || !view_ok(zo) || !a || !b) return fail(PF_EINVAL_ARG, "trimul combine: bad view or operand");
+  if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0 || c_z > 1024 || c_h > 1024 || ld < n_k)
+    return fail(PF_EINVAL_SHAPE, "trimul combine: bad sizes n_i=%lld n_j=%lld n_k=%lld ld=%lld",
+                (long long)n_i, (long long)n_j, (long long)n_k, (long long)ld);
+  if (n_i == 0 || n_j == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_trimul_combine_workspace_size(n_i, n_j, n_k, c_z, c_h, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "trimul combine"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype)) {
+    set_path("tc");
+    return tc::trimul_combine(w, a, b, ld, n_i, n_j, n_k, zg, zo, accumulate, workspace, workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::trimul_combine(w, a, b, ld, n_i, n_j, n_k, zg, zo, c_z, c_h, accumulate, dtype, workspace,
+                              workspace_bytes, st);
+}
+
 // ------------------------------------------------------------------ triangle attention
 static bool triatt_tc(int c, int H, int d, int dtype) {
   return dtype == PF_BF16 && !force_simt() && tc::triatt_supported(c, H, d);
@@ -287,7 +354,7 @@ int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, in
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   size_t pb = 0;
   PF_TRY(pf_apb_pair_bias_workspace_size(n, n, c_z > 0 ? c_z : 1, heads, dtype, &pb));
-  const size_t att = simt::apb_rows_ws_bytes(n, n, c_s);
+  const size_t att = simt::apb_rows_ws_bytes(n, n, c_s, heads > 0 ? heads : 1);
   *bytes = apb_own_bias_bytes(n, heads) + (pb > att ? pb : att);
   return PF_OK;
 }
@@ -327,8 +394,8 @@ int pf_apb_rows_workspace_size(int64_t n, int64_t n_q, int32_t c_s, int32_t head
                                size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  (void)heads;
-  *bytes = simt::apb_rows_ws_bytes(n, n_q, c_s);
+  if (n < 0 || n_q < 0 || c_s <= 0 || heads <= 0 || c_s % heads) return fail(PF_EINVAL_SHAPE, "apb rows: bad sizes");
+  *bytes = simt::apb_rows_ws_bytes(n, n_q, c_s, heads);
   return PF_OK;
 }
 

@@ -7,9 +7,10 @@
 // (pf_copy_regions), instead of point-to-point send/receive pairs plus packing and unpacking
 // copies on both sides. The loads are plain vectorised global loads; nothing here uses TMA.
 //
-// Regions are 2D byte rectangles (rows x row_bytes with independent source / destination
-// pitches): the intersection of a band with a tile is one such rectangle because a tile row is
-// contiguous over its columns and channels.
+// Regions are byte boxes (planes x rows x row_bytes with independent source / destination
+// pitches): the intersection of a band with a pair tile is one plane because a tile row is
+// contiguous over its columns and channels; a band of a channel-major projection has one plane
+// per channel.
 
 #include <string.h>
 
@@ -19,44 +20,65 @@
 namespace pf {
 namespace {
 
-struct RegionSet {
-  pf_copy_region r[PF_MAX_COPY_REGIONS];
-  int64_t row_start[PF_MAX_COPY_REGIONS + 1];  // prefix sums of rows (work items)
+struct Box {
+  const char* src;
+  char* dst;
+  int64_t src_pitch, dst_pitch, src_plane_pitch, dst_plane_pitch;
+  uint32_t rows;   // rows per plane
+  uint32_t nv;     // vectors per row
+  uint32_t lines;  // planes * rows
+  uint32_t lpi;    // lines per work item
+};
+
+struct BoxSet {
+  Box b[PF_MAX_COPY_REGIONS];
+  int64_t item_start[PF_MAX_COPY_REGIONS + 1];  // prefix sums of work items
   int32_t n;
 };
 
-// One work item = one row of one region; the CTA's threads stride over that row's vectors,
-// each thread keeping kUnroll loads in flight before it stores (peer loads cross NVLink and
-// need many bytes in flight per SM to reach link bandwidth).
+// A work item is a run of consecutive lines (plane-major rows) of one box, about 2048 vectors;
+// the CTA's threads stride over the run's (line, vector) pairs, each thread keeping kUnroll
+// loads in flight before it stores (peer loads cross NVLink and need many bytes in flight per
+// SM to reach link bandwidth).
 template <class V>
-__global__ void __launch_bounds__(256) k_copy_regions(const __grid_constant__ RegionSet rs) {
+__global__ void __launch_bounds__(256) k_copy_regions(const __grid_constant__ BoxSet bs) {
   constexpr int kUnroll = 4;
-  const int64_t items = rs.row_start[rs.n];
+  const int64_t items = bs.item_start[bs.n];
   int reg = 0;
   for (int64_t it = blockIdx.x; it < items; it += gridDim.x) {
-    while (it >= rs.row_start[reg + 1]) ++reg;  // items are visited in increasing order
-    const pf_copy_region& R = rs.r[reg];
-    const int64_t row = it - rs.row_start[reg];
-    const V* __restrict__ src = reinterpret_cast<const V*>((const char*)R.src + row * R.src_pitch);
-    V* __restrict__ dst = reinterpret_cast<V*>((char*)R.dst + row * R.dst_pitch);
-    const int64_t nv = R.row_bytes / (int64_t)sizeof(V);
-    int64_t v = threadIdx.x;
-    for (; v + (kUnroll - 1) * (int64_t)blockDim.x < nv; v += kUnroll * (int64_t)blockDim.x) {
+    while (it >= bs.item_start[reg + 1]) ++reg;  // items are visited in increasing order
+    const Box& B = bs.b[reg];
+    const uint32_t line0 = (uint32_t)(it - bs.item_start[reg]) * B.lpi;
+    const uint32_t nl = min(B.lpi, B.lines - line0);
+    const uint32_t total = nl * B.nv;
+    for (uint32_t base = threadIdx.x; base < total; base += kUnroll * blockDim.x) {
       V t[kUnroll];
+      V* dst[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) t[u] = src[v + u * blockDim.x];
+      for (int u = 0; u < kUnroll; ++u) {
+        const uint32_t e = base + u * blockDim.x;
+        dst[u] = nullptr;
+        if (e < total) {
+          const uint32_t l = e / B.nv, v = e - l * B.nv;
+          const uint32_t line = line0 + l;
+          const uint32_t plane = line / B.rows, row = line - plane * B.rows;
+          const V* src = reinterpret_cast<const V*>(B.src + plane * B.src_plane_pitch + row * B.src_pitch) + v;
+          dst[u] = reinterpret_cast<V*>(B.dst + plane * B.dst_plane_pitch + row * B.dst_pitch) + v;
+          t[u] = *src;
+        }
+      }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) dst[v + u * blockDim.x] = t[u];
+      for (int u = 0; u < kUnroll; ++u)
+        if (dst[u]) *dst[u] = t[u];
     }
-    for (; v < nv; v += blockDim.x) dst[v] = src[v];
   }
 }
 
 int widest_unit(const pf_copy_region* r, int n) {
   uintptr_t acc = 0;
   for (int i = 0; i < n; ++i)
-    acc |= (uintptr_t)r[i].src | (uintptr_t)r[i].dst | (uintptr_t)r[i].row_bytes |
-           (uintptr_t)r[i].src_pitch | (uintptr_t)r[i].dst_pitch;
+    acc |= (uintptr_t)r[i].src | (uintptr_t)r[i].dst | (uintptr_t)r[i].row_bytes | (uintptr_t)r[i].src_pitch |
+           (uintptr_t)r[i].dst_pitch | (uintptr_t)r[i].src_plane_pitch | (uintptr_t)r[i].dst_plane_pitch;
   if ((acc & 15) == 0) return 16;
   if ((acc & 7) == 0) return 8;
   if ((acc & 3) == 0) return 4;
@@ -110,36 +132,57 @@ extern "C" PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_r
   if (n_regions < 0 || n_regions > PF_MAX_COPY_REGIONS)
     return fail(PF_EINVAL_ARG, "n_regions %d outside [0, %d]", n_regions, PF_MAX_COPY_REGIONS);
   if (n_regions > 0 && regions == nullptr) return fail(PF_EINVAL_ARG, "null region list");
-  RegionSet rs;
-  memset(&rs, 0, sizeof(rs));
+  pf_copy_region live[PF_MAX_COPY_REGIONS];
   int n = 0;
-  rs.row_start[0] = 0;
   for (int i = 0; i < n_regions; ++i) {
     const pf_copy_region& r = regions[i];
-    if (r.rows < 0 || r.row_bytes < 0) return fail(PF_EINVAL_SHAPE, "region %d: negative size", i);
-    if (r.rows == 0 || r.row_bytes == 0) continue;
+    if (r.planes < 0 || r.rows < 0 || r.row_bytes < 0) return fail(PF_EINVAL_SHAPE, "region %d: negative size", i);
+    if (r.planes == 0 || r.rows == 0 || r.row_bytes == 0) continue;
     if (r.src == nullptr || r.dst == nullptr) return fail(PF_EINVAL_ARG, "region %d: null pointer", i);
     if (r.rows > 1 && (r.src_pitch < r.row_bytes || r.dst_pitch < r.row_bytes))
-      return fail(PF_EINVAL_SHAPE, "region %d: pitch smaller than the row", i);
-    rs.r[n] = r;
-    rs.row_start[n + 1] = rs.row_start[n] + r.rows;
-    ++n;
+      return fail(PF_EINVAL_SHAPE, "region %d: row pitch smaller than the row", i);
+    if (r.planes > 1 && (r.src_plane_pitch < r.rows * r.src_pitch || r.dst_plane_pitch < r.rows * r.dst_pitch))
+      return fail(PF_EINVAL_SHAPE, "region %d: plane pitch smaller than the plane", i);
+    if (r.planes * r.rows >= (1ll << 31)) return fail(PF_EINVAL_SHAPE, "region %d: more than 2^31 rows", i);
+    live[n++] = r;
   }
-  rs.n = n;
   if (n == 0) return PF_OK;
-  for (int i = n + 1; i <= PF_MAX_COPY_REGIONS; ++i) rs.row_start[i] = rs.row_start[n];
+  const int unit = widest_unit(live, n);
+  BoxSet bs;
+  memset(&bs, 0, sizeof(bs));
+  bs.n = n;
+  bs.item_start[0] = 0;
+  for (int i = 0; i < n; ++i) {
+    const pf_copy_region& r = live[i];
+    const int64_t nv = r.row_bytes / unit;
+    if (nv >= (1ll << 31)) return fail(PF_EINVAL_SHAPE, "region %d: row of 2^31 vectors or more", i);
+    Box& B = bs.b[i];
+    B.src = (const char*)r.src;
+    B.dst = (char*)r.dst;
+    B.src_pitch = r.src_pitch;
+    B.dst_pitch = r.dst_pitch;
+    B.src_plane_pitch = r.src_plane_pitch;
+    B.dst_plane_pitch = r.dst_plane_pitch;
+    B.rows = (uint32_t)r.rows;
+    B.nv = (uint32_t)nv;
+    B.lines = (uint32_t)(r.planes * r.rows);
+    B.lpi = (uint32_t)(nv >= 2048 ? 1 : (2048 + nv - 1) / nv);
+    if ((uint64_t)B.lpi * B.nv >= (1ull << 31)) return fail(PF_EINVAL_SHAPE, "region %d: work item too large", i);
+    bs.item_start[i + 1] = bs.item_start[i] + (B.lines + B.lpi - 1) / B.lpi;
+  }
+  for (int i = n + 1; i <= PF_MAX_COPY_REGIONS; ++i) bs.item_start[i] = bs.item_start[n];
   int dev = 0, sms = 0;
   PF_CUDA_TRY(cudaGetDevice(&dev));
   PF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const int64_t items = rs.row_start[n];
+  const int64_t items = bs.item_start[n];
   const int grid = (int)(items < (int64_t)sms * 4 ? items : (int64_t)sms * 4);
   cudaStream_t st = (cudaStream_t)stream;
   PF_LAUNCH_SCOPE(st, "k_copy_regions");
-  switch (widest_unit(rs.r, n)) {
-    case 16: k_copy_regions<uint4><<<grid, 256, 0, st>>>(rs); break;
-    case 8: k_copy_regions<uint2><<<grid, 256, 0, st>>>(rs); break;
-    case 4: k_copy_regions<uint32_t><<<grid, 256, 0, st>>>(rs); break;
-    default: k_copy_regions<unsigned char><<<grid, 256, 0, st>>>(rs); break;
+  switch (unit) {
+    case 16: k_copy_regions<uint4><<<grid, 256, 0, st>>>(bs); break;
+    case 8: k_copy_regions<uint2><<<grid, 256, 0, st>>>(bs); break;
+    case 4: k_copy_regions<uint32_t><<<grid, 256, 0, st>>>(bs); break;
+    default: k_copy_regions<unsigned char><<<grid, 256, 0, st>>>(bs); break;
   }
   PF_CHECK_LAUNCH();
   return PF_OK;

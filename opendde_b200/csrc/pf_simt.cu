@@ -138,10 +138,12 @@ __global__ void __launch_bounds__(256) k_gemm_nt(const TA* __restrict__ A, int64
   }
 }
 
-// a(ch, r, k) = m(r, k) * sigmoid(pg[p, ch]) * pa[p, ch],  p = r*n_k + k  (channel-major out)
+// a(ch, r, k) = m(r, k) * sigmoid(pg[p, ch]) * pa[p, ch],  p = r*n_k + k  (channel-major out,
+// element (ch, r, k) at out[(ch * n_r + r) * ld + k])
+template <class TO>
 __global__ void k_gate_to_cmajor(const float* __restrict__ pa, const float* __restrict__ pg,
                                  pf_mask_view m, int64_t n_r, int64_t n_k, int c_h,
-                                 float* __restrict__ out) {
+                                 TO* __restrict__ out, int64_t ld) {
   const int64_t P = n_r * n_k;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= P * c_h) return;
@@ -150,7 +152,7 @@ __global__ void k_gate_to_cmajor(const float* __restrict__ pa, const float* __re
   const float mv = m.ptr ? m.ptr[r * m.row_stride + k * m.col_stride] : 1.0f;
   // reference order: a = mask; a = a * sigmoid(g); a = a * p   (triangular.py:539-541)
   float v = mv * sigmoid_acc(pg[p * c_h + ch]);
-  out[idx] = v * pa[p * c_h + ch];
+  out[(ch * n_r + r) * ld + k] = from_f<TO>(v * pa[p * c_h + ch]);
 }
 
 // x[p, ch] = LN_out over ch of p_cm[ch, p]   (channel-major input, one warp per position)
@@ -303,6 +305,107 @@ __global__ void __launch_bounds__(64) k_attn_simt(
   for (int e = 0; e < D; ++e) op[e] = acc[e] * inv;
 }
 
+// Single-representation attention of AttentionPairBias split over the keys: a CTA handles 64
+// queries x one head x one key range and writes its unnormalised partial (acc[D], running max,
+// running sum) to part[((split * H + h) * n_q + j) * (D + 2)]; k_attn_merge combines the
+// splits. With N queries x 16 heads there are too few (query block, head) pairs to fill the
+// GPU (and fewer still per Fold-CP rank), so the keys supply the parallelism.
+template <int D>
+__global__ void __launch_bounds__(64) k_attn_split(const float* __restrict__ q, int64_t q_ps,
+                                                   const float* __restrict__ k, const float* __restrict__ v,
+                                                   int64_t kv_ps, const float* __restrict__ bias, int64_t b_hs,
+                                                   int64_t b_rs, int64_t n_q, int64_t n_keys, int64_t per_split,
+                                                   float inv_sqrt_d_div, int H, float* __restrict__ part) {
+  __shared__ float Ks[64][D + 1];
+  __shared__ float Vs[64][D + 1];
+  const int h = blockIdx.y;
+  const int64_t sp = blockIdx.z;
+  const int64_t j = (int64_t)blockIdx.x * 64 + threadIdx.x;
+  const bool active = j < n_q;
+  float qv[D];
+  const float* qp = q + (active ? j : 0) * q_ps + h * D;
+#pragma unroll
+  for (int t = 0; t < D; ++t) qv[t] = qp[t] / inv_sqrt_d_div;  // reference divides q by sqrt(d)
+  float mrun = -INFINITY, l = 0.f;
+  float acc[D];
+#pragma unroll
+  for (int t = 0; t < D; ++t) acc[t] = 0.f;
+  const int64_t kb0 = sp * per_split;
+  const int64_t kb1 = kb0 + per_split < n_keys ? kb0 + per_split : n_keys;
+  const float* kb = k + h * D;
+  const float* vb = v + h * D;
+  for (int64_t k0 = kb0; k0 < kb1; k0 += 64) {
+    __syncthreads();
+    {
+      const int64_t kk = k0 + threadIdx.x;
+      if (kk < kb1) {
+#pragma unroll
+        for (int t = 0; t < D; ++t) {
+          Ks[threadIdx.x][t] = kb[kk * kv_ps + t];
+          Vs[threadIdx.x][t] = vb[kk * kv_ps + t];
+        }
+      }
+    }
+    __syncthreads();
+    if (!active) continue;
+    const int64_t rem = kb1 - k0;
+    const int nk = rem < 64 ? (int)rem : 64;
+    const float* brow = bias + (int64_t)h * b_hs + j * b_rs + k0;
+    for (int t = 0; t < nk; ++t) {
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < D; ++e) s = fmaf(qv[e], Ks[t][e], s);
+      s = s + brow[t];
+      if (s > mrun) {
+        const float corr = expf(mrun - s);  // exp(-inf) = 0 on the first key
+        l *= corr;
+#pragma unroll
+        for (int e = 0; e < D; ++e) acc[e] *= corr;
+        mrun = s;
+      }
+      const float pexp = expf(s - mrun);
+      l += pexp;
+#pragma unroll
+      for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[t][e], acc[e]);
+    }
+  }
+  if (!active) return;
+  float* out = part + ((sp * H + h) * n_q + j) * (D + 2);
+#pragma unroll
+  for (int e = 0; e < D; ++e) out[e] = acc[e];
+  out[D] = mrun;
+  out[D + 1] = l;
+}
+
+// o(j, h*D + e) = sum_s acc_s[e] exp(m_s - M) / sum_s l_s exp(m_s - M),  M = max_s m_s.
+template <int D>
+__global__ void k_attn_merge(const float* __restrict__ part, int splits, int H, int64_t n_q,
+                             float* __restrict__ o, int64_t o_ps) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_q * H) return;
+  const int64_t j = idx / H;
+  const int h = (int)(idx - j * H);
+  float M = -INFINITY;
+  for (int sp = 0; sp < splits; ++sp) M = fmaxf(M, part[(((int64_t)sp * H + h) * n_q + j) * (D + 2) + D]);
+  float acc[D];
+#pragma unroll
+  for (int e = 0; e < D; ++e) acc[e] = 0.f;
+  float L = 0.f;
+  if (M > -INFINITY) {
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* pp = part + (((int64_t)sp * H + h) * n_q + j) * (D + 2);
+      const float w = expf(pp[D] - M);  // an empty split has m = -inf: weight 0
+      L = fmaf(pp[D + 1], w, L);
+#pragma unroll
+      for (int e = 0; e < D; ++e) acc[e] = fmaf(pp[e], w, acc[e]);
+    }
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  float* op = o + j * o_ps + h * D;
+#pragma unroll
+  for (int e = 0; e < D; ++e) op[e] = acc[e] * inv;
+}
+
 // ============================================================================ host side
 
 static inline unsigned nblk(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
@@ -349,19 +452,22 @@ int layernorm(const void* x, void* y, const float* g, const float* b, int64_t ro
 }
 
 // ---------------------------------------------------------------- triangle multiplication
-struct TrimulWs {
-  float *xa, *xb, *pa, *pg, *a, *b, *p, *xn, *y, *xo, *gg;
+// Stages: project (LN_in, the gated projection of one side into channel-major a/b) and
+// combine (the per-channel contraction, LN_out, W_z, the gate from zg, the residual). The
+// fused entry point runs project twice and combine once on fp32 intermediates; the split
+// entry points (Fold-CP exchanges the projections) keep a/b in the storage dtype.
+struct ProjWs {
+  float *x, *pa, *pg;
 };
-static void trimul_plan(Arena& ar, int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h,
-                        TrimulWs& w) {
-  int64_t Pa = n_i * n_k, Pb = n_j * n_k, Po = n_i * n_j;
-  int64_t Pm = Pa > Pb ? Pa : Pb;
-  w.xa = ar.take<float>(Pa * c_z);
-  w.xb = ar.take<float>(Pb * c_z);
-  w.pa = ar.take<float>(Pm * c_h);
-  w.pg = ar.take<float>(Pm * c_h);
-  w.a = ar.take<float>(Pa * c_h);
-  w.b = ar.take<float>(Pb * c_h);
+static void proj_plan(Arena& ar, int64_t P, int c_z, int c_h, ProjWs& w) {
+  w.x = ar.take<float>(P * c_z);
+  w.pa = ar.take<float>(P * c_h);
+  w.pg = ar.take<float>(P * c_h);
+}
+struct CombineWs {
+  float *p, *xn, *y, *xo, *gg;
+};
+static void combine_plan(Arena& ar, int64_t Po, int c_z, int c_h, CombineWs& w) {
   w.p = ar.take<float>(Po * c_h);
   w.xn = ar.take<float>(Po * c_h);
   w.y = ar.take<float>(Po * c_z);
@@ -369,47 +475,33 @@ static void trimul_plan(Arena& ar, int64_t n_i, int64_t n_j, int64_t n_k, int c_
   w.gg = ar.take<float>(Po * c_z);
 }
 
-size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h) {
-  Arena ar(nullptr, 0);
-  TrimulWs w;
-  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
-  return ar.used;
+template <class T, class TO>
+static int project_side(const pf_trimul_params* p, pf_pair_view z, pf_mask_view m, int64_t n_r, int64_t n_k,
+                        int c_z, int c_h, const T* W_p, const T* W_g, TO* out, int64_t ld, const ProjWs& w,
+                        cudaStream_t st) {
+  const float eps = 1e-5f;
+  const int64_t P = n_r * n_k;
+  PF_TRY((ln_view<T, float>((const T*)z.ptr, z.row_stride, z.col_stride, n_r, n_k, c_z, p->ln_in_w,
+                            p->ln_in_b, eps, w.x, c_z, st)));
+  PF_TRY((gemm<float, T>(w.x, 0, c_z, W_p, 0, c_z, w.pa, 0, c_h, 1, 1, P, c_h, c_z, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(w.x, 0, c_z, W_g, 0, c_z, w.pg, 0, c_h, 1, 1, P, c_h, c_z, 1.f, 0, st)));
+  {
+    PF_LAUNCH_SCOPE(st, "k_gate_to_cmajor");
+    k_gate_to_cmajor<TO><<<nblk(P * c_h, 256), 256, 0, st>>>(w.pa, w.pg, m, n_r, n_k, c_h, out, ld);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
 }
 
-template <class T>
-static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
-                    pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
-                    int c_z, int c_h, int acc, Arena& ar, cudaStream_t st) {
-  TrimulWs w;
-  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
-  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small (%zu < %zu)", ar.cap, ar.used);
+template <class T, class TA>
+static int combine(const pf_trimul_params* p, const TA* a, int64_t lda, const TA* b, int64_t ldb, int64_t n_i,
+                   int64_t n_j, int64_t n_k, pf_pair_view zg, pf_pair_view zo, int c_z, int c_h, int acc,
+                   const CombineWs& w, cudaStream_t st) {
   const float eps = 1e-5f;
-  int64_t Pa = n_i * n_k, Pb = n_j * n_k, Po = n_i * n_j;
-  const T* W_ap = (const T*)p->w_ap; const T* W_ag = (const T*)p->w_ag;
-  const T* W_bp = (const T*)p->w_bp; const T* W_bg = (const T*)p->w_bg;
-  // a
-  PF_TRY((ln_view<T, float>((const T*)za.ptr, za.row_stride, za.col_stride, n_i, n_k, c_z,
-                            p->ln_in_w, p->ln_in_b, eps, w.xa, c_z, st)));
-  PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ap, 0, c_z, w.pa, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
-  PF_TRY((gemm<float, T>(w.xa, 0, c_z, W_ag, 0, c_z, w.pg, 0, c_h, 1, 1, Pa, c_h, c_z, 1.f, 0, st)));
-  {
-    PF_LAUNCH_SCOPE(st, "k_gate_to_cmajor");
-    k_gate_to_cmajor<<<nblk(Pa * c_h, 256), 256, 0, st>>>(w.pa, w.pg, ma, n_i, n_k, c_h, w.a);
-  }
-  PF_CHECK_LAUNCH();
-  // b
-  PF_TRY((ln_view<T, float>((const T*)zb.ptr, zb.row_stride, zb.col_stride, n_j, n_k, c_z,
-                            p->ln_in_w, p->ln_in_b, eps, w.xb, c_z, st)));
-  PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bp, 0, c_z, w.pa, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
-  PF_TRY((gemm<float, T>(w.xb, 0, c_z, W_bg, 0, c_z, w.pg, 0, c_h, 1, 1, Pb, c_h, c_z, 1.f, 0, st)));
-  {
-    PF_LAUNCH_SCOPE(st, "k_gate_to_cmajor");
-    k_gate_to_cmajor<<<nblk(Pb * c_h, 256), 256, 0, st>>>(w.pa, w.pg, mb, n_j, n_k, c_h, w.b);
-  }
-  PF_CHECK_LAUNCH();
+  const int64_t Po = n_i * n_j;
   // x[ch] = a[ch] b[ch]^T  (batched over channels)
-  PF_TRY((gemm<float, float>(w.a, Pa, n_k, w.b, Pb, n_k, w.p, Po, n_j, 1, c_h, n_i, n_j, n_k,
-                             1.f, 0, st)));
+  PF_TRY((gemm<TA, TA>(a, n_i * lda, lda, b, n_j * ldb, ldb, w.p, Po, n_j, 1, c_h, n_i, n_j, n_k, 1.f, 0,
+                       st)));
   // LN_out, linear_z
   {
     PF_LAUNCH_SCOPE(st, "k_ln_cmajor");
@@ -432,6 +524,41 @@ static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb,
   return PF_OK;
 }
 
+struct TrimulWs {
+  ProjWs pr;
+  float *a, *b;
+  CombineWs cb;
+};
+static void trimul_plan(Arena& ar, int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h,
+                        TrimulWs& w) {
+  int64_t Pa = n_i * n_k, Pb = n_j * n_k, Po = n_i * n_j;
+  proj_plan(ar, Pa > Pb ? Pa : Pb, c_z, c_h, w.pr);
+  w.a = ar.take<float>(Pa * c_h);
+  w.b = ar.take<float>(Pb * c_h);
+  combine_plan(ar, Po, c_z, c_h, w.cb);
+}
+
+size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h) {
+  Arena ar(nullptr, 0);
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
+  return ar.used;
+}
+
+template <class T>
+static int trimul_t(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+                    pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+                    int c_z, int c_h, int acc, Arena& ar, cudaStream_t st) {
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, c_z, c_h, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small (%zu < %zu)", ar.cap, ar.used);
+  PF_TRY((project_side<T, float>(p, za, ma, n_i, n_k, c_z, c_h, (const T*)p->w_ap, (const T*)p->w_ag, w.a, n_k,
+                                 w.pr, st)));
+  PF_TRY((project_side<T, float>(p, zb, mb, n_j, n_k, c_z, c_h, (const T*)p->w_bp, (const T*)p->w_bg, w.b, n_k,
+                                 w.pr, st)));
+  return combine<T, float>(p, w.a, n_k, w.b, n_k, n_i, n_j, n_k, zg, zo, c_z, c_h, acc, w.cb, st);
+}
+
 int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
            pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
            int c_h, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
@@ -439,6 +566,54 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   if (dtype == PF_F32)
     return trimul_t<float>(p, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, acc, ar, st);
   return trimul_t<__nv_bfloat16>(p, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, acc, ar, st);
+}
+
+size_t trimul_project_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int c_h) {
+  Arena ar(nullptr, 0);
+  ProjWs w;
+  proj_plan(ar, n_rows * n_cols, c_z, c_h, w);
+  return ar.used;
+}
+
+int trimul_project(const pf_trimul_params* p, pf_pair_view z, pf_mask_view m, int64_t n_rows, int64_t n_cols,
+                   int c_z, int c_h, int dtype, void* a, void* b, int64_t ld, void* ws, size_t ws_bytes,
+                   cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  ProjWs w;
+  proj_plan(ar, n_rows * n_cols, c_z, c_h, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul project workspace too small (%zu < %zu)", ar.cap, ar.used);
+  if (dtype == PF_F32) {
+    PF_TRY((project_side<float, float>(p, z, m, n_rows, n_cols, c_z, c_h, (const float*)p->w_ap,
+                                       (const float*)p->w_ag, (float*)a, ld, w, st)));
+    return project_side<float, float>(p, z, m, n_rows, n_cols, c_z, c_h, (const float*)p->w_bp,
+                                      (const float*)p->w_bg, (float*)b, ld, w, st);
+  }
+  using B = __nv_bfloat16;
+  PF_TRY((project_side<B, B>(p, z, m, n_rows, n_cols, c_z, c_h, (const B*)p->w_ap, (const B*)p->w_ag, (B*)a,
+                             ld, w, st)));
+  return project_side<B, B>(p, z, m, n_rows, n_cols, c_z, c_h, (const B*)p->w_bp, (const B*)p->w_bg, (B*)b,
+                            ld, w, st);
+}
+
+size_t trimul_combine_ws_bytes(int64_t n_i, int64_t n_j, int c_z, int c_h) {
+  Arena ar(nullptr, 0);
+  CombineWs w;
+  combine_plan(ar, n_i * n_j, c_z, c_h, w);
+  return ar.used;
+}
+
+int trimul_combine(const pf_trimul_params* p, const void* a, const void* b, int64_t ld, int64_t n_i, int64_t n_j,
+                   int64_t n_k, pf_pair_view zg, pf_pair_view zo, int c_z, int c_h, int acc, int dtype, void* ws,
+                   size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  CombineWs w;
+  combine_plan(ar, n_i * n_j, c_z, c_h, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul combine workspace too small (%zu < %zu)", ar.cap, ar.used);
+  if (dtype == PF_F32)
+    return combine<float, float>(p, (const float*)a, ld, (const float*)b, ld, n_i, n_j, n_k, zg, zo, c_z, c_h,
+                                 acc, w, st);
+  using B = __nv_bfloat16;
+  return combine<B, B>(p, (const B*)a, ld, (const B*)b, ld, n_i, n_j, n_k, zg, zo, c_z, c_h, acc, w, st);
 }
 
 // ---------------------------------------------------------------- triangle attention
@@ -495,6 +670,59 @@ static int launch_attn(int d, const float* q, int64_t q_rs, int64_t q_ps, int64_
 #undef PF_ATTN_CASE
   PF_CHECK_LAUNCH();
   return PF_OK;
+}
+
+// Key splits of the APB single attention: enough CTAs (query blocks x heads x splits) for about
+// eight 64-thread CTAs per SM of a 148-SM part, each split at least one 64-key tile.
+static int64_t apb_splits(int64_t n, int64_t nq, int H) {
+  const int64_t pairs = (int64_t)nblk(nq, 64) * H;
+  int64_t s = (1184 + pairs - 1) / (pairs > 0 ? pairs : 1);
+  const int64_t tiles = (n + 63) / 64;
+  if (s > tiles) s = tiles;
+  return s < 1 ? 1 : s;
+}
+
+static int launch_attn_split(int d, const float* q, int64_t q_ps, const float* k, const float* v, int64_t kv_ps,
+                             const float* bias, int64_t b_hs, int64_t b_rs, int64_t n_q, int64_t n, int H,
+                             float* part, float* o, int64_t o_ps, cudaStream_t st) {
+  if (n_q == 0) return PF_OK;
+  const int64_t splits = apb_splits(n, n_q, H);
+  int64_t per = ((n + splits - 1) / splits + 63) / 64 * 64;
+  if (per < 64) per = 64;
+  const int64_t used = n > 0 ? (n + per - 1) / per : 1;
+  if (used > 65535) return fail(PF_EUNSUPPORTED, "too many key splits (%lld)", (long long)used);
+  dim3 grid(nblk(n_q, 64), H, (unsigned)used);
+  const float sd = sqrtf((float)d);
+  const unsigned mgrid = nblk(n_q * H, 128);
+#define PF_SPLIT_CASE(DD)                                                                          \
+  case DD: {                                                                                       \
+    {                                                                                              \
+      PF_LAUNCH_SCOPE(st, "k_attn_split");                                                         \
+      k_attn_split<DD><<<grid, 64, 0, st>>>(q, q_ps, k, v, kv_ps, bias, b_hs, b_rs, n_q, n, per,   \
+                                            sd, H, part);                                          \
+    }                                                                                              \
+    PF_CHECK_LAUNCH();                                                                             \
+    PF_LAUNCH_SCOPE(st, "k_attn_merge");                                                           \
+    k_attn_merge<DD><<<mgrid, 128, 0, st>>>(part, (int)used, H, n_q, o, o_ps);                     \
+    break;                                                                                         \
+  }
+  switch (d) {
+    PF_SPLIT_CASE(8)
+    PF_SPLIT_CASE(16)
+    PF_SPLIT_CASE(24)
+    PF_SPLIT_CASE(32)
+    PF_SPLIT_CASE(48)
+    PF_SPLIT_CASE(64)
+    default:
+      return fail(PF_EUNSUPPORTED, "head dim %d not in {8,16,24,32,48,64}", d);
+  }
+#undef PF_SPLIT_CASE
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+static size_t apb_part_floats(int64_t n, int64_t nq, int c_s, int H) {
+  return (size_t)apb_splits(n, nq, H) * nq * (c_s + 2 * H);  // splits x nq x H x (d + 2)
 }
 
 template <class T>
@@ -702,6 +930,7 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   float* qg = ar.take<float>(nq * c_s * 2);
   float* o = ar.take<float>(nq * c_s);
   float* y = ar.take<float>(nq * c_s);
+  float* part = ar.take<float>(apb_part_floats(n, nq, c_s, H));
   if (!ar.ok()) return fail(PF_EWORKSPACE, "apb workspace too small");
   float *k = kv, *v = kv + n * c_s, *q = qg, *g = qg + nq * c_s;
   const float* aq = a + q0 * c_s;
@@ -718,10 +947,8 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_k, 0, c_s, k, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(a, 0, c_s, (const T*)p->w_v, 0, c_s, v, 0, c_s, 1, 1, n, c_s, c_s, 1.f, 0, st)));
   PF_TRY((gemm<float, T>(aq, 0, c_s, (const T*)p->w_g, 0, c_s, g, 0, c_s, 1, 1, nq, c_s, c_s, 1.f, 0, st)));
-  pf_mask_view nomask{nullptr, 0, 0};
-  // one "row" (i = 0) of nq queries over n keys; bias(h, j, k) = bias[h*b_hs + j*b_rs + k]
-  PF_TRY((launch_attn<T, float>(d, q, 0, c_s, 0, k, v, 0, c_s, bias, b_hs, b_rs, 1.0f, nomask, 0.f,
-                                1, nq, H, n, o, 0, c_s, st)));
+  // nq queries over n keys; bias(h, j, k) = bias[h*b_hs + j*b_rs + k]
+  PF_TRY(launch_attn_split(d, q, c_s, k, v, c_s, bias, b_hs, b_rs, nq, n, H, part, o, c_s, st));
   {
     PF_LAUNCH_SCOPE(st, "k_gate_inplace");
     k_gate_inplace<<<nblk(nq * c_s, 256), 256, 0, st>>>(o, g, nq * c_s);
@@ -736,13 +963,14 @@ static int apb_t(const pf_apb_params* p, const T* s_in, T* s_out, const float* b
   return PF_OK;
 }
 
-size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s) {
+size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s, int H) {
   Arena ar(nullptr, 0);
   ar.take<float>(n * c_s);
   ar.take<float>(n * c_s * 2);
   ar.take<float>(nq * c_s * 2);
   ar.take<float>(nq * c_s);
   ar.take<float>(nq * c_s);
+  ar.take<float>(apb_part_floats(n, nq, c_s, H));
   return ar.used + 1024;
 }
 

@@ -13,6 +13,14 @@ size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
 int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
            pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
            int c_h, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t trimul_project_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int c_h);
+int trimul_project(const pf_trimul_params* p, pf_pair_view z, pf_mask_view m, int64_t n_rows, int64_t n_cols,
+                   int c_z, int c_h, int dtype, void* a, void* b, int64_t ld, void* ws, size_t ws_bytes,
+                   cudaStream_t st);
+size_t trimul_combine_ws_bytes(int64_t n_i, int64_t n_j, int c_z, int c_h);
+int trimul_combine(const pf_trimul_params* p, const void* a, const void* b, int64_t ld, int64_t n_i, int64_t n_j,
+                   int64_t n_k, pf_pair_view zg, pf_pair_view zo, int c_z, int c_h, int acc, int dtype, void* ws,
+                   size_t ws_bytes, cudaStream_t st);
 
 size_t triatt_ws_bytes(int64_t n_rows, int64_t n_keys, int64_t n_q, int c, int H, int d);
 int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const void* bias,
@@ -33,7 +41,7 @@ size_t apb_pair_bias_ws_bytes(int64_t P, int c_z, int H);
 int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
                   float* bias, int64_t hs, int64_t rs, int c_z, int H, int dtype, void* ws,
                   size_t ws_bytes, cudaStream_t st);
-size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s);
+size_t apb_rows_ws_bytes(int64_t n, int64_t nq, int c_s, int H);
 int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float* bias, int64_t b_hs,
              int64_t b_rs, int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, int dtype, void* ws,
              size_t ws_bytes, cudaStream_t st);

@@ -16,6 +16,12 @@ size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
 int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
            pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k, int c_z,
            int c_h, int acc, void* ws, size_t ws_bytes, cudaStream_t st);
+int trimul_project(const pf_trimul_params* p, pf_pair_view z, pf_mask_view m, int64_t n_rows,
+                   int64_t n_cols, void* a, void* b, int64_t ld, cudaStream_t st);
+size_t trimul_combine_ws_bytes(int64_t n_i, int64_t n_j);
+int trimul_combine(const pf_trimul_params* p, const void* a, const void* b, int64_t ld, int64_t n_i,
+                   int64_t n_j, int64_t n_k, pf_pair_view zg, pf_pair_view zo, int acc, void* ws,
+                   size_t ws_bytes, cudaStream_t st);
 
 bool triatt_bias_supported(int c, int H);
 int triatt_bias(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,

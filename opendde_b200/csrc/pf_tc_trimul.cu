@@ -666,17 +666,9 @@ size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int, int) {
   return ar.used;
 }
 
-int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
-           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
-           int, int, int acc, void* ws, size_t ws_bytes, cudaStream_t st) {
-  Arena ar(ws, ws_bytes);
-  TrimulWs w;
-  trimul_plan(ar, n_i, n_j, n_k, w);
-  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small");
-  if (zo.row_stride % 8 || zo.col_stride % 8 || ((uintptr_t)zo.ptr) % 16)
-    return fail(PF_EINVAL_SHAPE, "bf16 output view must be 16-byte aligned with strides multiple of 8");
-  unsigned int* status;
-  PF_TRY(device_status_ptr(&status));
+namespace {
+
+int ensure_attrs() {
   static bool attrs = false;
   if (!attrs) {
     PF_TRY(set_smem(k_trimul_proj, PROJ_SMEM + 1024));
@@ -684,7 +676,14 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     PF_TRY(set_smem(k_trimul_out, OUT_SMEM + 1024));
     attrs = true;
   }
-  // 1. projections (persistent)
+  return PF_OK;
+}
+
+// a(ch, i, k) = projection of za(i, k) (i < n_i), b(ch, j, k) of zb(j, k) (j < n_j), stored
+// channel-major with row pitch ld (elements, multiple of 8) and plane pitch n * ld.
+int launch_proj(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+                pf_mask_view mb, int64_t n_i, int64_t n_j, int64_t n_k, __nv_bfloat16* a,
+                __nv_bfloat16* b, int64_t ld, unsigned int* status, cudaStream_t st) {
   CUtensorMap tz0, tz1, to0, to1, tw0p, tw0g, tw1p, tw1g;
   PF_TRY(pair_tmap(&tz0, za, n_i, n_k));
   PF_TRY(pair_tmap(&tz1, zb, n_j, n_k));
@@ -695,11 +694,11 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   {
     const uint32_t bo[3] = {(uint32_t)TILE, 1, (uint32_t)CH};
     const uint64_t d0[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)CH};
-    const uint64_t s0[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_i * w.ld_k * 2};
-    PF_TRY(make_tmap(&to0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.a, d0, s0, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
+    const uint64_t s0[2] = {(uint64_t)ld * 2, (uint64_t)n_i * ld * 2};
+    PF_TRY(make_tmap(&to0, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, d0, s0, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
     const uint64_t d1[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)CH};
-    const uint64_t s1[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_j * w.ld_k * 2};
-    PF_TRY(make_tmap(&to1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.b, d1, s1, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
+    const uint64_t s1[2] = {(uint64_t)ld * 2, (uint64_t)n_j * ld * 2};
+    PF_TRY(make_tmap(&to1, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, b, d1, s1, bo, CU_TENSOR_MAP_SWIZZLE_NONE));
   }
   ProjArgs pa;
   const int64_t tpr_k = (n_k + TILE - 1) / TILE;
@@ -716,17 +715,25 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     k_trimul_proj<<<(unsigned)grid_p, 320, PROJ_SMEM + 1024, st>>>(tz0, tz1, to0, to1, tw0p, tw0g, tw1p, tw1g, pa);
   }
   PF_CHECK_LAUNCH();
-  // 2. contraction x[ch] = a[ch] b[ch]^T
+  return PF_OK;
+}
+
+// x(ch, i, j) = sum_k a(ch, i, k) b(ch, j, k) into x (row pitch ld_j), then
+// zo (+)= (W_z LN_out(x)) * sigmoid(W_g LN_in(zg)).
+int launch_contract_out(const pf_trimul_params* p, const __nv_bfloat16* a, int64_t lda,
+                        const __nv_bfloat16* b, int64_t ldb, int64_t n_i, int64_t n_j, int64_t n_k,
+                        __nv_bfloat16* x, int64_t ld_j, pf_pair_view zg, pf_pair_view zo, int acc,
+                        unsigned int* status, cudaStream_t st) {
   CUtensorMap ta, tb;
   {
     const uint64_t da[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)CH};
-    const uint64_t sa[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_i * w.ld_k * 2};
+    const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)n_i * lda * 2};
     const uint32_t ba[3] = {BK, BM, 1};
-    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B));
+    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B));
     const uint64_t db[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)CH};
-    const uint64_t sb[2] = {(uint64_t)w.ld_k * 2, (uint64_t)n_j * w.ld_k * 2};
+    const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)n_j * ldb * 2};
     const uint32_t bb[3] = {BK, BN, 1};
-    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
   }
   GemmArgs ga;
   ga.M = (int)n_i;
@@ -735,9 +742,9 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   ga.m_tiles = (int)((n_i + BM - 1) / BM);
   ga.n_tiles = (int)((n_j + BN - 1) / BN);
   ga.n_work = (int64_t)CH * ga.m_tiles * ga.n_tiles;
-  ga.out = w.x;
-  ga.ldo = w.ld_j;
-  ga.out_bstride = (int64_t)n_i * w.ld_j;
+  ga.out = x;
+  ga.ldo = ld_j;
+  ga.out_bstride = (int64_t)n_i * ld_j;
   ga.status = status;
   {
     const int64_t grid_g = ga.n_work < sm_count() ? ga.n_work : sm_count();
@@ -745,7 +752,7 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
     k_trimul_bgemm<<<(unsigned)grid_g, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
   }
   PF_CHECK_LAUNCH();
-  // 3. LN_out, W_z, gate, residual (persistent, one CTA per SM)
+  // LN_out, W_z, gate, residual (persistent, one CTA per SM)
   CUtensorMap tzg, tzo, txm, twz, twg;
   PF_TRY(pair_tmap(&tzg, zg, n_i, n_j));
   PF_TRY(pair_tmap(&tzo, zo, n_i, n_j));
@@ -753,9 +760,9 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   PF_TRY(weight_tmap(&twg, p->w_g, CH, CH, 128));
   {
     const uint64_t dx[3] = {(uint64_t)n_j, (uint64_t)n_i, (uint64_t)CH};
-    const uint64_t sx[2] = {(uint64_t)w.ld_j * 2, (uint64_t)n_i * w.ld_j * 2};
+    const uint64_t sx[2] = {(uint64_t)ld_j * 2, (uint64_t)n_i * ld_j * 2};
     const uint32_t bx[3] = {(uint32_t)TILE, 1, (uint32_t)CH};
-    PF_TRY(make_tmap(&txm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, w.x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_NONE));
+    PF_TRY(make_tmap(&txm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, x, dx, sx, bx, CU_TENSOR_MAP_SWIZZLE_NONE));
   }
   OutArgs oa;
   oa.n_i = n_i;
@@ -778,6 +785,69 @@ int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
+}
+
+int check_out_view(const pf_pair_view& zo) {
+  if (zo.row_stride % 8 || zo.col_stride % 8 || ((uintptr_t)zo.ptr) % 16)
+    return fail(PF_EINVAL_SHAPE, "bf16 output view must be 16-byte aligned with strides multiple of 8");
+  return PF_OK;
+}
+
+int check_cmajor(const void* ptr, int64_t ld, int64_t n_cols, const char* what) {
+  if (((uintptr_t)ptr) % 16 || ld % 8 || ld < n_cols)
+    return fail(PF_EINVAL_SHAPE, "%s: channel-major bf16 buffer needs a 16-byte aligned base and a row "
+                "pitch that is a multiple of 8 elements and >= %lld (got %lld)", what, (long long)n_cols,
+                (long long)ld);
+  return PF_OK;
+}
+
+}  // namespace
+
+int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
+           pf_mask_view mb, pf_pair_view zg, pf_pair_view zo, int64_t n_i, int64_t n_j, int64_t n_k,
+           int, int, int acc, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  TrimulWs w;
+  trimul_plan(ar, n_i, n_j, n_k, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul workspace too small");
+  PF_TRY(check_out_view(zo));
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  PF_TRY(ensure_attrs());
+  PF_TRY(launch_proj(p, za, zb, ma, mb, n_i, n_j, n_k, w.a, w.b, w.ld_k, status, st));
+  return launch_contract_out(p, w.a, w.ld_k, w.b, w.ld_k, n_i, n_j, n_k, w.x, w.ld_j, zg, zo, acc, status, st);
+}
+
+int trimul_project(const pf_trimul_params* p, pf_pair_view z, pf_mask_view m, int64_t n_rows,
+                   int64_t n_cols, void* a, void* b, int64_t ld, cudaStream_t st) {
+  PF_TRY(check_cmajor(a, ld, n_cols, "a"));
+  PF_TRY(check_cmajor(b, ld, n_cols, "b"));
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  PF_TRY(ensure_attrs());
+  return launch_proj(p, z, z, m, m, n_rows, n_rows, n_cols, (__nv_bfloat16*)a, (__nv_bfloat16*)b, ld,
+                     status, st);
+}
+
+size_t trimul_combine_ws_bytes(int64_t n_i, int64_t n_j) {
+  return (size_t)CH * n_i * ((n_j + 7) / 8 * 8) * 2 + 256;
+}
+
+int trimul_combine(const pf_trimul_params* p, const void* a, const void* b, int64_t ld, int64_t n_i,
+                   int64_t n_j, int64_t n_k, pf_pair_view zg, pf_pair_view zo, int acc, void* ws,
+                   size_t ws_bytes, cudaStream_t st) {
+  PF_TRY(check_cmajor(a, ld, n_k, "a"));
+  PF_TRY(check_cmajor(b, ld, n_k, "b"));
+  PF_TRY(check_out_view(zo));
+  Arena ar(ws, ws_bytes);
+  const int64_t ld_j = (n_j + 7) / 8 * 8;
+  __nv_bfloat16* x = ar.take<__nv_bfloat16>((size_t)CH * n_i * ld_j);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "trimul combine workspace too small");
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  PF_TRY(ensure_attrs());
+  return launch_contract_out(p, (const __nv_bfloat16*)a, ld, (const __nv_bfloat16*)b, ld, n_i, n_j, n_k, x,
+                             ld_j, zg, zo, acc, status, st);
 }
 
 }  // namespace tc

@@ -24,6 +24,16 @@ class KernelOps:
         """zo += TriangleMultiplicativeUpdate over the band views (x_ij = sum_k a(za_ik) b(zb_jk))."""
         kernels.trimul(module.weight_pack(zo.dtype, zo.device), za, zb, ma, mb, zg, zo, module.c_hidden, True)
 
+    def trimul_project(self, module, z_view, m_view, a_ptr: int, b_ptr: int, ld: int) -> None:
+        """a, b projections of ``z_view`` written channel-major [c_h][rows][ld] at raw device
+        addresses (a peer window)."""
+        kernels.trimul_project(module.weight_pack(z_view.dtype, z_view.device), z_view, m_view, module.c_hidden,
+                               a_ptr, b_ptr, ld)
+
+    def trimul_combine(self, module, a, b, n_k: int, zg, zo) -> None:
+        """zo += the triangle update from exchanged projection bands."""
+        kernels.trimul_combine(module.weight_pack(zo.dtype, zo.device), a, b, n_k, zg, zo, True)
+
     def triatt_bias(self, module, z_view, out) -> None:
         """out[h, r, s] = triangle bias of z_view(r, s), in ``bias_dtype`` format."""
         kernels.triatt_bias(module.weight_pack(z_view.dtype, z_view.device), z_view, module.no_heads, out)

@@ -24,18 +24,19 @@ from __future__ import annotations
 
 import ctypes
 import os
-from typing import Dict, List, Sequence, Tuple
+from typing import Callable, Dict, List, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
 
 from ... import _abi, kernels
-from .exchange import DistExchange, Need, Region, intersect, tile_region
+from .exchange import DistExchange, Need, Range, Region, intersect, tile_region
 from .pair_sharding import FoldCPPairShardSpec
 
 TRANSPORT_KEY = "OPENDDE_B200_FOLDCP_TRANSPORT"
 
-CopyRegion = Tuple[int, int, int, int, int, int]  # src, dst, rows, row_bytes, src_pitch, dst_pitch
+# src, dst, planes, rows, row_bytes, src_pitch, dst_pitch, src_plane_pitch, dst_plane_pitch
+CopyRegion = Tuple[int, int, int, int, int, int, int, int, int]
 
 
 def transport_choice(backend: str) -> str:
@@ -68,8 +69,47 @@ def band_copy_plan(spec: FoldCPPairShardSpec, layout, want: Region, slot_ptrs: S
         src_pitch = (tc1 - tc0) * pos_bytes
         src = slot_ptrs[q] + (ir[0] - tr0) * src_pitch + (ic[0] - tc0) * pos_bytes
         dst = out_ptr + (ir[0] - nr0) * out_pitch + (ic[0] - nc0) * pos_bytes
-        plan.append((src, dst, ir[1] - ir[0], (ic[1] - ic[0]) * pos_bytes, src_pitch, out_pitch))
+        plan.append((src, dst, 1, ir[1] - ir[0], (ic[1] - ic[0]) * pos_bytes, src_pitch, out_pitch, 0, 0))
     return plan
+
+
+def _round8(x: int) -> int:
+    return (x + 7) // 8 * 8
+
+
+def projection_geometry(spec: FoldCPPairShardSpec, coord, transposed: bool) -> Tuple[Range, Range]:
+    """(rows, cols) of rank ``coord``'s tile in the projection orientation: the tile itself
+    (rows R_r, cols C_c) or, transposed, (i, k) = z(k, i) (rows C_c, cols R_r)."""
+    rr, cc = spec.row_range_of(coord[0]), spec.col_range_of(coord[1])
+    return (cc, rr) if transposed else (rr, cc)
+
+
+def projection_copy_plan(spec: FoldCPPairShardSpec, layout, rows_req: Range, transposed: bool,
+                         slot_ptrs: Sequence[int], side_off: int, planes: int, elem: int, ld_t: int,
+                         out_ptr: int, ld_b: int) -> List[CopyRegion]:
+    """Boxes that assemble P[ch][i in rows_req][k < Np] (row pitch ld_b elements) from every
+    rank's channel-major projection of its tile, P_q[ch][x][y] with x, y over the tile's rows and
+    columns in the projection orientation (row pitch ld_t, at slot_ptrs[q] + side_off)."""
+    i0, i1 = rows_req
+    plan: List[CopyRegion] = []
+    for q in range(layout.numel):
+        xr, yr = projection_geometry(spec, layout.to_coord(q), transposed)
+        ir = intersect(xr, rows_req)
+        if ir is None or yr[1] <= yr[0]:
+            continue
+        nx = xr[1] - xr[0]
+        src = slot_ptrs[q] + side_off + (ir[0] - xr[0]) * ld_t * elem
+        dst = out_ptr + ((ir[0] - i0) * ld_b + yr[0]) * elem
+        plan.append((src, dst, planes, ir[1] - ir[0], (yr[1] - yr[0]) * elem, ld_t * elem, ld_b * elem,
+                     nx * ld_t * elem, (i1 - i0) * ld_b * elem))
+    return plan
+
+
+def _projection_side_bytes(spec: FoldCPPairShardSpec, planes: int, elem: int) -> Tuple[int, int, int]:
+    """(ld_t, bytes of one side) for either orientation of a tile: the larger of the two."""
+    tr, tc = spec.tile_rows, spec.tile_cols
+    ld_t = _round8(max(tr, tc))
+    return ld_t, _slot_bytes(planes * max(tr, tc) * ld_t * elem)
 
 
 class PeerWindows:
@@ -160,14 +200,13 @@ class PeerExchange(DistExchange):
         if not local.is_contiguous():
             raise ValueError("peer exchange publishes contiguous tiles")
         pos_bytes = local.element_size() * (local[0, 0].numel() if local.dim() > 2 else 1)
-        tile_bytes = local.numel() * local.element_size()
-        w = self._windows_fn(self.mesh, tile_bytes, local.device)
+        w = self._windows_fn(self.mesh, self._slot_need(local, spec), local.device)
         slot = w.slot
         w.slot ^= 1
         ptrs = w.slot_ptrs(slot)
         row_bytes = local.shape[1] * pos_bytes
-        kernels.copy_regions([(local.data_ptr(), ptrs[self.mesh.cp_rank], local.shape[0], row_bytes, row_bytes,
-                               row_bytes)])
+        kernels.copy_regions([(local.data_ptr(), ptrs[self.mesh.cp_rank], 1, local.shape[0], row_bytes, row_bytes,
+                               row_bytes, 0, 0)])
         w.barrier()
         outs, plan = [], []
         for need in needs:
@@ -181,3 +220,43 @@ class PeerExchange(DistExchange):
 
     def region(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need) -> torch.Tensor:
         return self.bands(local, spec, [need])[0]
+
+    @staticmethod
+    def _slot_need(local: torch.Tensor, spec: FoldCPPairShardSpec, c_h: int = 0) -> int:
+        """One slot holds a tile snapshot or the a and b projections of a tile (with c_h, by
+        default the tile's channel count, channels), whichever is larger, so the windows are
+        sized once."""
+        elem = local.element_size()
+        planes = max(c_h, local.shape[2] if local.dim() > 2 else 1)
+        _, side = _projection_side_bytes(spec, planes, elem)
+        return max(local.numel() * elem, 2 * side)
+
+    def trimul_bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, transposed: bool, c_h: int,
+                     project: Callable[[int, int, int], None], rows_a: Range, rows_b: Range):
+        """The triangle-update operand bands from the peers' projections.
+
+        ``project(a_ptr, b_ptr, ld)`` writes this rank's a and b projections (channel-major
+        [c_h][x][ld] over its tile in the projection orientation) into its window; after the
+        barrier, a rows ``rows_a`` and b rows ``rows_b`` over all Np columns are assembled from
+        every rank's window. Returns (a_band [c_h, |rows_a|, ld_b], b_band, Np). The projections
+        cross NVLink instead of z, so no rank recomputes another rank's projections.
+        """
+        elem = local.element_size()
+        ld_t, side = _projection_side_bytes(spec, c_h, elem)
+        w = self._windows_fn(self.mesh, self._slot_need(local, spec, c_h), local.device)
+        slot = w.slot
+        w.slot ^= 1
+        ptrs = w.slot_ptrs(slot)
+        me = self.mesh.cp_rank
+        project(ptrs[me], ptrs[me] + side, ld_t)
+        w.barrier()
+        n_pad = spec.n_padded
+        ld_b = _round8(n_pad)
+        a = local.new_empty((c_h, rows_a[1] - rows_a[0], ld_b))
+        b = local.new_empty((c_h, rows_b[1] - rows_b[0], ld_b))
+        plan = projection_copy_plan(spec, self.layout, rows_a, transposed, ptrs, 0, c_h, elem, ld_t,
+                                    a.data_ptr(), ld_b)
+        plan += projection_copy_plan(spec, self.layout, rows_b, transposed, ptrs, side, c_h, elem, ld_t,
+                                     b.data_ptr(), ld_b)
+        kernels.copy_regions(plan)
+        return a, b, n_pad

@@ -182,6 +182,18 @@ def _col_of(spec):
 def _trimul(module, z_local, ctx: FoldCPPairContext, ops) -> None:
     spec, ex, m = ctx.spec, ctx.exchange, ctx.mask
     (r0, r1), (c0, c1) = ctx.rows, ctx.cols
+    if hasattr(ex, "trimul_bands") and hasattr(ops, "trimul_project"):
+        # Exchange the projections (the reference's ring moves a_local / b_local too,
+        # real_pairformer.py:1308-1384): each rank projects only its own tile. Incoming works
+        # on x = z^T: a(i, k) = a(z(k, i)), so the tile is projected through a transposed view.
+        mt = m[r0:r1, c0:c1]
+        zt, mt = (z_local, mt) if module._outgoing else (z_local.transpose(0, 1), mt.t())
+        a, b, n_k = ex.trimul_bands(
+            z_local, spec, transposed=not module._outgoing, c_h=module.c_hidden,
+            project=lambda pa, pb, ld: ops.trimul_project(module, zt, mt, pa, pb, ld),
+            rows_a=(r0, r1), rows_b=(c0, c1))
+        ops.trimul_combine(module, a, b, n_k, z_local, z_local)
+        return
     if module._outgoing:
         # z rows R_r [Tr, Np, C] and z rows C_c [Tc, Np, C]
         za, zb = gather_bands(ex, z_local, spec, [("own_rows",), ("rows", _col_of(spec))])

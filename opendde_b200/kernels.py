@@ -233,12 +233,46 @@ def apb_rows(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, bias: to
 
 
 def copy_regions(regions) -> None:
-    """Copy 2D byte rectangles ``(src_ptr, dst_ptr, rows, row_bytes, src_pitch, dst_pitch)``
-    on the current stream, one kernel launch per PF_MAX_COPY_REGIONS rectangles (sources
-    may be peers' windows)."""
+    """Copy byte boxes ``(src_ptr, dst_ptr, planes, rows, row_bytes, src_pitch, dst_pitch,
+    src_plane_pitch, dst_plane_pitch)`` on the current stream, one kernel launch per
+    PF_MAX_COPY_REGIONS boxes (sources may be peers' windows)."""
     lib = _abi.load()
     step = _abi.PF_MAX_COPY_REGIONS
     for i in range(0, len(regions), step):
         chunk = regions[i:i + step]
         arr = (_abi.CopyRegion * len(chunk))(*[_abi.CopyRegion(*r) for r in chunk])
         check(lib.pf_copy_regions(arr, len(chunk), stream_ptr()))
+
+
+def trimul_project(pack: WeightPack, z: torch.Tensor, m: torch.Tensor, c_h: int, a_ptr: int, b_ptr: int,
+                   ld: int) -> None:
+    """a, b projections of the pair view ``z`` [R, C, c_z] (mask ``m`` [R, C]) written
+    channel-major [c_h][R][ld] at the raw device addresses ``a_ptr`` / ``b_ptr`` (storage dtype:
+    fp32 for fp32 z, bf16 for bf16 z)."""
+    require_cuda(z, m)
+    code = dtype_code(z)
+    rows, cols, c_z = z.shape
+    nbytes = _abi.workspace_bytes("pf_trimul_project_workspace_size", rows, cols, c_z, c_h, code)
+    ws = workspace(nbytes, z.device)
+    check(_abi.load().pf_trimul_project(ctypes.byref(pack.struct), pair_view(z), mask_view(m), rows, cols, c_z,
+                                        c_h, code, a_ptr, b_ptr, ld, ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def trimul_combine(pack: WeightPack, a: torch.Tensor, b: torch.Tensor, n_k: int, zg: torch.Tensor,
+                   zo: torch.Tensor, accumulate: bool) -> None:
+    """zo (+)= the triangle update from channel-major projections a [c_h][n_i][ld] and
+    b [c_h][n_j][ld] contracted over k < n_k, gated by LN_in(zg)."""
+    require_cuda(a, b, zg, zo)
+    code = dtype_code(zo)
+    c_h, n_i, ld = a.shape
+    n_j = b.shape[1]
+    if b.shape[0] != c_h or b.shape[2] != ld or not a.is_contiguous() or not b.is_contiguous():
+        raise ValueError("trimul_combine takes contiguous [c_h, n, ld] projections with one ld")
+    if a.dtype != zo.dtype or b.dtype != zo.dtype:
+        raise TypeError("projections must be in the pair tensor's dtype")
+    c_z = zo.shape[2]
+    nbytes = _abi.workspace_bytes("pf_trimul_combine_workspace_size", n_i, n_j, n_k, c_z, c_h, code)
+    ws = workspace(nbytes, zo.device)
+    check(_abi.load().pf_trimul_combine(ctypes.byref(pack.struct), a.data_ptr(), b.data_ptr(), ld, n_i, n_j, n_k,
+                                        pair_view(zg), pair_view(zo), c_z, c_h, int(accumulate), code,
+                                        ws.data_ptr(), ws.numel(), stream_ptr()))

@@ -12,9 +12,10 @@ from opendde_b200.distributed.foldcp.peer import band_copy_plan, transport_choic
 
 
 def _apply(plan):
-    for src, dst, rows, row_bytes, sp, dp in plan:
-        for r in range(rows):
-            ctypes.memmove(dst + r * dp, src + r * sp, row_bytes)
+    for src, dst, planes, rows, row_bytes, sp, dp, spp, dpp in plan:
+        for c in range(planes):
+            for r in range(rows):
+                ctypes.memmove(dst + c * dpp + r * dp, src + c * spp + r * sp, row_bytes)
 
 
 @pytest.mark.parametrize("shape", [(1, 2), (2, 1), (2, 2), (2, 4), (4, 2), (1, 3), (3, 3)])
@@ -59,3 +60,38 @@ def test_transport_choice(monkeypatch):
     monkeypatch.setenv("OPENDDE_B200_FOLDCP_TRANSPORT", "shm")
     with pytest.raises(ValueError):
         transport_choice("nccl")
+
+
+@pytest.mark.parametrize("shape", [(1, 2), (2, 1), (2, 2), (2, 4), (4, 2), (1, 3)])
+@pytest.mark.parametrize("n", [13, 37])
+@pytest.mark.parametrize("transposed", [False, True])
+def test_projection_plans_assemble_operand_bands(shape, n, transposed):
+    """Channel-major projection bands P[ch][i in I][k < Np] from per-rank tile projections in the
+    plain (i, k) = z(i, k) or transposed (i, k) = z(k, i) orientation."""
+    from opendde_b200.distributed.foldcp.peer import projection_copy_plan, projection_geometry
+    layout = FoldCP2DLayout(shape)
+    planes, elem = 3, 4
+    spec0 = _spec_for((n, n, 1), shape, (0, 0), (0, 1))
+    n_pad = spec0.n_padded
+    rng = np.random.default_rng(n + 100 * shape[0] + 10 * shape[1] + int(transposed))
+    plane = rng.standard_normal((planes, n_pad, n_pad)).astype(np.float32)   # P[ch][i][k]
+    ld_t = (max(spec0.tile_rows, spec0.tile_cols) + 7) // 8 * 8 + 8         # padded pitch
+    slots = []
+    for q in range(layout.numel):
+        sp = _spec_for((n, n, 1), shape, layout.to_coord(q), (0, 1))
+        xr, yr = projection_geometry(sp, layout.to_coord(q), transposed)
+        t = np.full((planes, xr[1] - xr[0], ld_t), np.nan, dtype=np.float32)
+        t[:, :, :yr[1] - yr[0]] = plane[:, xr[0]:xr[1], yr[0]:yr[1]]
+        slots.append(t)
+    ptrs = [t.ctypes.data for t in slots]
+    ld_b = (n_pad + 7) // 8 * 8
+    for q in range(layout.numel):
+        coord = layout.to_coord(q)
+        spec = _spec_for((n, n, 1), shape, coord, (0, 1))
+        for rows in (spec.row_range, spec.col_range):
+            out = np.full((planes, rows[1] - rows[0], ld_b), np.nan, dtype=np.float32)
+            plan = projection_copy_plan(spec, layout, rows, transposed, ptrs, 0, planes, elem, ld_t,
+                                        out.ctypes.data, ld_b)
+            assert len(plan) <= layout.numel
+            _apply(plan)
+            np.testing.assert_array_equal(out[:, :, :n_pad], plane[:, rows[0]:rows[1], :])

@@ -91,18 +91,21 @@ def test_copy_regions_every_vector_width(unit, cuda_device):
     src = torch.randint(0, 255, (size,), generator=g, dtype=torch.uint8).to(cuda_device)
     dst = torch.zeros_like(src)
     u = unit
-    #        offset  rows  row_bytes  src_pitch  dst_pitch   (odd multiples of u: alignment is u)
-    rects = [(u, 100, 37 * u, 103 * u, 70 * u),
-             (64 * u, 3, 4097 * u, 4099 * u, 4098 * u),
-             (2 * u, 1, 25000 * u, 25000 * u, 25000 * u)]
+    #  offset  planes rows row_bytes  src_pitch  dst_pitch src_plane dst_plane (odd multiples of u)
+    boxes = [(u, 1, 100, 37 * u, 103 * u, 70 * u, 0, 0),
+             (64 * u, 1, 3, 4097 * u, 4099 * u, 4098 * u, 0, 0),
+             (2 * u, 1, 1, 25000 * u, 25000 * u, 25000 * u, 0, 0),
+             (3 * u, 5, 7, 11 * u, 13 * u, 12 * u, 97 * u, 89 * u)]
     regions, want = [], dst.clone()
-    for i, (off, rows, row_bytes, sp, dp) in enumerate(rects):
+    for i, (off, planes, rows, row_bytes, sp, dp, spp, dpp) in enumerate(boxes):
         s_off, d_off = off, off + (1 << 20) * i
-        assert s_off + (rows - 1) * sp + row_bytes <= size      # every access in bounds
-        assert d_off + (rows - 1) * dp + row_bytes <= size
-        regions.append((src.data_ptr() + s_off, dst.data_ptr() + d_off, rows, row_bytes, sp, dp))
-        for r in range(rows):
-            want[d_off + r * dp:d_off + r * dp + row_bytes] = src[s_off + r * sp:s_off + r * sp + row_bytes]
+        assert s_off + (planes - 1) * spp + (rows - 1) * sp + row_bytes <= size      # every access in bounds
+        assert d_off + (planes - 1) * dpp + (rows - 1) * dp + row_bytes <= size
+        regions.append((src.data_ptr() + s_off, dst.data_ptr() + d_off, planes, rows, row_bytes, sp, dp, spp, dpp))
+        for c in range(planes):
+            for r in range(rows):
+                so, do = s_off + c * spp + r * sp, d_off + c * dpp + r * dp
+                want[do:do + row_bytes] = src[so:so + row_bytes]
     kernels.copy_regions(regions)
     torch.cuda.synchronize()
     assert torch.equal(dst, want)
