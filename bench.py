@@ -13,7 +13,9 @@ reference PyTorch modules; the reference itself is not installed on the GPU box)
 host cores for a bounded row sample of the same workload, extrapolated to ms per block.
 
 N > 1 GPUs: Fold-CP 2D pair sharding (1x2, 2x2, 2x4 grids) of the same trunk; total work
-fixed ("strong" scaling); time = max over ranks.
+fixed ("strong" scaling); time = max over ranks. Each step is captured once as a CUDA graph
+(kernels, peer copies, NCCL collectives) and replayed; per-kernel times then come from one
+extra eager step.
 """
 
 from __future__ import annotations
@@ -222,6 +224,9 @@ def main():
     ap.add_argument("--blocks", type=int, default=48)
     ap.add_argument("--cpu-rows", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
+                    help="replay each step as one CUDA graph (auto: on for N > 1, where the per-op host "
+                         "work and collective launches would otherwise show between short kernels)")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -305,29 +310,64 @@ def main():
     step_e2e()
     barrier()
 
-    # ---- timed: resident inputs (value) with per-kernel events (roofline)
+    use_graph = args.graph == "on" or (args.graph == "auto" and distributed)
+    graphs = {}
+    if use_graph:
+        # one CUDA graph per step kind (kernels, peer copies and NCCL collectives of all blocks),
+        # captured after the eager warm-up has created every window, communicator and workspace
+        for name, fn in (("resident", step_resident), ("e2e", step_e2e)):
+            graphs[name] = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graphs[name]):
+                fn()
+        barrier()
+        for name in graphs:   # warm replay
+            graphs[name].replay()
+        barrier()
+    def run_resident():
+        graphs["resident"].replay() if use_graph else step_resident()
+
+    def run_e2e():
+        graphs["e2e"].replay() if use_graph else step_e2e()
+
     st = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    _abi.profile_enable(True)
-    _abi.profile_report()  # clear
+    launches_per_step = None
+    if use_graph:
+        # per-kernel launch times from one eager step (graph replays carry no per-launch events)
+        _abi.profile_enable(True)
+        _abi.profile_report()
+        l0 = _abi.launch_count()
+        step_resident()
+        launches_per_step = _abi.launch_count() - l0
+        _abi.profile_enable(False)
+        prof = _abi.profile_report()
+        barrier()
+
+    # ---- timed: resident inputs (value); eager runs carry per-kernel events (roofline)
+    if not use_graph:
+        _abi.profile_enable(True)
+        _abi.profile_report()  # clear
     launches0 = _abi.launch_count()
     with ClockSampler(local_rank) as clk:
         barrier()
         ev0.record(st)
         for _ in range(args.steps):
-            step_resident()
+            run_resident()
         ev1.record(st)
         barrier()
-    launches = _abi.launch_count() - launches0
-    _abi.profile_enable(False)
-    prof = _abi.profile_report()
+    if use_graph:
+        launches = launches_per_step * args.steps
+    else:
+        launches = _abi.launch_count() - launches0
+        _abi.profile_enable(False)
+        prof = _abi.profile_report()
     ms_step = ev0.elapsed_time(ev1) / args.steps
 
     # ---- timed: end to end through the public API with host buffers
     barrier()
     ev0.record(st)
     for _ in range(args.steps):
-        step_e2e()
+        run_e2e()
     ev1.record(st)
     barrier()
     ms_e2e = ev0.elapsed_time(ev1) / args.steps
@@ -409,10 +449,14 @@ def main():
             "tri_mul": fracs.get("k_trimul_bgemm"),
             "kernels": kernels,
             "gpu_launches": launches,
+            "cuda_graph": use_graph,
             "clocks": clocks,
             "cpu_baseline": cpu_baseline,
         }
         print(json.dumps(out), flush=True)
+    # graphs holding NCCL calls must be destroyed before the process group: drop every reference
+    graphs.clear()
+    torch.cuda.synchronize()
     if distributed:
         from opendde_b200.distributed.foldcp import clear_mesh_cache
         torch.distributed.barrier()
