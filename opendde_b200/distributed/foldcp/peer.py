@@ -195,6 +195,10 @@ class PeerExchange(DistExchange):
         super().__init__(mesh)
         self._windows_fn = windows_fn
 
+    def _copy(self, plan: List[CopyRegion]) -> None:
+        """Execute a copy plan (one pf_copy_regions launch per 32 boxes on the current stream)."""
+        kernels.copy_regions(plan)
+
     def bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, needs: Sequence[Need]) -> List[torch.Tensor]:
         """Every rectangle ``need(coord)`` of ``needs``, from one snapshot of ``local``."""
         if not local.is_contiguous():
@@ -205,7 +209,7 @@ class PeerExchange(DistExchange):
         w.slot ^= 1
         ptrs = w.slot_ptrs(slot)
         row_bytes = local.shape[1] * pos_bytes
-        kernels.copy_regions([(local.data_ptr(), ptrs[self.mesh.cp_rank], 1, local.shape[0], row_bytes, row_bytes,
+        self._copy([(local.data_ptr(), ptrs[self.mesh.cp_rank], 1, local.shape[0], row_bytes, row_bytes,
                                row_bytes, 0, 0)])
         w.barrier()
         outs, plan = [], []
@@ -215,7 +219,7 @@ class PeerExchange(DistExchange):
             out = local.new_empty((r1 - r0, c1 - c0) + tuple(local.shape[2:]))
             plan += band_copy_plan(spec, self.layout, want, ptrs, out.data_ptr(), pos_bytes)
             outs.append(out)
-        kernels.copy_regions(plan)
+        self._copy(plan)
         return outs
 
     def region(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need) -> torch.Tensor:
@@ -258,5 +262,5 @@ class PeerExchange(DistExchange):
                                     a.data_ptr(), ld_b)
         plan += projection_copy_plan(spec, self.layout, rows_b, transposed, ptrs, side, c_h, elem, ld_t,
                                      b.data_ptr(), ld_b)
-        kernels.copy_regions(plan)
+        self._copy(plan)
         return a, b, n_pad

@@ -12,6 +12,7 @@ on a GPU, the real kernels) for every rank of a mesh on a single device.
 
 from __future__ import annotations
 
+import ctypes
 import math
 import threading
 from typing import Callable, Dict, List, Optional, Tuple
@@ -44,6 +45,29 @@ class OracleBandOps:
         a = ma[..., None] * torch.sigmoid(O.linear(xa, p["linear_a_g.weight"])) * O.linear(xa, p["linear_a_p.weight"])
         b = mb[..., None] * torch.sigmoid(O.linear(xb, p["linear_b_g.weight"])) * O.linear(xb, p["linear_b_p.weight"])
         x = torch.einsum("ikc,jkc->ijc", a, b)
+        x = O.layer_norm(x, p["layer_norm_out.weight"], p["layer_norm_out.bias"])
+        x = O.linear(x, p["linear_z.weight"])
+        g = torch.sigmoid(O.linear(O.layer_norm(zg, ln_w, ln_b), p["linear_g.weight"]))
+        zo += x * g
+
+    def trimul_project(self, module, z_view, m_view, a_ptr, b_ptr, ld):
+        """a, b of a tile view written channel-major [c_h][rows][ld] (fp32) at raw host
+        addresses, like the library's pf_trimul_project."""
+        p = _params(module)
+        ln_w, ln_b = p["layer_norm_in.weight"], p["layer_norm_in.bias"]
+        x = O.layer_norm(z_view, ln_w, ln_b)
+        rows, cols = z_view.shape[:2]
+        for name, ptr in (("a", a_ptr), ("b", b_ptr)):
+            v = m_view[..., None] * torch.sigmoid(O.linear(x, p[f"linear_{name}_g.weight"])) * \
+                O.linear(x, p[f"linear_{name}_p.weight"])
+            out = torch.zeros((v.shape[2], rows, ld), dtype=torch.float32)
+            out[:, :, :cols] = v.permute(2, 0, 1)
+            ctypes.memmove(ptr, out.data_ptr(), out.numel() * 4)
+
+    def trimul_combine(self, module, a, b, n_k, zg, zo):
+        p = _params(module)
+        ln_w, ln_b = p["layer_norm_in.weight"], p["layer_norm_in.bias"]
+        x = torch.einsum("cik,cjk->ijc", a[:, :, :n_k], b[:, :, :n_k])
         x = O.layer_norm(x, p["layer_norm_out.weight"], p["layer_norm_out.bias"])
         x = O.linear(x, p["linear_z.weight"])
         g = torch.sigmoid(O.linear(O.layer_norm(zg, ln_w, ln_b), p["linear_g.weight"]))
@@ -151,7 +175,8 @@ class _ThreadWindows:
         return [b.data_ptr() + slot * self.m.win_bytes for b in self.m.win_bufs]
 
     def barrier(self) -> None:
-        torch.cuda.synchronize()
+        if self.m.win_bufs and self.m.win_bufs[0].is_cuda:
+            torch.cuda.synchronize()
         self.m.wait()
 
 
@@ -161,11 +186,25 @@ class ThreadPeerExchange(PeerExchange):
 
     def __init__(self, mesh: "ThreadMesh", rank: int) -> None:
         self._t = _ThreadExchange(mesh, rank)
+        self.m = mesh
         fake = SimpleNamespace(layout=mesh.layout, coord=self._t.coord, cp_rank=rank)
         super().__init__(fake, windows_fn=lambda _m, nbytes, dev: mesh.peer_windows(rank, nbytes, dev))
 
     def all_gather(self, t, axis):
         return self._t.all_gather(t, axis)
+
+    def _copy(self, plan):
+        if self.m.win_bufs and self.m.win_bufs[0].is_cuda:
+            return super()._copy(plan)
+        apply_copy_plan(plan)
+
+
+def apply_copy_plan(plan) -> None:
+    """Host execution of a pf_copy_regions plan on CPU memory (byte boxes)."""
+    for src, dst, planes, rows, row_bytes, sp, dp, spp, dpp in plan:
+        for c in range(planes):
+            for r in range(rows):
+                ctypes.memmove(dst + c * dpp + r * dp, src + c * spp + r * sp, row_bytes)
 
 
 class ThreadMesh:

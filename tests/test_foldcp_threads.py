@@ -34,8 +34,8 @@ def _inputs(n, seed=1):
     return s, z, mask
 
 
-def _run_cp(shape, stack, s, z, mask):
-    mesh = ThreadMesh(shape)
+def _run_cp(shape, stack, s, z, mask, transport="copy"):
+    mesh = ThreadMesh(shape, transport=transport)
 
     def rank_fn(ex, rank):
         spec = _spec_for(tuple(z.shape), shape, ex.coord, (0, 1))
@@ -47,15 +47,18 @@ def _run_cp(shape, stack, s, z, mask):
     return mesh.run(rank_fn)
 
 
+@pytest.mark.parametrize("transport", ["copy", "peer"])
 @pytest.mark.parametrize("shape", [(1, 2), (2, 2), (2, 4), (4, 2), (1, 3)])
 @pytest.mark.parametrize("n", [13, 16])
-def test_cp_stack_matches_serial_oracle(shape, n):
+def test_cp_stack_matches_serial_oracle(shape, n, transport):
+    """"peer": the peer-memory transport's snapshot / projection-exchange logic with host
+    windows (copy plans applied by memmove), including the trimul projection exchange."""
     torch.manual_seed(0)
     stack, p = _stack(2)
     s, z, mask = _inputs(n)
     with torch.no_grad():
         s_ref, z_ref = O.pairformer_stack(s, z, mask, p, 2, no_heads_pair=4, n_heads=HEADS, c_s=C_S)
-        outs = _run_cp(shape, stack, s, z, mask)
+        outs = _run_cp(shape, stack, s, z, mask, transport)
     for s_out, z_out in outs:     # every rank returns the full, identical result
         assert (z_out - z_ref).abs().max().item() <= TOL
         assert (s_out - s_ref).abs().max().item() <= TOL
