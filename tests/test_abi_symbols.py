@@ -57,3 +57,40 @@ def test_workspace_queries_and_validation_without_gpu():
                            1e9, 1, _abi.PF_F32, None, 0, None)
     assert st == _abi.PF_EINVAL_SHAPE
     assert b"outside the slab" in lib.pf_last_error_string()
+
+
+def test_split_trimul_and_peer_entry_points_validate_on_the_host():
+    """The Fold-CP entry points reject bad arguments before touching a device."""
+    lib = _abi.load()
+    v = _abi.PairView(None, 0, 0)
+    mv = _abi.MaskView(None, 0, 0)
+    st = lib.pf_trimul_project(ctypes.byref(_abi.TrimulParams()), v, mv, 4, 4, 128, 128, _abi.PF_BF16,
+                               None, None, 8, None, 0, None)
+    assert st == _abi.PF_EINVAL_ARG                      # null weights
+    w = _abi.TrimulParams(*([16] * 10))
+    good = _abi.PairView(16, 128 * 8, 128)
+    st = lib.pf_trimul_project(ctypes.byref(w), good, mv, 4, 16, 128, 128, _abi.PF_BF16, 16, 16, 8, None, 0, None)
+    assert st == _abi.PF_EINVAL_SHAPE                    # ld < n_cols
+    st = lib.pf_trimul_combine(ctypes.byref(w), 16, 16, 4, 4, 4, 8, good, good, 128, 128, 1, _abi.PF_BF16,
+                               None, 0, None)
+    assert st == _abi.PF_EINVAL_SHAPE                    # ld < n_k
+    assert _abi.workspace_bytes("pf_trimul_combine_workspace_size", 64, 64, 64, 128, 128, _abi.PF_F32) > 0
+    with pytest.raises(_abi.PFError):
+        _abi.workspace_bytes("pf_trimul_project_workspace_size", -1, 4, 128, 128, _abi.PF_F32)
+    # copy regions: count, sizes and pitches are checked first
+    assert lib.pf_copy_regions(None, 33, None) == _abi.PF_EINVAL_ARG
+    assert lib.pf_copy_regions(None, 0, None) == _abi.PF_OK
+    bad_pitch = (_abi.CopyRegion * 1)(_abi.CopyRegion(16, 32, 1, 4, 64, 32, 64, 0, 0))
+    assert lib.pf_copy_regions(bad_pitch, 1, None) == _abi.PF_EINVAL_SHAPE
+    bad_plane = (_abi.CopyRegion * 1)(_abi.CopyRegion(16, 32, 2, 4, 64, 64, 64, 100, 256))
+    assert lib.pf_copy_regions(bad_plane, 1, None) == _abi.PF_EINVAL_SHAPE
+    null_src = (_abi.CopyRegion * 1)(_abi.CopyRegion(None, 32, 1, 1, 16, 16, 16, 0, 0))
+    assert lib.pf_copy_regions(null_src, 1, None) == _abi.PF_EINVAL_ARG
+    empty = (_abi.CopyRegion * 1)(_abi.CopyRegion(None, None, 0, 5, 16, 16, 16, 0, 0))
+    assert lib.pf_copy_regions(empty, 1, None) == _abi.PF_OK   # empty boxes are skipped
+    # peer windows
+    assert lib.pf_peer_handle_bytes() == 64
+    assert lib.pf_peer_window_alloc(0, None, None) == _abi.PF_EINVAL_ARG
+    assert lib.pf_peer_window_open(None, None) == _abi.PF_EINVAL_ARG
+    assert lib.pf_peer_window_close(None) == _abi.PF_EINVAL_ARG
+    assert lib.pf_peer_window_free(None) == _abi.PF_EINVAL_ARG
