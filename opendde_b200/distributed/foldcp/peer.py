@@ -40,7 +40,9 @@ CopyRegion = Tuple[int, int, int, int, int, int, int, int, int]
 
 
 def transport_choice(backend: str) -> str:
-    """"peer" or "nccl" for a mesh whose CP group runs on ``backend``."""
+    """The band transport of a mesh whose CP group runs on ``backend``: "peer" (the default on
+    NCCL) or "nccl" (NCCL point-to-point batches) as ``OPENDDE_B200_FOLDCP_TRANSPORT`` selects;
+    "dist" (torch.distributed point-to-point) for any other backend, e.g. gloo on CPU."""
     v = os.environ.get(TRANSPORT_KEY, "").strip().lower()
     if v not in ("", "peer", "nccl"):
         raise ValueError(f"{TRANSPORT_KEY} must be 'peer' or 'nccl', got {v!r}")
@@ -167,9 +169,10 @@ class PeerWindows:
 _WINDOWS: Dict[int, PeerWindows] = {}
 
 
-def windows_for(mesh, tile_bytes: int, device: torch.device) -> PeerWindows:
-    """The mesh's cached windows, grown (collectively) when a larger tile arrives."""
-    need = _slot_bytes(tile_bytes)
+def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
+    """The mesh's cached windows with slots of at least ``slot_bytes``, grown (collectively:
+    every rank asks for the same size at the same op) when a larger request arrives."""
+    need = _slot_bytes(slot_bytes)
     w = _WINDOWS.get(id(mesh))
     if w is not None and w.slot_bytes >= need and w.device == device:
         return w
