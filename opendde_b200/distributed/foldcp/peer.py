@@ -204,26 +204,64 @@ class PeerExchange(DistExchange):
 
     def bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, needs: Sequence[Need]) -> List[torch.Tensor]:
         """Every rectangle ``need(coord)`` of ``needs``, from one snapshot of ``local``."""
+        return self._publish_and_gather(local, spec, needs, None)[0]
+
+    def attention_bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need,
+                        bias_tile: torch.Tensor, transposed: bool, bias_rows: Range):
+        """The z band ``need(coord)`` and rows ``bias_rows`` of the triangle-bias plane (all Np
+        columns, row pitch rounded to 8 elements), from one snapshot, one barrier and one copy
+        launch. ``bias_tile`` [H, x, y] is this rank's tile of the plane in its orientation
+        (``transposed``: the ending node's plane, (a, b) = bias of z(b, a)). Only the requested
+        bias rows travel, not the whole plane."""
+        bands, bias = self._publish_and_gather(local, spec, [need], (bias_tile, transposed, bias_rows))
+        return bands[0], bias
+
+    def _publish_and_gather(self, local, spec, needs, bias_req):
         if not local.is_contiguous():
             raise ValueError("peer exchange publishes contiguous tiles")
         pos_bytes = local.element_size() * (local[0, 0].numel() if local.dim() > 2 else 1)
-        w = self._windows_fn(self.mesh, self._slot_need(local, spec), local.device)
+        tile_bytes = _slot_bytes(local.numel() * local.element_size())
+        need_bytes = self._slot_need(local, spec)
+        if bias_req is not None:
+            bias_tile = bias_req[0]
+            eb = bias_tile.element_size()
+            ld_t, bias_bytes = _projection_side_bytes(spec, bias_tile.shape[0], eb)
+            need_bytes = max(need_bytes, tile_bytes + bias_bytes)
+        w = self._windows_fn(self.mesh, need_bytes, local.device)
         slot = w.slot
         w.slot ^= 1
         ptrs = w.slot_ptrs(slot)
+        me = self.mesh.cp_rank
+        mine = tile_region(spec, self.coord)
         row_bytes = local.shape[1] * pos_bytes
-        self._copy([(local.data_ptr(), ptrs[self.mesh.cp_rank], 1, local.shape[0], row_bytes, row_bytes,
-                               row_bytes, 0, 0)])
+        publish = [(local.data_ptr(), ptrs[me], 1, local.shape[0], row_bytes, row_bytes, row_bytes, 0, 0)]
+        if bias_req is not None:
+            H, nx, ny = bias_tile.shape
+            if bias_tile.stride(2) != 1:
+                raise ValueError("bias tile columns must be contiguous")
+            publish.append((bias_tile.data_ptr(), ptrs[me] + tile_bytes, H, nx, ny * eb, bias_tile.stride(1) * eb,
+                            ld_t * eb, bias_tile.stride(0) * eb, nx * ld_t * eb))
+        self._copy(publish)
         w.barrier()
         outs, plan = [], []
         for need in needs:
             want = need(self.coord)
+            if want == mine:            # the band is this rank's own tile: no copy
+                outs.append(local)
+                continue
             (r0, r1), (c0, c1) = want
             out = local.new_empty((r1 - r0, c1 - c0) + tuple(local.shape[2:]))
             plan += band_copy_plan(spec, self.layout, want, ptrs, out.data_ptr(), pos_bytes)
             outs.append(out)
+        bias = None
+        if bias_req is not None:
+            _, transposed, rows = bias_req
+            ld_b = _round8(spec.n_padded)
+            bias = bias_tile.new_empty((bias_tile.shape[0], rows[1] - rows[0], ld_b))
+            plan += projection_copy_plan(spec, self.layout, rows, transposed, ptrs, tile_bytes, bias_tile.shape[0], eb,
+                                         ld_t, bias.data_ptr(), ld_b)
         self._copy(plan)
-        return outs
+        return outs, bias
 
     def region(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need) -> torch.Tensor:
         return self.bands(local, spec, [need])[0]

@@ -210,6 +210,24 @@ def _triatt(module, z_local, ctx: FoldCPPairContext, ending: bool, ops) -> None:
     spec, ex, m = ctx.spec, ctx.exchange, ctx.mask
     (r0, r1), (c0, c1) = ctx.rows, ctx.cols
     n_pad = ctx.n_pad
+    if hasattr(ex, "attention_bands"):
+        # one snapshot of the tile and of its bias tile, one barrier, one copy launch: the z band
+        # and only the bias rows of this rank's queries
+        view = z_local.transpose(0, 1) if ending else z_local
+        tile = torch.empty((module.no_heads, view.shape[0], view.shape[1]), device=z_local.device,
+                           dtype=ops.bias_dtype(z_local.dtype))
+        ops.triatt_bias(module, view, tile)
+        full = (0, n_pad)
+        if not ending:
+            zs, bias = ex.attention_bands(z_local, spec, lambda c: (spec.row_range_of(c[0]), full), tile,
+                                          transposed=False, bias_rows=(c0, c1))
+            ops.triatt(module, zs, m[r0:r1], bias[:, :, :n_pad], z_local, q_col0=c0, n_q=c1 - c0, n_valid=ctx.n)
+        else:
+            zs, bias = ex.attention_bands(z_local, spec, lambda c: (full, spec.col_range_of(c[1])), tile,
+                                          transposed=True, bias_rows=(r0, r1))
+            ops.triatt(module, zs.transpose(0, 1), m[:, c0:c1].t(), bias[:, :, :n_pad], z_local.transpose(0, 1),
+                       q_col0=r0, n_q=r1 - r0, n_valid=ctx.n)
+        return
     plane = _triatt_bias_plane(module, z_local, ctx, ending, ops)
     if not ending:
         zs, = gather_bands(ex, z_local, spec, [("own_rows",)])   # rows R_r, keys = all columns
