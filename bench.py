@@ -1,4 +1,4 @@
-"""Benchmark: ms per Pairformer block at N_token=1536, bf16, B200.
+"""Benchmark: ms per Pairformer block at N_token=1536 (48-block trunk), bf16, B200.
 
 A step is one forward of the 48-block Pairformer trunk (PairformerStack, c_z=128, c_s=384,
 4x32 triangle heads, c_hidden=128, transition x4, 16 single heads) over one synthetic

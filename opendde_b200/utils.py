@@ -58,7 +58,7 @@ def seeded_init_(module: torch.nn.Module, seed: int = 0, perturb_1d: bool = Fals
 
 
 def token_mask(n: int, pad_frac: float = 0.0) -> torch.Tensor:
-    """Token mask with the last ceil(pad_frac * n) tokens set to 0 (BASELINE C1: 0.1, C4: 0.07)."""
+    """Token mask with the last ceil(pad_frac * n) tokens set to 0 (config C1: 0.1, C4: 0.07)."""
     m = torch.ones(n)
     n_pad = int(math.ceil(pad_frac * n)) if pad_frac > 0 else 0
     if n_pad:

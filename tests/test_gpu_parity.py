@@ -1,6 +1,6 @@
 """CUDA path vs the reference's golden vectors and vs the CPU oracle (parity tests proper).
 
-Tolerances: fp32 mode max-abs <= 1e-4; bf16 mode relative-L2 <= 2e-2
+Tolerances (the parity contract of this path): fp32 mode max-abs <= 1e-4; bf16 mode relative-L2 <= 2e-2
 against the fp32 oracle on the same seeded inputs and weights.
 """
 import pytest
@@ -54,7 +54,7 @@ def test_fp32_edge_sizes_vs_oracle(kind, n, cuda_device):
 
 
 def test_c0_block_fp32_n128(cuda_device):
-    """one block, fp32, N=128, all-ones mask, seed-0 weights."""
+    """Config C0: one block, fp32, N=128, all-ones mask, seed-0 weights."""
     mod = module_for("block")
     params = seeded_params([(k, tuple(p.shape)) for k, p in mod.named_parameters()], seed=0)
     s, z, mask = make_inputs(128, seed=1)
