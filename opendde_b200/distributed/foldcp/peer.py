@@ -216,7 +216,52 @@ class PeerExchange(DistExchange):
         bands, bias = self._publish_and_gather(local, spec, [need], (bias_tile, transposed, bias_rows))
         return bands[0], bias
 
+    def attention_chunks(self, local: torch.Tensor, spec: FoldCPPairShardSpec, needs: Sequence[Need],
+                         bias_tile: torch.Tensor, transposed: bool, bias_rows: Range,
+                         consume: Callable[[int, torch.Tensor, torch.Tensor], None]) -> None:
+        """attention_bands for a band requested as consecutive chunks ``needs``, overlapped:
+        after the snapshot and the barrier, a side stream assembles chunk after chunk (the bias
+        rows with the first) while ``consume(i, band_i, bias)`` enqueues chunk i's compute on
+        the current stream behind chunk i's copy. Every chunk buffer is allocated before the side
+        stream forks, so no memory the current stream still uses is handed to it."""
+        plans, outs, bias = self._publish_and_plan(local, spec, needs, (bias_tile, transposed, bias_rows))
+        if local.is_cuda and any(plans):
+            main = torch.cuda.current_stream(local.device)
+            side = self._side_stream(local.device)
+            side.wait_stream(main)
+            done = []
+            with torch.cuda.stream(side):
+                for plan in plans:
+                    if plan:
+                        self._copy(plan)
+                    ev = torch.cuda.Event()
+                    ev.record(side)
+                    done.append(ev)
+            for i, out in enumerate(outs):
+                main.wait_event(done[i])
+                consume(i, out, bias)
+            return
+        for i, (plan, out) in enumerate(zip(plans, outs)):
+            if plan:
+                self._copy(plan)
+            consume(i, out, bias)
+
+    def _side_stream(self, device) -> "torch.cuda.Stream":
+        st = getattr(self, "_side", None)
+        if st is None or st.device != device:
+            st = torch.cuda.Stream(device=device)
+            self._side = st
+        return st
+
     def _publish_and_gather(self, local, spec, needs, bias_req):
+        plans, outs, bias = self._publish_and_plan(local, spec, needs, bias_req)
+        self._copy([r for plan in plans for r in plan])
+        return outs, bias
+
+    def _publish_and_plan(self, local, spec, needs, bias_req):
+        """Snapshot (and bias tile) into this rank's slot, barrier, then one copy plan per
+        requested band (the bias rows ride with the first) and the band buffers. A band inside
+        this rank's own tile is a view of the tile (empty plan)."""
         if not local.is_contiguous():
             raise ValueError("peer exchange publishes contiguous tiles")
         pos_bytes = local.element_size() * (local[0, 0].numel() if local.dim() > 2 else 1)
@@ -243,25 +288,25 @@ class PeerExchange(DistExchange):
                             ld_t * eb, bias_tile.stride(0) * eb, nx * ld_t * eb))
         self._copy(publish)
         w.barrier()
-        outs, plan = [], []
+        outs, plans = [], []
+        (mr0, mr1), (mc0, mc1) = mine
         for need in needs:
-            want = need(self.coord)
-            if want == mine:            # the band is this rank's own tile: no copy
-                outs.append(local)
+            (r0, r1), (c0, c1) = need(self.coord)
+            if mr0 <= r0 and r1 <= mr1 and mc0 <= c0 and c1 <= mc1:   # inside the own tile: a view
+                outs.append(local[r0 - mr0:r1 - mr0, c0 - mc0:c1 - mc0])
+                plans.append([])
                 continue
-            (r0, r1), (c0, c1) = want
             out = local.new_empty((r1 - r0, c1 - c0) + tuple(local.shape[2:]))
-            plan += band_copy_plan(spec, self.layout, want, ptrs, out.data_ptr(), pos_bytes)
+            plans.append(band_copy_plan(spec, self.layout, ((r0, r1), (c0, c1)), ptrs, out.data_ptr(), pos_bytes))
             outs.append(out)
         bias = None
         if bias_req is not None:
             _, transposed, rows = bias_req
             ld_b = _round8(spec.n_padded)
             bias = bias_tile.new_empty((bias_tile.shape[0], rows[1] - rows[0], ld_b))
-            plan += projection_copy_plan(spec, self.layout, rows, transposed, ptrs, tile_bytes, bias_tile.shape[0], eb,
-                                         ld_t, bias.data_ptr(), ld_b)
-        self._copy(plan)
-        return outs, bias
+            plans[0] = plans[0] + projection_copy_plan(spec, self.layout, rows, transposed, ptrs, tile_bytes,
+                                                       bias_tile.shape[0], eb, ld_t, bias.data_ptr(), ld_b)
+        return plans, outs, bias
 
     def region(self, local: torch.Tensor, spec: FoldCPPairShardSpec, need: Need) -> torch.Tensor:
         return self.bands(local, spec, [need])[0]

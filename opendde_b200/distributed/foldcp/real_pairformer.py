@@ -29,6 +29,7 @@ then the rows are all-gathered.
 
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Optional, Tuple
 
@@ -171,6 +172,21 @@ def _triatt_bias_plane(module, z_local: torch.Tensor, ctx: FoldCPPairContext, en
 
 # ------------------------------------------------------------------------------ per-op drivers
 
+OVERLAP_KEY = "OPENDDE_B200_FOLDCP_OVERLAP"
+
+
+def overlap_chunks() -> int:
+    """Row chunks of the overlapped attention band exchange (``OPENDDE_B200_FOLDCP_OVERLAP``;
+    0 or 1: one band per op, the default)."""
+    v = os.environ.get(OVERLAP_KEY, "").strip()
+    if not v:
+        return 0
+    n = int(v)
+    if n < 0:
+        raise ValueError(f"{OVERLAP_KEY} must be a chunk count >= 0, got {v!r}")
+    return n
+
+
 def _row_of(spec):
     return lambda coord: spec.row_range_of(coord[0])
 
@@ -218,6 +234,30 @@ def _triatt(module, z_local, ctx: FoldCPPairContext, ending: bool, ops) -> None:
                            dtype=ops.bias_dtype(z_local.dtype))
         ops.triatt_bias(module, view, tile)
         full = (0, n_pad)
+        chunks = overlap_chunks()
+        if chunks > 1 and hasattr(ex, "attention_chunks"):
+            # the attention rows (z rows R_r, or z columns C_c for the ending node) in chunks:
+            # chunk i's band copy on a side stream overlaps chunk i-1's attention
+            lo, hi = (c0, c1) if ending else (r0, r1)
+            step = -(-(hi - lo) // chunks)
+            parts = [(a, min(a + step, hi)) for a in range(lo, hi, step)]
+            if not ending:
+                needs = [lambda c, a=a, b=b: ((a, b), full) for a, b in parts]
+
+                def consume(i, zs, bias):
+                    a, b = parts[i]
+                    ops.triatt(module, zs, m[a:b], bias[:, :, :n_pad], z_local[a - r0:b - r0], q_col0=c0,
+                               n_q=c1 - c0, n_valid=ctx.n)
+            else:
+                needs = [lambda c, a=a, b=b: (full, (a, b)) for a, b in parts]
+
+                def consume(i, zs, bias):
+                    a, b = parts[i]
+                    ops.triatt(module, zs.transpose(0, 1), m[:, a:b].t(), bias[:, :, :n_pad],
+                               z_local[:, a - c0:b - c0].transpose(0, 1), q_col0=r0, n_q=r1 - r0, n_valid=ctx.n)
+            ex.attention_chunks(z_local, spec, needs, tile, transposed=ending,
+                                bias_rows=(r0, r1) if ending else (c0, c1), consume=consume)
+            return
         if not ending:
             zs, bias = ex.attention_bands(z_local, spec, lambda c: (spec.row_range_of(c[0]), full), tile,
                                           transposed=False, bias_rows=(c0, c1))

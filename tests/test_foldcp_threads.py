@@ -108,3 +108,20 @@ def test_cp_single_ops_reference_return_convention(shape):
     for _, got in res:
         for k in want:
             assert (got[k] - want[k]).abs().max().item() <= TOL, k
+
+
+@pytest.mark.parametrize("shape", [(1, 2), (2, 2), (2, 4)])
+@pytest.mark.parametrize("chunks", [2, 3])
+def test_cp_stack_overlapped_attention_chunks(shape, chunks, monkeypatch):
+    """The chunked attention band exchange (side-stream overlap on GPUs) computes the same
+    stack: every chunk of attention rows gets its own band and the shared bias rows."""
+    monkeypatch.setenv("OPENDDE_B200_FOLDCP_OVERLAP", str(chunks))
+    torch.manual_seed(0)
+    stack, p = _stack(1)
+    s, z, mask = _inputs(13)
+    with torch.no_grad():
+        s_ref, z_ref = O.pairformer_stack(s, z, mask, p, 1, no_heads_pair=4, n_heads=HEADS, c_s=C_S)
+        outs = _run_cp(shape, stack, s, z, mask, "peer")
+    for s_out, z_out in outs:
+        assert (z_out - z_ref).abs().max().item() <= TOL
+        assert (s_out - s_ref).abs().max().item() <= TOL
