@@ -41,3 +41,18 @@ def test_cpu_tensors_are_rejected_no_fallback():
     blk = PairformerBlock(c_z=32, c_s=0, c_hidden_mul=32, no_heads_pair=1)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         blk(None, torch.zeros(4, 4, 32), torch.ones(4, 4))
+
+
+@pytest.mark.parametrize("config", ["trunk_block", "msa_pair_stack", "msa_pair_stack_scaled", "template_stack",
+                                    "confidence_stack", "refiner_stack_scaled"])
+def test_state_dict_matches_reference_in_every_caller_configuration(config):
+    """Checkpoints of every Pairformer user load unchanged: the same state_dict keys and
+    shapes as the reference modules (tests/golden/api_shapes.json, made by
+    tests/golden/make_api_fixtures.py from the reference)."""
+    import json
+    import os
+    from opendde_b200 import model as M
+    ref = json.load(open(os.path.join(GOLDEN_DIR, "api_shapes.json")))[config]
+    mod = getattr(M, ref["class"])(**ref["kwargs"])
+    got = {k: list(v.shape) for k, v in mod.state_dict().items()}
+    assert got == ref["params"]
