@@ -8,9 +8,11 @@ square mesh: a band request works for any R x C grid, and the ending-node / inco
 read column bands through transposed views instead of transposing z across ranks.
 
 An exchange object carries the transport: ``DistExchange`` runs over torch.distributed
-(NCCL on GPUs, gloo on CPU). The drivers only call ``region`` and ``all_gather``; the band of
-a rank's own mesh row (or column) is an all-gather over the row (column) group, the other
-bands are point-to-point batches.
+(NCCL on GPUs, gloo on CPU): the band of a rank's own mesh row (or column) is an all-gather
+over the row (column) group, the other bands are point-to-point batches. ``PeerExchange``
+(``peer.py``, the default on NCCL meshes) serves the same requests from the peers' memory over
+NVLink. The drivers ask for bands through ``gather_bands`` (and the peer transport's
+projection / attention variants) and for collectives through ``all_gather``.
 """
 
 from __future__ import annotations
