@@ -221,6 +221,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n", type=int, default=N_TOKEN)
+    ap.add_argument("--pad-frac", type=float, default=0.0,
+                    help="fraction of trailing tokens masked as padding (config C4: 0.07)")
     ap.add_argument("--blocks", type=int, default=48)
     ap.add_argument("--cpu-rows", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -277,7 +279,7 @@ def main():
     stack = PairformerStack(n_blocks=args.blocks, n_heads=N_SINGLE_HEADS, c_z=C_Z, c_s=C_S)
     seeded_init_(stack, seed=0)
     stack = stack.to(dev)
-    s0, z0, m0 = make_inputs(args.n, c_z=C_Z, c_s=C_S, seed=1)
+    s0, z0, m0 = make_inputs(args.n, c_z=C_Z, c_s=C_S, seed=1, pad_frac=args.pad_frac)
     z_dev = z0.to(dev, torch.bfloat16)
     s_dev = s0.to(dev, torch.bfloat16)
     m_dev = m0.to(dev)
@@ -441,6 +443,7 @@ def main():
             "data": "synthetic: z,s ~ N(0,1), all-ones mask, seed-0 N(0,1/fan_in) weights",
             "config": {"workload": f"pairformer_trunk_{args.blocks}blk_N{args.n}_bf16", "n_token": args.n,
                        "c_z": C_Z, "c_s": C_S, "blocks": args.blocks, "grid": f"{grid[0]}x{grid[1]}",
+                       "pad_frac": args.pad_frac,
                        "l2": "inputs larger than L2 (pair tensor 604 MB)"},
             "e2e": {"value": ms_e2e / args.blocks, "unit": "ms/block", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
