@@ -87,6 +87,12 @@ PF_API int pf_device_status(int* status_out, int clear);
 PF_API long long pf_launch_count(void);
 PF_API int pf_profile_enable(int on);
 PF_API int pf_profile_report(char* buf, size_t len);
+/* Self-test of the failure path of the bounded device-side waits (no reference counterpart):
+ * one thread waits on an mbarrier that nothing arrives on, gives up after limit_ns
+ * (1 ms .. 10 s), sets bit 0 of the device status word and returns; no fault, the context stays
+ * usable. Read and clear the word with pf_device_status before the next library call (a set
+ * word makes every other bounded wait give up at once). */
+PF_API int pf_selftest_bounded_wait(int64_t limit_ns, void* stream);
 
 /* ---- LayerNorm ------------------------------------------------------------------------
  * y[r, :] = (x[r, :] - mean) / sqrt(var + eps) * gamma + beta over the last dim c.

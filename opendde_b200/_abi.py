@@ -37,7 +37,7 @@ _STATUS_NAMES = {
 # Every symbol the header declares (checked by tests/test_abi_symbols.py).
 EXPORTED = (
     "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path", "pf_device_status",
-    "pf_launch_count", "pf_profile_enable", "pf_profile_report",
+    "pf_launch_count", "pf_profile_enable", "pf_profile_report", "pf_selftest_bounded_wait",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
     "pf_trimul_project_workspace_size", "pf_trimul_project", "pf_trimul_combine_workspace_size",
@@ -118,6 +118,7 @@ def load(path: str = LIB_PATH):
         "pf_launch_count": ([], ctypes.c_longlong),
         "pf_profile_enable": ([c_int], c_int),
         "pf_profile_report": ([ctypes.c_char_p, c_size_t], c_int),
+        "pf_selftest_bounded_wait": ([c_int64, c_void_p], c_int),
         "pf_layernorm_fwd": ([c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_float, c_int32, c_void_p], c_int),
         "pf_trimul_workspace_size": ([c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_trimul_fwd": ([POINTER(TrimulParams), PairView, PairView, MaskView, MaskView, PairView, PairView,
