@@ -176,6 +176,9 @@ def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
     w = _WINDOWS.get(id(mesh))
     if w is not None and w.slot_bytes >= need and w.device == device:
         return w
+    if torch.cuda.is_current_stream_capturing():
+        raise RuntimeError("Fold-CP peer windows must be allocated before CUDA graph capture: run one "
+                           "eager step of the same shapes first")
     if w is not None:
         w.release()
     w = PeerWindows(mesh.group_2d, mesh.cp_rank, mesh.layout.numel, need, device)
