@@ -78,13 +78,10 @@ int pf_layernorm_fwd(const void* x, void* y, const float* gamma, const float* be
   if (!x || !y) return fail(PF_EINVAL_ARG, "layernorm: null input/output");
   if (rows < 0 || c <= 0 || c > 1024) return fail(PF_EINVAL_SHAPE, "layernorm: rows=%lld c=%d", (long long)rows, c);
   if (rows == 0) return PF_OK;
-  cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == PF_BF16 && !force_simt() && tc::layernorm_supported(c, x, y)) {
-    set_path("tc");
-    return tc::layernorm_bf16(x, y, gamma, beta, rows, c, eps, st);
-  }
+  // LayerNorm is fused into every producing tensor-core kernel; the standalone entry point runs
+  // the vectorised warp-per-row kernel in both dtypes (HBM-bound, no MMA to feed).
   set_path("simt");
-  return simt::layernorm(x, y, gamma, beta, rows, c, eps, dtype, st);
+  return simt::layernorm(x, y, gamma, beta, rows, c, eps, dtype, (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------ triangle multiplication

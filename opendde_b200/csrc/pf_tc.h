@@ -7,10 +7,6 @@
 namespace pf {
 namespace tc {
 
-bool layernorm_supported(int c, const void* x, const void* y);
-int layernorm_bf16(const void* x, void* y, const float* g, const float* b, int64_t rows, int c,
-                   float eps, cudaStream_t st);
-
 bool trimul_supported(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
 size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h);
 int trimul(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_mask_view ma,
