@@ -119,18 +119,6 @@ class DistExchange:
         return torch.stack(parts, 0)
 
 
-def row_band(ex, local, spec: FoldCPPairShardSpec, rows_of: Callable[[Tuple[int, int]], Range]) -> torch.Tensor:
-    """Rows ``rows_of(coord)`` x all padded columns."""
-    full = (0, spec.n_padded)
-    return ex.region(local, spec, lambda c: (rows_of(c), full))
-
-
-def col_band(ex, local, spec: FoldCPPairShardSpec, cols_of: Callable[[Tuple[int, int]], Range]) -> torch.Tensor:
-    """All padded rows x columns ``cols_of(coord)``."""
-    full = (0, spec.n_padded)
-    return ex.region(local, spec, lambda c: (full, cols_of(c)))
-
-
 def own_row_band(ex, local: torch.Tensor) -> torch.Tensor:
     """This rank's mesh-row band (rows R_r x all padded columns), gathered over the row group
     (one all-gather of the tiles, then one reorder into row-major)."""
