@@ -78,6 +78,11 @@ PF_API const char* pf_last_path(void);
  * device (it copies the word to the host); clear != 0 resets it. No reference counterpart
  * (the reference has no device-side waits). */
 PF_API int pf_device_status(int* status_out, int clear);
+/* Stream-ordered copy of the same word into dst (pinned host or device memory, 4 bytes) on
+ * `stream`, without synchronising: a caller checks dst once the copy has completed (e.g. at its
+ * next call), so a timed-out wait is reported without adding a device synchronisation to every
+ * forward. No reference counterpart. */
+PF_API int pf_device_status_async(unsigned int* dst, void* stream);
 /* Measurement hooks (no reference counterpart; the reference times whole stages with
  * host wall clocks, opendde/distributed/foldcp/metrics.py:136-234):
  * pf_launch_count  -- number of kernels this library has launched in the process;

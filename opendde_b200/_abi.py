@@ -37,6 +37,7 @@ _STATUS_NAMES = {
 # Every symbol the header declares (checked by tests/test_abi_symbols.py).
 EXPORTED = (
     "pf_abi_version", "pf_last_error_string", "pf_set_option", "pf_last_path", "pf_device_status",
+    "pf_device_status_async",
     "pf_launch_count", "pf_profile_enable", "pf_profile_report", "pf_selftest_bounded_wait",
     "pf_layernorm_fwd",
     "pf_trimul_workspace_size", "pf_trimul_fwd",
@@ -115,6 +116,7 @@ def load(path: str = LIB_PATH):
         "pf_last_path": ([], c_char_p),
         "pf_set_option": ([c_int, c_int64], c_int),
         "pf_device_status": ([POINTER(c_int), c_int], c_int),
+        "pf_device_status_async": ([c_void_p, c_void_p], c_int),
         "pf_launch_count": ([], ctypes.c_longlong),
         "pf_profile_enable": ([c_int], c_int),
         "pf_profile_report": ([ctypes.c_char_p, c_size_t], c_int),
@@ -186,7 +188,52 @@ def device_status(clear: bool = False) -> int:
     """Read (and optionally clear) the device status word; synchronises the device."""
     v = c_int(0)
     check(load().pf_device_status(ctypes.byref(v), 1 if clear else 0))
+    if clear:  # forget copies taken before the clear
+        for w in _WATCH.values():
+            w.buf.zero_()
+            w.event = None
     return int(v.value)
+
+
+class _StatusWatch:
+    """A pinned host copy of one device's status word, refreshed stream-ordered."""
+
+    def __init__(self):
+        import torch
+        self.buf = torch.zeros(1, dtype=torch.int32).pin_memory()
+        self.event = None
+
+
+_WATCH = {}
+
+TIMEOUT_MESSAGE = ("a device-side bounded wait of an opendde_b200 kernel timed out: the outputs of the "
+                   "launches since then are invalid (the kernels drained instead of hanging). The status "
+                   "word stays set until it is cleared with device_status(clear=True).")
+
+
+def status_checkpoint(device) -> None:
+    """Raise if a copy of ``device``'s status word made at an earlier checkpoint has completed
+    and shows a timed-out wait, then enqueue a fresh copy on the current stream.
+
+    No device synchronisation: a timed-out wait is reported at the first checkpoint after the
+    copy that saw it completes, i.e. at most one checkpoint late. Skipped inside CUDA graph
+    capture (a captured graph's caller checks with :func:`device_status`).
+    """
+    import torch
+    if torch.cuda.is_current_stream_capturing():
+        return
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _WATCH.get(idx)
+    if w is None:
+        w = _WATCH[idx] = _StatusWatch()
+    if w.event is not None and w.event.query() and int(w.buf[0]) != 0:
+        w.event = None
+        raise PFError(PF_ETIMEOUT, TIMEOUT_MESSAGE)
+    if w.event is None or w.event.query():
+        stream = torch.cuda.current_stream(device)
+        check(load().pf_device_status_async(w.buf.data_ptr(), stream.cuda_stream))
+        w.event = torch.cuda.Event()
+        w.event.record(stream)
 
 
 def launch_count() -> int:

@@ -136,11 +136,11 @@ int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_
                   int64_t rs, cudaStream_t st) {
   if (z.row_stride % 8 || z.col_stride % 8 || ((uintptr_t)z.ptr) % 16)
     return fail(PF_EINVAL_SHAPE, "bf16 pair views need 16-byte alignment and strides multiple of 8 elements");
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<unsigned long long> attr_done{0};
+  PF_TRY(once_per_device(attr_done, []() -> int {
     PF_CUDA_TRY(cudaFuncSetAttribute(k_apb_bias, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(APB_SMEM + 1024)));
-    attr = true;
-  }
+    return PF_OK;
+  }));
   unsigned int* status;
   PF_TRY(device_status_ptr(&status));
   CUtensorMap tz, tw;

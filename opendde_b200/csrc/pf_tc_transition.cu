@@ -281,11 +281,11 @@ int transition(const pf_transition_params* p, const void* x, int64_t xs, void* o
                int, int, int acc, cudaStream_t st) {
   if (xs % 8 || os % 8 || ((uintptr_t)x) % 16 || ((uintptr_t)out) % 16)
     return fail(PF_EINVAL_SHAPE, "bf16 transition rows must be 16-byte aligned (row strides multiple of 8)");
-  static bool attr = false;
-  if (!attr) {
+  static std::atomic<unsigned long long> attr_done{0};
+  PF_TRY(once_per_device(attr_done, []() -> int {
     PF_CUDA_TRY(cudaFuncSetAttribute(k_transition, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(TR_SMEM + 1024)));
-    attr = true;
-  }
+    return PF_OK;
+  }));
   unsigned int* status;
   PF_TRY(device_status_ptr(&status));
   CUtensorMap tx, twa, twb, two;

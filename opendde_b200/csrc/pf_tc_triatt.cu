@@ -544,15 +544,15 @@ int set_smem(K kernel, uint32_t bytes) {
   return PF_OK;
 }
 
+// Dynamic shared-memory limits, set once on every device that runs these kernels.
 int ensure_attrs() {
-  static bool done = false;
-  if (!done) {
+  static std::atomic<unsigned long long> done{0};
+  return once_per_device(done, []() -> int {
     PF_TRY(set_smem(k_triatt_proj, PROJ_SMEM + 1024));
     PF_TRY(set_smem(k_triatt_core, CORE3_SMEM + 1024));
     PF_TRY(set_smem(k_triatt_out, OUT_SMEM + 1024));
-    done = true;
-  }
-  return PF_OK;
+    return PF_OK;
+  });
 }
 
 struct TriattWs {

@@ -668,15 +668,15 @@ size_t trimul_ws_bytes(int64_t n_i, int64_t n_j, int64_t n_k, int, int) {
 
 namespace {
 
+// Dynamic shared-memory limits, set once on every device that runs these kernels.
 int ensure_attrs() {
-  static bool attrs = false;
-  if (!attrs) {
+  static std::atomic<unsigned long long> done{0};
+  return once_per_device(done, []() -> int {
     PF_TRY(set_smem(k_trimul_proj, PROJ_SMEM + 1024));
     PF_TRY(set_smem(k_trimul_bgemm, GEMM_SMEM + 1024));
     PF_TRY(set_smem(k_trimul_out, OUT_SMEM + 1024));
-    attrs = true;
-  }
-  return PF_OK;
+    return PF_OK;
+  });
 }
 
 // a(ch, i, k) = projection of za(i, k) (i < n_i), b(ch, j, k) of zb(j, k) (j < n_j), stored

@@ -50,16 +50,23 @@ int device_status_ptr(unsigned int** out) {
 }
 
 int64_t sm_count() {
-  static int n[64] = {0};
+  static std::atomic<int> n[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (n[dev] == 0) {
-    int v = 0;
+  int v = n[dev].load(std::memory_order_relaxed);
+  if (v == 0) {
     cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
-    n[dev] = v > 0 ? v : 148;
+    if (v <= 0) v = 148;
+    n[dev].store(v, std::memory_order_relaxed);
   }
-  return n[dev];
+  return v;
+}
+
+int current_device(int* dev) {
+  PF_CUDA_TRY(cudaGetDevice(dev));
+  if (*dev < 0 || *dev >= 64) return fail(PF_EUNSUPPORTED, "device ordinal %d out of range (< 64)", *dev);
+  return PF_OK;
 }
 
 }  // namespace pf
@@ -74,5 +81,13 @@ extern "C" PF_API int pf_device_status(int* status_out, int clear) {
     PF_CUDA_TRY(cudaMemcpyToSymbol(g_device_status, &z, sizeof(z)));
   }
   *status_out = (int)v;
+  return PF_OK;
+}
+
+extern "C" PF_API int pf_device_status_async(unsigned int* dst, void* stream) {
+  using namespace pf;
+  if (!dst) return fail(PF_EINVAL_ARG, "dst is NULL");
+  PF_CUDA_TRY(cudaMemcpyFromSymbolAsync(dst, g_device_status, sizeof(unsigned int), 0, cudaMemcpyDefault,
+                                        (cudaStream_t)stream));
   return PF_OK;
 }

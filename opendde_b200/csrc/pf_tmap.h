@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace pf {
 
 // Encode a tiled tensor map. dims[0] is the contiguous dim; strides_bytes has rank-1
@@ -20,5 +22,25 @@ int device_status_ptr(unsigned int** out);
 
 // Number of SMs of the current device (persistent grids are sized by it).
 int64_t sm_count();
+
+// Ordinal of the current device, checked against the per-device tables (< 64).
+int current_device(int* dev);
+
+// Runs `fn` (returning a pf_status) once per device, with that device current. Kernel
+// attributes such as the dynamic shared-memory limit are per device, so a process that drives
+// several GPUs needs them set on each. Thread-safe: racing first calls may both run `fn`,
+// which only repeats idempotent attribute settings.
+template <class F>
+int once_per_device(std::atomic<unsigned long long>& done, F&& fn) {
+  int dev = 0;
+  int st = current_device(&dev);
+  if (st != 0) return st;
+  const unsigned long long bit = 1ull << dev;
+  if (done.load(std::memory_order_acquire) & bit) return 0;
+  st = fn();
+  if (st != 0) return st;
+  done.fetch_or(bit, std::memory_order_acq_rel);
+  return 0;
+}
 
 }  // namespace pf

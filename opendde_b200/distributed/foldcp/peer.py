@@ -166,14 +166,22 @@ class PeerWindows:
         self.own = 0
 
 
-_WINDOWS: Dict[int, PeerWindows] = {}
+# Keyed by the CP process group and this rank's place in it. The key holds the group object
+# itself, so a group that is still cached is never collected and its identity never reused by a
+# new group; a new mesh over the same group reuses the same windows.
+_WINDOWS: Dict[tuple, PeerWindows] = {}
+
+
+def _window_key(mesh) -> tuple:
+    return (mesh.group_2d, mesh.cp_rank)
 
 
 def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
     """The mesh's cached windows with slots of at least ``slot_bytes``, grown (collectively:
     every rank asks for the same size at the same op) when a larger request arrives."""
     need = _slot_bytes(slot_bytes)
-    w = _WINDOWS.get(id(mesh))
+    key = _window_key(mesh)
+    w = _WINDOWS.get(key)
     if w is not None and w.slot_bytes >= need and w.device == device:
         return w
     if torch.cuda.is_current_stream_capturing():
@@ -182,7 +190,7 @@ def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
     if w is not None:
         w.release()
     w = PeerWindows(mesh.group_2d, mesh.cp_rank, mesh.layout.numel, need, device)
-    _WINDOWS[id(mesh)] = w
+    _WINDOWS[key] = w
     return w
 
 

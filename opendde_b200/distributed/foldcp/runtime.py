@@ -10,6 +10,7 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from ... import _abi
 from .config import FoldCPConfig
 from .mesh import FoldCPProcessMesh
 from .pair_sharding import shard_pair_tensor
@@ -39,12 +40,16 @@ def stack_forward(stack, s: Optional[torch.Tensor], z: torch.Tensor, pair_mask: 
     _check(z)
     mesh = current_mesh()
     if s is not None and stack.blocks and getattr(stack.blocks[0], "c_s", 0) > 0:
-        return distributed_pairformer_stack_single_bridge_update(
+        out = distributed_pairformer_stack_single_bridge_update(
             stack, s, z, mesh, pair_mask=pair_mask, extra_attn_bias=extra_attn_bias)
+        _abi.status_checkpoint(z.device)
+        return out
     z_local, spec = shard_pair_tensor(z, mesh, pair_dims=(-3, -2))
     ctx = make_context(mesh, z_local, spec, mask_full=pair_mask)
     z_local = distributed_pairformer_stack_pair_update(stack, z_local, mesh, context=ctx)
-    return s, gather_full(z_local, ctx)
+    out = s, gather_full(z_local, ctx)
+    _abi.status_checkpoint(z.device)
+    return out
 
 
 def block_pair_only(block, s: Optional[torch.Tensor], z: torch.Tensor, pair_mask: Optional[torch.Tensor],
@@ -54,4 +59,6 @@ def block_pair_only(block, s: Optional[torch.Tensor], z: torch.Tensor, pair_mask
     z_local, spec = shard_pair_tensor(z, mesh, pair_dims=(-3, -2))
     ctx = make_context(mesh, z_local, spec, mask_full=pair_mask)
     z_local = distributed_pairformer_block_pair_update(block, z_local, mesh, context=ctx)
-    return s, gather_full(z_local, ctx)
+    out = s, gather_full(z_local, ctx)
+    _abi.status_checkpoint(z.device)
+    return out

@@ -6,6 +6,11 @@ pair_transition, then (c_s > 0) s += AttentionPairBias(s, z); s += single Transi
 Every pair update is fused with its residual add and written in place into one working
 copy of ``z``; the ending-node attention reads and writes transposed *views* (no physical
 transposes, unlike the reference's two ``.transpose().contiguous()`` copies).
+
+Each forward ends with a status checkpoint: if a device-side bounded wait of an earlier launch
+timed out (its outputs are invalid), the forward raises ``PFError`` (``PF_ETIMEOUT``) instead of
+returning; the check reads a copy of the device status word made without synchronising, so it
+reports the timeout at most one forward late.
 """
 
 from __future__ import annotations
@@ -17,7 +22,7 @@ import torch
 import torch.distributed as dist
 import torch.nn as nn
 
-from .. import kernels
+from .. import _abi, kernels
 from .primitives import Transition
 from .transformer import AttentionPairBias
 from .triangular import (
@@ -109,6 +114,7 @@ class PairformerBlock(nn.Module):
                 e = extra_attn_bias.to(device=bias.device, dtype=torch.float32)
                 bias = (bias + (e if e.dim() == 3 else e[None])).contiguous()
             s = self.single_updates(s, zw if bias is None else None, bias)
+        _abi.status_checkpoint(zw.device)
         return s, zw
 
 
@@ -157,4 +163,5 @@ class PairformerStack(nn.Module):
                     e = extra_attn_bias.to(device=bias.device, dtype=torch.float32)
                     bias = (bias + (e if e.dim() == 3 else e[None])).contiguous()
                 s = block.single_updates(s, zw if bias is None else None, bias)
+        _abi.status_checkpoint(zw.device)
         return s, zw
