@@ -74,7 +74,10 @@ PF_API int pf_set_option(int option, int64_t value);
 /* Name of the kernel family the last call on this thread dispatched to ("tc" or "simt"). */
 PF_API const char* pf_last_path(void);
 /* Device status word of the current device: bit 0 = a bounded device-side wait (mbarrier
- * pipeline wait) gave up; the kernel then drained instead of hanging. Synchronises with the
+ * pipeline wait) gave up; the kernel then drained instead of hanging. Bit 1 = a bf16
+ * triangle-attention logit exceeded the f16 range of the logit accumulator (the affected rows
+ * are invalid). The word is sticky: while it is non-zero every later tensor-core kernel drains
+ * at once and leaves its outputs unwritten, so callers must check it. Synchronises with the
  * device (it copies the word to the host); clear != 0 resets it. No reference counterpart
  * (the reference has no device-side waits). */
 PF_API int pf_device_status(int* status_out, int clear);

@@ -206,9 +206,18 @@ class _StatusWatch:
 
 _WATCH = {}
 
-TIMEOUT_MESSAGE = ("a device-side bounded wait of an opendde_b200 kernel timed out: the outputs of the "
-                   "launches since then are invalid (the kernels drained instead of hanging). The status "
-                   "word stays set until it is cleared with device_status(clear=True).")
+STATUS_BITS = {
+    1: "a device-side bounded wait of an opendde_b200 kernel timed out (the kernels drained instead of "
+       "hanging)",
+    2: "a triangle-attention logit exceeded the f16 range of the bf16 path's logit accumulator "
+       "(|q.k| log2(e)/sqrt(d) > 65504); run such inputs in fp32 mode",
+}
+
+
+def status_message(word: int) -> str:
+    what = "; ".join(m for b, m in STATUS_BITS.items() if word & b) or f"status word {word:#x}"
+    return (f"{what}: the outputs of the launches since then are invalid. The status word stays set "
+            "until it is cleared with device_status(clear=True).")
 
 
 def status_checkpoint(device) -> None:
@@ -227,8 +236,9 @@ def status_checkpoint(device) -> None:
     if w is None:
         w = _WATCH[idx] = _StatusWatch()
     if w.event is not None and w.event.query() and int(w.buf[0]) != 0:
+        word = int(w.buf[0])
         w.event = None
-        raise PFError(PF_ETIMEOUT, TIMEOUT_MESSAGE)
+        raise PFError(PF_ETIMEOUT, status_message(word))
     if w.event is None or w.event.query():
         stream = torch.cuda.current_stream(device)
         check(load().pf_device_status_async(w.buf.data_ptr(), stream.cuda_stream))

@@ -79,7 +79,8 @@ int pf_layernorm_fwd(const void* x, void* y, const float* gamma, const float* be
   if (rows < 0 || c <= 0 || c > 1024) return fail(PF_EINVAL_SHAPE, "layernorm: rows=%lld c=%d", (long long)rows, c);
   if (rows == 0) return PF_OK;
   // LayerNorm is fused into every producing tensor-core kernel; the standalone entry point runs
-  // the vectorised warp-per-row kernel in both dtypes (HBM-bound, no MMA to feed).
+  // a row kernel with 128-bit loads and stores in both dtypes (HBM-bound, no MMA to feed), or
+  // the scalar warp-per-row kernel when rows are not whole 16-byte vectors.
   set_path("simt");
   return simt::layernorm(x, y, gamma, beta, rows, c, eps, dtype, (cudaStream_t)stream);
 }

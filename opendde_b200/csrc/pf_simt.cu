@@ -74,6 +74,113 @@ __global__ void k_ln_view(const T* __restrict__ x, int64_t rs, int64_t cs, int64
   }
 }
 
+// Standalone LayerNorm of contiguous rows with 128-bit accesses: each row is read and written
+// as 16-byte vectors (8 bf16 or 4 fp32 channels), L = 2^k <= 32 lanes per row (the largest
+// power of two not above the row's vector count), 32 / L rows per warp; the row stays in
+// registers between the two statistics passes (mean, then centred variance) and the output
+// pass, so x is read from HBM once. Requires c * sizeof(T) % 16 == 0 and 16-byte aligned
+// pointers (checked by the host).
+template <class T>
+struct VecTraits;
+template <>
+struct VecTraits<float> {
+  static constexpr int E = 4;
+  __device__ static void unpack(const uint4& u, float (&f)[4]) {
+    f[0] = __uint_as_float(u.x); f[1] = __uint_as_float(u.y); f[2] = __uint_as_float(u.z); f[3] = __uint_as_float(u.w);
+  }
+  __device__ static uint4 pack(const float (&f)[4]) {
+    return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+  }
+};
+template <>
+struct VecTraits<__nv_bfloat16> {
+  static constexpr int E = 8;
+  __device__ static void unpack(const uint4& u, float (&f)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = __uint_as_float(w[i] << 16);
+      f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+  __device__ static uint4 pack(const float (&f)[8]) {
+    uint32_t w[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 v = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+      w[i] = *reinterpret_cast<uint32_t*>(&v);
+    }
+    return make_uint4(w[0], w[1], w[2], w[3]);
+  }
+};
+
+template <class T, int L>
+__global__ void __launch_bounds__(256) k_layernorm_rows(const T* __restrict__ x, T* __restrict__ y, int64_t rows,
+                                                        int c, const float* __restrict__ gamma,
+                                                        const float* __restrict__ beta, float eps) {
+  constexpr int E = VecTraits<T>::E;
+  // vectors per lane: L < 32 is chosen only for rows of fewer than 2L vectors; L = 32 up to c = 1024
+  constexpr int MAXV = L < 32 ? 2 : (1024 / E) / 32;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane & (L - 1);
+  const int64_t row = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * (32 / L) + lane / L;
+  const bool live = row < rows;
+  const int nv = c / E;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (live ? row : 0) * (int64_t)c);
+  uint4 raw[MAXV];
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    const int v = sub + t * L;
+    raw[t] = (live && v < nv) ? __ldg(xr + v) : make_uint4(0, 0, 0, 0);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    float f[E];
+    VecTraits<T>::unpack(raw[t], f);
+#pragma unroll
+    for (int e = 0; e < E; ++e) sum += f[e];
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+  const float mean = sum / (float)c;
+  float sq = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (sub + t * L < nv) {
+      float f[E];
+      VecTraits<T>::unpack(raw[t], f);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        const float d = f[e] - mean;
+        sq += d * d;
+      }
+    }
+  }
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float rstd = rsqrtf(sq / (float)c + eps);
+  if (!live) return;
+  uint4* yr = reinterpret_cast<uint4*>(y + row * (int64_t)c);
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    const int v = sub + t * L;
+    if (v < nv) {
+      float f[E];
+      VecTraits<T>::unpack(raw[t], f);
+      const int ch0 = v * E;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        float o = (f[e] - mean) * rstd;
+        if (gamma) o *= __ldg(gamma + ch0 + e);
+        if (beta) o += __ldg(beta + ch0 + e);
+        f[e] = o;
+      }
+      yr[v] = VecTraits<T>::pack(f);
+    }
+  }
+}
+
 // C[b](m, n) = alpha * sum_k A[b](m, k) * B[b](n, k)  (+ C if accumulate)
 // A(m,k) = A + b*sAb + m*sAm + k ; B(n,k) = B + b*sBb + n*sBn + k ;
 // C(m,n) = C + b*sCb + m*sCm + n*sCn.
@@ -443,8 +550,41 @@ static int gemm(const TA* A, int64_t sAb, int64_t sAm, const TB* B, int64_t sBb,
   return PF_OK;
 }
 
+template <class T, int L>
+static int ln_rows_launch(const T* x, T* y, int64_t rows, int c, const float* g, const float* b, float eps,
+                          cudaStream_t st) {
+  const int64_t rows_per_block = 8 * (32 / L);
+  const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > 0x7FFFFFFF) return fail(PF_EUNSUPPORTED, "LayerNorm: %lld rows is too many", (long long)rows);
+  {
+    PF_LAUNCH_SCOPE(st, "k_layernorm_rows");
+    k_layernorm_rows<T, L><<<(unsigned)blocks, 256, 0, st>>>(x, y, rows, c, g, b, eps);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+template <class T>
+static int ln_rows(const T* x, T* y, int64_t rows, int c, const float* g, const float* b, float eps,
+                   cudaStream_t st) {
+  const int nv = c * (int)sizeof(T) / 16;
+  if (nv >= 32) return ln_rows_launch<T, 32>(x, y, rows, c, g, b, eps, st);
+  if (nv >= 16) return ln_rows_launch<T, 16>(x, y, rows, c, g, b, eps, st);
+  if (nv >= 8) return ln_rows_launch<T, 8>(x, y, rows, c, g, b, eps, st);
+  if (nv >= 4) return ln_rows_launch<T, 4>(x, y, rows, c, g, b, eps, st);
+  if (nv >= 2) return ln_rows_launch<T, 2>(x, y, rows, c, g, b, eps, st);
+  return ln_rows_launch<T, 1>(x, y, rows, c, g, b, eps, st);
+}
+
 int layernorm(const void* x, void* y, const float* g, const float* b, int64_t rows, int c,
               float eps, int dtype, cudaStream_t st) {
+  const size_t esz = dtype == PF_F32 ? 4 : 2;
+  const bool vec = (c * esz) % 16 == 0 && ((uintptr_t)x) % 16 == 0 && ((uintptr_t)y) % 16 == 0;
+  if (vec) {
+    if (dtype == PF_F32) return ln_rows<float>((const float*)x, (float*)y, rows, c, g, b, eps, st);
+    return ln_rows<__nv_bfloat16>((const __nv_bfloat16*)x, (__nv_bfloat16*)y, rows, c, g, b, eps, st);
+  }
+  // channel counts whose rows are not whole 16-byte vectors: the warp-per-row scalar kernel
   if (dtype == PF_F32)
     return ln_view<float, float>((const float*)x, c, 0, rows, 1, c, g, b, eps, (float*)y, c, st);
   return ln_view<__nv_bfloat16, __nv_bfloat16>((const __nv_bfloat16*)x, c, 0, rows, 1, c, g, b,

@@ -12,9 +12,11 @@ namespace pf {
 namespace sm100 {
 
 // ------------------------------------------------------------------ status word
-// Bit 0: a bounded wait gave up. Once set, every later bounded wait in the process returns
-// at once, so a faulty pipeline drains instead of spinning; the host reads the word with
-// pf_device_status().
+// Bit 0: a bounded wait gave up. Once it is set, every later bounded wait in the process
+// returns at once, so a faulty pipeline drains instead of spinning. Bit 1: a triangle-attention
+// logit overflowed the f16 logit accumulator (reported only; the kernels run to completion).
+// The host reads the word with pf_device_status() (or a stream-ordered copy,
+// pf_device_status_async) and clears it.
 struct DeviceStatus {
   unsigned int* word;
 };
@@ -55,15 +57,15 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity. Returns false (and sets the status
-// word) when the limit passes or an earlier wait anywhere already gave up.
+// Bounded wait for the phase with the given parity. Returns false (and sets status bit 0)
+// when the limit passes or an earlier wait anywhere already gave up (bit 0 already set).
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* status,
                                           unsigned long long limit_ns = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (*(volatile unsigned int*)status != 0u) return false;
+    if ((*(volatile unsigned int*)status & 1u) != 0u) return false;
     if (globaltimer() - t0 > limit_ns) {
       atomicOr(status, 1u);
       return false;

@@ -476,6 +476,9 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
       if (lane == 0) mbar_arrive(bar_of);
       ++n;
       const int64_t j = (int64_t)it.jt * TILE + row_tid;
+      // A logit past the f16 range (|q.k| log2(e)/sqrt(d) > 65504) turns the row sum into inf
+      // or NaN: report it (status bit 1) instead of returning a silently wrong row.
+      if (j < a.n_q && !(__uint_as_float(lv[0]) <= 3.0e38f)) atomicOr(a.status, 2u);
       if (j < a.n_q) {
         const float l = __uint_as_float(lv[0]);
         const float inv = l > 0.f ? 1.0f / l : 0.f;
