@@ -109,12 +109,25 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------ CPU sample
-def cpu_block_sample_ms(n: int, rows: int, threads: int) -> float:
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def cpu_block_sample_ms(n: int, rows: int, threads: int, z_full=None) -> float:
     """The reference algorithm on the host (oracle restatement, fp32 torch CPU), one block.
 
-    Every op of the block is row-separable: rows [0, rows) of each op's output are computed
-    with everything they need (the O(N^2) projections for those rows, and the full-K
-    contraction / full-key attention for them), and the time is scaled by n / rows.
+    Every op of the block is row-separable once its O(N^2) shared operands exist: rows
+    [0, rows) of each op's output are computed with everything they need (the projections of
+    those rows, the full-K contraction and full-key attention for them) and timed x n / rows;
+    the triangle update's second operand (b over all N^2 positions, which every output row
+    contracts with) is projected once, in full, and timed unscaled.
     """
     from oracle import pairformer_oracle as O
     from opendde_b200.utils import seeded_params
@@ -125,8 +138,9 @@ def cpu_block_sample_ms(n: int, rows: int, threads: int) -> float:
     p = seeded_params([(k, tuple(v.shape)) for k, v in blk.named_parameters()], seed=0)
     sub = lambda pre: {k[len(pre) + 1:]: v for k, v in p.items() if k.startswith(pre + ".")}  # noqa: E731
     g = torch.Generator().manual_seed(1)
-    zr = torch.randn((rows, n, C_Z), generator=g)
-    bfull = torch.empty((C_H, n, n)).uniform_(-1, 1, generator=g)  # stands in for the projected b
+    if z_full is None:
+        z_full = torch.randn((n, n, C_Z), generator=g)
+    zr = z_full[:rows]
     bias = torch.empty((HEADS_PAIR, n, n)).uniform_(-1, 1, generator=g)
     s = torch.randn((n, C_S), generator=g)
     mask = torch.ones((rows, n))
@@ -135,15 +149,21 @@ def cpu_block_sample_ms(n: int, rows: int, threads: int) -> float:
     with torch.no_grad():
         for pre in ("tri_mul_out", "tri_mul_in"):
             q = sub(pre)
+            # b over every position (each output row contracts with all of it): once, unscaled
+            t0 = time.perf_counter()
+            zf = O.layer_norm(z_full, q["layer_norm_in.weight"], q["layer_norm_in.bias"])
+            bfull = (torch.sigmoid(O.linear(zf, q["linear_b_g.weight"])) *
+                     O.linear(zf, q["linear_b_p.weight"])).permute(2, 0, 1)       # [c_h, j, k]
+            t += time.perf_counter() - t0
+            del zf
             t0 = time.perf_counter()
             zn = O.layer_norm(zr, q["layer_norm_in.weight"], q["layer_norm_in.bias"])
             a = mask[..., None] * torch.sigmoid(O.linear(zn, q["linear_a_g.weight"])) * O.linear(zn, q["linear_a_p.weight"])
-            b = mask[..., None] * torch.sigmoid(O.linear(zn, q["linear_b_g.weight"])) * O.linear(zn, q["linear_b_p.weight"])
             x = torch.matmul(a.permute(2, 0, 1), bfull.transpose(-1, -2)).permute(1, 2, 0)
             x = O.layer_norm(x, q["layer_norm_out.weight"], q["layer_norm_out.bias"])
             x = O.linear(x, q["linear_z.weight"]) * torch.sigmoid(O.linear(zn, q["linear_g.weight"]))
             t += (time.perf_counter() - t0) * scale
-            del a, b, x
+            del a, x, bfull
         for pre in ("tri_att_start", "tri_att_end"):
             q = sub(pre)
             t0 = time.perf_counter()
@@ -180,21 +200,63 @@ def cpu_block_sample_ms(n: int, rows: int, threads: int) -> float:
     return t * 1e3
 
 
-# ------------------------------------------------------------------------------ work model
-def kernel_work(name: str, n: int):
-    """Algorithmic work of one launch at the bench workload: (bound, amount, unit)."""
-    n3 = float(n) ** 3
-    n2 = float(n) ** 2
-    table = {
-        "k_triatt_core": ("tensor", 4 * HEADS_PAIR * HEAD_DIM * n3, "flop"),
-        "k_trimul_bgemm": ("tensor", 2 * C_H * n3, "flop"),
-        "k_trimul_proj": ("hbm", n2 * (C_Z + 2 * C_H) * 2, "byte"),       # read z, write a and b
-        "k_trimul_out": ("hbm", n2 * (C_H + 2 * C_Z) * 2, "byte"),        # read x and z (gate + residual), write z
-        "k_triatt_proj": ("hbm", n2 * (C_Z + 3 * HEADS_PAIR * HEAD_DIM + HEADS_PAIR) * 2, "byte"),
-        "k_triatt_out": ("hbm", n2 * (HEADS_PAIR * HEAD_DIM + 2 * C_Z) * 2, "byte"),  # read o and z, write z
-        "k_transition": ("tensor", 3 * 2 * C_Z * 4 * C_Z * n2, "flop"),
-    }
-    return table.get(name)
+def cpu_sample_check(threads: int, n: int = 384, rows: int = 32) -> dict:
+    """The row-sample extrapolation against one full block of the same algorithm at a size
+    where the full block takes seconds: ratio = sampled estimate / full time."""
+    from oracle import pairformer_oracle as O
+    from opendde_b200.utils import seeded_params
+    from opendde_b200.model import PairformerBlock
+
+    torch.set_num_threads(threads)
+    blk = PairformerBlock(n_heads=N_SINGLE_HEADS, c_z=C_Z, c_s=C_S)
+    p = seeded_params([(k, tuple(v.shape)) for k, v in blk.named_parameters()], seed=0)
+    g = torch.Generator().manual_seed(1)
+    z = torch.randn((n, n, C_Z), generator=g)
+    s = torch.randn((n, C_S), generator=g)
+    mask = torch.ones((n, n))
+    with torch.no_grad():
+        cpu_block_sample_ms(n, rows, threads, z)     # warm-up
+        est = cpu_block_sample_ms(n, rows, threads, z)
+        t0 = time.perf_counter()
+        O.pairformer_block(s, z, mask, p)
+        full = (time.perf_counter() - t0) * 1e3
+    return {"n": n, "rows": rows, "full_block_ms": full, "sample_estimate_ms": est, "ratio": est / full}
+
+
+# ------------------------------------------------------------------------------ roofline
+# The library states every launch's algorithmic work from its arguments (flops of the
+# contraction over the rows / queries / keys that launch processes, or the minimum HBM bytes it
+# moves), so on a Fold-CP rank the figures are that rank's share. k_copy_regions is measured
+# against the peer-copy bandwidth: its bytes read from peers' windows (over NVLink) per second.
+def kernel_entry(name, launches, total_ms, work, unit, peaks, nvlink=None):
+    if total_ms <= 0:
+        return None
+    avg_s = total_ms / launches / 1e3
+    base = {"kernel": name, "avg_launch_ms": avg_s * 1e3, "launches": launches}
+    if name == "k_copy_regions" and nvlink is not None and nvlink.get("remote_bytes"):
+        rb = nvlink["remote_bytes"] / launches
+        ach = rb / avg_s / 1e9
+        peak = nvlink["peak_gbs"]
+        base.update({"bound": "nvlink", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "traffic": None, "work_per_launch": rb, "work_unit": "byte read from peers",
+                     "peak_kind": nvlink["peak_kind"]})
+        return base
+    if not work or not unit:
+        return None
+    per = work / launches
+    if unit == "flop":
+        ach = per / avg_s / 1e12
+        peak = peaks["bf16_tflops_sustained"]
+        base.update({"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
+                     "traffic": read_traffic(name), "work_per_launch": per, "work_unit": "flop",
+                     "peak_kind": f"bf16 dense sustained ({peaks['source']})"})
+    else:
+        ach = per / avg_s / 1e9
+        peak = peaks["hbm_gbs"]
+        base.update({"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
+                     "traffic": read_traffic(name), "work_per_launch": per, "work_unit": "byte",
+                     "peak_kind": f"HBM copy ({peaks['source']})"})
+    return base
 
 
 def read_traffic(kernel: str):
@@ -213,6 +275,35 @@ def read_traffic(kernel: str):
     return None
 
 
+def current_mesh():
+    from opendde_b200.distributed.foldcp import runtime
+    return runtime.current_mesh()
+
+
+def parity_vs_one_gpu(stack, s_dev, z_dev, m_dev, blocks, rank, barrier):
+    """The first ``blocks`` blocks of the timed trunk, run under Fold-CP on every rank and then
+    on rank 0 alone (single-device mode): rel-L2 of the final z and s between the two."""
+    from opendde_b200.model import PairformerStack
+    sub = PairformerStack(n_blocks=0, n_heads=N_SINGLE_HEADS, c_z=C_Z, c_s=C_S)
+    sub.blocks = torch.nn.ModuleList(list(stack.blocks)[:blocks])
+    out = None
+    with torch.no_grad():
+        s_d, z_d = sub(s_dev, z_dev, m_dev)
+        barrier()
+        if rank == 0:
+            old = os.environ.get("OPENDDE_FOLDCP_MODE")
+            os.environ["OPENDDE_FOLDCP_MODE"] = "single"
+            try:
+                s_1, z_1 = sub(s_dev, z_dev, m_dev)
+            finally:
+                os.environ["OPENDDE_FOLDCP_MODE"] = old
+            rel = lambda a, b: ((a.float() - b.float()).norm() / b.float().norm()).item()  # noqa: E731
+            out = {"blocks": blocks, "rel_l2_z": rel(z_d, z_1), "rel_l2_s": rel(s_d, s_1),
+                   "against": "the same seeded trunk on 1 GPU (bf16)"}
+        barrier()
+    return out
+
+
 # ------------------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -226,6 +317,9 @@ def main():
     ap.add_argument("--blocks", type=int, default=48)
     ap.add_argument("--cpu-rows", type=int, default=32)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--parity-blocks", type=int, default=2,
+                    help="N > 1: blocks of the same trunk run once more under Fold-CP and on rank 0 alone; "
+                         "the line's parity field is their rel-L2")
     ap.add_argument("--graph", choices=["auto", "on", "off"], default="auto",
                     help="replay each step as one CUDA graph (auto: on for N > 1, where the per-op host "
                          "work and collective launches would otherwise show between short kernels)")
@@ -334,21 +428,30 @@ def main():
     st = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     launches_per_step = None
+    copy_bytes = {"remote": 0, "local": 0}
+    if distributed:
+        from opendde_b200.distributed.foldcp import peer as foldcp_peer
     if use_graph:
         # per-kernel launch times from one eager step (graph replays carry no per-launch events)
         _abi.profile_enable(True)
         _abi.profile_report()
+        if distributed:
+            foldcp_peer.reset_copy_bytes()
         l0 = _abi.launch_count()
         step_resident()
         launches_per_step = _abi.launch_count() - l0
         _abi.profile_enable(False)
         prof = _abi.profile_report()
+        if distributed:
+            copy_bytes = foldcp_peer.reset_copy_bytes()
         barrier()
 
     # ---- timed: resident inputs (value); eager runs carry per-kernel events (roofline)
     if not use_graph:
         _abi.profile_enable(True)
         _abi.profile_report()  # clear
+        if distributed:
+            foldcp_peer.reset_copy_bytes()
     launches0 = _abi.launch_count()
     with ClockSampler(local_rank) as clk:
         barrier()
@@ -363,6 +466,8 @@ def main():
         launches = _abi.launch_count() - launches0
         _abi.profile_enable(False)
         prof = _abi.profile_report()
+        if distributed:
+            copy_bytes = foldcp_peer.reset_copy_bytes()
     ms_step = ev0.elapsed_time(ev1) / args.steps
 
     # ---- timed: end to end through the public API with host buffers
@@ -380,48 +485,43 @@ def main():
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         ms_step, ms_e2e = t.tolist()
 
+    # ---- N > 1: the transport's measured bandwidth, and parity against one GPU at reduced depth
+    nvlink = None
+    parity = None
+    if distributed:
+        mesh = current_mesh()
+        gbs = foldcp_peer.peer_copy_gbs(mesh, dev) if foldcp_peer.transport_choice("nccl") == "peer" else None
+        if gbs is not None:
+            t = torch.tensor([gbs], device=dev)
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MIN)
+            nvlink = {"peak_gbs": t.item(), "remote_bytes": copy_bytes["remote"],
+                      "peak_kind": "peer copy measured in this run with pf_copy_regions (min over ranks)"}
+        parity = parity_vs_one_gpu(stack, s_dev, z_dev, m_dev, args.parity_blocks, rank, barrier)
+
     peaks = load_peaks()
     clocks = clk.summary()
-    # dominant kernel and its roofline
-    kernels = {k: {"launches": v[0], "total_ms": v[1], "share": None} for k, v in prof.items()}
+    kernels = {k: {"launches": v[0], "total_ms": v[1], "share": None, "work": v[2], "work_unit": v[3]}
+               for k, v in prof.items()}
     tot = sum(v[1] for v in prof.values()) or 1.0
     for k in kernels:
         kernels[k]["share"] = kernels[k]["total_ms"] / tot
+    entries = {k: kernel_entry(k, v[0], v[1], v[2], v[3], peaks, nvlink) for k, v in prof.items()}
+    for k, e in entries.items():
+        if e is not None:
+            kernels[k]["roofline_frac"] = e["frac"]
+    # the roofline entry is the dominant kernel of the timed region (most device time)
     dom = max(prof.items(), key=lambda kv: kv[1][1])[0] if prof else None
-    roofline = None
-    fracs = {}
-    for name in ("k_triatt_core", "k_trimul_bgemm", dom):
-        if name is None or name not in prof:
-            continue
-        w = kernel_work(name, args.n)
-        if w is None:
-            continue
-        bound, amount, unit = w
-        avg_s = prof[name][1] / prof[name][0] / 1e3
-        if bound == "tensor":
-            ach = amount / avg_s / 1e12
-            peak = peaks["bf16_tflops_sustained"]
-            entry = {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                     "traffic": read_traffic(name), "kernel": name,
-                     "peak_kind": f"bf16 dense sustained ({peaks['source']})",
-                     "work_per_launch": amount, "avg_launch_ms": avg_s * 1e3}
-        else:
-            ach = amount / avg_s / 1e9
-            peak = peaks["hbm_gbs"]
-            entry = {"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                     "traffic": read_traffic(name), "kernel": name, "peak_kind": f"HBM copy ({peaks['source']})",
-                     "work_per_launch": amount, "avg_launch_ms": avg_s * 1e3}
-        fracs[name] = entry
-        if name == dom:
-            roofline = entry
+    roofline = entries.get(dom)
 
     cpu_baseline = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         rows = max(8, min(args.cpu_rows, args.n))
         v = cpu_block_sample_ms(args.n, rows, cores)
-        cpu_baseline = {"value": v, "unit": "ms/block", "cores": cores, "kind": "port",
-                        "sample": f"rows 0..{rows - 1} of every op of one block at N={args.n}, scaled x{args.n}/{rows}; "
-                                  "fp32 torch CPU restatement of the reference modules"}
+        cpu_baseline = {"value": v, "unit": "ms/block", "cores": cores, "kind": "port", "cpu": cpu_model(),
+                        "sample": f"rows 0..{rows - 1} of every op of one block at N={args.n}, scaled x{args.n}/{rows} "
+                                  "(the triangle update's full b projection timed once, unscaled); fp32 torch CPU "
+                                  "restatement of the reference modules",
+                        "sample_check": cpu_sample_check(cores)}
 
     z_bytes = z_host.numel() * 2
     h2d = z_bytes + s_host.numel() * 2 + m_host.numel() * 4
@@ -448,8 +548,9 @@ def main():
             "e2e": {"value": ms_e2e / args.blocks, "unit": "ms/block", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": roofline,
-            "tri_attn": fracs.get("k_triatt_core"),
-            "tri_mul": fracs.get("k_trimul_bgemm"),
+            "tri_attn": entries.get("k_triatt_core"),
+            "tri_mul": entries.get("k_trimul_bgemm"),
+            "parity": parity,
             "kernels": kernels,
             "gpu_launches": launches,
             "cuda_graph": use_graph,

@@ -255,11 +255,14 @@ def profile_enable(on: bool) -> None:
 
 
 def profile_report() -> dict:
-    """Per-kernel {name: (launches, total_ms)} since the last report (synchronises)."""
+    """Per-kernel {name: (launches, total_ms, total_work, unit)} since the last report
+    (synchronises). ``total_work`` is the algorithmic work the launches stated: flops of their
+    contractions (unit "flop") or the minimum HBM bytes they move (unit "byte"); 0 and "" for
+    kernels without a work model."""
     import json
     buf = ctypes.create_string_buffer(1 << 16)
     check(load().pf_profile_report(buf, len(buf)))
-    return {k: (int(v[0]), float(v[1])) for k, v in json.loads(buf.value.decode()).items()}
+    return {k: (int(v[0]), float(v[1]), float(v[2]), str(v[3])) for k, v in json.loads(buf.value.decode()).items()}
 
 
 def workspace_bytes(fn_name: str, *args) -> int:

@@ -177,7 +177,9 @@ extern "C" PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_r
   const int64_t items = bs.item_start[n];
   const int grid = (int)(items < (int64_t)sms * 4 ? items : (int64_t)sms * 4);
   cudaStream_t st = (cudaStream_t)stream;
-  PF_LAUNCH_SCOPE(st, "k_copy_regions");
+  double copied = 0.0;  // bytes copied (each read once from its source, written once)
+  for (int i = 0; i < n; ++i) copied += (double)live[i].planes * live[i].rows * live[i].row_bytes;
+  PF_LAUNCH_SCOPE_WORK(st, "k_copy_regions", copied, 'b');
   switch (unit) {
     case 16: k_copy_regions<uint4><<<grid, 256, 0, st>>>(bs); break;
     case 8: k_copy_regions<uint2><<<grid, 256, 0, st>>>(bs); break;

@@ -18,6 +18,8 @@ static std::atomic<int> g_enabled{0};
 struct Rec {
   const char* name;
   cudaEvent_t a, b;
+  double work;
+  char unit;
 };
 static std::mutex g_mu;
 static std::vector<Rec> g_recs;
@@ -35,11 +37,11 @@ static cudaEvent_t take_event() {
   return e;
 }
 
-void on_launch_begin(cudaStream_t st, const char* name) {
+void on_launch_begin(cudaStream_t st, const char* name, double work, char unit) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
   if (!g_enabled.load(std::memory_order_relaxed)) return;
   std::lock_guard<std::mutex> lk(g_mu);
-  Rec r{name, take_event(), take_event()};
+  Rec r{name, take_event(), take_event(), work, unit};
   cudaEventRecord(r.a, st);
   g_recs.push_back(r);
   t_open = (int)g_recs.size() - 1;
@@ -67,15 +69,22 @@ extern "C" PF_API long long pf_launch_count(void) { return prof::g_launches.load
 extern "C" PF_API int pf_profile_report(char* buf, size_t len) {
   using namespace prof;
   std::lock_guard<std::mutex> lk(g_mu);
-  std::map<std::string, std::pair<long long, double>> agg;
+  struct Agg {
+    long long launches = 0;
+    double ms = 0.0, work = 0.0;
+    char unit = 0;
+  };
+  std::map<std::string, Agg> agg;
   for (auto& r : g_recs) {
     cudaError_t e = cudaEventSynchronize(r.b);
     if (e != cudaSuccess) return fail(PF_ECUDA, "profile event sync failed: %s", cudaGetErrorString(e));
     float ms = 0.f;
     cudaEventElapsedTime(&ms, r.a, r.b);
     auto& v = agg[r.name];
-    v.first += 1;
-    v.second += ms;
+    v.launches += 1;
+    v.ms += ms;
+    v.work += r.work;
+    if (r.unit) v.unit = r.unit;
     g_pool.push_back(r.a);
     g_pool.push_back(r.b);
   }
@@ -83,9 +92,10 @@ extern "C" PF_API int pf_profile_report(char* buf, size_t len) {
   std::string out = "{";
   bool first = true;
   for (auto& kv : agg) {
-    char tmp[256];
-    snprintf(tmp, sizeof(tmp), "%s\"%s\": [%lld, %.6f]", first ? "" : ", ", kv.first.c_str(),
-             kv.second.first, kv.second.second);
+    char tmp[320];
+    const char* unit = kv.second.unit == 'f' ? "flop" : kv.second.unit == 'b' ? "byte" : "";
+    snprintf(tmp, sizeof(tmp), "%s\"%s\": [%lld, %.6f, %.6e, \"%s\"]", first ? "" : ", ", kv.first.c_str(),
+             kv.second.launches, kv.second.ms, kv.second.work, unit);
     out += tmp;
     first = false;
   }

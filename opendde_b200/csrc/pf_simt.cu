@@ -557,7 +557,7 @@ static int ln_rows_launch(const T* x, T* y, int64_t rows, int c, const float* g,
   const int64_t blocks = (rows + rows_per_block - 1) / rows_per_block;
   if (blocks > 0x7FFFFFFF) return fail(PF_EUNSUPPORTED, "LayerNorm: %lld rows is too many", (long long)rows);
   {
-    PF_LAUNCH_SCOPE(st, "k_layernorm_rows");
+    PF_LAUNCH_SCOPE_WORK(st, "k_layernorm_rows", 2.0 * (double)rows * c * sizeof(T), 'b');
     k_layernorm_rows<T, L><<<(unsigned)blocks, 256, 0, st>>>(x, y, rows, c, g, b, eps);
   }
   PF_CHECK_LAUNCH();

@@ -158,7 +158,8 @@ int apb_pair_bias(const pf_apb_params* p, pf_pair_view z, int64_t n_rows, int64_
   const int64_t nt = n_rows * a.tiles_per_row;
   if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "pair-bias grid too large");
   {
-    PF_LAUNCH_SCOPE(st, "k_apb_bias");
+    // read z (bf16 C channels), write the fp32 bias of HB heads
+    PF_LAUNCH_SCOPE_WORK(st, "k_apb_bias", (double)n_rows * n_cols * (2.0 * C + 4.0 * HB), 'b');
     k_apb_bias<<<(unsigned)nt, 128, APB_SMEM + 1024, st>>>(tz, tw, a);
   }
   PF_CHECK_LAUNCH();

@@ -309,7 +309,8 @@ int transition(const pf_transition_params* p, const void* x, int64_t xs, void* o
   const int64_t nt = (rows + 2 * TILE - 1) / (2 * TILE);
   if (nt > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "transition grid too large");
   {
-    PF_LAUNCH_SCOPE(st, "k_transition");
+    // [W_a; W_b] (2 x C x HID) and W_out (HID x C) per row: 6 C HID flops
+    PF_LAUNCH_SCOPE_WORK(st, "k_transition", 6.0 * C * HID * (double)rows, 'f');
     k_transition<<<(unsigned)nt, 320, TR_SMEM + 1024, st>>>(tx, tout, twa, twb, two, a);
   }
   PF_CHECK_LAUNCH();

@@ -597,7 +597,12 @@ int launch_proj(const pf_triatt_params* p, const void* zptr, int64_t rs, int64_t
   pa.n_tiles = n_rows * pa.tiles_per_row;
   {
     const int64_t grid_p = pa.n_tiles < num_sms() ? pa.n_tiles : num_sms();
-    PF_LAUNCH_SCOPE(st, "k_triatt_proj");
+    // read z; write q (queries), k and v^T (all keys) and / or the bias (f16)
+    const double pos = (double)n_rows * n_cols;
+    double bytes = 2.0 * pos * CH;
+    if (pa.want_qkv) bytes += 2.0 * ((double)n_rows * pa.n_q * HD + 2.0 * pos * HD);
+    if (pa.want_bias) bytes += 2.0 * H * (pa.want_qkv ? (double)pa.n_q * n_cols : pos);
+    PF_LAUNCH_SCOPE_WORK(st, "k_triatt_proj", bytes, 'b');
     k_triatt_proj<<<(unsigned)grid_p, 320, PROJ_SMEM + 1024, st>>>(tz, twq, twk, twv, twb, tvt, pa);
   }
   PF_CHECK_LAUNCH();
@@ -717,7 +722,8 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
     ca.o = w.o;
     ca.status = status;
     const int64_t grid = ca.n_items < num_sms() ? ca.n_items : num_sms();
-    PF_LAUNCH_SCOPE(st, "k_triatt_core");
+    // QK^T and PV over every existing key: 4 H d flops per (row, query, key)
+    PF_LAUNCH_SCOPE_WORK(st, "k_triatt_core", 4.0 * H * D * (double)n_rows * n_q * n_valid, 'f');
     k_triatt_core<<<(unsigned)grid, 320, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
   }
   PF_CHECK_LAUNCH();
@@ -749,7 +755,10 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   oa.status = status;
   {
     const int64_t grid_o = oa.n_tiles < num_sms() ? oa.n_tiles : num_sms();
-    PF_LAUNCH_SCOPE(st, "k_triatt_out");
+    // read o and the gate source z, (read the residual if it is another view), write the output
+    const bool resid_apart = acc && (zo.ptr != zs.ptr || zo.row_stride != zs.row_stride || q_col0 != 0);
+    const double bytes = 2.0 * (double)n_rows * n_q * (HD + CH + (resid_apart ? CH : 0) + CH);
+    PF_LAUNCH_SCOPE_WORK(st, "k_triatt_out", bytes, 'b');
     k_triatt_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tz, to, tzo, twg, two, oa);
   }
   PF_CHECK_LAUNCH();

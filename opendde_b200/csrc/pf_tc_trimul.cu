@@ -711,7 +711,12 @@ int launch_proj(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_
   pa.status = status;
   {
     const int64_t grid_p = pa.n_items < sm_count() ? pa.n_items : sm_count();
-    PF_LAUNCH_SCOPE(st, "k_trimul_proj");
+    // read each z view once (once in all when both sides project the same view), write a and b
+    const bool same = za.ptr == zb.ptr && za.row_stride == zb.row_stride && za.col_stride == zb.col_stride &&
+                      n_i == n_j;
+    const double pos_a = (double)n_i * n_k, pos_b = (double)n_j * n_k;
+    const double bytes = 2.0 * ((same ? pos_a : pos_a + pos_b) * CH + (pos_a + pos_b) * CH);
+    PF_LAUNCH_SCOPE_WORK(st, "k_trimul_proj", bytes, 'b');
     k_trimul_proj<<<(unsigned)grid_p, 320, PROJ_SMEM + 1024, st>>>(tz0, tz1, to0, to1, tw0p, tw0g, tw1p, tw1g, pa);
   }
   PF_CHECK_LAUNCH();
@@ -748,7 +753,7 @@ int launch_contract_out(const pf_trimul_params* p, const __nv_bfloat16* a, int64
   ga.status = status;
   {
     const int64_t grid_g = ga.n_work < sm_count() ? ga.n_work : sm_count();
-    PF_LAUNCH_SCOPE(st, "k_trimul_bgemm");
+    PF_LAUNCH_SCOPE_WORK(st, "k_trimul_bgemm", 2.0 * CH * (double)n_i * n_j * n_k, 'f');
     k_trimul_bgemm<<<(unsigned)grid_g, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
   }
   PF_CHECK_LAUNCH();
@@ -780,7 +785,10 @@ int launch_contract_out(const pf_trimul_params* p, const __nv_bfloat16* a, int64
   oa.status = status;
   const int64_t grid_o = oa.n_tiles < sm_count() ? oa.n_tiles : sm_count();
   {
-    PF_LAUNCH_SCOPE(st, "k_trimul_out");
+    // read x and the gate source, (read the residual if it is another view), write the output
+    const bool resid_apart = acc && (zo.ptr != zg.ptr || zo.row_stride != zg.row_stride);
+    const double bytes = 2.0 * (double)n_i * n_j * (CH + CH + (resid_apart ? CH : 0) + CH);
+    PF_LAUNCH_SCOPE_WORK(st, "k_trimul_out", bytes, 'b');
     k_trimul_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tzg, txm, tzo, twz, twg, oa);
   }
   PF_CHECK_LAUNCH();

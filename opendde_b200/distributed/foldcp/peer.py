@@ -147,6 +147,11 @@ class PeerWindows:
     def slot_ptrs(self, slot: int) -> List[int]:
         return [b + slot * self.slot_bytes for b in self.bases]
 
+    def is_remote(self, ptr: int) -> bool:
+        """Whether ``ptr`` lies in a peer's window (its bytes cross NVLink when loaded)."""
+        span = 2 * self.slot_bytes
+        return any(b <= ptr < b + span for q, b in enumerate(self.bases) if q != self.cp_rank)
+
     def barrier(self) -> None:
         """Stream-ordered: work enqueued after it runs once every rank has enqueued and
         completed the work before its own barrier."""
@@ -171,6 +176,16 @@ class PeerWindows:
 # new group; a new mesh over the same group reuses the same windows.
 _WINDOWS: Dict[tuple, PeerWindows] = {}
 
+# Bytes the band copies moved since the last reset, split by where their source lives: in a
+# peer's window (read over NVLink) or in this GPU's memory (the tile snapshots, own bands).
+COPY_BYTES = {"remote": 0, "local": 0}
+
+
+def reset_copy_bytes() -> Dict[str, int]:
+    out = dict(COPY_BYTES)
+    COPY_BYTES["remote"] = COPY_BYTES["local"] = 0
+    return out
+
 
 def _window_key(mesh) -> tuple:
     return (mesh.group_2d, mesh.cp_rank)
@@ -194,6 +209,32 @@ def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
     return w
 
 
+def peer_copy_gbs(mesh, device: torch.device, reps: int = 5) -> float:
+    """Bandwidth of the band copies' transport, measured with the band-copy kernel itself: every
+    rank at once loads one whole slot of the next rank's window into local memory
+    (``pf_copy_regions``, 4 KB rows) ``reps`` times; returns this rank's GB/s of peer reads.
+    Collective over the mesh's CP group (its windows must exist: run one op first)."""
+    w = _WINDOWS.get(_window_key(mesh))
+    if w is None or w.numel < 2:
+        raise RuntimeError("peer_copy_gbs needs the mesh's peer windows: run one Fold-CP op first")
+    src = w.bases[(w.cp_rank + 1) % w.numel]
+    row = 4096
+    rows = w.slot_bytes // row
+    dst = torch.empty(rows * row, dtype=torch.uint8, device=device)
+    plan = [(src, dst.data_ptr(), 1, rows, row, row, row, 0, 0)]
+    kernels.copy_regions(plan)                      # warm
+    torch.cuda.synchronize(device)
+    dist.barrier(group=w.group)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        kernels.copy_regions(plan)
+    e1.record()
+    torch.cuda.synchronize(device)
+    dist.barrier(group=w.group)
+    return rows * row * reps / (e0.elapsed_time(e1) / 1e3) / 1e9
+
+
 def release_windows() -> None:
     """Free every cached window (collective over each window's group)."""
     for w in list(_WINDOWS.values()):
@@ -212,6 +253,10 @@ class PeerExchange(DistExchange):
     def _copy(self, plan: List[CopyRegion]) -> None:
         """Execute a copy plan (one pf_copy_regions launch per 32 boxes on the current stream)."""
         kernels.copy_regions(plan)
+        is_remote = getattr(getattr(self, "_w", None), "is_remote", None)
+        for r in plan:
+            n = r[2] * r[3] * r[4]
+            COPY_BYTES["remote" if (is_remote is not None and is_remote(r[0])) else "local"] += n
 
     def bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, needs: Sequence[Need]) -> List[torch.Tensor]:
         """Every rectangle ``need(coord)`` of ``needs``, from one snapshot of ``local``."""
@@ -284,6 +329,7 @@ class PeerExchange(DistExchange):
             ld_t, bias_bytes = _projection_side_bytes(spec, bias_tile.shape[0], eb)
             need_bytes = max(need_bytes, tile_bytes + bias_bytes)
         w = self._windows_fn(self.mesh, need_bytes, local.device)
+        self._w = w
         slot = w.slot
         w.slot ^= 1
         ptrs = w.slot_ptrs(slot)
@@ -345,6 +391,7 @@ class PeerExchange(DistExchange):
         elem = local.element_size()
         ld_t, side = _projection_side_bytes(spec, c_h, elem)
         w = self._windows_fn(self.mesh, self._slot_need(local, spec, c_h), local.device)
+        self._w = w
         slot = w.slot
         w.slot ^= 1
         ptrs = w.slot_ptrs(slot)

@@ -174,6 +174,11 @@ class _ThreadWindows:
     def slot_ptrs(self, slot: int) -> List[int]:
         return [b.data_ptr() + slot * self.m.win_bytes for b in self.m.win_bufs]
 
+    def is_remote(self, ptr: int) -> bool:
+        mine = self.m.win_views.index(self)
+        return any(b.data_ptr() <= ptr < b.data_ptr() + 2 * self.m.win_bytes
+                   for q, b in enumerate(self.m.win_bufs) if q != mine)
+
     def barrier(self) -> None:
         if self.m.win_bufs and self.m.win_bufs[0].is_cuda:
             torch.cuda.synchronize()
