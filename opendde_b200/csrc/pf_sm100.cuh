@@ -301,6 +301,32 @@ __device__ __forceinline__ uint32_t ex2_f16x2(uint32_t a) {
   asm("ex2.approx.f16x2 %0, %1;" : "=r"(r) : "r"(a));
   return r;
 }
+__device__ __forceinline__ uint32_t hfma2_u(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+// 2^y for packed f16 y <= 8 on the FMA pipe (no MUFU op), for softmax exponentials next to
+// ex2.approx.f16x2: y is clamped to -15 (-inf gives 0), split as n + f with n = round(y) taken
+// from the f16 spacing of 1536 + y and f in [-1/2, 1/2]; 2^f is a degree-3 polynomial (fitted
+// for relative error 7.5e-5 on [-1/2, 1/2]), scaled by 2^n built directly as f16 bits
+// (n + 15) << 10 per half (0, i.e. a result of 0, for n = -15). Every f16 input in [-14, 8] is
+// within 0.85 ulp of 2^y; inputs below -14.5 give 0.
+__device__ __forceinline__ uint32_t ex2_poly_f16x2(uint32_t y) {
+  const uint32_t yc = hmax2_u(y, 0xCB80CB80u);                  // max(y, -15)
+  const uint32_t t = hadd2_u(yc, 0x66006600u);                  // 1536 + round(yc)
+  const uint32_t f = hsub2_u(yc, hsub2_u(t, 0x66006600u));      // yc - round(yc)
+  uint32_t p = hfma2_u(f, 0x2B102B10u, 0x33C433C4u);            // 0.05518 f + 0.2427
+  p = hfma2_u(p, f, 0x398C398Cu);                               //  (.) f + 0.6934
+  p = hfma2_u(p, f, 0x3C003C00u);                               //  (.) f + 1
+  const uint32_t scale = (t - 0x65F165F1u) << 10;               // f16 bits of 2^round(yc) per half
+  return hmul2_u(p, scale);
+}
 __device__ __forceinline__ float f16lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFFu))); }
 __device__ __forceinline__ float f16hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }

@@ -724,7 +724,7 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
     const int64_t grid = ca.n_items < num_sms() ? ca.n_items : num_sms();
     // QK^T and PV over every existing key: 4 H d flops per (row, query, key)
     PF_LAUNCH_SCOPE_WORK(st, "k_triatt_core", 4.0 * H * D * (double)n_rows * n_q * n_valid, 'f');
-    k_triatt_core<<<(unsigned)grid, 320, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
+    k_triatt_core<<<(unsigned)grid, CORE_THREADS, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
   }
   PF_CHECK_LAUNCH();
   // 3. gate, output projection, residual

@@ -5,22 +5,26 @@
 // walks items w = blockIdx.x, blockIdx.x + gridDim.x, ... and a key-tile "step" stream runs
 // through a 3-stage TMA ring continuously across items. The two rows of an item share the
 // triangle-bias tile (bias[h][j][k] does not depend on i).
-// Warp roles (320 threads):
+// Warp roles (352 threads):
 //   warps 0-3  softmax for row A (thread = query; TMEM lanes 0..127)
 //   warps 4-7  softmax for row B
 //   warp 8     TMA producer: per step the bias tile, K, V^T and key-mask rows of both rows
-//   warp 9     MMA issuer (single thread) and TMEM owner
-// TMEM (per row R, base 256*R): S [0,128) f16 accumulator (one value per column), P aliased
-// on [0,64) (f16, two per column), [O | l] [128,176) fp32, Q slots [192,208) and [208,224)
-// (f16, two per column).
+//   warp 9     MMA issuer of row A (single thread) and TMEM owner
+//   warp 10    MMA issuer of row B (single thread)
+// TMEM (per row R, base 256*R): S [0,128) f16 accumulator (one value per column), P [128,192)
+// (f16, two per column), [O | l] [192,240) fp32, Q [240,256) (f16, two per column).
 //   S = Q K^T           A = Q (TMEM), B = K tile (smem, 64B swizzle), f16 x f16 -> f16
 //   [O | l] += P [V^T; 1]^T   A = P (TMEM), B = V^T tile with a row of ones appended
 //                       (smem, 128B swizzle), -> fp32; l is the sum of exactly the P used.
-// An M=128, K=16 MMA costs ~45 cycles at N=48 whatever its dependencies, so the row sum rides
-// in the same instructions as P.V, and every descriptor is precomputed (issue = one add).
-// Q rows are written into TMEM by the softmax threads themselves (thread = query = lane), one
-// item ahead. Issue order per step: PV_A(t), S_A(t+1), PV_B(t), S_B(t+1), so the two softmax
-// groups run half a step apart while the tensor core serves the other one.
+// P has its own columns, so S of the next step is computed while the softmax threads are still
+// exponentiating the current one: a softmax thread reads S(t), tells the MMA thread that the S
+// columns are free (for the item's last tile, after writing the next item's Q into the Q
+// columns), and the MMA thread issues S(t+1) at once; P(t) and PV(t) follow. Per step and row
+// the softmax threads therefore wait only for their own previous P.V (before overwriting P or
+// rescaling O), not for a P -> PV -> S round trip through the tensor pipe.
+// Each row has its own MMA-issuing thread (a tcgen05.mma costs the issuing thread far more than
+// these small MMAs cost the tensor pipe), per step t: S(t+1) after the row has read S(t), then
+// PV(t) after the row's P(t), then its half of the stage release.
 // Softmax is packed f16x2 on log2-domain logits read straight from TMEM (tcgen05.ld
 // .pack::16b): + bias, + key mask (0 / -inf), max, - m, ex2.f16x2. The running max is updated
 // lazily (O, L rescaled in TMEM only when a tile's max exceeds it by more than 8).
@@ -36,6 +40,10 @@ struct CoreArgs {
   unsigned int* status;
 };
 
+#ifndef PF_CORE_FMA_PAIRS
+#define PF_CORE_FMA_PAIRS 0
+#endif
+constexpr int CORE_THREADS = 352;
 constexpr int CORE_STAGES = 3;
 // per-stage layout (bytes from the stage base)
 constexpr uint32_t CS_KA = 0;                  // 128 x 64 B (SW64) f16
@@ -51,9 +59,10 @@ constexpr uint32_t CC_BAR = CORE_STAGES * CS_BYTES;
 constexpr uint32_t CORE3_SMEM = CC_BAR + 256;
 static_assert(CS_BYTES % 1024 == 0 && CS_BIAS % 1024 == 0 && CS_VTB % 1024 == 0, "1 KB alignment");
 static_assert(CS_MBB + 256 <= CS_BYTES, "stage overflow");
+static_assert(CORE3_SMEM + 1024 <= 227 * 1024, "dynamic shared memory limit");
 
 // TMEM column offsets within a row's 256-column block
-constexpr uint32_t T_S = 0, T_O = 128, T_Q = 192;
+constexpr uint32_t T_S = 0, T_P = 128, T_O = 192, T_Q = 240;
 
 __device__ __forceinline__ int next_tile(const uint8_t* fa, const uint8_t* fb, int kt, int n_tiles) {
   while (kt < n_tiles && fa[kt] == TF_SKIP && (fb == nullptr || fb[kt] == TF_SKIP)) ++kt;
@@ -95,6 +104,7 @@ __device__ __forceinline__ void tmem_ld32_16b(uint32_t taddr, uint32_t (&r)[32])
 // One query row of a 128-key tile in log2 units, packed f16x2: x[p] holds keys (2p, 2p+1).
 // BIAS: add the triangle-bias row (SW128 tile in smem); uniform rows (BIAS = false) drop the
 // logits entirely. MASK: add the key-mask row (0 / -inf). Returns the packed running max.
+// The shared-memory rows are read 32 keys at a time (16 + 16 registers in flight).
 template <bool BIAS, bool MASK>
 __device__ __forceinline__ uint32_t tile_logits(uint32_t t_s, const uint8_t* brow, const uint8_t* mbrow,
                                                 int row_tid, uint32_t (&x)[64]) {
@@ -102,63 +112,47 @@ __device__ __forceinline__ uint32_t tile_logits(uint32_t t_s, const uint8_t* bro
 #pragma unroll
   for (int c = 0; c < 2; ++c) {
     uint32_t v[32];
-    if (BIAS) {
-      tmem_ld32_16b(t_s + c * 64, v);  // keys 64c .. 64c+63
-    }
-    uint4 b[8], mv[8];
+    if (BIAS) tmem_ld32_16b(t_s + c * 64, v);  // keys 64c .. 64c+63
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int ch = c * 8 + q;  // 16-byte chunk = 8 keys
-      if (BIAS) b[q] = *reinterpret_cast<const uint4*>(brow + (ch >> 3) * 16384 + sw128_off(row_tid, ch & 7));
-      if (MASK) mv[q] = reinterpret_cast<const uint4*>(mbrow)[ch];
-    }
-    if (BIAS) tmem_ld_wait();
+    for (int hq = 0; hq < 2; ++hq) {
+      uint4 b[4], mv[4];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      const int ch = c * 8 + q;
-      uint32_t y0 = 0u, y1 = 0u, y2 = 0u, y3 = 0u;
-      if (BIAS) {
-        y0 = hadd2_u(v[q * 4 + 0], b[q].x);
-        y1 = hadd2_u(v[q * 4 + 1], b[q].y);
-        y2 = hadd2_u(v[q * 4 + 2], b[q].z);
-        y3 = hadd2_u(v[q * 4 + 3], b[q].w);
+      for (int e = 0; e < 4; ++e) {
+        const int ch = c * 8 + hq * 4 + e;  // 16-byte chunk = 8 keys
+        if (BIAS) b[e] = *reinterpret_cast<const uint4*>(brow + (ch >> 3) * 16384 + sw128_off(row_tid, ch & 7));
+        if (MASK) mv[e] = reinterpret_cast<const uint4*>(mbrow)[ch];
       }
-      if (MASK) {
-        y0 = hadd2_u(y0, mv[q].x);
-        y1 = hadd2_u(y1, mv[q].y);
-        y2 = hadd2_u(y2, mv[q].z);
-        y3 = hadd2_u(y3, mv[q].w);
+      if (BIAS && hq == 0) tmem_ld_wait();
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int q = hq * 4 + e, ch = c * 8 + q;
+        uint32_t y0 = 0u, y1 = 0u, y2 = 0u, y3 = 0u;
+        if (BIAS) {
+          y0 = hadd2_u(v[q * 4 + 0], b[e].x);
+          y1 = hadd2_u(v[q * 4 + 1], b[e].y);
+          y2 = hadd2_u(v[q * 4 + 2], b[e].z);
+          y3 = hadd2_u(v[q * 4 + 3], b[e].w);
+        }
+        if (MASK) {
+          y0 = hadd2_u(y0, mv[e].x);
+          y1 = hadd2_u(y1, mv[e].y);
+          y2 = hadd2_u(y2, mv[e].z);
+          y3 = hadd2_u(y3, mv[e].w);
+        }
+        mx = hmax2_u(mx, hmax2_u(hmax2_u(y0, y1), hmax2_u(y2, y3)));
+        x[ch * 4 + 0] = y0;
+        x[ch * 4 + 1] = y1;
+        x[ch * 4 + 2] = y2;
+        x[ch * 4 + 3] = y3;
       }
-      mx = hmax2_u(mx, hmax2_u(hmax2_u(y0, y1), hmax2_u(y2, y3)));
-      x[ch * 4 + 0] = y0;
-      x[ch * 4 + 1] = y1;
-      x[ch * 4 + 2] = y2;
-      x[ch * 4 + 3] = y3;
     }
   }
   return mx;
 }
 
-// Softmax thread: fetch its query row (32 f16) of item `it`, row r, into registers.
-__device__ __forceinline__ void fetch_q_row(const CoreArgs& a, const Item& it, int r, int row_tid,
-                                            uint32_t (&qv)[16]) {
-  const int64_t j = (int64_t)it.jt * TILE + row_tid;
-  if (j < a.n_q) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.q + (((it.i0 + r) * H + it.h) * a.n_q + j) * D);
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const uint4 u = src[e];
-      qv[e * 4 + 0] = u.x; qv[e * 4 + 1] = u.y; qv[e * 4 + 2] = u.z; qv[e * 4 + 3] = u.w;
-    }
-  } else {
-#pragma unroll
-    for (int e = 0; e < 16; ++e) qv[e] = 0u;
-  }
-}
-
-// Softmax thread: copy its query row (32 f16) of item `it`, row r, into TMEM Q slot `slot`.
+// Softmax thread: copy its query row (32 f16) of item `it`, row r, into the TMEM Q columns.
 __device__ __forceinline__ void load_q_row(const CoreArgs& a, const Item& it, int r, int row_tid,
-                                           uint32_t tmem_row, int slot, uint32_t lane_base) {
+                                           uint32_t tmem_row, uint32_t lane_base) {
   const int64_t j = (int64_t)it.jt * TILE + row_tid;
   uint32_t qv[16];
   if (j < a.n_q) {
@@ -172,22 +166,23 @@ __device__ __forceinline__ void load_q_row(const CoreArgs& a, const Item& it, in
 #pragma unroll
     for (int e = 0; e < 16; ++e) qv[e] = 0u;
   }
-  tmem_st16(tmem_row + lane_base + T_Q + 16 * slot, qv);
+  tmem_st16(tmem_row + lane_base + T_Q, qv);
 }
 
-__global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ CUtensorMap tk,
-                                                        const __grid_constant__ CUtensorMap tvt,
-                                                        const __grid_constant__ CUtensorMap tb,
-                                                        const __grid_constant__ CUtensorMap tmb,
-                                                        const CoreArgs a) {
+__global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_constant__ CUtensorMap tk,
+                                                                 const __grid_constant__ CUtensorMap tvt,
+                                                                 const __grid_constant__ CUtensorMap tb,
+                                                                 const __grid_constant__ CUtensorMap tmb,
+                                                                 const CoreArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
   const uint32_t bars = base + CC_BAR;
-  // barriers: full[3] @0, empty[3] @24, then per row r: s @48+8r, p @64+8r, o @80+8r,
-  // q[slot] @96+16r+8slot (one per TMEM Q slot, so a slot's barrier is never two phases
-  // ahead of its waiter), ofree @128+8r; drain @176; TMEM slot @200
+  // barriers: full[3] @0, empty[3] @24, then per row r: s @48+8r (S ready), p @64+8r (P
+  // written), o @80+8r (P.V done), sfree @96+8r (S read: its columns are free, and Q is in
+  // place for the next S), ofree @112+8r (O read out by the item epilogue); drain @128;
+  // TMEM slot @200
   const uint32_t bar_full0 = bars, bar_empty0 = bars + 24;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + CC_BAR + 200);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -196,17 +191,17 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
   if (tid == 0) {
     for (int s = 0; s < CORE_STAGES; ++s) {
       mbar_init(bar_full0 + 8 * s, 1);
-      mbar_init(bar_empty0 + 8 * s, 1);
+      mbar_init(bar_empty0 + 8 * s, 2);  // one arrival per row's MMA thread
     }
     for (int r = 0; r < 2; ++r) {
-      mbar_init(bars + 48 + 8 * r, 1);   // S ready (tcgen05.commit)
-      mbar_init(bars + 64 + 8 * r, 4);   // P written (one arrive per softmax warp)
-      mbar_init(bars + 80 + 8 * r, 1);   // O/L ready (tcgen05.commit)
-      mbar_init(bars + 96 + 16 * r, 4);      // Q rows written into slot 0
-      mbar_init(bars + 96 + 16 * r + 8, 4);  // Q rows written into slot 1
-      mbar_init(bars + 128 + 8 * r, 4);      // O/L read out, free for the next item
+      mbar_init(bars + 48 + 8 * r, 1);    // S ready (tcgen05.commit)
+      mbar_init(bars + 64 + 8 * r, 4);    // P written (one arrive per softmax warp)
+      mbar_init(bars + 80 + 8 * r, 1);    // P.V done (tcgen05.commit)
+      mbar_init(bars + 96 + 8 * r, 4);    // S read / Q written
+      mbar_init(bars + 112 + 8 * r, 4);   // O/L read out, free for the next item
     }
-    mbar_init(bars + 176, 1);                // drain
+    mbar_init(bars + 128, 1);             // drain (row A's MMA thread)
+    mbar_init(bars + 136, 1);             // drain (row B's MMA thread)
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -214,7 +209,7 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
     tmem_relinquish();
   }
   // constant rows 32..47 of every V^T buffer: row 32 = 1.0 (f16), rows 33..47 = 0
-  for (int idx = tid; idx < CORE_STAGES * 2 * 2 * 16 * 8; idx += 320) {
+  for (int idx = tid; idx < CORE_STAGES * 2 * 2 * 16 * 8; idx += CORE_THREADS) {
     const int ch = idx & 7, rr = 32 + ((idx >> 3) & 15), atom = (idx >> 7) & 1, which = (idx >> 8) & 1,
               st = idx >> 9;
     const uint32_t one2 = (rr == 32) ? 0x3C003C00u : 0u;
@@ -259,42 +254,46 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         }
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers (one per row)
+    // Warp 9 issues row A's MMAs, warp 10 row B's: each thread walks the same step stream,
+    // and a stage is released once both rows' P.V of that step are done (two arrivals).
     if (lane == 0) {
+      const int r = warp - 9;
       constexpr uint32_t id_s = idesc_f16_f16acc(128, 128);               // f16 x f16 -> f16
       constexpr uint32_t id_o = idesc_f16(128, 48, false);                // f16 x f16 -> fp32
-      uint32_t t_r[2] = {0, 0};  // tile steps issued per row (bar_s/p/o phases)
-      uint32_t n_r[2] = {0, 0};  // items begun per row (bar_q / bar_ofree phases)
-      uint32_t step = 0;
+      uint32_t ns = 0;   // S issued for this row (sfree phases)
+      uint32_t np = 0;   // P.V issued (p phases)
+      uint32_t ni = 0;   // items begun (ofree phases)
       bool ok = true;
-      // Descriptors of stage 0, row A; other stages / row B / K-steps differ only in the start
+      const uint32_t tb_r = tmem + 256u * r;
+      const uint32_t bar_s = bars + 48 + 8 * r, bar_p = bars + 64 + 8 * r, bar_o = bars + 80 + 8 * r,
+                     bar_sf = bars + 96 + 8 * r, bar_of = bars + 112 + 8 * r;
+      // Descriptors of stage 0 for this row; other stages / K-steps differ only in the start
       // address field (address >> 4), so each MMA's descriptor is one 64-bit add.
-      const uint64_t dK0 = sdesc(base + CS_KA, 512, SWZ_64B);
-      const uint64_t dV0 = sdesc(base + CS_VTA, 1024, SWZ_128B);
-      constexpr uint64_t kStageD = CS_BYTES >> 4, kRowKD = (CS_KB - CS_KA) >> 4, kRowVD = (CS_VTB - CS_VTA) >> 4;
-      // S for (row r, step at stage s) of an item; Q slot = item parity of that row
-      auto issue_s = [&](int r, uint32_t s, uint32_t qslot) {
-        const uint32_t tb_r = tmem + 256u * r;
-        const uint64_t dk = dK0 + s * kStageD + (r ? kRowKD : 0);
-        umma_f16_ts(tb_r + T_S, tb_r + T_Q + 16 * qslot, dk, id_s, 0u);
-        umma_f16_ts(tb_r + T_S, tb_r + T_Q + 16 * qslot + 8, dk + 2, id_s, 1u);  // +32 B
-        umma_commit(bars + 48 + 8 * r);
+      const uint64_t dK0 = sdesc(base + (r ? CS_KB : CS_KA), 512, SWZ_64B);
+      const uint64_t dV0 = sdesc(base + (r ? CS_VTB : CS_VTA), 1024, SWZ_128B);
+      constexpr uint64_t kStageD = CS_BYTES >> 4;
+      // S for the step in stage s, once this row's softmax has read its previous S
+      auto issue_s = [&](uint32_t s) {
+        ok = ok && mbar_wait(bar_sf, ns & 1, a.status);
+        tc_fence_after();
+        const uint64_t dk = dK0 + s * kStageD;
+        umma_f16_ts(tb_r + T_S, tb_r + T_Q, dk, id_s, 0u);
+        umma_f16_ts(tb_r + T_S, tb_r + T_Q + 8, dk + 2, id_s, 1u);  // +32 B
+        umma_commit(bar_s);
+        ns += 1;
       };
-      // the first step of the first item
       int64_t w = blockIdx.x;
       Item it;
       int kt = n_tiles;
+      uint32_t step = 0;
       if (w < a.n_items) {
         it = decode_item(a, w);
         kt = next_tile(it.fa, it.fb, 0, n_tiles);
         ok = mbar_wait(bar_full0, 0, a.status);
         tc_fence_after();
-        for (int r = 0; r < (it.has_b ? 2 : 1) && ok; ++r) {
-          ok = mbar_wait(bars + 96 + 16 * r, 0, a.status);  // item 0 -> slot 0, first use
-          tc_fence_after();
-          issue_s(r, 0, 0);
-        }
+        if (r == 0 || it.has_b) issue_s(0);
       }
       bool first = true;
       while (w < a.n_items && ok) {
@@ -313,37 +312,31 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
           }
         }
         const bool more = w2 < a.n_items;
-        const uint32_t s2 = (step + 1) % CORE_STAGES;
-        const int nr = it.has_b ? 2 : 1;
-        for (int r = 0; r < nr && ok; ++r) {
-          const uint32_t tb_r = tmem + 256u * r;
-          ok = mbar_wait(bars + 64 + 8 * r, t_r[r] & 1, a.status);
-          if (first && n_r[r] > 0) ok = ok && mbar_wait(bars + 128 + 8 * r, (n_r[r] - 1) & 1, a.status);
+        if (r == 1 && !it.has_b) {
+          mbar_arrive(bar_empty0 + 8 * s);  // no row B at the odd last row pair
+        } else {
+          // 1. S of the next step as soon as this row has read this step's S
+          if (more && (r == 0 || it2.has_b)) {
+            const uint32_t s2 = (step + 1) % CORE_STAGES;
+            ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
+            tc_fence_after();
+            issue_s(s2);
+          }
+          // 2. P.V of this step once its P is written
+          ok = ok && mbar_wait(bar_p, np & 1, a.status);
+          if (first && ni > 0) ok = ok && mbar_wait(bar_of, (ni - 1) & 1, a.status);
           tc_fence_after();
-          const uint64_t dv = dV0 + s * kStageD + (r ? kRowVD : 0);
+          const uint64_t dv = dV0 + s * kStageD;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             // key step kk: atom kk/4 (6 KB apart), 32 B into the 128 B swizzle row per step
             const uint64_t d = dv + (uint64_t)((kk >> 2) * (CS_VT_ATOM >> 4) + (kk & 3) * 2);
-            umma_f16_ts(tb_r + T_O, tb_r + T_S + kk * 8, d, id_o, (!first || kk > 0) ? 1u : 0u);
+            umma_f16_ts(tb_r + T_O, tb_r + T_P + kk * 8, d, id_o, (!first || kk > 0) ? 1u : 0u);
           }
-          umma_commit(bars + 80 + 8 * r);
-          t_r[r] += 1;
-          if (first) n_r[r] += 1;
-          if (r == nr - 1) umma_commit(bar_empty0 + 8 * s);
-          const bool r_in_next = more && (r == 0 || it2.has_b);
-          if (r_in_next) {
-            if (r == 0) {
-              ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
-              tc_fence_after();
-            }
-            if (first2) {
-              // item n_r[r] of this row uses slot n_r & 1 for the (n_r >> 1)-th time
-              ok = ok && mbar_wait(bars + 96 + 16 * r + 8 * (n_r[r] & 1), (n_r[r] >> 1) & 1, a.status);
-              tc_fence_after();
-            }
-            issue_s(r, s2, first2 ? (n_r[r] & 1) : ((n_r[r] - 1) & 1));
-          }
+          umma_commit(bar_o);
+          umma_commit(bar_empty0 + 8 * s);
+          np += 1;
+          if (first) ni += 1;
         }
         w = w2;
         it = it2;
@@ -351,8 +344,8 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         first = first2;
         ++step;
       }
-      umma_commit(bars + 176);  // drain: every MMA complete before TMEM is released
-      mbar_wait_drain(bars + 176, 0);
+      umma_commit(bars + 128 + 8 * r);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 128 + 8 * r, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax (row r)
@@ -362,41 +355,29 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
     const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
     const uint32_t tb_r = tmem + 256u * r;
     const uint32_t bar_s = bars + 48 + 8 * r, bar_p = bars + 64 + 8 * r, bar_o = bars + 80 + 8 * r,
-                   bar_q0 = bars + 96 + 16 * r, bar_of = bars + 128 + 8 * r;
-    uint32_t t = 0, n = 0;
+                   bar_sf = bars + 96 + 8 * r, bar_of = bars + 112 + 8 * r;
+    uint32_t t = 0;
     bool ok = true;
-    for (int64_t w = blockIdx.x; w < a.n_items && ok; w += gridDim.x) {
-      const Item it = decode_item(a, w);
-      if (r == 1 && !it.has_b) break;  // rows B end at the odd last row pair
-      if (n == 0) {
-        load_q_row(a, it, r, row_tid, tb_r, 0, lane_base);
+    // Q of this row's first item, then "S columns free" for the first S
+    if (blockIdx.x < a.n_items) {
+      const Item it0 = decode_item(a, blockIdx.x);
+      if (r == 0 || it0.has_b) {
+        load_q_row(a, it0, r, row_tid, tb_r, lane_base);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_q0);
+        if (lane == 0) mbar_arrive(bar_sf);
       }
-      // Q of this row's next item, one item ahead, into the other slot: fetched from global
-      // memory now, written to TMEM after this item's first tile so the fetch latency is hidden.
-      // Slot (n+1)&1 was last read by the S MMAs of item n-1, all complete by now.
-      uint32_t qnext[16];
-      bool q_pending = false;
-      {
-        const int64_t wn = w + gridDim.x;
-        if (wn < a.n_items) {
-          const Item itn = decode_item(a, wn);
-          if (r == 0 || itn.has_b) {
-            fetch_q_row(a, itn, r, row_tid, qnext);
-            q_pending = true;
-          }
-        }
-      }
+    }
+    for (int64_t w = blockIdx.x; w < a.n_items && ok; w += gridDim.x) {
+      const Item it = decode_item(a, w);
+      if (r == 1 && !it.has_b) break;  // rows B end at the odd last row pair
       const int64_t i = it.i0 + r;
       const uint8_t* fr = r ? it.fb : it.fa;
       const bool uniform = (a.rowflags[i] & 1) != 0;
       float m_run = -INFINITY;
       int it_in = 0;
-      for (int kt = next_tile(it.fa, it.fb, 0, n_tiles); kt < n_tiles && ok;
-           kt = next_tile(it.fa, it.fb, kt + 1, n_tiles), ++t, ++it_in) {
+      for (int kt = next_tile(it.fa, it.fb, 0, n_tiles); kt < n_tiles && ok; ++t, ++it_in) {
         const uint32_t s = t % CORE_STAGES;
         const uint8_t fl = fr[kt];
         const uint8_t* sb = g + s * CS_BYTES;
@@ -415,12 +396,32 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
           mx = tile_logits<true, true>(tb_r + T_S + lane_base, brow, mbrow, row_tid, x);
         else
           mx = tile_logits<true, false>(tb_r + T_S + lane_base, brow, mbrow, row_tid, x);
+        // S is in registers: its columns are free for the next S. Before the item's last S is
+        // released, the next item's Q goes into the Q columns (every S of this item is done).
+        kt = next_tile(it.fa, it.fb, kt + 1, n_tiles);
+        if (kt >= n_tiles) {
+          const int64_t wn = w + gridDim.x;
+          if (wn < a.n_items) {
+            const Item itn = decode_item(a, wn);
+            if (r == 0 || itn.has_b) {
+              load_q_row(a, itn, r, row_tid, tb_r, lane_base);
+              tmem_st_wait();
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_sf);
         const float tmax = fmaxf(f16lo(mx), f16hi(mx));
-        // lazy rescale, warp-collective (tcgen05.ld/st need all lanes)
         const bool need = tmax > m_run + 8.0f;
-        if (__any_sync(0xffffffffu, need && m_run != -INFINITY) && it_in > 0) {
+        // the previous P.V must be done before O is rescaled or P is overwritten (within an
+        // item; the item epilogue already waited for the previous item's last one)
+        if (it_in > 0) {
           ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (t - 1) & 1, a.status)) && ok;
           tc_fence_after();
+        }
+        // lazy rescale, warp-collective (tcgen05.ld/st need all lanes)
+        if (__any_sync(0xffffffffu, need && m_run != -INFINITY) && it_in > 0) {
           const float alpha = (need && m_run != -INFINITY) ? ex2_approx(m_run - tmax) : 1.0f;
           uint32_t ov[16], lv[16];   // [O | l] columns 0..15 and 32..47 (l in column 32)
           tmem_ld16(tb_r + T_O + lane_base, ov);
@@ -438,7 +439,6 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
 #pragma unroll
           for (int e = 0; e < 16; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
           tmem_st16(tb_r + T_O + 16 + lane_base, ov);
-          tmem_st_wait();
         }
         if (need) m_run = tmax;
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
@@ -447,21 +447,17 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
         for (int c = 0; c < 4; ++c) {
           uint32_t p[16];
 #pragma unroll
-          for (int e = 0; e < 16; ++e) p[e] = ex2_f16x2(hsub2_u(x[c * 16 + e], mh));
-          tmem_st16(tb_r + T_S + lane_base + c * 16, p);
+          for (int e = 0; e < 16; ++e) {
+            // PF_CORE_FMA_PAIRS of every 16 pairs (evenly spread) on the FMA pipe, the rest on MUFU
+            const uint32_t y = hsub2_u(x[c * 16 + e], mh);
+            p[e] = ((e * PF_CORE_FMA_PAIRS) % 16 < PF_CORE_FMA_PAIRS) ? ex2_poly_f16x2(y) : ex2_f16x2(y);
+          }
+          tmem_st16(tb_r + T_P + lane_base + c * 16, p);
         }
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(bar_p);
-        if (q_pending) {  // warp-uniform
-          tmem_st16(tb_r + lane_base + T_Q + 16 * ((n + 1) & 1), qnext);
-          tmem_st_wait();
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar_q0 + 8 * ((n + 1) & 1));
-          q_pending = false;
-        }
       }
       // item epilogue: o = O / l
       ok = __all_sync(0xffffffffu, mbar_wait(bar_o, (t - 1) & 1, a.status)) && ok;
@@ -474,7 +470,6 @@ __global__ void __launch_bounds__(320, 1) k_triatt_core(const __grid_constant__ 
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar_of);
-      ++n;
       const int64_t j = (int64_t)it.jt * TILE + row_tid;
       // A logit past the f16 range (|q.k| log2(e)/sqrt(d) > 65504) turns the row sum into inf
       // or NaN: report it (status bit 1) instead of returning a silently wrong row.

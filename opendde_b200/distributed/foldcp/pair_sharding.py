@@ -69,25 +69,28 @@ class FoldCPPairShardSpec:
         return asdict(self)
 
 
-def _normalize_pair_dims(ndim: int, pair_dims: Tuple[int, int]) -> Tuple[int, int]:
-    row_dim, col_dim = pair_dims
-    if row_dim < 0:
-        row_dim += ndim
-    if col_dim < 0:
-        col_dim += ndim
-    if row_dim == col_dim:
-        raise ValueError("pair_dims must point to two different dimensions.")
-    if not (0 <= row_dim < ndim and 0 <= col_dim < ndim):
-        raise ValueError(f"pair_dims {pair_dims} are outside tensor ndim={ndim}.")
-    return row_dim, col_dim
+def _resolve_pair_dims(ndim: int, pair_dims: Tuple[int, int]) -> Tuple[int, int]:
+    """Absolute (row, column) dims of the token-pair plane; negative dims count from the end."""
+    dims = []
+    for d in pair_dims:
+        a = d + ndim if d < 0 else d
+        if not 0 <= a < ndim:
+            raise ValueError(f"pair dim {d} does not exist in a {ndim}-d tensor (pair_dims={pair_dims})")
+        dims.append(a)
+    if dims[0] == dims[1]:
+        raise ValueError(f"pair_dims {pair_dims} name the same dimension twice")
+    return dims[0], dims[1]
 
 
 def infer_pair_dims(tensor: torch.Tensor, n_token: int) -> Optional[Tuple[int, int]]:
-    """Token-pair dims of common OpenDDE tensors: [..., N, N] or [..., N, N, C]."""
-    if tensor.ndim >= 2 and tuple(tensor.shape[-2:]) == (n_token, n_token):
-        return (tensor.ndim - 2, tensor.ndim - 1)
-    if tensor.ndim >= 3 and tuple(tensor.shape[-3:-1]) == (n_token, n_token):
-        return (tensor.ndim - 3, tensor.ndim - 2)
+    """Token-pair dims of common OpenDDE tensors: [..., N, N] (masks, biases) or
+    [..., N, N, C] (pair representations); None when neither layout matches."""
+    shape = tuple(tensor.shape)
+    for lead in (2, 3):  # the pair dims end the shape, or sit just before a channel dim
+        if len(shape) >= lead:
+            a = len(shape) - lead
+            if shape[a] == n_token and shape[a + 1] == n_token:
+                return a, a + 1
     return None
 
 
@@ -97,11 +100,10 @@ def padded_pair_size(n_pair: int, mesh_shape: Tuple[int, int]) -> int:
     return int(math.ceil(n_pair / step) * step)
 
 
-def _slice_for_pair(ndim: int, pair_dims: Tuple[int, int], row_range: Range, col_range: Range):
-    slices = [slice(None)] * ndim
-    slices[pair_dims[0]] = slice(*row_range)
-    slices[pair_dims[1]] = slice(*col_range)
-    return tuple(slices)
+def _pair_index(ndim: int, pair_dims: Tuple[int, int], rows: Range, cols: Range):
+    """Index tuple selecting rows x cols of the pair plane and everything of the other dims."""
+    return tuple(slice(*rows) if d == pair_dims[0] else slice(*cols) if d == pair_dims[1] else slice(None)
+                 for d in range(ndim))
 
 
 def _spec_for(original_shape, mesh_shape, coord, pair_dims) -> FoldCPPairShardSpec:
@@ -122,14 +124,14 @@ def _spec_for(original_shape, mesh_shape, coord, pair_dims) -> FoldCPPairShardSp
 def make_pair_shard_spec(original_shape: Tuple[int, ...], mesh: FoldCPProcessMesh,
                          pair_dims: Tuple[int, int]) -> FoldCPPairShardSpec:
     """Pair-shard metadata without materialising the full pair tensor."""
-    pair_dims = _normalize_pair_dims(len(original_shape), pair_dims)
+    pair_dims = _resolve_pair_dims(len(original_shape), pair_dims)
     return _spec_for(tuple(original_shape), mesh.layout.shape, mesh.coord, pair_dims)
 
 
 def shard_pair_tensor(tensor: torch.Tensor, mesh: FoldCPProcessMesh, pair_dims: Tuple[int, int],
                       pad_value: float = 0.0) -> Tuple[torch.Tensor, FoldCPPairShardSpec]:
     """This rank's (padded) tile of a full pair tensor."""
-    pair_dims = _normalize_pair_dims(tensor.ndim, pair_dims)
+    pair_dims = _resolve_pair_dims(tensor.ndim, pair_dims)
     spec = _spec_for(tuple(tensor.shape), mesh.layout.shape, mesh.coord, pair_dims)
     return shard_with_spec(tensor, spec, pad_value), spec
 
@@ -140,8 +142,8 @@ def shard_with_spec(tensor: torch.Tensor, spec: FoldCPPairShardSpec, pad_value: 
     (r0, r1), (c0, c1) = spec.row_range, spec.col_range
     vr, vc = min(r1, n), min(c1, n)
     if r0 < vr and c0 < vc:
-        local[_slice_for_pair(tensor.ndim, spec.pair_dims, (0, vr - r0), (0, vc - c0))] = \
-            tensor[_slice_for_pair(tensor.ndim, spec.pair_dims, (r0, vr), (c0, vc))]
+        local[_pair_index(tensor.ndim, spec.pair_dims, (0, vr - r0), (0, vc - c0))] = \
+            tensor[_pair_index(tensor.ndim, spec.pair_dims, (r0, vr), (c0, vc))]
     return local
 
 
@@ -167,8 +169,8 @@ def _assemble(shards: List[torch.Tensor], layout: FoldCP2DLayout, pair_dims, out
         r1, c1 = min(r0 + tr, n_r), min(c0 + tc, n_c)
         if r0 >= r1 or c0 >= c1:
             continue
-        full[_slice_for_pair(full.ndim, pair_dims, (r0, r1), (c0, c1))] = \
-            shard[_slice_for_pair(shard.ndim, pair_dims, (0, r1 - r0), (0, c1 - c0))]
+        full[_pair_index(full.ndim, pair_dims, (r0, r1), (c0, c1))] = \
+            shard[_pair_index(shard.ndim, pair_dims, (0, r1 - r0), (0, c1 - c0))]
     return full
 
 
