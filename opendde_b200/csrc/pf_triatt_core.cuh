@@ -5,12 +5,11 @@
 // walks items w = blockIdx.x, blockIdx.x + gridDim.x, ... and a key-tile "step" stream runs
 // through a 3-stage TMA ring continuously across items. The two rows of an item share the
 // triangle-bias tile (bias[h][j][k] does not depend on i).
-// Warp roles (352 threads):
+// Warp roles (320 threads):
 //   warps 0-3  softmax for row A (thread = query; TMEM lanes 0..127)
 //   warps 4-7  softmax for row B
 //   warp 8     TMA producer: per step the bias tile, K, V^T and key-mask rows of both rows
-//   warp 9     MMA issuer of row A (single thread) and TMEM owner
-//   warp 10    MMA issuer of row B (single thread)
+//   warp 9     MMA issuer (single thread) and TMEM owner
 // TMEM (per row R, base 256*R): S [0,128) f16 accumulator (one value per column), P [128,192)
 // (f16, two per column), [O | l] [192,240) fp32, Q [240,256) (f16, two per column).
 //   S = Q K^T           A = Q (TMEM), B = K tile (smem, 64B swizzle), f16 x f16 -> f16
@@ -22,9 +21,8 @@
 // columns), and the MMA thread issues S(t+1) at once; P(t) and PV(t) follow. Per step and row
 // the softmax threads therefore wait only for their own previous P.V (before overwriting P or
 // rescaling O), not for a P -> PV -> S round trip through the tensor pipe.
-// Each row has its own MMA-issuing thread (a tcgen05.mma costs the issuing thread far more than
-// these small MMAs cost the tensor pipe), per step t: S(t+1) after the row has read S(t), then
-// PV(t) after the row's P(t), then its half of the stage release.
+// MMA thread, per step t: S_A(t+1), S_B(t+1) (each after its row has read S(t)), then PV_A(t),
+// PV_B(t) (each after its row's P(t)), then release of the stage's shared memory.
 // Softmax is packed f16x2 on log2-domain logits read straight from TMEM (tcgen05.ld
 // .pack::16b): + bias, + key mask (0 / -inf), max, - m, ex2.f16x2. The running max is updated
 // lazily (O, L rescaled in TMEM only when a tile's max exceeds it by more than 8).
@@ -41,9 +39,9 @@ struct CoreArgs {
 };
 
 #ifndef PF_CORE_FMA_PAIRS
-#define PF_CORE_FMA_PAIRS 0
+#define PF_CORE_FMA_PAIRS 4
 #endif
-constexpr int CORE_THREADS = 352;
+constexpr int CORE_THREADS = 320;
 constexpr int CORE_STAGES = 3;
 // per-stage layout (bytes from the stage base)
 constexpr uint32_t CS_KA = 0;                  // 128 x 64 B (SW64) f16
@@ -191,7 +189,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
   if (tid == 0) {
     for (int s = 0; s < CORE_STAGES; ++s) {
       mbar_init(bar_full0 + 8 * s, 1);
-      mbar_init(bar_empty0 + 8 * s, 2);  // one arrival per row's MMA thread
+      mbar_init(bar_empty0 + 8 * s, 1);
     }
     for (int r = 0; r < 2; ++r) {
       mbar_init(bars + 48 + 8 * r, 1);    // S ready (tcgen05.commit)
@@ -200,8 +198,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       mbar_init(bars + 96 + 8 * r, 4);    // S read / Q written
       mbar_init(bars + 112 + 8 * r, 4);   // O/L read out, free for the next item
     }
-    mbar_init(bars + 128, 1);             // drain (row A's MMA thread)
-    mbar_init(bars + 136, 1);             // drain (row B's MMA thread)
+    mbar_init(bars + 128, 1);             // drain
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -254,35 +251,30 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         }
       }
     }
-  } else if (warp == 9 || warp == 10) {
-    // ------------------------------------------------------------ MMA issuers (one per row)
-    // Warp 9 issues row A's MMAs, warp 10 row B's: each thread walks the same step stream,
-    // and a stage is released once both rows' P.V of that step are done (two arrivals).
+  } else if (warp == 9) {
+    // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const int r = warp - 9;
       constexpr uint32_t id_s = idesc_f16_f16acc(128, 128);               // f16 x f16 -> f16
       constexpr uint32_t id_o = idesc_f16(128, 48, false);                // f16 x f16 -> fp32
-      uint32_t ns = 0;   // S issued for this row (sfree phases)
-      uint32_t np = 0;   // P.V issued (p phases)
-      uint32_t ni = 0;   // items begun (ofree phases)
+      uint32_t ns[2] = {0, 0};   // S issued per row (sfree phases)
+      uint32_t np[2] = {0, 0};   // P.V issued per row (p phases)
+      uint32_t ni[2] = {0, 0};   // items begun per row (ofree phases)
       bool ok = true;
-      const uint32_t tb_r = tmem + 256u * r;
-      const uint32_t bar_s = bars + 48 + 8 * r, bar_p = bars + 64 + 8 * r, bar_o = bars + 80 + 8 * r,
-                     bar_sf = bars + 96 + 8 * r, bar_of = bars + 112 + 8 * r;
-      // Descriptors of stage 0 for this row; other stages / K-steps differ only in the start
+      // Descriptors of stage 0, row A; other stages / row B / K-steps differ only in the start
       // address field (address >> 4), so each MMA's descriptor is one 64-bit add.
-      const uint64_t dK0 = sdesc(base + (r ? CS_KB : CS_KA), 512, SWZ_64B);
-      const uint64_t dV0 = sdesc(base + (r ? CS_VTB : CS_VTA), 1024, SWZ_128B);
-      constexpr uint64_t kStageD = CS_BYTES >> 4;
-      // S for the step in stage s, once this row's softmax has read its previous S
-      auto issue_s = [&](uint32_t s) {
-        ok = ok && mbar_wait(bar_sf, ns & 1, a.status);
+      const uint64_t dK0 = sdesc(base + CS_KA, 512, SWZ_64B);
+      const uint64_t dV0 = sdesc(base + CS_VTA, 1024, SWZ_128B);
+      constexpr uint64_t kStageD = CS_BYTES >> 4, kRowKD = (CS_KB - CS_KA) >> 4, kRowVD = (CS_VTB - CS_VTA) >> 4;
+      // S of row r for the step in stage s, once row r's softmax has read its previous S
+      auto issue_s = [&](int r, uint32_t s) {
+        ok = ok && mbar_wait(bars + 96 + 8 * r, ns[r] & 1, a.status);
         tc_fence_after();
-        const uint64_t dk = dK0 + s * kStageD;
+        const uint32_t tb_r = tmem + 256u * r;
+        const uint64_t dk = dK0 + s * kStageD + (r ? kRowKD : 0);
         umma_f16_ts(tb_r + T_S, tb_r + T_Q, dk, id_s, 0u);
         umma_f16_ts(tb_r + T_S, tb_r + T_Q + 8, dk + 2, id_s, 1u);  // +32 B
-        umma_commit(bar_s);
-        ns += 1;
+        umma_commit(bars + 48 + 8 * r);
+        ns[r] += 1;
       };
       int64_t w = blockIdx.x;
       Item it;
@@ -293,7 +285,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         kt = next_tile(it.fa, it.fb, 0, n_tiles);
         ok = mbar_wait(bar_full0, 0, a.status);
         tc_fence_after();
-        if (r == 0 || it.has_b) issue_s(0);
+        for (int r = 0; r < (it.has_b ? 2 : 1) && ok; ++r) issue_s(r, 0);
       }
       bool first = true;
       while (w < a.n_items && ok) {
@@ -312,40 +304,40 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
           }
         }
         const bool more = w2 < a.n_items;
-        if (r == 1 && !it.has_b) {
-          mbar_arrive(bar_empty0 + 8 * s);  // no row B at the odd last row pair
-        } else {
-          // 1. S of the next step as soon as this row has read this step's S
-          if (more && (r == 0 || it2.has_b)) {
-            const uint32_t s2 = (step + 1) % CORE_STAGES;
-            ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
-            tc_fence_after();
-            issue_s(s2);
-          }
-          // 2. P.V of this step once its P is written
-          ok = ok && mbar_wait(bar_p, np & 1, a.status);
-          if (first && ni > 0) ok = ok && mbar_wait(bar_of, (ni - 1) & 1, a.status);
+        const int nr = it.has_b ? 2 : 1;
+        // 1. S of the next step, for each row as soon as it has read this step's S
+        if (more) {
+          const uint32_t s2 = (step + 1) % CORE_STAGES;
+          ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
           tc_fence_after();
-          const uint64_t dv = dV0 + s * kStageD;
+          for (int r = 0; r < (it2.has_b ? 2 : 1) && ok; ++r) issue_s(r, s2);
+        }
+        // 2. P.V of this step, for each row once its P is written
+        for (int r = 0; r < nr && ok; ++r) {
+          const uint32_t tb_r = tmem + 256u * r;
+          ok = mbar_wait(bars + 64 + 8 * r, np[r] & 1, a.status);
+          if (first && ni[r] > 0) ok = ok && mbar_wait(bars + 112 + 8 * r, (ni[r] - 1) & 1, a.status);
+          tc_fence_after();
+          const uint64_t dv = dV0 + s * kStageD + (r ? kRowVD : 0);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             // key step kk: atom kk/4 (6 KB apart), 32 B into the 128 B swizzle row per step
             const uint64_t d = dv + (uint64_t)((kk >> 2) * (CS_VT_ATOM >> 4) + (kk & 3) * 2);
             umma_f16_ts(tb_r + T_O, tb_r + T_P + kk * 8, d, id_o, (!first || kk > 0) ? 1u : 0u);
           }
-          umma_commit(bar_o);
-          umma_commit(bar_empty0 + 8 * s);
-          np += 1;
-          if (first) ni += 1;
+          umma_commit(bars + 80 + 8 * r);
+          np[r] += 1;
+          if (first) ni[r] += 1;
         }
+        umma_commit(bar_empty0 + 8 * s);
         w = w2;
         it = it2;
         kt = kt2;
         first = first2;
         ++step;
       }
-      umma_commit(bars + 128 + 8 * r);  // drain: every MMA complete before TMEM is released
-      mbar_wait_drain(bars + 128 + 8 * r, 0);
+      umma_commit(bars + 128);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bars + 128, 0);
     }
   } else {
     // ------------------------------------------------------------ softmax (row r)
