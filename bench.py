@@ -304,6 +304,72 @@ def parity_vs_one_gpu(stack, s_dev, z_dev, m_dev, blocks, rank, barrier):
     return out
 
 
+# ------------------------------------------------------------------------------ C1 / C2
+def run_op_workload(args, kind):
+    """Standalone triangle attention (C1: start and end, N = 384 / 768 / 1536, last 10 % of tokens
+    padded) or triangle multiplicative update (C2: outgoing and incoming, N = 1024), bf16, one
+    GPU: ms per call through the module forward (inputs resident), and the core kernel's
+    fraction of the measured peak from the library's per-launch work and CUDA-event times."""
+    from opendde_b200 import _abi
+    from opendde_b200.model import (TriangleAttention, TriangleMultiplicationIncoming,
+                                    TriangleMultiplicationOutgoing)
+    from opendde_b200.utils import make_inputs, seeded_init_
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    if kind == "c1":
+        sizes, pad, core = [384, 768, 1536], 0.1, "k_triatt_core"
+        mods = [("start", TriangleAttention(c_in=C_Z, c_hidden=HEAD_DIM, no_heads=HEADS_PAIR, starting=True)),
+                ("end", TriangleAttention(c_in=C_Z, c_hidden=HEAD_DIM, no_heads=HEADS_PAIR, starting=False))]
+        metric = "ms per standalone triangle-attention call (C1), bf16; tri-attn % peak"
+    else:
+        sizes, pad, core = [1024], 0.0, "k_trimul_bgemm"
+        mods = [("out", TriangleMultiplicationOutgoing(c_z=C_Z, c_hidden=C_H)),
+                ("in", TriangleMultiplicationIncoming(c_z=C_Z, c_hidden=C_H))]
+        metric = "ms per standalone triangle multiplicative update call (C2), bf16; tri-mul % peak"
+    for _, m in mods:
+        seeded_init_(m, seed=0)
+        m.to(dev)
+    rows = []
+    st = torch.cuda.current_stream()
+    with ClockSampler(0) as clk:
+        for n in sizes:
+            _, z, mask = make_inputs(n, c_z=C_Z, seed=1, pad_frac=pad, with_s=False)
+            zb, md = z.to(dev, torch.bfloat16), mask.to(dev)
+            for name, m in mods:
+                with torch.no_grad():
+                    for _ in range(args.warmup):
+                        m(zb, mask=md)
+                    torch.cuda.synchronize()
+                    _abi.profile_enable(True)
+                    _abi.profile_report()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(st)
+                    for _ in range(args.steps):
+                        m(zb, mask=md)
+                    e1.record(st)
+                    torch.cuda.synchronize()
+                    _abi.profile_enable(False)
+                    prof = _abi.profile_report()
+                ms = e0.elapsed_time(e1) / args.steps
+                e = kernel_entry(core, *prof[core], peaks) if core in prof else None
+                kern = {k: round(v[1] / v[0], 4) for k, v in prof.items()}
+                rows.append({"n": n, "op": name, "ms_per_call": ms, "core": e, "kernels_ms_per_launch": kern})
+    assert _abi.device_status() == 0, "a device-side bounded wait timed out"
+    big = [r for r in rows if r["n"] == sizes[-1]]
+    value = statistics.mean(r["ms_per_call"] for r in big)
+    print(json.dumps({
+        "metric": metric, "value": value, "unit": "ms/call", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": value, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": f"synthetic: z ~ N(0,1), last {int(pad * 100)} % of tokens padded, seed-0 N(0,1/fan_in) weights",
+        "config": {"workload": f"{kind}_" + "_".join(str(n) for n in sizes), "c_z": C_Z,
+                   "l2": "inputs at N >= 768 larger than L2; smaller ones repeat from L2"},
+        "roofline": big[0]["core"], "sweep": rows, "clocks": clk.summary(),
+    }), flush=True)
+
+
 # ------------------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -311,6 +377,9 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=["trunk", "c1", "c2"], default="trunk",
+                    help="trunk: the 48-block trunk (the headline); c1 / c2: standalone triangle attention / "
+                         "triangle multiplicative update at their configurations (1 GPU)")
     ap.add_argument("--n", type=int, default=N_TOKEN)
     ap.add_argument("--pad-frac", type=float, default=0.0,
                     help="fraction of trailing tokens masked as padding (config C4: 0.07)")
@@ -329,6 +398,10 @@ def main():
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     cores = os.cpu_count() or 1
+    if args.workload != "trunk" and args.impl == "ours":
+        if rank == 0:
+            run_op_workload(args, args.workload)
+        return
 
     if args.impl == "reference":
         if rank != 0:

@@ -284,22 +284,28 @@ def _check_tile(z_local: torch.Tensor) -> None:
         raise ValueError("Fold-CP pair ops take a contiguous [Tr, Tc, C] local tile")
 
 
-def _finish(z_local: torch.Tensor, residual_local: Optional[torch.Tensor], before: Optional[torch.Tensor]):
-    """The reference returns residual + update when a residual is given, else the update."""
-    if residual_local is not None:
-        return z_local
-    return z_local - before
+def _in_place(z_local: torch.Tensor, residual_local: Optional[torch.Tensor]) -> bool:
+    return residual_local is not None and (residual_local is z_local or (
+        residual_local.data_ptr() == z_local.data_ptr() and residual_local.shape == z_local.shape and
+        residual_local.stride() == z_local.stride()))
 
 
 def _prepare(z_local, residual_local):
-    """The tile the kernels accumulate into, and a copy of the input when only the update
-    is wanted."""
+    """The tile the kernels accumulate into (the kernels add the update to it) and the input
+    it started from when that is not the result: the update is fused into z_local itself when
+    residual_local is z_local (the block's usage); otherwise a copy takes the update."""
     _check_tile(z_local)
-    if residual_local is not None and residual_local is not z_local:
-        if residual_local.data_ptr() != z_local.data_ptr():
-            raise ValueError("residual_local must be z_local (the update is fused into the tile)")
-    before = None if residual_local is not None else z_local.clone()
-    return z_local, before
+    if _in_place(z_local, residual_local):
+        return z_local, None
+    return z_local.clone(), z_local
+
+
+def _finish(work: torch.Tensor, residual_local: Optional[torch.Tensor], before: Optional[torch.Tensor]):
+    """The reference returns residual + update when a residual is given, else the update."""
+    if before is None:
+        return work
+    update = work - before
+    return update if residual_local is None else residual_local + update
 
 
 def distributed_triangle_multiplication_update(module, z_local: torch.Tensor, mesh: FoldCPProcessMesh,
@@ -310,11 +316,9 @@ def distributed_triangle_multiplication_update(module, z_local: torch.Tensor, me
     """z_local + TriMul(z) on this rank's tile (update only when no residual is given)."""
     ops = _ops(ops)
     ctx = context or make_context(mesh, z_local, z_spec, mask_local)
-    z_local, before = _prepare(z_local, residual_local)
-    if before is not None:
-        z_local = z_local.clone()
-    _trimul(module, z_local, ctx, ops)
-    return _finish(z_local, residual_local, before)
+    work, before = _prepare(z_local, residual_local)
+    _trimul(module, work, ctx, ops)
+    return _finish(work, residual_local, before)
 
 
 def distributed_triangle_attention_update(module, z_local: torch.Tensor, mesh: FoldCPProcessMesh,
@@ -327,11 +331,9 @@ def distributed_triangle_attention_update(module, z_local: torch.Tensor, mesh: F
     the starting or ending node (the ending node without the reference's transposes)."""
     ops = _ops(ops)
     ctx = context or make_context(mesh, z_local, z_spec, mask_local)
-    z_local, before = _prepare(z_local, residual_local)
-    if before is not None:
-        z_local = z_local.clone()
-    _triatt(module, z_local, ctx, not module.starting, ops)
-    return _finish(z_local, residual_local, before)
+    work, before = _prepare(z_local, residual_local)
+    _triatt(module, work, ctx, not module.starting, ops)
+    return _finish(work, residual_local, before)
 
 
 def distributed_pair_transition_update(module, z_local: torch.Tensor, mesh: FoldCPProcessMesh,
@@ -339,11 +341,9 @@ def distributed_pair_transition_update(module, z_local: torch.Tensor, mesh: Fold
                                        z_spec: Optional[FoldCPPairShardSpec] = None, *, ops=None):
     """z_local + Transition(z_local): pointwise, no communication."""
     ops = _ops(ops)
-    z_local, before = _prepare(z_local, residual_local)
-    if before is not None:
-        z_local = z_local.clone()
-    ops.transition(module, z_local.view(-1, z_local.shape[-1]))
-    return _finish(z_local, residual_local, before)
+    work, before = _prepare(z_local, residual_local)
+    ops.transition(module, work.view(-1, work.shape[-1]))
+    return _finish(work, residual_local, before)
 
 
 def _single_rows(ctx: FoldCPPairContext) -> Tuple[int, int, int]:
@@ -383,6 +383,10 @@ def distributed_attention_pair_bias_update(attention_pair_bias, a: torch.Tensor,
     tr, tc = spec.tile_rows, spec.tile_cols
     tile = torch.empty((H, tr, tc), device=z_local.device, dtype=torch.float32)
     ops.apb_pair_bias(attention_pair_bias, z_local, tile)
+    if extra_attn_bias_full is None and extra_attn_bias_local is not None:
+        # this rank's tile of the extra bias ([H or 1, Tr, Tc]) rides in the same row gather
+        e = extra_attn_bias_local.to(device=tile.device, dtype=torch.float32)
+        tile = tile + (e if e.dim() == 3 else e[None])[..., :tr, :tc]
     row_tiles = ctx.exchange.all_gather(tile, "row")                      # [C, H, Tr, Tc]
     q0, nq, per = _single_rows(ctx)
     lo = q0 - ctx.rows[0]
@@ -394,8 +398,6 @@ def distributed_attention_pair_bias_update(attention_pair_bias, a: torch.Tensor,
             e = extra_attn_bias_full.to(device=bias_rows.device, dtype=torch.float32)
             e = e if e.dim() == 3 else e[None]
             bias_rows = bias_rows + e[:, q0:q0 + nq, :n]
-        elif extra_attn_bias_local is not None:
-            raise ValueError("pass the extra attention bias whole (extra_attn_bias_full) on an R x C mesh")
         bias_rows = bias_rows.contiguous()
         ops.apb_rows(attention_pair_bias, a, rows, bias_rows, q0)
         if single_transition is not None:

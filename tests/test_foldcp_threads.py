@@ -125,3 +125,76 @@ def test_cp_stack_overlapped_attention_chunks(shape, chunks, monkeypatch):
     for s_out, z_out in outs:
         assert (z_out - z_ref).abs().max().item() <= TOL
         assert (s_out - s_ref).abs().max().item() <= TOL
+
+
+@pytest.mark.parametrize("shape", [(1, 2), (2, 2)])
+def test_cp_single_ops_with_a_separate_residual(shape):
+    """residual_local that is not the tile itself: the result is residual + update, and the
+    tile is left as it was (reference real_pairformer.py:1226 semantics)."""
+    n = 11
+    stack, p = _stack(1)
+    blk = stack.blocks[0]
+    s, z, mask = _inputs(n, seed=6)
+    g = torch.Generator().manual_seed(9)
+    resid = torch.randn(z.shape, generator=g)
+    sub = lambda pre: {k[len(pre) + 1:]: v for k, v in p.items() if k.startswith(pre + ".")}  # noqa: E731
+    with torch.no_grad():
+        upd = {"tmo": O.triangle_multiplication(z, mask, sub("blocks.0.tri_mul_out"), outgoing=True),
+               "tas": O.triangle_attention(z, mask, sub("blocks.0.tri_att_start"), 4, starting=True),
+               "tr": O.transition(z, sub("blocks.0.pair_transition"))}
+    mesh = ThreadMesh(shape)
+
+    def rank_fn(ex, rank):
+        spec = _spec_for(tuple(z.shape), shape, ex.coord, (0, 1))
+        z_local = shard_with_spec(z, spec)
+        r_local = shard_with_spec(resid, spec)
+        keep = z_local.clone()
+        ctx = RP.make_context(None, z_local, spec, mask_full=mask, exchange=ex)
+        ops = OracleBandOps()
+        got = {
+            "tmo": RP.distributed_triangle_multiplication_update(blk.tri_mul_out, z_local, None, residual_local=r_local,
+                                                                 ops=ops, context=ctx),
+            "tas": RP.distributed_triangle_attention_update(blk.tri_att_start, z_local, None, residual_local=r_local,
+                                                            ops=ops, context=ctx),
+            "tr": RP.distributed_pair_transition_update(blk.pair_transition, z_local, None, residual_local=r_local,
+                                                        ops=ops),
+        }
+        assert torch.equal(z_local, keep)
+        return {k: RP.gather_full(v.contiguous(), ctx) for k, v in got.items()}
+
+    with torch.no_grad():
+        res = mesh.run(rank_fn)
+    for got in res:
+        for k in upd:
+            assert (got[k] - (resid + upd[k])).abs().max().item() <= TOL, k
+
+
+@pytest.mark.parametrize("shape", [(2, 2), (2, 4)])
+def test_cp_attention_pair_bias_with_a_local_extra_bias(shape):
+    """extra_attn_bias_local (each rank's tile of an extra [H, N, N] bias) on an R x C mesh
+    equals passing the whole bias."""
+    n = 13
+    stack, p = _stack(1)
+    blk = stack.blocks[0]
+    s, z, mask = _inputs(n, seed=7)
+    g = torch.Generator().manual_seed(11)
+    extra = torch.randn((HEADS, n, n), generator=g)
+    mesh = ThreadMesh(shape)
+
+    def rank_fn(ex, rank):
+        spec = _spec_for(tuple(z.shape), shape, ex.coord, (0, 1))
+        z_local = shard_with_spec(z, spec)
+        espec = _spec_for((HEADS, n, n), shape, ex.coord, (1, 2))
+        e_local = shard_with_spec(extra, espec)
+        ctx = RP.make_context(None, z_local, spec, mask_full=mask, exchange=ex)
+        ops = OracleBandOps()
+        a = RP.distributed_attention_pair_bias_update(blk.attention_pair_bias, s, z_local, None, spec,
+                                                      extra_attn_bias_local=e_local, ops=ops, context=ctx)
+        b = RP.distributed_attention_pair_bias_update(blk.attention_pair_bias, s, z_local, None, spec, ops=ops,
+                                                      context=ctx, extra_attn_bias_full=extra)
+        return a, b
+
+    with torch.no_grad():
+        res = mesh.run(rank_fn)
+    for a, b in res:
+        assert (a - b).abs().max().item() <= 1e-5
