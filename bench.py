@@ -248,30 +248,32 @@ def kernel_entry(name, launches, total_ms, work, unit, peaks, nvlink=None):
         ach = per / avg_s / 1e12
         peak = peaks["bf16_tflops_sustained"]
         base.update({"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s", "frac": ach / peak,
-                     "traffic": read_traffic(name), "work_per_launch": per, "work_unit": "flop",
+                     "traffic": read_traffic(name, per), "work_per_launch": per, "work_unit": "flop",
                      "peak_kind": f"bf16 dense sustained ({peaks['source']})"})
     else:
         ach = per / avg_s / 1e9
         peak = peaks["hbm_gbs"]
         base.update({"bound": "hbm", "achieved": ach, "peak": peak, "unit": "GB/s", "frac": ach / peak,
-                     "traffic": read_traffic(name), "work_per_launch": per, "work_unit": "byte",
+                     "traffic": read_traffic(name, per), "work_per_launch": per, "work_unit": "byte",
                      "peak_kind": f"HBM copy ({peaks['source']})"})
     return base
 
 
-def read_traffic(kernel: str):
-    """DRAM bytes per launch for `kernel` from the committed ncu summary, if any."""
+def read_traffic(kernel: str, work_per_launch: float):
+    """DRAM bytes per launch for `kernel` from the committed ncu summary, when this launch
+    does the same work as the captured one (the summary's third column), else None."""
     p = os.path.join(ROOT, "profiles", "dram_traffic_per_launch.txt")
     if not os.path.exists(p):
         return None
     with open(p) as f:
         for line in f:
             parts = line.split()
-            if len(parts) >= 2 and parts[0] == kernel:
+            if len(parts) >= 3 and parts[0] == kernel:
                 try:
-                    return float(parts[1])
+                    traffic, ref_work = float(parts[1]), float(parts[2])
                 except ValueError:
                     return None
+                return traffic if abs(work_per_launch - ref_work) <= 1e-3 * ref_work else None
     return None
 
 
@@ -305,6 +307,24 @@ def parity_vs_one_gpu(stack, s_dev, z_dev, m_dev, blocks, rank, barrier):
 
 
 # ------------------------------------------------------------------------------ C1 / C2
+def executed_key_fraction(mask: torch.Tensor, tile: int = 128) -> float:
+    """Fraction of the (row, key) pairs whose 128-key tile the attention core executes. The core
+    skips a key tile of a row when every key in it is masked while the row has a key of mask 1
+    (exp() of those logits is exactly 0 in the reference too); a row with no such key attends
+    uniformly over all keys, so none of its tiles is skipped."""
+    n_rows, n = mask.shape
+    n_tiles = (n + tile - 1) // tile
+    full = mask >= 1.0
+    row_full = full.any(dim=1, keepdim=True)
+    live = full | ~row_full
+    pad = n_tiles * tile - n
+    live_t = torch.nn.functional.pad(live, (0, pad), value=False).view(n_rows, n_tiles, tile)
+    run = live_t.any(dim=2)                                         # tile executed
+    keys = torch.full((n_tiles,), tile, device=mask.device)
+    keys[-1] = n - (n_tiles - 1) * tile
+    return float((run.float() * keys).sum() / (n_rows * n))
+
+
 def run_op_workload(args, kind):
     """Standalone triangle attention (C1: start and end, N = 384 / 768 / 1536, last 10 % of tokens
     padded) or triangle multiplicative update (C2: outgoing and incoming, N = 1024), bf16, one
@@ -354,6 +374,14 @@ def run_op_workload(args, kind):
                     prof = _abi.profile_report()
                 ms = e0.elapsed_time(e1) / args.steps
                 e = kernel_entry(core, *prof[core], peaks) if core in prof else None
+                if e is not None and kind == "c1":
+                    # the stated flops count every key (as the reference computes them); the
+                    # core skips fully masked key tiles, so also report the executed work
+                    frac_run = executed_key_fraction(md if name == "start" else md.t())
+                    e.update({"executed_key_fraction": frac_run,
+                              "executed_work_per_launch": e["work_per_launch"] * frac_run,
+                              "achieved_executed": e["achieved"] * frac_run,
+                              "frac_executed": e["frac"] * frac_run})
                 kern = {k: round(v[1] / v[0], 4) for k, v in prof.items()}
                 rows.append({"n": n, "op": name, "ms_per_call": ms, "core": e, "kernels_ms_per_launch": kern})
     assert _abi.device_status() == 0, "a device-side bounded wait timed out"
