@@ -204,7 +204,7 @@ typedef struct {
 
 /* bias(h, r, s) for positions r < n_rows, s < n_cols of z, written to
  * bias + h*bias_head_stride + r*bias_row_stride + s. Format: fp32 natural units for PF_F32;
- * bf16 scaled by log2(e) for PF_BF16 (the tensor-core attention works in base 2). */
+ * f16 (IEEE half) scaled by log2(e) for PF_BF16 (the tensor-core attention works in base 2). */
 PF_API int pf_triatt_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c, int32_t heads,
                                   int32_t dtype, size_t* bytes);
 PF_API int pf_triatt_bias(const pf_triatt_params* w, pf_pair_view z, int64_t n_rows, int64_t n_cols,

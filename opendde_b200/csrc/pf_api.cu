@@ -2,8 +2,9 @@
 //
 // Host-side validation (shapes, dtypes, pointers, workspace size) happens here, before any
 // launch; failures return a status code and leave a message in a thread-local buffer.
-// Dispatch: bf16 requests with the tuned channel counts go to the tcgen05 kernels
-// (pf_tc_*.cu); fp32 requests and every other shape go to the SIMT kernels (pf_simt.cu).
+// Dispatch: bf16 requests with the tuned channel counts go to the fused tcgen05 kernels
+// (pf_tc_*.cu, path "tc"), other bf16 widths to the general-width tcgen05 path (pf_tc_rows.cu,
+// path "tc.rows"); fp32 requests and shapes neither covers go to the SIMT kernels (pf_simt.cu).
 
 #include <cstdarg>
 #include <cstdio>
@@ -89,6 +90,12 @@ int pf_layernorm_fwd(const void* x, void* y, const float* gamma, const float* be
 static bool trimul_tc(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h, int dtype) {
   return dtype == PF_BF16 && !force_simt() && tc::trimul_supported(n_i, n_j, n_k, c_z, c_h);
 }
+// the general-width tensor-core path (every bf16 width the fused c = 128 kernels do not take)
+static bool trimul_rows(int64_t n_i, int64_t n_j, int64_t n_k, int c_z, int c_h, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && !tc::trimul_supported(n_i, n_j, n_k, c_z, c_h) &&
+         tc::rows_trimul_supported(c_z, c_h) && n_i >= 1 && n_j >= 1 && n_k >= 1 && n_i < (1ll << 31) &&
+         n_j < (1ll << 31) && n_k < (1ll << 31);
+}
 
 int pf_trimul_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z, int32_t c_h,
                              int32_t dtype, size_t* bytes) {
@@ -96,8 +103,9 @@ int pf_trimul_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int32_t c_z,
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0)
     return fail(PF_EINVAL_SHAPE, "trimul: bad sizes");
-  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h)
-                                                      : simt::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h);
+  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype)     ? tc::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h)
+           : trimul_rows(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::rows_trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h)
+                                                         : simt::trimul_ws_bytes(n_i, n_j, n_k, c_z, c_h);
   return PF_OK;
 }
 
@@ -123,6 +131,11 @@ int pf_trimul_fwd(const pf_trimul_params* w, pf_pair_view za, pf_pair_view zb, p
     return tc::trimul(w, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, accumulate, workspace,
                       workspace_bytes, st);
   }
+  if (trimul_rows(n_i, n_j, n_k, c_z, c_h, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_trimul(w, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, accumulate, workspace,
+                           workspace_bytes, st);
+  }
   set_path("simt");
   return simt::trimul(w, za, zb, ma, mb, zg, zo, n_i, n_j, n_k, c_z, c_h, accumulate, dtype, workspace,
                       workspace_bytes, st);
@@ -135,7 +148,9 @@ int pf_trimul_project_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_h <= 0) return fail(PF_EINVAL_SHAPE, "trimul project: bad sizes");
   *bytes = trimul_tc(n_rows, n_rows, n_cols, c_z, c_h, dtype) ? 0
-                                                             : simt::trimul_project_ws_bytes(n_rows, n_cols, c_z, c_h);
+           : trimul_rows(n_rows, n_rows, n_cols, c_z, c_h, dtype)
+               ? tc::rows_trimul_project_ws_bytes(n_rows, n_cols, c_z, c_h)
+               : simt::trimul_project_ws_bytes(n_rows, n_cols, c_z, c_h);
   return PF_OK;
 }
 
@@ -157,6 +172,11 @@ int pf_trimul_project(const pf_trimul_params* w, pf_pair_view z, pf_mask_view m,
     set_path("tc");
     return tc::trimul_project(w, z, m, n_rows, n_cols, a_out, b_out, ld, st);
   }
+  if (trimul_rows(n_rows, n_rows, n_cols, c_z, c_h, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_trimul_project(w, z, m, n_rows, n_cols, c_z, c_h, a_out, b_out, ld, workspace, workspace_bytes,
+                                   st);
+  }
   set_path("simt");
   return simt::trimul_project(w, z, m, n_rows, n_cols, c_z, c_h, dtype, a_out, b_out, ld, workspace,
                               workspace_bytes, st);
@@ -167,8 +187,9 @@ int pf_trimul_combine_workspace_size(int64_t n_i, int64_t n_j, int64_t n_k, int3
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   if (n_i < 0 || n_j < 0 || n_k < 0 || c_z <= 0 || c_h <= 0) return fail(PF_EINVAL_SHAPE, "trimul combine: bad sizes");
-  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::trimul_combine_ws_bytes(n_i, n_j)
-                                                      : simt::trimul_combine_ws_bytes(n_i, n_j, c_z, c_h);
+  *bytes = trimul_tc(n_i, n_j, n_k, c_z, c_h, dtype)     ? tc::trimul_combine_ws_bytes(n_i, n_j)
+           : trimul_rows(n_i, n_j, n_k, c_z, c_h, dtype) ? tc::rows_trimul_combine_ws_bytes(n_i, n_j, c_z, c_h)
+                                                         : simt::trimul_combine_ws_bytes(n_i, n_j, c_z, c_h);
   return PF_OK;
 }
 
@@ -190,6 +211,11 @@ int pf_trimul_combine(const pf_trimul_params* w, const void* a, const void* b, i
     set_path("tc");
     return tc::trimul_combine(w, a, b, ld, n_i, n_j, n_k, zg, zo, accumulate, workspace, workspace_bytes, st);
   }
+  if (trimul_rows(n_i, n_j, n_k, c_z, c_h, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_trimul_combine(w, a, b, ld, n_i, n_j, n_k, zg, zo, c_z, c_h, accumulate, workspace,
+                                   workspace_bytes, st);
+  }
   set_path("simt");
   return simt::trimul_combine(w, a, b, ld, n_i, n_j, n_k, zg, zo, c_z, c_h, accumulate, dtype, workspace,
                               workspace_bytes, st);
@@ -199,14 +225,23 @@ int pf_trimul_combine(const pf_trimul_params* w, const void* a, const void* b, i
 static bool triatt_tc(int c, int H, int d, int dtype) {
   return dtype == PF_BF16 && !force_simt() && tc::triatt_supported(c, H, d);
 }
+static bool triatt_rows(int c, int H, int d, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && !tc::triatt_supported(c, H, d) && tc::rows_triatt_supported(c, H, d);
+}
+static bool triatt_bias_tc(int c, int H, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::triatt_bias_supported(c, H);
+}
+static bool triatt_bias_rows(int c, int H, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && !tc::triatt_bias_supported(c, H) && tc::rows_bias_supported(c, H);
+}
 
 int pf_triatt_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c, int32_t heads,
                                   int32_t dtype, size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = (dtype == PF_BF16 && !force_simt() && tc::triatt_bias_supported(c, heads))
-               ? 0
-               : simt::triatt_bias_ws_bytes(n_rows, n_cols, c, heads);
+  *bytes = triatt_bias_tc(c, heads, dtype)     ? 0
+           : triatt_bias_rows(c, heads, dtype) ? tc::rows_bias_ws_bytes(n_rows, n_cols, c)
+                                               : simt::triatt_bias_ws_bytes(n_rows, n_cols, c, heads);
   return PF_OK;
 }
 
@@ -222,9 +257,14 @@ int pf_triatt_bias(const pf_triatt_params* w, pf_pair_view z, int64_t n_rows, in
   PF_TRY(pf_triatt_bias_workspace_size(n_rows, n_cols, c, heads, dtype, &need));
   PF_TRY(check_ws(workspace, workspace_bytes, need, "triatt_bias"));
   cudaStream_t st = (cudaStream_t)stream;
-  if (dtype == PF_BF16 && !force_simt() && tc::triatt_bias_supported(c, heads)) {
+  if (triatt_bias_tc(c, heads, dtype)) {
     set_path("tc");
     return tc::triatt_bias(w, z, n_rows, n_cols, bias, hs, rs, c, heads, st);
+  }
+  if (triatt_bias_rows(c, heads, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_head_bias(w->ln_w, w->ln_b, w->w_bias, z, n_rows, n_cols, c, heads, bias, hs, rs, true,
+                              workspace, workspace_bytes, st);
   }
   set_path("simt");
   return simt::triatt_bias(w, z, n_rows, n_cols, bias, hs, rs, c, heads, dtype, workspace,
@@ -235,9 +275,9 @@ int pf_triatt_workspace_size(int64_t n_rows, int64_t n_keys, int64_t n_q, int32_
                              int32_t head_dim, int32_t dtype, size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = triatt_tc(c, heads, head_dim, dtype)
-               ? tc::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim)
-               : simt::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim);
+  *bytes = triatt_tc(c, heads, head_dim, dtype)     ? tc::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim)
+           : triatt_rows(c, heads, head_dim, dtype) ? tc::rows_triatt_ws_bytes(n_rows, n_keys, n_q, c, heads)
+                                                    : simt::triatt_ws_bytes(n_rows, n_keys, n_q, c, heads, head_dim);
   return PF_OK;
 }
 
@@ -270,6 +310,11 @@ int pf_triatt_fwd(const pf_triatt_params* w, pf_pair_view zs, pf_mask_view m, co
     return tc::triatt(w, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid_keys, q_col0, n_q,
                       c, heads, head_dim, inf, accumulate, workspace, workspace_bytes, st);
   }
+  if (triatt_rows(c, heads, head_dim, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_triatt(w, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid_keys, q_col0, n_q, c, heads, inf,
+                           accumulate, workspace, workspace_bytes, st);
+  }
   set_path("simt");
   return simt::triatt(w, zs, m, bias, b_hs, b_rs, zo, n_rows, n_keys, n_valid_keys, q_col0, n_q, c,
                       heads, head_dim, inf, accumulate, dtype, workspace, workspace_bytes, st);
@@ -279,12 +324,17 @@ int pf_triatt_fwd(const pf_triatt_params* w, pf_pair_view zs, pf_mask_view m, co
 static bool transition_tc(int c, int nm, int dtype) {
   return dtype == PF_BF16 && !force_simt() && tc::transition_supported(c, nm);
 }
+static bool transition_rows(int c, int nm, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && !tc::transition_supported(c, nm) && tc::rows_transition_supported(c, nm);
+}
 
 int pf_transition_workspace_size(int64_t rows, int32_t c, int32_t n_mult, int32_t dtype,
                                  size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = transition_tc(c, n_mult, dtype) ? 0 : simt::transition_ws_bytes(rows, c, n_mult);
+  *bytes = transition_tc(c, n_mult, dtype)     ? 0
+           : transition_rows(c, n_mult, dtype) ? tc::rows_transition_ws_bytes(rows, c, n_mult)
+                                               : simt::transition_ws_bytes(rows, c, n_mult);
   return PF_OK;
 }
 
@@ -305,6 +355,11 @@ int pf_transition_fwd(const pf_transition_params* w, const void* x, int64_t x_st
     set_path("tc");
     return tc::transition(w, x, x_stride, out, out_stride, rows, c, n_mult, accumulate, st);
   }
+  if (transition_rows(c, n_mult, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_transition(w, x, x_stride, out, out_stride, rows, c, n_mult, accumulate, workspace,
+                               workspace_bytes, st);
+  }
   set_path("simt");
   return simt::transition(w, x, x_stride, out, out_stride, rows, c, n_mult, accumulate, dtype,
                           workspace, workspace_bytes, st);
@@ -314,12 +369,18 @@ int pf_transition_fwd(const pf_transition_params* w, const void* x, int64_t x_st
 static bool apb_bias_tc(int c_z, int heads, int dtype) {
   return dtype == PF_BF16 && !force_simt() && tc::apb_pair_bias_supported(c_z, heads);
 }
+static bool apb_bias_rows(int c_z, int heads, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && !tc::apb_pair_bias_supported(c_z, heads) &&
+         tc::rows_bias_supported(c_z, heads);
+}
 
 int pf_apb_pair_bias_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t heads,
                                     int32_t dtype, size_t* bytes) {
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
-  *bytes = apb_bias_tc(c_z, heads, dtype) ? 0 : simt::apb_pair_bias_ws_bytes(n_rows * n_cols, c_z, heads);
+  *bytes = apb_bias_tc(c_z, heads, dtype)     ? 0
+           : apb_bias_rows(c_z, heads, dtype) ? tc::rows_bias_ws_bytes(n_rows, n_cols, c_z)
+                                              : simt::apb_pair_bias_ws_bytes(n_rows * n_cols, c_z, heads);
   return PF_OK;
 }
 
@@ -338,9 +399,19 @@ int pf_apb_pair_bias(const pf_apb_params* w, pf_pair_view z, int64_t n_rows, int
     set_path("tc");
     return tc::apb_pair_bias(w, z, n_rows, n_cols, bias, hs, rs, (cudaStream_t)stream);
   }
+  if (apb_bias_rows(c_z, heads, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_head_bias(w->ln_z_w, w->ln_z_b, w->w_z, z, n_rows, n_cols, c_z, heads, bias, hs, rs, false,
+                              workspace, workspace_bytes, (cudaStream_t)stream);
+  }
   set_path("simt");
   return simt::apb_pair_bias(w, z, n_rows, n_cols, bias, hs, rs, c_z, heads, dtype, workspace,
                              workspace_bytes, (cudaStream_t)stream);
+}
+
+// the single path's projections on tcgen05 (bf16); the attention itself stays on the fp32 split kernel
+static bool apb_single_rows(int c_s, int heads, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && heads > 0 && tc::rows_apb_supported(c_s, heads);
 }
 
 // workspace of pf_apb_fwd: [own pair bias (only when bias == NULL)] [pair-bias scratch | attention]
@@ -352,7 +423,8 @@ int pf_apb_workspace_size(int64_t n, int32_t c_s, int32_t c_z, int32_t heads, in
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   size_t pb = 0;
   PF_TRY(pf_apb_pair_bias_workspace_size(n, n, c_z > 0 ? c_z : 1, heads, dtype, &pb));
-  const size_t att = simt::apb_rows_ws_bytes(n, n, c_s, heads > 0 ? heads : 1);
+  const size_t att = apb_single_rows(c_s, heads, dtype) ? tc::rows_apb_ws_bytes(n, n, c_s, heads)
+                                                        : simt::apb_rows_ws_bytes(n, n, c_s, heads > 0 ? heads : 1);
   *bytes = apb_own_bias_bytes(n, heads) + (pb > att ? pb : att);
   return PF_OK;
 }
@@ -379,10 +451,15 @@ int pf_apb_fwd(const pf_apb_params* w, const void* s_in, void* s_out, pf_pair_vi
     PF_TRY(pf_apb_pair_bias(w, z, n, n, own_bias, n * n, n, c_z, heads, dtype, ws + own,
                             workspace_bytes - own, stream));
     bias = own_bias;
-    bias_tc = apb_bias_tc(c_z, heads, dtype);
+    bias_tc = apb_bias_tc(c_z, heads, dtype) || apb_bias_rows(c_z, heads, dtype);
   }
   // The pair bias (one pass over the N x N x c_z pair tensor) dominates; the single-row
-  // attention over N tokens is SIMT in both modes.
+  // attention over N tokens is SIMT in both modes, its projections tensor-core in bf16.
+  if (apb_single_rows(c_s, heads, dtype)) {
+    set_path(bias_tc ? "tc+simt" : "simt");
+    return tc::rows_apb(w, s_in, s_out, bias, n * n, n, n, 0, n, c_s, heads, accumulate, ws + own,
+                        workspace_bytes - own, (cudaStream_t)stream);
+  }
   set_path(bias_tc ? "tc+simt" : "simt");
   return simt::apb_rows(w, s_in, s_out, bias, n * n, n, n, 0, n, c_s, heads, accumulate, dtype, ws + own,
                         workspace_bytes - own, (cudaStream_t)stream);
@@ -393,7 +470,8 @@ int pf_apb_rows_workspace_size(int64_t n, int64_t n_q, int32_t c_s, int32_t head
   PF_TRY(check_dtype(dtype));
   if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
   if (n < 0 || n_q < 0 || c_s <= 0 || heads <= 0 || c_s % heads) return fail(PF_EINVAL_SHAPE, "apb rows: bad sizes");
-  *bytes = simt::apb_rows_ws_bytes(n, n_q, c_s, heads);
+  *bytes = apb_single_rows(c_s, heads, dtype) ? tc::rows_apb_ws_bytes(n, n_q, c_s, heads)
+                                              : simt::apb_rows_ws_bytes(n, n_q, c_s, heads);
   return PF_OK;
 }
 
@@ -412,6 +490,11 @@ int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out, const
   size_t need;
   PF_TRY(pf_apb_rows_workspace_size(n, n_q, c_s, heads, dtype, &need));
   PF_TRY(check_ws(workspace, workspace_bytes, need, "apb_rows"));
+  if (apb_single_rows(c_s, heads, dtype)) {
+    set_path("tc.rows+simt");
+    return tc::rows_apb(w, s_in, s_out, bias, head_stride, row_stride, n, q_row0, n_q, c_s, heads, accumulate,
+                        workspace, workspace_bytes, (cudaStream_t)stream);
+  }
   set_path("simt");
   return simt::apb_rows(w, s_in, s_out, bias, head_stride, row_stride, n, q_row0, n_q, c_s, heads,
                         accumulate, dtype, workspace, workspace_bytes, (cudaStream_t)stream);

@@ -865,6 +865,14 @@ static size_t apb_part_floats(int64_t n, int64_t nq, int c_s, int H) {
   return (size_t)apb_splits(n, nq, H) * nq * (c_s + 2 * H);  // splits x nq x H x (d + 2)
 }
 
+size_t attn_split_part_floats(int64_t n, int64_t nq, int c_s, int H) { return apb_part_floats(n, nq, c_s, H); }
+
+int attn_split(int d, const float* q, int64_t q_ps, const float* k, const float* v, int64_t kv_ps, const float* bias,
+               int64_t b_hs, int64_t b_rs, int64_t n_q, int64_t n, int H, float* part, float* o, int64_t o_ps,
+               cudaStream_t st) {
+  return launch_attn_split(d, q, q_ps, k, v, kv_ps, bias, b_hs, b_rs, n_q, n, H, part, o, o_ps, st);
+}
+
 template <class T>
 static int triatt_bias_t(const pf_triatt_params* p, pf_pair_view z, int64_t n_rows, int64_t n_cols,
                          void* bias, int64_t hs, int64_t rs, int c, int H, float scale,

@@ -46,5 +46,13 @@ int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float*
              int64_t b_rs, int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, int dtype, void* ws,
              size_t ws_bytes, cudaStream_t st);
 
+// Single-representation attention with a pair bias (fp32), split over the keys and merged:
+// o(j, h*d + e) for queries j < n_q over keys < n; q(j) at q + j*q_ps, k/v(key) at + key*kv_ps,
+// bias(h, j, key) at bias + h*b_hs + j*b_rs + key; `part` holds attn_split_part_floats floats.
+size_t attn_split_part_floats(int64_t n, int64_t nq, int c_s, int H);
+int attn_split(int d, const float* q, int64_t q_ps, const float* k, const float* v, int64_t kv_ps, const float* bias,
+               int64_t b_hs, int64_t b_rs, int64_t n_q, int64_t n, int H, float* part, float* o, int64_t o_ps,
+               cudaStream_t st);
+
 }  // namespace simt
 }  // namespace pf

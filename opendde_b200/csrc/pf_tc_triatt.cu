@@ -22,6 +22,7 @@
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tc_internal.h"
 #include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
@@ -549,7 +550,8 @@ int ensure_attrs() {
   static std::atomic<unsigned long long> done{0};
   return once_per_device(done, []() -> int {
     PF_TRY(set_smem(k_triatt_proj, PROJ_SMEM + 1024));
-    PF_TRY(set_smem(k_triatt_core, CORE3_SMEM + 1024));
+    PF_TRY(set_smem(k_triatt_core<H>, CORE3_SMEM + 1024));
+    PF_TRY(set_smem(k_triatt_core<0>, CORE3_SMEM + 1024));
     PF_TRY(set_smem(k_triatt_out, OUT_SMEM + 1024));
     return PF_OK;
   });
@@ -659,12 +661,8 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   unsigned int* status;
   PF_TRY(device_status_ptr(&status));
   // 0. mask bias + tile flags
-  {
-    PF_LAUNCH_SCOPE(st, "k_triatt_maskprep");
-    k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, w.mb, w.ld_mb, w.flags, w.rowflags,
-                                                        (int)w.n_tiles_k);
-  }
-  PF_CHECK_LAUNCH();
+  const CoreIO io{w.q, w.k, w.vt, nullptr, 0, 0, w.o, w.mb, w.flags, w.rowflags, w.ld_keys, w.ld_mb, w.n_tiles_k};
+  PF_TRY(triatt_masks(m, n_rows, n_keys, n_valid, inf, io, st));
   // 1. projections (+ own bias in the square single-device case)
   ProjArgs pa{};
   pa.n_rows = n_rows;
@@ -685,48 +683,11 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
   pa.status = status;
   PF_TRY(launch_proj(p, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys, pa, w.vt, st));
   // 2. attention core
-  const void* bptr = bias ? bias : (const void*)w.bias;
-  const int64_t bhs = bias ? b_hs : pa.b_hs, brs = bias ? b_rs : pa.b_rs;
-  CUtensorMap tk, tvt, tb, tmb;
-  {
-    const uint32_t bq[3] = {D, TILE, 1};
-    const uint64_t dk[3] = {(uint64_t)D, (uint64_t)n_keys, (uint64_t)(n_rows * H)};
-    const uint64_t sk[2] = {(uint64_t)D * 2, (uint64_t)w.ld_keys * D * 2};
-    PF_TRY(make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.k, dk, sk, bq, CU_TENSOR_MAP_SWIZZLE_64B));
-    const uint64_t dv[3] = {(uint64_t)n_keys, (uint64_t)D, (uint64_t)(n_rows * H)};
-    const uint64_t sv[2] = {(uint64_t)w.ld_keys * 2, (uint64_t)D * w.ld_keys * 2};
-    const uint32_t bv[3] = {64, D, 1};
-    PF_TRY(make_tmap(&tvt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, w.vt, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B));
-    const uint64_t db[3] = {(uint64_t)n_keys, (uint64_t)n_q, (uint64_t)H};
-    const uint64_t sb[2] = {(uint64_t)brs * 2, (uint64_t)bhs * 2};
-    const uint32_t bb[3] = {64, TILE, 1};
-    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, bptr, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
-    const uint64_t dm[2] = {(uint64_t)w.ld_mb, (uint64_t)n_rows};
-    const uint64_t sm[1] = {(uint64_t)w.ld_mb * 2};
-    const uint32_t bm[2] = {TILE, 1};
-    PF_TRY(make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w.mb, dm, sm, bm, CU_TENSOR_MAP_SWIZZLE_NONE));
-  }
-  if (n_valid == 0) {
-    // no key exists: every attention output is zero
-    PF_CUDA_TRY(cudaMemsetAsync(w.o, 0, (size_t)n_rows * n_q * HD * sizeof(__nv_bfloat16), st));
-  } else {
-    CoreArgs ca{};
-    ca.n_rows = n_rows;
-    ca.n_q = n_q;
-    ca.n_tiles_k = w.n_tiles_k;
-    ca.n_qt = (n_q + TILE - 1) / TILE;
-    ca.n_items = ((n_rows + 1) / 2) * H * ca.n_qt;
-    ca.flags = w.flags;
-    ca.rowflags = w.rowflags;
-    ca.q = w.q;
-    ca.o = w.o;
-    ca.status = status;
-    const int64_t grid = ca.n_items < num_sms() ? ca.n_items : num_sms();
-    // QK^T and PV over every existing key: 4 H d flops per (row, query, key)
-    PF_LAUNCH_SCOPE_WORK(st, "k_triatt_core", 4.0 * H * D * (double)n_rows * n_q * n_valid, 'f');
-    k_triatt_core<<<(unsigned)grid, CORE_THREADS, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
-  }
-  PF_CHECK_LAUNCH();
+  CoreIO cio = io;
+  cio.bias = bias ? bias : (const void*)w.bias;
+  cio.b_hs = bias ? b_hs : pa.b_hs;
+  cio.b_rs = bias ? b_rs : pa.b_rs;
+  PF_TRY(triatt_core(cio, n_rows, n_keys, n_valid, n_q, H, status, st));
   // 3. gate, output projection, residual
   CUtensorMap tz, to, twg, two;
   PF_TRY(pair_tmap(&tz, zs.ptr, zs.row_stride, zs.col_stride, n_rows, n_keys));
@@ -760,6 +721,76 @@ int triatt(const pf_triatt_params* p, pf_pair_view zs, pf_mask_view m, const voi
     const double bytes = 2.0 * (double)n_rows * n_q * (HD + CH + (resid_apart ? CH : 0) + CH);
     PF_LAUNCH_SCOPE_WORK(st, "k_triatt_out", bytes, 'b');
     k_triatt_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tz, to, tzo, twg, two, oa);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+
+// ------------------------------------------------------------------ shared with the general path
+int triatt_masks(pf_mask_view m, int64_t n_rows, int64_t n_keys, int64_t n_valid, float inf, const CoreIO& io,
+                 cudaStream_t st) {
+  {
+    PF_LAUNCH_SCOPE(st, "k_triatt_maskprep");
+    k_triatt_maskprep<<<(unsigned)n_rows, 128, 0, st>>>(m, n_keys, n_valid, inf, io.mb, io.ld_mb, io.flags,
+                                                        io.rowflags, (int)io.n_tiles_k);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int triatt_core(const CoreIO& io, int64_t n_rows, int64_t n_keys, int64_t n_valid, int64_t n_q, int heads,
+                unsigned int* status, cudaStream_t st) {
+  if (n_rows * heads > 0x7fffffffll || io.n_tiles_k > 0x7fffffffll)
+    return fail(PF_EUNSUPPORTED, "triatt problem too large");
+  if (io.bias == nullptr || io.b_hs % 8 || io.b_rs % 8 || ((uintptr_t)io.bias) % 16)
+    return fail(PF_EINVAL_SHAPE, "bias buffer must be 16-byte aligned with strides multiple of 8");
+  PF_TRY(ensure_attrs());
+  const int64_t hd = (int64_t)heads * D;
+  if (n_valid == 0) {
+    // no key exists: every attention output is zero
+    PF_CUDA_TRY(cudaMemsetAsync(io.o, 0, (size_t)n_rows * n_q * hd * sizeof(__nv_bfloat16), st));
+    return PF_OK;
+  }
+  CUtensorMap tk, tvt, tb, tmb;
+  {
+    const uint32_t bq[3] = {D, TILE, 1};
+    const uint64_t dk[3] = {(uint64_t)D, (uint64_t)n_keys, (uint64_t)(n_rows * heads)};
+    const uint64_t sk[2] = {(uint64_t)D * 2, (uint64_t)io.ld_keys * D * 2};
+    PF_TRY(make_tmap(&tk, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, io.k, dk, sk, bq, CU_TENSOR_MAP_SWIZZLE_64B));
+    const uint64_t dv[3] = {(uint64_t)n_keys, (uint64_t)D, (uint64_t)(n_rows * heads)};
+    const uint64_t sv[2] = {(uint64_t)io.ld_keys * 2, (uint64_t)D * io.ld_keys * 2};
+    const uint32_t bv[3] = {64, D, 1};
+    PF_TRY(make_tmap(&tvt, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, io.vt, dv, sv, bv, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t db[3] = {(uint64_t)n_keys, (uint64_t)n_q, (uint64_t)heads};
+    const uint64_t sb[2] = {(uint64_t)io.b_rs * 2, (uint64_t)io.b_hs * 2};
+    const uint32_t bb[3] = {64, TILE, 1};
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, io.bias, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t dm[2] = {(uint64_t)io.ld_mb, (uint64_t)n_rows};
+    const uint64_t sm[1] = {(uint64_t)io.ld_mb * 2};
+    const uint32_t bm[2] = {TILE, 1};
+    PF_TRY(make_tmap(&tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, io.mb, dm, sm, bm, CU_TENSOR_MAP_SWIZZLE_NONE));
+  }
+  CoreArgs ca{};
+  ca.n_rows = n_rows;
+  ca.n_q = n_q;
+  ca.n_tiles_k = io.n_tiles_k;
+  ca.n_qt = (n_q + TILE - 1) / TILE;
+  ca.n_items = ((n_rows + 1) / 2) * heads * ca.n_qt;
+  ca.heads = heads;
+  ca.flags = io.flags;
+  ca.rowflags = io.rowflags;
+  ca.q = io.q;
+  ca.o = io.o;
+  ca.status = status;
+  const int64_t grid = ca.n_items < num_sms() ? ca.n_items : num_sms();
+  {
+    // QK^T and PV over every existing key: 4 H d flops per (row, query, key)
+    PF_LAUNCH_SCOPE_WORK(st, "k_triatt_core", 4.0 * heads * D * (double)n_rows * n_q * n_valid, 'f');
+    if (heads == H)
+      k_triatt_core<H><<<(unsigned)grid, CORE_THREADS, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
+    else
+      k_triatt_core<0><<<(unsigned)grid, CORE_THREADS, CORE3_SMEM + 1024, st>>>(tk, tvt, tb, tmb, ca);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;

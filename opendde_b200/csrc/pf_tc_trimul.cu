@@ -20,6 +20,7 @@
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tc_internal.h"
 #include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
@@ -729,34 +730,7 @@ int launch_contract_out(const pf_trimul_params* p, const __nv_bfloat16* a, int64
                         const __nv_bfloat16* b, int64_t ldb, int64_t n_i, int64_t n_j, int64_t n_k,
                         __nv_bfloat16* x, int64_t ld_j, pf_pair_view zg, pf_pair_view zo, int acc,
                         unsigned int* status, cudaStream_t st) {
-  CUtensorMap ta, tb;
-  {
-    const uint64_t da[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)CH};
-    const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)n_i * lda * 2};
-    const uint32_t ba[3] = {BK, BM, 1};
-    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B));
-    const uint64_t db[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)CH};
-    const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)n_j * ldb * 2};
-    const uint32_t bb[3] = {BK, BN, 1};
-    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
-  }
-  GemmArgs ga;
-  ga.M = (int)n_i;
-  ga.N = (int)n_j;
-  ga.K = (int)n_k;
-  ga.m_tiles = (int)((n_i + BM - 1) / BM);
-  ga.n_tiles = (int)((n_j + BN - 1) / BN);
-  ga.n_work = (int64_t)CH * ga.m_tiles * ga.n_tiles;
-  ga.out = x;
-  ga.ldo = ld_j;
-  ga.out_bstride = (int64_t)n_i * ld_j;
-  ga.status = status;
-  {
-    const int64_t grid_g = ga.n_work < sm_count() ? ga.n_work : sm_count();
-    PF_LAUNCH_SCOPE_WORK(st, "k_trimul_bgemm", 2.0 * CH * (double)n_i * n_j * n_k, 'f');
-    k_trimul_bgemm<<<(unsigned)grid_g, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
-  }
-  PF_CHECK_LAUNCH();
+  PF_TRY(trimul_contract(a, lda, b, ldb, n_i, n_j, n_k, CH, x, ld_j, status, st));
   // LN_out, W_z, gate, residual (persistent, one CTA per SM)
   CUtensorMap tzg, tzo, txm, twz, twg;
   PF_TRY(pair_tmap(&tzg, zg, n_i, n_j));
@@ -856,6 +830,43 @@ int trimul_combine(const pf_trimul_params* p, const void* a, const void* b, int6
   PF_TRY(ensure_attrs());
   return launch_contract_out(p, (const __nv_bfloat16*)a, ld, (const __nv_bfloat16*)b, ld, n_i, n_j, n_k, x,
                              ld_j, zg, zo, acc, status, st);
+}
+
+
+// ------------------------------------------------------------------ shared with the general path
+int trimul_contract(const __nv_bfloat16* a, int64_t lda, const __nv_bfloat16* b, int64_t ldb, int64_t n_i,
+                    int64_t n_j, int64_t n_k, int channels, __nv_bfloat16* x, int64_t ld_j, unsigned int* status,
+                    cudaStream_t st) {
+  PF_TRY(ensure_attrs());
+  CUtensorMap ta, tb;
+  {
+    const uint64_t da[3] = {(uint64_t)n_k, (uint64_t)n_i, (uint64_t)channels};
+    const uint64_t sa[2] = {(uint64_t)lda * 2, (uint64_t)n_i * lda * 2};
+    const uint32_t ba[3] = {BK, BM, 1};
+    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a, da, sa, ba, CU_TENSOR_MAP_SWIZZLE_128B));
+    const uint64_t db[3] = {(uint64_t)n_k, (uint64_t)n_j, (uint64_t)channels};
+    const uint64_t sb[2] = {(uint64_t)ldb * 2, (uint64_t)n_j * ldb * 2};
+    const uint32_t bb[3] = {BK, BN, 1};
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, b, db, sb, bb, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  GemmArgs ga;
+  ga.M = (int)n_i;
+  ga.N = (int)n_j;
+  ga.K = (int)n_k;
+  ga.m_tiles = (int)((n_i + BM - 1) / BM);
+  ga.n_tiles = (int)((n_j + BN - 1) / BN);
+  ga.n_work = (int64_t)channels * ga.m_tiles * ga.n_tiles;
+  ga.out = x;
+  ga.ldo = ld_j;
+  ga.out_bstride = (int64_t)n_i * ld_j;
+  ga.status = status;
+  {
+    const int64_t grid_g = ga.n_work < sm_count() ? ga.n_work : sm_count();
+    PF_LAUNCH_SCOPE_WORK(st, "k_trimul_bgemm", 2.0 * channels * (double)n_i * n_j * n_k, 'f');
+    k_trimul_bgemm<<<(unsigned)grid_g, 192, GEMM_SMEM + 1024, st>>>(ta, tb, ga);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
 }
 
 }  // namespace tc

@@ -31,10 +31,11 @@
 
 struct CoreArgs {
   int64_t n_rows, n_q, n_tiles_k, n_qt, n_items;
+  int heads;                // H (d = 32 each); o rows hold heads * 32 channels
   const uint8_t* flags;     // [n_rows][n_tiles_k]  TF_*
   const uint8_t* rowflags;  // [n_rows]  bit 0: uniform row
-  const __half* q;          // [(i*H+h)*n_q + j][D] f16, pre-scaled by log2(e)/sqrt(d)
-  __nv_bfloat16* o;         // [(i*n_q + j)][HD]
+  const __half* q;          // [(i*heads+h)*n_q + j][D] f16, pre-scaled by log2(e)/sqrt(d)
+  __nv_bfloat16* o;         // [(i*n_q + j)][heads*D]
   unsigned int* status;
 };
 
@@ -75,11 +76,17 @@ struct Item {
   const uint8_t* fb;
 };
 
+// NH > 0: the head count as a compile-time constant (the c = 128 path); 0: CoreArgs::heads.
+template <int NH>
+__device__ __forceinline__ int core_heads(const CoreArgs& a) { return NH > 0 ? NH : a.heads; }
+
+template <int NH>
 __device__ __forceinline__ Item decode_item(const CoreArgs& a, int64_t w) {
+  const int heads = core_heads<NH>(a);
   Item it;
   it.jt = (int)(w % a.n_qt);
-  it.h = (int)((w / a.n_qt) % H);
-  it.i0 = 2 * (w / (a.n_qt * H));
+  it.h = (int)((w / a.n_qt) % heads);
+  it.i0 = 2 * (w / (a.n_qt * heads));
   it.has_b = it.i0 + 1 < a.n_rows;
   it.fa = a.flags + it.i0 * a.n_tiles_k;
   it.fb = it.has_b ? it.fa + a.n_tiles_k : nullptr;
@@ -149,12 +156,13 @@ __device__ __forceinline__ uint32_t tile_logits(uint32_t t_s, const uint8_t* bro
 }
 
 // Softmax thread: copy its query row (32 f16) of item `it`, row r, into the TMEM Q columns.
+template <int NH>
 __device__ __forceinline__ void load_q_row(const CoreArgs& a, const Item& it, int r, int row_tid,
                                            uint32_t tmem_row, uint32_t lane_base) {
   const int64_t j = (int64_t)it.jt * TILE + row_tid;
   uint32_t qv[16];
   if (j < a.n_q) {
-    const uint4* src = reinterpret_cast<const uint4*>(a.q + (((it.i0 + r) * H + it.h) * a.n_q + j) * D);
+    const uint4* src = reinterpret_cast<const uint4*>(a.q + (((it.i0 + r) * core_heads<NH>(a) + it.h) * a.n_q + j) * D);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const uint4 u = src[e];
@@ -167,6 +175,7 @@ __device__ __forceinline__ void load_q_row(const CoreArgs& a, const Item& it, in
   tmem_st16(tmem_row + lane_base + T_Q, qv);
 }
 
+template <int NH>
 __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_constant__ CUtensorMap tk,
                                                                  const __grid_constant__ CUtensorMap tvt,
                                                                  const __grid_constant__ CUtensorMap tb,
@@ -225,8 +234,8 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       uint32_t step = 0;
       bool ok = true;
       for (int64_t w = blockIdx.x; w < a.n_items && ok; w += gridDim.x) {
-        const Item it = decode_item(a, w);
-        const int ihA = (int)(it.i0 * H + it.h), ihB = ihA + H;
+        const Item it = decode_item<NH>(a, w);
+        const int ihA = (int)(it.i0 * core_heads<NH>(a) + it.h), ihB = ihA + core_heads<NH>(a);
         const uint32_t bytes = 32768 + (8192 + 8192 + 256) * (it.has_b ? 2 : 1);
         for (int kt = next_tile(it.fa, it.fb, 0, n_tiles); kt < n_tiles && ok;
              kt = next_tile(it.fa, it.fb, kt + 1, n_tiles), ++step) {
@@ -281,7 +290,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       int kt = n_tiles;
       uint32_t step = 0;
       if (w < a.n_items) {
-        it = decode_item(a, w);
+        it = decode_item<NH>(a, w);
         kt = next_tile(it.fa, it.fb, 0, n_tiles);
         ok = mbar_wait(bar_full0, 0, a.status);
         tc_fence_after();
@@ -298,7 +307,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         if (kt2 >= n_tiles) {
           w2 = w + gridDim.x;
           if (w2 < a.n_items) {
-            it2 = decode_item(a, w2);
+            it2 = decode_item<NH>(a, w2);
             kt2 = next_tile(it2.fa, it2.fb, 0, n_tiles);
             first2 = true;
           }
@@ -352,9 +361,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
     bool ok = true;
     // Q of this row's first item, then "S columns free" for the first S
     if (blockIdx.x < a.n_items) {
-      const Item it0 = decode_item(a, blockIdx.x);
+      const Item it0 = decode_item<NH>(a, blockIdx.x);
       if (r == 0 || it0.has_b) {
-        load_q_row(a, it0, r, row_tid, tb_r, lane_base);
+        load_q_row<NH>(a, it0, r, row_tid, tb_r, lane_base);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -362,7 +371,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       }
     }
     for (int64_t w = blockIdx.x; w < a.n_items && ok; w += gridDim.x) {
-      const Item it = decode_item(a, w);
+      const Item it = decode_item<NH>(a, w);
       if (r == 1 && !it.has_b) break;  // rows B end at the odd last row pair
       const int64_t i = it.i0 + r;
       const uint8_t* fr = r ? it.fb : it.fa;
@@ -394,9 +403,9 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         if (kt >= n_tiles) {
           const int64_t wn = w + gridDim.x;
           if (wn < a.n_items) {
-            const Item itn = decode_item(a, wn);
+            const Item itn = decode_item<NH>(a, wn);
             if (r == 0 || itn.has_b) {
-              load_q_row(a, itn, r, row_tid, tb_r, lane_base);
+              load_q_row<NH>(a, itn, r, row_tid, tb_r, lane_base);
               tmem_st_wait();
             }
           }
@@ -469,7 +478,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       if (j < a.n_q) {
         const float l = __uint_as_float(lv[0]);
         const float inv = l > 0.f ? 1.0f / l : 0.f;
-        uint4* dst = reinterpret_cast<uint4*>(a.o + ((int64_t)i * a.n_q + j) * HD + it.h * D);
+        uint4* dst = reinterpret_cast<uint4*>(a.o + ((int64_t)i * a.n_q + j) * (core_heads<NH>(a) * D) + it.h * D);
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           uint4 w0;
