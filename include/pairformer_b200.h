@@ -280,6 +280,31 @@ PF_API int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out
                            int64_t n_q, int32_t c_s, int32_t heads, int32_t accumulate, int32_t dtype,
                            void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- OuterProductMean (Algorithm 10) ---------------------------------------------------------
+ * Replaces OuterProductMean.forward (opendde/model/triangular/layers.py:497-627) and the Fold-CP
+ * pair-tile update (opendde/model/modules/pairformer.py:979-1046). For i in
+ * [row0, row0 + n_rows), j in [col0, col0 + n_cols):
+ *   z_out(i - row0, j - col0) = (accumulate ? z_out : 0)
+ *       + (W_out vec_{c,e}(sum_s a(s, i, c) b(s, j, e)) + b_out) / (sum_s mask(s, i) mask(s, j) + eps)
+ * with a = linear_1(LN(m)) * mask, b = linear_2(LN(m)) * mask; m(s, i) = m.ptr + s*m.row_stride
+ * + i*m.col_stride (n_seq x n_res positions, c_m contiguous channels), mask(s, i) the MSA mask
+ * (ptr NULL = ones). z_out is an n_rows x n_cols view of c_z channels. bf16 runs the
+ * projections, the outer product (K = n_seq) and W_out (K = c_hidden^2) on tcgen05 when
+ * c_hidden = 32; fp32 (and other c_hidden) on the SIMT kernels. */
+typedef struct {
+  const float* ln_w; const float* ln_b;   /* [c_m]              layer_norm      */
+  const void* w_1; const void* w_2;       /* [c_hidden, c_m]    linear_1, linear_2 (no bias) */
+  const void* w_out;                      /* [c_z, c_hidden^2]  linear_out      */
+  const float* b_out;                     /* [c_z]              linear_out.bias */
+} pf_opm_params;
+
+PF_API int pf_opm_workspace_size(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int32_t c_m,
+                                 int32_t c_hidden, int32_t c_z, int32_t dtype, size_t* bytes);
+PF_API int pf_opm_fwd(const pf_opm_params* w, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out,
+                      int64_t n_seq, int64_t n_res, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols,
+                      int32_t c_m, int32_t c_hidden, int32_t c_z, float eps, int32_t accumulate, int32_t dtype,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Fold-CP band exchange through peer memory ------------------------------------------
  * Replace the reference's ring / transpose band exchanges over NCCL send/receive
  * (opendde/distributed/foldcp/comm.py:26-184, used by real_pairformer.py:1226-1404 and

@@ -50,6 +50,7 @@ EXPORTED = (
     "pf_apb_rows_workspace_size", "pf_apb_rows_fwd",
     "pf_peer_handle_bytes", "pf_peer_window_alloc", "pf_peer_window_free", "pf_peer_window_open",
     "pf_peer_window_close", "pf_copy_regions",
+    "pf_opm_workspace_size", "pf_opm_fwd",
 )
 
 
@@ -94,6 +95,10 @@ PF_MAX_COPY_REGIONS = 32
 class ApbParams(Structure):
     _fields_ = [(n, c_void_p) for n in (
         "ln_a_w", "ln_a_b", "w_q", "b_q", "w_k", "w_v", "w_g", "w_o", "ln_z_w", "ln_z_b", "w_z")]
+
+
+class OpmParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w_1", "w_2", "w_out", "b_out")]
 
 
 _lib = None
@@ -161,6 +166,10 @@ def load(path: str = LIB_PATH):
         "pf_peer_window_open": ([c_void_p, POINTER(c_void_p)], c_int),
         "pf_peer_window_close": ([c_void_p], c_int),
         "pf_copy_regions": ([POINTER(CopyRegion), c_int32, c_void_p], c_int),
+        "pf_opm_workspace_size": ([c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_opm_fwd": ([POINTER(OpmParams), PairView, MaskView, PairView, c_int64, c_int64, c_int64, c_int64, c_int64,
+                        c_int64, c_int32, c_int32, c_int32, c_float, c_int32, c_int32, c_void_p, c_size_t, c_void_p],
+                       c_int),
     }
     for name, (args, res) in sig.items():
         fn = getattr(lib, name)

@@ -500,4 +500,52 @@ int pf_apb_rows_fwd(const pf_apb_params* w, const void* s_in, void* s_out, const
                         accumulate, dtype, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
+// ------------------------------------------------------------------ OuterProductMean
+static bool opm_rows(int c_m, int c_hidden, int c_z, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::rows_opm_supported(c_m, c_hidden, c_z);
+}
+
+int pf_opm_workspace_size(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int32_t c_m,
+                          int32_t c_hidden, int32_t c_z, int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_seq < 0 || n_res < 0 || n_rows < 0 || n_cols < 0 || c_m <= 0 || c_hidden <= 0 || c_z <= 0)
+    return fail(PF_EINVAL_SHAPE, "opm: bad sizes");
+  *bytes = opm_rows(c_m, c_hidden, c_z, dtype)
+               ? tc::rows_opm_ws_bytes(n_seq, n_res, n_rows, n_cols, c_m, c_hidden)
+               : simt::opm_ws_bytes(n_seq, n_res, n_rows, n_cols, c_m, c_hidden, c_z);
+  return PF_OK;
+}
+
+int pf_opm_fwd(const pf_opm_params* w, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out, int64_t n_seq,
+               int64_t n_res, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int32_t c_m,
+               int32_t c_hidden, int32_t c_z, float eps, int32_t accumulate, int32_t dtype, void* workspace,
+               size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_1 || !w->w_2 || !w->w_out || !w->ln_w) return fail(PF_EINVAL_ARG, "opm: null weight pointer");
+  if (!view_ok(m) || !view_ok(z_out)) return fail(PF_EINVAL_ARG, "opm: bad view");
+  if (n_seq < 0 || n_res < 0 || c_m <= 0 || c_m > 1024 || c_hidden <= 0 || c_hidden > 64 || c_z <= 0 ||
+      c_z > 1024)
+    return fail(PF_EINVAL_SHAPE, "opm: bad sizes n_seq=%lld n_res=%lld c_m=%d c_hidden=%d c_z=%d",
+                (long long)n_seq, (long long)n_res, c_m, c_hidden, c_z);
+  if (row0 < 0 || n_rows < 0 || row0 + n_rows > n_res || col0 < 0 || n_cols < 0 || col0 + n_cols > n_res)
+    return fail(PF_EINVAL_SHAPE, "opm: tile rows [%lld, %lld) x cols [%lld, %lld) outside the %lld residues",
+                (long long)row0, (long long)(row0 + n_rows), (long long)col0, (long long)(col0 + n_cols),
+                (long long)n_res);
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_opm_workspace_size(n_seq, n_res, n_rows, n_cols, c_m, c_hidden, c_z, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "opm"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (n_seq == 0) return fail(PF_EINVAL_SHAPE, "opm: the MSA representation has no sequences (n_seq = 0)");
+  if (opm_rows(c_m, c_hidden, c_z, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_opm(w, m, mask, z_out, n_seq, n_res, row0, n_rows, col0, n_cols, c_m, c_hidden, c_z, eps,
+                        accumulate, workspace, workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::opm(w, m, mask, z_out, n_seq, n_res, row0, n_rows, col0, n_cols, c_m, c_hidden, c_z, eps, accumulate,
+                   dtype, workspace, workspace_bytes, st);
+}
+
 }  // extern "C"

@@ -1133,5 +1133,148 @@ int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float*
                               q0, nq, c_s, H, acc, ar, st);
 }
 
+// ---------------------------------------------------------------- OuterProductMean
+// norm[i*n_cols + j] = sum_s mask(s, row0 + i) mask(s, col0 + j) + eps, 16 x 16 outputs per CTA,
+// the mask rows staged 64 sequences at a time (the reference's einsum "...abc,...adc->...bdc").
+__global__ void __launch_bounds__(256) k_opm_norm(pf_mask_view m, int64_t n_seq, int64_t row0, int64_t n_rows,
+                                                  int64_t col0, int64_t n_cols, float eps, float* __restrict__ norm) {
+  __shared__ float mi[64][17], mj[64][17];
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int64_t i0 = (int64_t)blockIdx.y * 16, j0 = (int64_t)blockIdx.x * 16;
+  float acc = 0.f;
+  for (int64_t s0 = 0; s0 < n_seq; s0 += 64) {
+    __syncthreads();
+    for (int t = threadIdx.x; t < 64 * 16; t += 256) {
+      const int ss = t >> 4, e = t & 15;
+      const int64_t s = s0 + ss;
+      const int64_t i = i0 + e, j = j0 + e;
+      mi[ss][e] = (s < n_seq && i < n_rows) ? m.ptr[s * m.row_stride + (row0 + i) * m.col_stride] : 0.f;
+      mj[ss][e] = (s < n_seq && j < n_cols) ? m.ptr[s * m.row_stride + (col0 + j) * m.col_stride] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int ss = 0; ss < 64; ++ss) acc = fmaf(mi[ss][ty], mj[ss][tx], acc);
+  }
+  const int64_t i = i0 + ty, j = j0 + tx;
+  if (i < n_rows && j < n_cols) norm[i * n_cols + j] = acc + eps;
+}
+
+int opm_norm(pf_mask_view m, int64_t n_seq, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, float eps,
+             float* norm, cudaStream_t st) {
+  if ((n_rows + 15) / 16 > 65535) return fail(PF_EUNSUPPORTED, "OuterProductMean: too many rows");
+  dim3 grid(nblk(n_cols, 16), nblk(n_rows, 16));
+  PF_LAUNCH_SCOPE(st, "k_opm_norm");
+  k_opm_norm<<<grid, 256, 0, st>>>(m, n_seq, row0, n_rows, col0, n_cols, eps, norm);
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+// aT[(i*C + c)*n_seq + s] *= mask(s, r0 + i)
+__global__ void k_opm_mask(float* __restrict__ at, pf_mask_view m, int64_t r0, int64_t n, int C, int64_t n_seq) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n * C * n_seq || m.ptr == nullptr) return;
+  const int64_t s = idx % n_seq, i = idx / (n_seq * C);
+  at[idx] *= m.ptr[s * m.row_stride + (r0 + i) * m.col_stride];
+}
+
+// xr[((i*n_cols + j)*C + c)*C + e] = x[(i*C + c)*(n_cols*C) + j*C + e]
+__global__ void k_opm_relayout(const float* __restrict__ x, int64_t n_rows, int64_t n_cols, int C,
+                               float* __restrict__ xr) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t cc = (int64_t)C * C;
+  if (idx >= n_rows * n_cols * cc) return;
+  const int64_t p = idx / cc, k = idx - p * cc;
+  const int64_t i = p / n_cols, j = p - i * n_cols;
+  const int64_t c = k / C, e = k - c * C;
+  xr[idx] = x[(i * C + c) * (n_cols * C) + j * C + e];
+}
+
+// z(i, j, n) = (acc ? z : 0) + (y[p*c_z + n] + b[n]) / (norm ? norm[p] : norm_const), p = i*n_cols + j
+template <class T>
+__global__ void k_opm_out(T* __restrict__ z, int64_t rs, int64_t cs, const float* __restrict__ y,
+                          const float* __restrict__ b, const float* __restrict__ norm, float norm_const,
+                          int64_t n_rows, int64_t n_cols, int c_z, int acc) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= n_rows * n_cols * c_z) return;
+  const int64_t p = idx / c_z;
+  const int n = (int)(idx - p * c_z);
+  const int64_t i = p / n_cols, j = p - i * n_cols;
+  const float v = (y[idx] + (b ? b[n] : 0.f)) / (norm ? norm[p] : norm_const);
+  T* d = z + i * rs + j * cs + n;
+  *d = from_f<T>((acc ? to_f(*d) : 0.f) + v);
+}
+
+size_t opm_ws_bytes(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int c_m, int C, int c_z) {
+  Arena ar(nullptr, 0);
+  ar.take<float>((size_t)n_res * n_seq * c_m);
+  ar.take<float>((size_t)n_rows * C * n_seq);
+  ar.take<float>((size_t)n_cols * C * n_seq);
+  ar.take<float>((size_t)n_rows * C * n_cols * C);
+  ar.take<float>((size_t)n_rows * n_cols * C * C);
+  ar.take<float>((size_t)n_rows * n_cols * c_z);
+  ar.take<float>((size_t)n_rows * n_cols);
+  return ar.used;
+}
+
+template <class T>
+static int opm_t(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view zo, int64_t S, int64_t N,
+                 int64_t row0, int64_t nr, int64_t col0, int64_t nc, int c_m, int C, int c_z, float eps, int acc,
+                 Arena& ar, cudaStream_t st) {
+  float* ln = ar.take<float>((size_t)N * S * c_m);
+  float* at = ar.take<float>((size_t)nr * C * S);
+  float* bt = ar.take<float>((size_t)nc * C * S);
+  float* x = ar.take<float>((size_t)nr * C * nc * C);
+  float* xr = ar.take<float>((size_t)nr * nc * C * C);
+  float* y = ar.take<float>((size_t)nr * nc * c_z);
+  float* norm = ar.take<float>((size_t)nr * nc);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "OuterProductMean workspace too small");
+  // LN over the (i, s) order of the positions, so that a residue's sequences are contiguous
+  PF_TRY((ln_view<T, float>((const T*)m.ptr, m.col_stride, m.row_stride, N, S, c_m, p->ln_w, p->ln_b, 1e-5f, ln,
+                            c_m, st)));
+  // aT[(i*C + c)*S + s] = linear_1(ln(s, row0 + i))[c]; the same for bT with linear_2
+  PF_TRY((gemm<float, T>(ln + row0 * S * c_m, S * c_m, c_m, (const T*)p->w_1, 0, c_m, at, (int64_t)C * S, 1, S, nr,
+                         S, C, c_m, 1.f, 0, st)));
+  PF_TRY((gemm<float, T>(ln + col0 * S * c_m, S * c_m, c_m, (const T*)p->w_2, 0, c_m, bt, (int64_t)C * S, 1, S, nc,
+                         S, C, c_m, 1.f, 0, st)));
+  {
+    PF_LAUNCH_SCOPE(st, "k_opm_mask");
+    k_opm_mask<<<nblk(nr * C * S, 256), 256, 0, st>>>(at, mask, row0, nr, C, S);
+  }
+  PF_CHECK_LAUNCH();
+  {
+    PF_LAUNCH_SCOPE(st, "k_opm_mask");
+    k_opm_mask<<<nblk(nc * C * S, 256), 256, 0, st>>>(bt, mask, col0, nc, C, S);
+  }
+  PF_CHECK_LAUNCH();
+  // x[(i, c)][(j, e)] = sum_s aT[(i, c)][s] bT[(j, e)][s]
+  PF_TRY((gemm<float, float>(at, 0, S, bt, 0, S, x, 0, nc * C, 1, 1, nr * C, nc * C, S, 1.f, 0, st)));
+  {
+    PF_LAUNCH_SCOPE(st, "k_opm_relayout");
+    k_opm_relayout<<<nblk(nr * nc * C * C, 256), 256, 0, st>>>(x, nr, nc, C, xr);
+  }
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(xr, 0, (int64_t)C * C, (const T*)p->w_out, 0, (int64_t)C * C, y, 0, c_z, 1, 1, nr * nc, c_z,
+                         (int64_t)C * C, 1.f, 0, st)));
+  if (mask.ptr) PF_TRY(opm_norm(mask, S, row0, nr, col0, nc, eps, norm, st));
+  {
+    PF_LAUNCH_SCOPE(st, "k_opm_out");
+    k_opm_out<T><<<nblk(nr * nc * c_z, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride, y, p->b_out,
+                                                          mask.ptr ? norm : nullptr, (float)S + eps, nr, nc, c_z,
+                                                          acc);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out, int64_t n_seq, int64_t n_res,
+        int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int c_m, int C, int c_z, float eps, int acc,
+        int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return opm_t<float>(p, m, mask, z_out, n_seq, n_res, row0, n_rows, col0, n_cols, c_m, C, c_z, eps, acc, ar, st);
+  return opm_t<__nv_bfloat16>(p, m, mask, z_out, n_seq, n_res, row0, n_rows, col0, n_cols, c_m, C, c_z, eps, acc, ar,
+                              st);
+}
+
 }  // namespace simt
 }  // namespace pf

@@ -54,5 +54,14 @@ int attn_split(int d, const float* q, int64_t q_ps, const float* k, const float*
                int64_t b_hs, int64_t b_rs, int64_t n_q, int64_t n, int H, float* part, float* o, int64_t o_ps,
                cudaStream_t st);
 
+// OuterProductMean (fp32 arithmetic) of the rows [row0, row0 + n_rows) x cols [col0, col0 + n_cols),
+// and the norm tile sum_s mask(s, i) mask(s, j) + eps it divides by (shared with the bf16 path).
+size_t opm_ws_bytes(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int c_m, int C, int c_z);
+int opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out, int64_t n_seq, int64_t n_res,
+        int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int c_m, int C, int c_z, float eps, int acc,
+        int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+int opm_norm(pf_mask_view m, int64_t n_seq, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, float eps,
+             float* norm, cudaStream_t st);
+
 }  // namespace simt
 }  // namespace pf

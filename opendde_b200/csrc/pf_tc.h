@@ -77,5 +77,13 @@ size_t rows_apb_ws_bytes(int64_t n, int64_t nq, int c_s, int H);
 int rows_apb(const pf_apb_params* p, const void* s_in, void* s_out, const float* bias, int64_t b_hs, int64_t b_rs,
              int64_t n, int64_t q0, int64_t nq, int c_s, int H, int acc, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// OuterProductMean (bf16, c_hidden = 32): projections, the outer product over the sequences and
+// W_out on tcgen05; see pf_opm_fwd.
+bool rows_opm_supported(int c_m, int c_hidden, int c_z);
+size_t rows_opm_ws_bytes(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int c_m, int C);
+int rows_opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out, int64_t S, int64_t N,
+             int64_t row0, int64_t nr, int64_t col0, int64_t nc, int c_m, int C, int c_z, float eps, int acc,
+             void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace tc
 }  // namespace pf

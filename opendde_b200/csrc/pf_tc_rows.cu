@@ -224,7 +224,10 @@ constexpr uint32_t R_B_BYTES = RB_NMAX * RB_K * 2;  // 32 KB
 constexpr uint32_t R_STAGE = R_A_BYTES + R_B_BYTES;
 constexpr uint32_t R_SMEM = R_STAGES * R_STAGE + 256;
 
-enum Epi : int { E_STORE = 0, E_AB = 1, E_RESID = 2, E_SWIGLU = 3, E_QKVG = 4, E_HBIAS = 5, E_STOREF = 6 };
+enum Epi : int { E_STORE = 0, E_AB = 1, E_RESID = 2, E_SWIGLU = 3, E_QKVG = 4, E_HBIAS = 5, E_STOREF = 6, E_OPMAB = 7 };
+// A operand: contiguous rows (A_ROWS), or the outer products X[(i, c)][(j, e)] of
+// OuterProductMean read as rows (i, j) of K = (c, e) through a 4-D tensor map (A_OUTER)
+enum AMode : int { A_ROWS = 0, A_OUTER = 1 };
 
 struct RowArgs {
   int64_t n_pos;          // rows of A (positions)
@@ -252,6 +255,14 @@ struct RowArgs {
   int accumulate;
   const __nv_bfloat16* gate;
   int64_t ldg;
+  //   (E_RESID, optional) acc + colbias[n], divided by rownorm[p] (or norm_const if rownorm is null)
+  const float* rownorm;
+  float norm_const;
+  int divide;
+  // A_OUTER: position tiles are (i, 128 j) of an a_rows x e_cols grid, a_tpr tiles per i
+  int64_t a_tpr;
+  // E_OPMAB: dst[0][(r*C + ch)*ld + c] = mask(r, c) * acc  (the a^T / b^T operands of the outer
+  // product, C = n_out channels)
   // E_QKVG: columns [q | k | v | g], heads x 32 each; queries are the columns
   // [q_col0, q_col0 + n_q) of the view
   __half* q;
@@ -278,10 +289,8 @@ __device__ __forceinline__ uint4 pack8_f16(const float* f) {
 // Epilogue of one 128 x bn accumulator: thread = one position (TMEM lane), taddr = its lane's
 // address at column 0 of the accumulator. Every tcgen05.ld is executed by all 32 lanes.
 template <int E>
-__device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, int64_t p, int n0) {
-  const bool valid = p < a.n_pos;
-  const int64_t r = valid ? p / a.e_cols : 0;
-  const int64_t c = valid ? p - r * a.e_cols : 0;
+__device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, bool valid, int64_t p, int64_t r,
+                                             int64_t c, int n0) {
   if constexpr (E == E_STOREF) {
     for (int cc = 0; cc < a.bn; cc += 16) {
       uint32_t v[16];
@@ -306,7 +315,9 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, i
       tmem_ld_wait();
       const int n = n0 + cc;
       if (!valid || n >= a.n_out) continue;
-      const int cnt = a.n_out - n < 32 ? a.n_out - n : 32;
+      // columns of this tile (bn is a multiple of 16, not of 32) that exist
+      int cnt = a.n_out - n < 32 ? a.n_out - n : 32;
+      if (a.bn - cc < cnt) cnt = a.bn - cc;
       float f[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
@@ -327,6 +338,14 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, i
       } else {
         __nv_bfloat16* o = a.out + r * a.rs + c * a.cs + n;
         const __nv_bfloat16* gp = a.gate ? a.gate + p * a.ldg + n : nullptr;
+        if (a.divide) {
+          const float nrm = a.rownorm ? a.rownorm[p] : a.norm_const;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float bias = (a.colbias && e < cnt) ? a.colbias[n + e] : 0.f;
+            f[e] = (f[e] + bias) / nrm;
+          }
+        }
         if (cnt == 32) {
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -403,6 +422,19 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, i
         }
       }
     }
+  } else if constexpr (E == E_OPMAB) {
+    float mk = 0.f;
+    if (valid) mk = a.mask.ptr ? a.mask.ptr[r * a.mask.row_stride + c * a.mask.col_stride] : 1.f;
+#pragma unroll 1
+    for (int cc = 0; cc < a.bn; cc += 16) {
+      uint32_t v[16];
+      tmem_ld16(taddr + cc, v);
+      tmem_ld_wait();
+      if (!valid) continue;
+      __nv_bfloat16* d = a.dst[0] + (r * a.n_out + n0 + cc) * a.ld + c;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) d[e * a.ld] = __float2bfloat16_rn(mk * __uint_as_float(v[e]));
+    }
   } else if constexpr (E == E_QKVG) {
     const int hd = a.heads * RD;
     const int part = n0 / hd, w0 = n0 - part * hd;
@@ -465,7 +497,7 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, i
 // Persistent: one CTA per SM walks the (position tile, output tile) list, output tile fastest
 // (the CTAs running at one time share an A tile in L2). Warp 0: TMA producer; warp 1: TMEM
 // allocation and the MMA thread; warps 2-5: epilogue (thread = TMEM lane = position).
-template <int E>
+template <int E, int AM>
 __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUtensorMap ta,
                                                     const __grid_constant__ CUtensorMap tb, const RowArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -512,13 +544,19 @@ __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUte
       uint32_t cnt = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < a.n_work && ok; t += G) {
-        const int m0 = (int)((t / a.n_tiles) * RB_M), n0 = (int)(t % a.n_tiles) * a.bn;
+        const int64_t mt = t / a.n_tiles;
+        const int n0 = (int)(t % a.n_tiles) * a.bn;
         for (int kb = 0; kb < a.kb; ++kb, ++cnt) {
           const uint32_t s = cnt % R_STAGES, u = cnt / R_STAGES;
           if (u > 0) ok = mbar_wait(empty(s), (u - 1) & 1, a.status) && ok;
           const uint32_t sa = base + s * R_STAGE, sb = sa + R_A_BYTES;
           mbar_arrive_expect_tx(full(s), stage_tx);
-          tma_load_2d(sa, &ta, full(s), kb * RB_K, m0);
+          if constexpr (AM == A_OUTER) {
+            // rows (i, j0 .. j0 + 127), K block = outer-product channels c = 2 kb, 2 kb + 1
+            tma_load_4d(sa, &ta, full(s), 0, (int)(mt % a.a_tpr) * RB_M, 2 * kb, (int)(mt / a.a_tpr));
+          } else {
+            tma_load_2d(sa, &ta, full(s), kb * RB_K, (int)(mt * RB_M));
+          }
           tma_load_2d(sb, &tb, full(s), kb * RB_K, n0);
         }
       }
@@ -540,7 +578,9 @@ __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUte
           const uint32_t sa = base + s * R_STAGE, sb = sa + R_A_BYTES;
 #pragma unroll
           for (int kk = 0; kk < RB_K / 16; ++kk) {
-            const uint64_t ad = sdesc(sa + kk * 32, 1024, SWZ_128B);
+            // A_OUTER: two 64-byte-row SW64 atoms (one per outer-product channel c) of 8 KB
+            const uint64_t ad = AM == A_OUTER ? sdesc(sa + (kk >> 1) * 8192 + (kk & 1) * 32, 512, SWZ_64B)
+                                              : sdesc(sa + kk * 32, 1024, SWZ_128B);
             const uint64_t bd = sdesc(sb + kk * 32, 1024, SWZ_128B);
             umma_f16(acc, ad, bd, idesc, (kb > 0 || kk > 0) ? 1u : 0u);
           }
@@ -556,12 +596,25 @@ __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUte
     const int row = q * 32 + lane;
     uint32_t j = 0;
     for (int64_t t = blockIdx.x; t < a.n_work; t += G, ++j) {
-      const int64_t m0 = (t / a.n_tiles) * RB_M;
+      const int64_t mt = t / a.n_tiles;
       const int n0 = (int)(t % a.n_tiles) * a.bn;
       const uint32_t b = j & 1;
       mbar_wait(acc_full(b), (j >> 1) & 1, a.status);
       tc_fence_after();
-      row_epilogue<E>(a, tmem + 256 * b + ((uint32_t)(q * 32) << 16), m0 + row, n0);
+      bool valid;
+      int64_t p, r, c;
+      if constexpr (AM == A_OUTER) {
+        r = mt / a.a_tpr;
+        c = (mt % a.a_tpr) * RB_M + row;
+        valid = c < a.e_cols;
+        p = r * a.e_cols + c;
+      } else {
+        p = mt * RB_M + row;
+        valid = p < a.n_pos;
+        r = valid ? p / a.e_cols : 0;
+        c = valid ? p - r * a.e_cols : 0;
+      }
+      row_epilogue<E>(a, tmem + 256 * b + ((uint32_t)(q * 32) << 16), valid, p, r, c, n0);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty(b));
@@ -588,13 +641,15 @@ constexpr int CM_MAX_C = 768;  // k_ln_cmajor: c * 256 B of shared memory
 int ensure_attrs() {
   static std::atomic<unsigned long long> done{0};
   return once_per_device(done, []() -> int {
-    PF_TRY(set_smem(k_rowgemm<E_STORE>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_AB>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_RESID>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_SWIGLU>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_QKVG>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_HBIAS>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_rowgemm<E_STOREF>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_STORE, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_AB, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_RESID, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_SWIGLU, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_QKVG, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_HBIAS, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_STOREF, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_OPMAB, A_ROWS>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_RESID, A_OUTER>, R_SMEM + 1024));
     PF_TRY(set_smem(k_ln_cmajor, CM_MAX_C * 128 * 2));
     return PF_OK;
   });
@@ -694,6 +749,16 @@ int rowgemm(const __nv_bfloat16* A, int64_t lda, int64_t n_pos, int k, const voi
   if (n_pos == 0) return PF_OK;
   if (!aligned16(A) || !aligned16(W) || lda % 8 || k % 8)
     return fail(PF_EINVAL_SHAPE, "%s: operands need 16-byte alignment and widths that are multiples of 8", name);
+  if (E == E_STORE || E == E_STOREF || E == E_RESID) {
+    // few positions (the single representation: N rows): narrower output tiles, so that the
+    // persistent grid still covers the SMs. Chosen before the B tensor map, whose box is bn rows.
+    const int64_t m_tiles = (n_pos + RB_M - 1) / RB_M;
+    while (ra.bn > 32 && m_tiles * ((ra.n_out + ra.bn - 1) / ra.bn) < sm_count()) {
+      const int half = (ra.bn / 2 + 15) / 16 * 16;
+      if (half < 32) break;
+      ra.bn = half;
+    }
+  }
   if (ra.bn < 16 || ra.bn > RB_NMAX || ra.bn % 16) return fail(PF_EUNSUPPORTED, "%s: tile width %d", name, ra.bn);
   CUtensorMap ta, tb;
   {
@@ -716,13 +781,52 @@ int rowgemm(const __nv_bfloat16* A, int64_t lda, int64_t n_pos, int k, const voi
   const int64_t grid = ra.n_work < sm_count() ? ra.n_work : sm_count();
   {
     PF_LAUNCH_SCOPE_WORK(st, name, 2.0 * (double)n_pos * ra.n_out * k, 'f');
-    k_rowgemm<E><<<(unsigned)grid, 192, R_SMEM + 1024, st>>>(ta, tb, ra);
+    k_rowgemm<E, A_ROWS><<<(unsigned)grid, 192, R_SMEM + 1024, st>>>(ta, tb, ra);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
 
 int64_t pad8(int64_t n) { return (n + 7) / 8 * 8; }
+
+// W_out applied to the outer products: rows (i, j) of an n_rows x n_cols grid, K = C*C read
+// from x[(i*C + c)*ld_x + j*C + e] (bf16) through a 4-D tensor map {e, j, c, i}: one 64-channel K
+// block is the two 32 x 128 boxes of channels c = 2 kb, 2 kb + 1, each a SW64 atom of 64-byte rows.
+int rowgemm_outer(const __nv_bfloat16* x, int64_t ld_x, int64_t n_rows, int64_t n_cols, int C, const void* W,
+                  int w_rows, RowArgs ra, const char* name, unsigned int* status, cudaStream_t st) {
+  if (n_rows * n_cols == 0) return PF_OK;
+  if (C != 32 || !aligned16(x) || !aligned16(W) || ld_x % 8)
+    return fail(PF_EUNSUPPORTED, "%s: outer-product operand needs C = 32 and 16-byte alignment", name);
+  CUtensorMap ta, tb;
+  {
+    const uint64_t d[4] = {(uint64_t)C, (uint64_t)n_cols, (uint64_t)C, (uint64_t)n_rows};
+    const uint64_t str[3] = {(uint64_t)C * 2, (uint64_t)ld_x * 2, (uint64_t)C * ld_x * 2};
+    const uint32_t bx[4] = {32, RB_M, 2, 1};
+    PF_TRY(make_tmap(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, x, d, str, bx, CU_TENSOR_MAP_SWIZZLE_64B));
+    const uint64_t dw[2] = {(uint64_t)C * C, (uint64_t)w_rows};
+    const uint64_t sw[1] = {(uint64_t)C * C * 2};
+    const uint32_t bw[2] = {RB_K, (uint32_t)ra.bn};
+    PF_TRY(make_tmap(&tb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, W, dw, sw, bw, CU_TENSOR_MAP_SWIZZLE_128B));
+  }
+  ra.n_pos = n_rows * n_cols;
+  ra.e_cols = n_cols;
+  ra.a_tpr = (n_cols + RB_M - 1) / RB_M;
+  ra.m_tiles = n_rows * ra.a_tpr;
+  ra.n_tiles = (ra.n_out + ra.bn - 1) / ra.bn;
+  ra.kb = C * C / RB_K;
+  ra.n_work = ra.m_tiles * ra.n_tiles;
+  ra.status = status;
+  PF_TRY(ensure_attrs());
+  const int64_t grid = ra.n_work < sm_count() ? ra.n_work : sm_count();
+  {
+    PF_LAUNCH_SCOPE_WORK(st, name, 2.0 * (double)ra.n_pos * ra.n_out * C * C, 'f');
+    k_rowgemm<E_RESID, A_OUTER><<<(unsigned)grid, 192, R_SMEM + 1024, st>>>(ta, tb, ra);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+
 
 // ---------------------------------------------------------------- triangle update, by stage
 struct ProjWs {
@@ -1076,6 +1180,77 @@ int rows_transition(const pf_transition_params* p, const void* x, int64_t xs, vo
   ro.cs = os;
   ro.accumulate = acc;
   return rowgemm<E_RESID>(h, hid, rows, hid, p->w_o, c, ro, "k_rowgemm_resid", status, st);
+}
+
+// ---------------------------------------------------------------- OuterProductMean
+bool rows_opm_supported(int c_m, int c_hidden, int c_z) {
+  return c_m >= 8 && c_m % 8 == 0 && c_m <= 1024 && c_hidden == 32 && c_z >= 8 && c_z % 8 == 0 && c_z <= 1024;
+}
+
+namespace {
+struct OpmWs {
+  __nv_bfloat16 *ln, *at, *bt, *x;
+  float* norm;
+  int64_t ld_s, ld_x;
+};
+void opm_plan(Arena& ar, int64_t S, int64_t N, int64_t nr, int64_t nc, int c_m, int C, bool masked, OpmWs& w) {
+  w.ld_s = pad8(S);
+  w.ld_x = pad8(nc * C);
+  w.ln = ar.take<__nv_bfloat16>((size_t)N * S * c_m);
+  w.at = ar.take<__nv_bfloat16>((size_t)nr * C * w.ld_s);
+  w.bt = ar.take<__nv_bfloat16>((size_t)nc * C * w.ld_s);
+  w.x = ar.take<__nv_bfloat16>((size_t)nr * C * w.ld_x);
+  w.norm = masked ? ar.take<float>((size_t)nr * nc) : nullptr;
+}
+}  // namespace
+
+size_t rows_opm_ws_bytes(int64_t n_seq, int64_t n_res, int64_t n_rows, int64_t n_cols, int c_m, int C) {
+  Arena ar(nullptr, 0);
+  OpmWs w;
+  opm_plan(ar, n_seq, n_res, n_rows, n_cols, c_m, C, true, w);
+  return ar.used;
+}
+
+int rows_opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view z_out, int64_t S, int64_t N,
+             int64_t row0, int64_t nr, int64_t col0, int64_t nc, int c_m, int C, int c_z, float eps, int acc,
+             void* ws, size_t ws_bytes, cudaStream_t st) {
+  PF_TRY(check_view(m, "opm m"));
+  PF_TRY(check_view(z_out, "opm z_out"));
+  Arena ar(ws, ws_bytes);
+  OpmWs w;
+  opm_plan(ar, S, N, nr, nc, c_m, C, mask.ptr != nullptr, w);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "OuterProductMean workspace too small");
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  // LN of every position in (i, s) order: a residue's sequences are contiguous rows
+  PF_TRY(ln_pos((const __nv_bfloat16*)m.ptr, m.col_stride, m.row_stride, N, S, c_m, p->ln_w, p->ln_b, w.ln, st));
+  // aT[(i*C + c)*ld_s + s] = mask(s, row0 + i) * linear_1(ln(s, row0 + i))[c]; bT likewise
+  RowArgs ra{};
+  ra.n_out = C;
+  ra.bn = C;
+  ra.e_cols = S;
+  ra.ld = w.ld_s;
+  ra.dst[0] = w.at;
+  ra.mask = pf_mask_view{mask.ptr ? mask.ptr + row0 * mask.col_stride : nullptr, mask.col_stride, mask.row_stride};
+  PF_TRY(rowgemm<E_OPMAB>(w.ln + row0 * S * c_m, c_m, nr * S, c_m, p->w_1, C, ra, "k_rowgemm_opm_ab", status, st));
+  ra.dst[0] = w.bt;
+  ra.mask = pf_mask_view{mask.ptr ? mask.ptr + col0 * mask.col_stride : nullptr, mask.col_stride, mask.row_stride};
+  PF_TRY(rowgemm<E_OPMAB>(w.ln + col0 * S * c_m, c_m, nc * S, c_m, p->w_2, C, ra, "k_rowgemm_opm_ab", status, st));
+  // x[(i, c)][(j, e)] = sum_s aT[(i, c)][s] bT[(j, e)][s]: one channel of the per-channel contraction
+  PF_TRY(trimul_contract(w.at, w.ld_s, w.bt, w.ld_s, nr * C, nc * C, S, 1, w.x, w.ld_x, status, st));
+  if (mask.ptr) PF_TRY(simt::opm_norm(mask, S, row0, nr, col0, nc, eps, w.norm, st));
+  RowArgs ro{};
+  ro.n_out = c_z;
+  ro.bn = pick_bn(c_z, 16);
+  ro.out = (__nv_bfloat16*)z_out.ptr;
+  ro.rs = z_out.row_stride;
+  ro.cs = z_out.col_stride;
+  ro.accumulate = acc;
+  ro.colbias = p->b_out;
+  ro.divide = 1;
+  ro.rownorm = w.norm;
+  ro.norm_const = (float)S + eps;
+  return rowgemm_outer(w.x, w.ld_x, nr, nc, C, p->w_out, c_z, ro, "k_rowgemm_opm_out", status, st);
 }
 
 // ---------------------------------------------------------------- AttentionPairBias, single path

@@ -193,6 +193,24 @@ def apb_pair_bias(pack: WeightPack, z: torch.Tensor, heads: int, out: torch.Tens
                                        code, ws.data_ptr(), ws.numel(), stream_ptr()))
 
 
+def opm(pack: WeightPack, m: torch.Tensor, mask: Optional[torch.Tensor], z_out: torch.Tensor, row0: int,
+        col0: int, c_hidden: int, eps: float, accumulate: bool) -> None:
+    """z_out (+)= the OuterProductMean update of rows [row0, row0 + R) x cols [col0, col0 + C)
+    (z_out is [R, C, c_z]) from the MSA representation ``m`` [S, N, c_m] and its mask [S, N]
+    (see pf_opm_fwd)."""
+    require_cuda(m, z_out, mask)
+    code = dtype_code(m)
+    if z_out.dtype != m.dtype:
+        raise TypeError("the pair update must be in the MSA representation's dtype")
+    n_seq, n_res, c_m = m.shape
+    n_rows, n_cols, c_z = z_out.shape
+    nbytes = _abi.workspace_bytes("pf_opm_workspace_size", n_seq, n_res, n_rows, n_cols, c_m, c_hidden, c_z, code)
+    ws = workspace(nbytes, m.device)
+    check(_abi.load().pf_opm_fwd(ctypes.byref(pack.struct), pair_view(m), mask_view(mask), pair_view(z_out), n_seq,
+                                 n_res, row0, n_rows, col0, n_cols, c_m, c_hidden, c_z, float(eps), int(accumulate),
+                                 code, ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
 def apb(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, z: Optional[torch.Tensor],
         bias: Optional[torch.Tensor], heads: int, accumulate: bool) -> None:
     """s_out (+)= AttentionPairBias(s_in, z) (bias from z when ``bias`` is None)."""

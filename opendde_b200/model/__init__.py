@@ -1,4 +1,5 @@
 """Module mirror of opendde.model (Pairformer pair stack only)."""
+from .outer_product_mean import OuterProductMean  # noqa: F401
 from .pairformer import PairformerBlock, PairformerStack  # noqa: F401
 from .primitives import Linear, LinearNoBias, Transition  # noqa: F401
 from .transformer import AttentionPairBias  # noqa: F401

@@ -61,7 +61,7 @@ def _mask(n, device):
     return ragged_pair_mask(n, seed=3, drop=0.2, full_rows=[5]).to(device)
 
 
-@pytest.mark.parametrize("c_z,c_h", [(64, 128), (384, 384), (40, 64)])
+@pytest.mark.parametrize("c_z,c_h", [(64, 128), (384, 384), (40, 64), (288, 64)])
 @pytest.mark.parametrize("outgoing", [True, False])
 def test_trimul_general_width(c_z, c_h, outgoing, cuda_device):
     n = 97

@@ -56,3 +56,15 @@ def test_state_dict_matches_reference_in_every_caller_configuration(config):
     mod = getattr(M, ref["class"])(**ref["kwargs"])
     got = {k: list(v.shape) for k, v in mod.state_dict().items()}
     assert got == ref["params"]
+
+
+def test_outer_product_mean_parameter_names_match_reference():
+    """The parameter names and shapes of the reference OuterProductMean (the golden fixture was
+    made by tests/golden/make_opm_golden.py from the reference module)."""
+    from opendde_b200.model import OuterProductMean
+    rec = np.load(f"{GOLDEN_DIR}/opm/opm_s7_n13_masked.npz")
+    mod = OuterProductMean(c_m=int(rec["c_m"]), c_z=int(rec["c_z"]), c_hidden=int(rec["c_hidden"]))
+    assert sorted(n for n, _ in mod.named_parameters()) == list(rec["param_names"])
+    assert tuple(mod.linear_out.weight.shape) == (int(rec["c_z"]), int(rec["c_hidden"]) ** 2)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        mod(torch.zeros(3, 5, int(rec["c_m"])))
