@@ -34,14 +34,18 @@ constexpr int CH = 128;    // c_z == c_h on this path
 constexpr int TILE = 128;  // positions per projection / output CTA
 
 // ------------------------------------------------------------------ kernel 1: projections
-// Persistent, one CTA per SM. Work item = (tile of 128 positions, side a or b), items of the
-// two sides interleaved so a z tile shared by both sides is read from DRAM once. Item k of a
-// CTA goes to compute warpgroup k & 1 (its own stage and 256 TMEM columns).
-//   warp 0     TMA producer: both sides' [W_p ; W_g] once, then z tiles
-//   warp 1     MMA issuer: [p | g] = [W_p ; W_g] LN(z)   (N = 256)
-//   warps 2-9  LN in place; epilogue mask * sigmoid(g) * p (reference order,
-//              triangular.py:539-544) transposed into the stage as [channel][position] and
-//              TMA-stored into the channel-major operand a[c][row][k] (or b).
+// Persistent, one CTA per SM, an even grid: CTA b projects side b & 1 only (items of the two
+// sides of a tile run on neighbouring CTAs at the same time, so a z tile shared by both sides
+// is read from DRAM once and from L2 the second time), so it holds one side's [W_p ; W_g]
+// (64 KB). That leaves room for a 3-deep ring of z tiles and two output stages: the next z
+// tiles stream in while earlier items are normalised, multiplied and stored.
+//   warp 0     TMA producer: the side's [W_p ; W_g] once, then z tiles into the ring
+//   warp 1     MMA issuer: [p | g] = [W_p ; W_g] LN(z) (N = 256) into the item's warpgroup's 256
+//              TMEM columns; the MMA completion frees the ring slot
+//   warps 2-9  two warpgroups, alternate items: LN in place in the ring slot; epilogue
+//              mask * sigmoid(g) * p (reference order, triangular.py:539-544) transposed into
+//              the warpgroup's output stage as [channel][position] and TMA-stored into the
+//              channel-major operand a[c][row][k] (or b)
 struct ProjSide {
   int64_t n_rows, n_cols;
   pf_mask_view mask;
@@ -50,15 +54,17 @@ struct ProjSide {
 };
 struct ProjArgs {
   ProjSide side[2];
-  int64_t n_items;
   const float* ln_w;
   const float* ln_b;
   unsigned int* status;
 };
 
-constexpr uint32_t P_W = 0, P_WSIDE = 65536, P_STAGE = 131072, P_STAGE_BYTES = 32768;
-constexpr uint32_t P_LN = P_STAGE + 2 * P_STAGE_BYTES, P_BAR = P_LN + 1024;
+constexpr int P_RING = 3;
+constexpr uint32_t P_W = 0, P_TILE = 32768;
+constexpr uint32_t P_RING0 = 65536, P_OUT0 = P_RING0 + P_RING * P_TILE;
+constexpr uint32_t P_LN = P_OUT0 + 2 * P_TILE, P_BAR = P_LN + 1024;
 constexpr uint32_t PROJ_SMEM = P_BAR + 256;
+static_assert(PROJ_SMEM + 1024 <= 232448, "dynamic shared memory limit");
 
 __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ CUtensorMap tz0,
                                                         const __grid_constant__ CUtensorMap tz1,
@@ -74,22 +80,29 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
   const uint32_t bars = base + P_BAR, wbar = bars;
-  auto full = [&](int w) { return bars + 8 + 8 * w; };
-  auto empty = [&](int w) { return bars + 24 + 8 * w; };
-  auto ready = [&](int w) { return bars + 40 + 8 * w; };
-  auto done = [&](int w) { return bars + 56 + 8 * w; };
+  // wbar @0, full[3] @8, empty[3] @32, ready[2] @56, done[2] @72, drain @88; TMEM slot @128
+  auto full = [&](uint32_t sl) { return bars + 8 + 8 * sl; };
+  auto empty = [&](uint32_t sl) { return bars + 32 + 8 * sl; };
+  auto ready = [&](int w) { return bars + 56 + 8 * w; };
+  auto done = [&](int w) { return bars + 72 + 8 * w; };
+  const uint32_t bar_drain = bars + 88;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + P_BAR + 128);
   float* lnp = reinterpret_cast<float*>(g + P_LN);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int side = (int)(blockIdx.x & 1);
+  const ProjSide& sd = args.side[side];
+  const int64_t first = blockIdx.x >> 1, stride = gridDim.x >> 1;  // this side's tiles
   if (tid == 0) {
     mbar_init(wbar, 1);
+    for (int sl = 0; sl < P_RING; ++sl) {
+      mbar_init(full(sl), 1);
+      mbar_init(empty(sl), 1);
+    }
     for (int w = 0; w < 2; ++w) {
-      mbar_init(full(w), 1);
-      mbar_init(empty(w), 1);
       mbar_init(ready(w), 1);
       mbar_init(done(w), 1);
     }
-    mbar_init(bars + 72, 1);
+    mbar_init(bar_drain, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < CH; c += blockDim.x) {
@@ -104,66 +117,47 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const int64_t G = gridDim.x;
-  // item -> (side, tile); false when that side has fewer tiles
-  auto decode = [&](int64_t item, int& side, int64_t& t) {
-    side = (int)(item & 1);
-    t = item >> 1;
-    return t < args.side[side].ntiles;
-  };
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tz0);
-      tma_prefetch_desc(&tz1);
-      mbar_arrive_expect_tx(wbar, 131072);
-      // per side: atom 0 = [W_p ; W_g] channels 0..63 (32 KB), atom 1 = channels 64..127
-      tma_load_2d(base + P_W, &tw0p, wbar, 0, 0);
-      tma_load_2d(base + P_W + 16384, &tw0g, wbar, 0, 0);
-      tma_load_2d(base + P_W + 32768, &tw0p, wbar, 64, 0);
-      tma_load_2d(base + P_W + 49152, &tw0g, wbar, 64, 0);
-      tma_load_2d(base + P_W + P_WSIDE, &tw1p, wbar, 0, 0);
-      tma_load_2d(base + P_W + P_WSIDE + 16384, &tw1g, wbar, 0, 0);
-      tma_load_2d(base + P_W + P_WSIDE + 32768, &tw1p, wbar, 64, 0);
-      tma_load_2d(base + P_W + P_WSIDE + 49152, &tw1g, wbar, 64, 0);
+      const CUtensorMap* tz = side ? &tz1 : &tz0;
+      tma_prefetch_desc(tz);
+      mbar_arrive_expect_tx(wbar, 65536);
+      // atom 0 = [W_p ; W_g] channels 0..63 (32 KB), atom 1 = channels 64..127
+      const CUtensorMap* twp = side ? &tw1p : &tw0p;
+      const CUtensorMap* twg = side ? &tw1g : &tw0g;
+      tma_load_2d(base + P_W, twp, wbar, 0, 0);
+      tma_load_2d(base + P_W + 16384, twg, wbar, 0, 0);
+      tma_load_2d(base + P_W + 32768, twp, wbar, 64, 0);
+      tma_load_2d(base + P_W + 49152, twg, wbar, 64, 0);
+      bool ok = true;
       int64_t k = 0;
-      for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
-        int side;
-        int64_t t;
-        if (!decode(item, side, t)) continue;
-        const int w = (int)(k & 1);
-        const int64_t n = k >> 1;
-        ++k;
-        if (n > 0) mbar_wait(empty(w), (uint32_t)((n - 1) & 1), args.status);
-        const ProjSide& sd = args.side[side];
+      for (int64_t t = first; t < sd.ntiles && ok; t += stride, ++k) {
+        const uint32_t sl = (uint32_t)(k % P_RING), u = (uint32_t)(k / P_RING);
+        if (u > 0) ok = mbar_wait(empty(sl), (u - 1) & 1, args.status) && ok;
         const int r = (int)(t / sd.tiles_per_row);
         const int c0 = (int)((t % sd.tiles_per_row) * TILE);
-        const uint32_t st = base + P_STAGE + w * P_STAGE_BYTES;
-        const CUtensorMap* tz = side ? &tz1 : &tz0;
-        mbar_arrive_expect_tx(full(w), 32768);
-        tma_load_3d(st, tz, full(w), 0, c0, r);
-        tma_load_3d(st + 16384, tz, full(w), 64, c0, r);
+        const uint32_t st = base + P_RING0 + sl * P_TILE;
+        mbar_arrive_expect_tx(full(sl), 32768);
+        tma_load_3d(st, tz, full(sl), 0, c0, r);
+        tma_load_3d(st + 16384, tz, full(sl), 64, c0, r);
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      mbar_wait(wbar, 0, args.status);
+      bool ok = mbar_wait(wbar, 0, args.status);
       int64_t k = 0;
-      for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
-        int side;
-        int64_t t;
-        if (!decode(item, side, t)) continue;
+      for (int64_t t = first; t < sd.ntiles && ok; t += stride, ++k) {
         const int w = (int)(k & 1);
-        const uint32_t par = (uint32_t)((k >> 1) & 1);
-        ++k;
-        mbar_wait(ready(w), par, args.status);
+        const uint32_t sl = (uint32_t)(k % P_RING);
+        ok = mbar_wait(ready(w), (uint32_t)((k >> 1) & 1), args.status) && ok;
         tc_fence_after();
-        tile::umma_k128(tmem + w * 256, base + P_STAGE + w * P_STAGE_BYTES, base + P_W + side * P_WSIDE, 32768,
-                        idesc_f16(128, 256, true));
+        tile::umma_k128(tmem + w * 256, base + P_RING0 + sl * P_TILE, base + P_W, 32768, idesc_f16(128, 256, true));
         umma_commit(done(w));
+        umma_commit(empty(sl));  // the ring slot is free once these MMAs have read it
       }
-      umma_commit(bars + 72);  // drain: every MMA complete before TMEM is released
-      mbar_wait_drain(bars + 72, 0);
+      umma_commit(bar_drain);  // drain: every MMA complete before TMEM is released
+      mbar_wait_drain(bar_drain, 0);
     }
   } else {
     const int wg = (warp - 2) >> 2;
@@ -171,21 +165,16 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
     const int row = q * 32 + lane;
     const bool leader = (warp == 2 + 4 * wg) && lane == 0;
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-    uint8_t* zt = g + P_STAGE + wg * P_STAGE_BYTES;
-    const uint32_t st = base + P_STAGE + wg * P_STAGE_BYTES;
-    int64_t k = 0;
-    for (int64_t item = blockIdx.x; item < args.n_items; item += G) {
-      int side;
-      int64_t t;
-      if (!decode(item, side, t)) continue;
-      const int w = (int)(k & 1);
-      const uint32_t par = (uint32_t)((k >> 1) & 1);
-      ++k;
-      if (w != wg) continue;
-      const ProjSide& sd = args.side[side];
+    const uint32_t ost = base + P_OUT0 + wg * P_TILE;
+    unsigned short* ot = reinterpret_cast<unsigned short*>(g + P_OUT0 + wg * P_TILE);
+    int64_t k = 0, mine = 0;
+    for (int64_t t = first; t < sd.ntiles; t += stride, ++k) {
+      if ((int)(k & 1) != wg) continue;
+      const uint32_t sl = (uint32_t)(k % P_RING);
       const int r = (int)(t / sd.tiles_per_row);
       const int c0 = (int)((t % sd.tiles_per_row) * TILE);
-      mbar_wait(full(wg), par, args.status);
+      uint8_t* zt = g + P_RING0 + sl * P_TILE;
+      mbar_wait(full(sl), (uint32_t)((k / P_RING) & 1), args.status);
       {
         uint32_t zr[64];
         float m, rs;
@@ -201,10 +190,14 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
       float mk = 0.f;
       if (col < sd.n_cols)
         mk = sd.mask.ptr ? sd.mask.ptr[(int64_t)r * sd.mask.row_stride + col * sd.mask.col_stride] : 1.f;
-      mbar_wait(done(wg), par, args.status);
+      // the output stage's previous TMA store must have read it before it is overwritten
+      if (mine > 0) {
+        if (leader) bulk_wait_group_read0();
+        named_bar_sync(1 + wg, 128);
+      }
+      mbar_wait(done(wg), (uint32_t)(mine & 1), args.status);
       tc_fence_after();
-      // [channel][position] bf16 tile over the (consumed) z tile: 256 B per channel
-      unsigned short* ot = reinterpret_cast<unsigned short*>(zt);
+      // [channel][position] bf16 tile: 256 B per channel
 #pragma unroll
       for (int cc = 0; cc < CH; cc += 16) {
         uint32_t pv[16], gv[16];
@@ -221,11 +214,10 @@ __global__ void __launch_bounds__(320, 1) k_trimul_proj(const __grid_constant__ 
       fence_proxy_async_smem();
       named_bar_sync(1 + wg, 128);
       if (leader) {
-        tma_store_3d(side ? &to1 : &to0, st, c0, r, 0);
+        tma_store_3d(side ? &to1 : &to0, ost, c0, r, 0);
         bulk_commit_group();
-        bulk_wait_group_read0();
-        mbar_arrive(empty(wg));
       }
+      ++mine;
     }
     if (leader) bulk_wait_group0();
   }
@@ -706,12 +698,13 @@ int launch_proj(const pf_trimul_params* p, pf_pair_view za, pf_pair_view zb, pf_
   pa.side[0] = ProjSide{n_i, n_k, ma, tpr_k, n_i * tpr_k};
   pa.side[1] = ProjSide{n_j, n_k, mb, tpr_k, n_j * tpr_k};
   const int64_t nt = pa.side[0].ntiles > pa.side[1].ntiles ? pa.side[0].ntiles : pa.side[1].ntiles;
-  pa.n_items = 2 * nt;
   pa.ln_w = p->ln_in_w;
   pa.ln_b = p->ln_in_b;
   pa.status = status;
   {
-    const int64_t grid_p = pa.n_items < sm_count() ? pa.n_items : sm_count();
+    // an even grid: CTA b works on side b & 1 (tile b >> 1, then every (grid / 2)-th tile)
+    const int64_t half = sm_count() / 2;
+    const int64_t grid_p = 2 * (nt < half ? nt : half);
     // read each z view once (once in all when both sides project the same view), write a and b
     const bool same = za.ptr == zb.ptr && za.row_stride == zb.row_stride && za.col_stride == zb.col_stride &&
                       n_i == n_j;

@@ -4,6 +4,7 @@
 from .config import FOLDCP_ENVIRONMENT_KEYS, FOLDCP_MESH_KEY, FoldCPConfig, apply_foldcp_config
 from .layout import FoldCP2DLayout
 from .mesh import FoldCPProcessMesh, clear_mesh_cache
+from .opm import outer_product_mean_local_update
 from .pair_sharding import (
     FoldCPPairShardSpec,
     gather_pair_tensor,
@@ -34,5 +35,5 @@ __all__ = [
     "distributed_attention_pair_bias_update", "distributed_pair_transition_update",
     "distributed_pairformer_block_pair_update", "distributed_pairformer_stack_pair_update",
     "distributed_pairformer_stack_single_bridge_update", "distributed_triangle_attention_update",
-    "distributed_triangle_multiplication_update",
+    "distributed_triangle_multiplication_update", "outer_product_mean_local_update",
 ]
