@@ -624,6 +624,12 @@ def main():
                                   "restatement of the reference modules",
                         "sample_check": cpu_sample_check(cores)}
 
+    # device memory: the peak held by one rank (max over ranks), the pair tensor's share of it
+    mem_gb = torch.cuda.max_memory_allocated(dev) / 1e9
+    if distributed:
+        t = torch.tensor([mem_gb], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        mem_gb = t.item()
     z_bytes = z_host.numel() * 2
     h2d = z_bytes + s_host.numel() * 2 + m_host.numel() * 4
     d2h = z_bytes + s_host.numel() * 2
@@ -641,11 +647,13 @@ def main():
             "scaling": "strong",
             "vs_baseline": None,
             "dtype": "bf16",
-            "data": "synthetic: z,s ~ N(0,1), all-ones mask, seed-0 N(0,1/fan_in) weights",
+            "data": ("synthetic: z,s ~ N(0,1), " + (f"last {args.pad_frac:.0%} of tokens padded" if args.pad_frac > 0
+                                                       else "all-ones mask") + ", seed-0 N(0,1/fan_in) weights"),
             "config": {"workload": f"pairformer_trunk_{args.blocks}blk_N{args.n}_bf16", "n_token": args.n,
                        "c_z": C_Z, "c_s": C_S, "blocks": args.blocks, "grid": f"{grid[0]}x{grid[1]}",
                        "pad_frac": args.pad_frac,
-                       "l2": "inputs larger than L2 (pair tensor 604 MB)"},
+                       "l2": f"inputs larger than L2 (pair tensor {z_bytes / 1e6:.0f} MB)"},
+            "memory": {"max_allocated_gb_per_rank": mem_gb, "pair_tensor_gb": z_bytes / 1e9},
             "e2e": {"value": ms_e2e / args.blocks, "unit": "ms/block", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "roofline": roofline,
