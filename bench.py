@@ -233,7 +233,7 @@ def kernel_entry(name, launches, total_ms, work, unit, peaks, nvlink=None):
         return None
     avg_s = total_ms / launches / 1e3
     base = {"kernel": name, "avg_launch_ms": avg_s * 1e3, "launches": launches}
-    if name == "k_copy_regions" and nvlink is not None and nvlink.get("remote_bytes"):
+    if name in ("k_copy_regions", "dma_copy_regions") and nvlink is not None and nvlink.get("remote_bytes"):
         rb = nvlink["remote_bytes"] / launches
         ach = rb / avg_s / 1e9
         peak = nvlink["peak_gbs"]
@@ -408,7 +408,9 @@ def main():
     ap.add_argument("--workload", choices=["trunk", "c1", "c2"], default="trunk",
                     help="trunk: the 48-block trunk (the headline); c1 / c2: standalone triangle attention / "
                          "triangle multiplicative update at their configurations (1 GPU)")
-    ap.add_argument("--n", type=int, default=N_TOKEN)
+    # "--n-token" first: torchrun resolves abbreviated options even after the script name, and a
+    # bare "--n" is ambiguous to it
+    ap.add_argument("--n-token", "--n", dest="n", type=int, default=N_TOKEN)
     ap.add_argument("--pad-frac", type=float, default=0.0,
                     help="fraction of trailing tokens masked as padding (config C4: 0.07)")
     ap.add_argument("--blocks", type=int, default=48)

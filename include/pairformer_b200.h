@@ -76,7 +76,8 @@ PF_API const char* pf_last_path(void);
 /* Device status word of the current device: bit 0 = a bounded device-side wait (mbarrier
  * pipeline wait) gave up; the kernel then drained instead of hanging. Bit 1 = a bf16
  * triangle-attention logit exceeded the f16 range of the logit accumulator (the affected rows
- * are invalid). The word is sticky: while it is non-zero every later tensor-core kernel drains
+ * are invalid). Bit 2 = a kernel's shared-memory layout did not fit the dynamic shared memory it
+ * was given (it returned without writing its outputs). The word is sticky: while it is non-zero every later tensor-core kernel drains
  * at once and leaves its outputs unwritten, so callers must check it. Synchronises with the
  * device (it copies the word to the host); clear != 0 resets it. No reference counterpart
  * (the reference has no device-side waits). */
@@ -305,6 +306,47 @@ PF_API int pf_opm_fwd(const pf_opm_params* w, pf_pair_view m, pf_mask_view mask,
                       int32_t c_m, int32_t c_hidden, int32_t c_z, float eps, int32_t accumulate, int32_t dtype,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Trunk pair initialisation and recycling ------------------------------------------------
+ * Replaces the trunk's pair input, opendde/model/opendde.py:812-835, and its Fold-CP local
+ * construction (opendde/distributed/foldcp/trunk_init.py:90-178). For i in [row0, row0 + n_rows),
+ * j in [col0, col0 + n_cols):
+ *   z_out(i - row0, j - col0) = W_1 s(i) + W_2 s(j) + W_relp relp(i, j) + W_bond bond(i, j)
+ * with relp(i, j) the one-hot relative-position features of RelativePositionEncoding
+ * (opendde/model/modules/embedders.py:87-302; 4 r_max + 2 s_max + 7 of them) computed from the
+ * per-token ids, so W_relp relp is a sum of four weight columns (no feature tensor is formed),
+ * and bond(i, j) = token_bonds(i, j) (ptr NULL: no bonds). s_init rows are s_stride elements
+ * apart in the storage dtype; the ids are int32 [n_token]. */
+typedef struct {
+  const void* w_zinit1; const void* w_zinit2;  /* [c_z, c_s] linear_no_bias_zinit1 / 2        */
+  const void* w_relp;                          /* [c_z, 4 r_max + 2 s_max + 7]                 */
+  const void* w_bond;                          /* [c_z, 1]    linear_no_bias_token_bond          */
+} pf_trunk_init_params;
+typedef struct {
+  const int32_t* asym_id; const int32_t* residue_index; const int32_t* entity_id;
+  const int32_t* token_index; const int32_t* sym_id;
+} pf_token_ids;
+
+PF_API int pf_trunk_init_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_s, int32_t c_z, int32_t r_max,
+                                        int32_t s_max, int32_t dtype, size_t* bytes);
+PF_API int pf_trunk_init_fwd(const pf_trunk_init_params* w, const void* s_init, int64_t s_stride, pf_token_ids ids,
+                             pf_mask_view token_bonds, pf_pair_view z_out, int64_t n_token, int64_t row0,
+                             int64_t n_rows, int64_t col0, int64_t n_cols, int32_t c_s, int32_t c_z, int32_t r_max,
+                             int32_t s_max, int32_t dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* z_out (+)= W LN(z_in) over the positions of two pair views (c_in -> c_out channels): the
+ * recycling update z = z_init + linear_no_bias_z_cycle(layernorm_z_cycle(z)) of opendde.py:835
+ * with z_out holding z_init and accumulate = 1 (z_out must not alias z_in). bf16 on tcgen05. */
+typedef struct {
+  const float* ln_w; const float* ln_b;  /* [c_in] */
+  const void* w;                         /* [c_out, c_in] */
+} pf_pair_linear_params;
+
+PF_API int pf_pair_ln_linear_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_in, int32_t c_out,
+                                            int32_t dtype, size_t* bytes);
+PF_API int pf_pair_ln_linear_fwd(const pf_pair_linear_params* w, pf_pair_view z_in, pf_pair_view z_out, int64_t n_rows,
+                                 int64_t n_cols, int32_t c_in, int32_t c_out, int32_t accumulate, int32_t dtype,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Fold-CP band exchange through peer memory ------------------------------------------
  * Replace the reference's ring / transpose band exchanges over NCCL send/receive
  * (opendde/distributed/foldcp/comm.py:26-184, used by real_pairformer.py:1226-1404 and
@@ -343,6 +385,9 @@ typedef struct {
  * when every pointer, pitch and row length allows). The caller orders it after the peers'
  * writes (the barrier) and before anything overwrites the sources. */
 PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_regions, void* stream);
+/* The same copies by the GPU's copy engines (any number of regions; one 2-D or 3-D copy per
+ * region, no SMs), so a band copied on a side stream overlaps kernels on another stream. */
+PF_API int pf_copy_regions_dma(const pf_copy_region* regions, int32_t n_regions, void* stream);
 
 #ifdef __cplusplus
 }

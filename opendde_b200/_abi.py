@@ -51,6 +51,9 @@ EXPORTED = (
     "pf_peer_handle_bytes", "pf_peer_window_alloc", "pf_peer_window_free", "pf_peer_window_open",
     "pf_peer_window_close", "pf_copy_regions",
     "pf_opm_workspace_size", "pf_opm_fwd",
+    "pf_trunk_init_workspace_size", "pf_trunk_init_fwd", "pf_pair_ln_linear_workspace_size",
+    "pf_pair_ln_linear_fwd",
+    "pf_copy_regions_dma",
 )
 
 
@@ -99,6 +102,18 @@ class ApbParams(Structure):
 
 class OpmParams(Structure):
     _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w_1", "w_2", "w_out", "b_out")]
+
+
+class TrunkInitParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("w_zinit1", "w_zinit2", "w_relp", "w_bond")]
+
+
+class TokenIds(Structure):
+    _fields_ = [(n, c_void_p) for n in ("asym_id", "residue_index", "entity_id", "token_index", "sym_id")]
+
+
+class PairLinearParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w")]
 
 
 _lib = None
@@ -166,6 +181,14 @@ def load(path: str = LIB_PATH):
         "pf_peer_window_open": ([c_void_p, POINTER(c_void_p)], c_int),
         "pf_peer_window_close": ([c_void_p], c_int),
         "pf_copy_regions": ([POINTER(CopyRegion), c_int32, c_void_p], c_int),
+        "pf_copy_regions_dma": ([POINTER(CopyRegion), c_int32, c_void_p], c_int),
+        "pf_trunk_init_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_trunk_init_fwd": ([POINTER(TrunkInitParams), c_void_p, c_int64, TokenIds, MaskView, PairView, c_int64,
+                               c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                               c_void_p, c_size_t, c_void_p], c_int),
+        "pf_pair_ln_linear_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_pair_ln_linear_fwd": ([POINTER(PairLinearParams), PairView, PairView, c_int64, c_int64, c_int32, c_int32,
+                                   c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
         "pf_opm_workspace_size": ([c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
         "pf_opm_fwd": ([POINTER(OpmParams), PairView, MaskView, PairView, c_int64, c_int64, c_int64, c_int64, c_int64,
                         c_int64, c_int32, c_int32, c_int32, c_float, c_int32, c_int32, c_void_p, c_size_t, c_void_p],
@@ -220,6 +243,8 @@ STATUS_BITS = {
        "hanging)",
     2: "a triangle-attention logit exceeded the f16 range of the bf16 path's logit accumulator "
        "(|q.k| log2(e)/sqrt(d) > 65504); run such inputs in fp32 mode",
+    4: "a tensor-core kernel's shared-memory layout did not fit the dynamic shared memory it was "
+       "given (the kernel returned without writing its outputs)",
 }
 
 

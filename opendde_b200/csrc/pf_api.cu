@@ -548,4 +548,84 @@ int pf_opm_fwd(const pf_opm_params* w, pf_pair_view m, pf_mask_view mask, pf_pai
                    dtype, workspace, workspace_bytes, st);
 }
 
+// ------------------------------------------------------------------ trunk pair input, recycling
+int pf_trunk_init_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_s, int32_t c_z, int32_t r_max,
+                                 int32_t s_max, int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_s <= 0 || c_z <= 0 || r_max < 0 || s_max < 0)
+    return fail(PF_EINVAL_SHAPE, "trunk init: bad sizes");
+  *bytes = trunk::init_ws_bytes(n_rows, n_cols, c_z, r_max, s_max);
+  return PF_OK;
+}
+
+int pf_trunk_init_fwd(const pf_trunk_init_params* w, const void* s_init, int64_t s_stride, pf_token_ids ids,
+                      pf_mask_view token_bonds, pf_pair_view z_out, int64_t n_token, int64_t row0, int64_t n_rows,
+                      int64_t col0, int64_t n_cols, int32_t c_s, int32_t c_z, int32_t r_max, int32_t s_max,
+                      int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_zinit1 || !w->w_zinit2 || !w->w_relp || !w->w_bond || !s_init)
+    return fail(PF_EINVAL_ARG, "trunk init: null weight or s_init");
+  if (!ids.asym_id || !ids.residue_index || !ids.entity_id || !ids.token_index || !ids.sym_id)
+    return fail(PF_EINVAL_ARG, "trunk init: null token id array");
+  if (!view_ok(z_out)) return fail(PF_EINVAL_ARG, "trunk init: bad output view");
+  if (n_token < 0 || c_s <= 0 || c_s > 4096 || c_z <= 0 || c_z > 1024 || c_z % 8 || r_max < 0 || r_max > 1024 ||
+      s_max < 0 || s_max > 1024 || s_stride < c_s)
+    return fail(PF_EINVAL_SHAPE, "trunk init: bad sizes c_s=%d c_z=%d (c_z a multiple of 8) r_max=%d s_max=%d", c_s,
+                c_z, r_max, s_max);
+  if (row0 < 0 || n_rows < 0 || row0 + n_rows > n_token || col0 < 0 || n_cols < 0 || col0 + n_cols > n_token)
+    return fail(PF_EINVAL_SHAPE, "trunk init: tile rows [%lld, %lld) x cols [%lld, %lld) outside %lld tokens",
+                (long long)row0, (long long)(row0 + n_rows), (long long)col0, (long long)(col0 + n_cols),
+                (long long)n_token);
+  const size_t esz = dtype == PF_F32 ? 4 : 2;
+  if (((uintptr_t)z_out.ptr) % 16 || (z_out.row_stride * esz) % 16 || (z_out.col_stride * esz) % 16)
+    return fail(PF_EINVAL_SHAPE, "trunk init: the output view needs 16-byte aligned positions");
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  if (n_rows > 65535) return fail(PF_EUNSUPPORTED, "trunk init: tile of %lld rows > 65535", (long long)n_rows);
+  size_t need;
+  PF_TRY(pf_trunk_init_workspace_size(n_rows, n_cols, c_s, c_z, r_max, s_max, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "trunk init"));
+  set_path("simt");
+  return trunk::init(w, s_init, s_stride, ids, token_bonds, z_out, row0, n_rows, col0, n_cols, c_s, c_z, r_max,
+                     s_max, dtype, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+static bool pair_ln_linear_rows(int c_in, int c_out, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::rows_pair_ln_linear_supported(c_in, c_out);
+}
+
+int pf_pair_ln_linear_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_in, int32_t c_out, int32_t dtype,
+                                     size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_in <= 0 || c_out <= 0) return fail(PF_EINVAL_SHAPE, "pair LN-linear: bad sizes");
+  *bytes = pair_ln_linear_rows(c_in, c_out, dtype) ? tc::rows_pair_ln_linear_ws_bytes(n_rows, n_cols, c_in)
+                                                   : simt::pair_ln_linear_ws_bytes(n_rows, n_cols, c_in, c_out);
+  return PF_OK;
+}
+
+int pf_pair_ln_linear_fwd(const pf_pair_linear_params* w, pf_pair_view z_in, pf_pair_view z_out, int64_t n_rows,
+                          int64_t n_cols, int32_t c_in, int32_t c_out, int32_t accumulate, int32_t dtype,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w || !w->ln_w) return fail(PF_EINVAL_ARG, "pair LN-linear: null weight pointer");
+  if (!view_ok(z_in) || !view_ok(z_out)) return fail(PF_EINVAL_ARG, "pair LN-linear: bad view");
+  if (n_rows < 0 || n_cols < 0 || c_in <= 0 || c_in > 1024 || c_out <= 0 || c_out > 1024)
+    return fail(PF_EINVAL_SHAPE, "pair LN-linear: bad sizes c_in=%d c_out=%d", c_in, c_out);
+  if (z_in.ptr == z_out.ptr) return fail(PF_EINVAL_ARG, "pair LN-linear: z_out must not alias z_in");
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_pair_ln_linear_workspace_size(n_rows, n_cols, c_in, c_out, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "pair LN-linear"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (pair_ln_linear_rows(c_in, c_out, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_pair_ln_linear(w, z_in, z_out, n_rows, n_cols, c_in, c_out, accumulate, workspace,
+                                   workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::pair_ln_linear(w, z_in, z_out, n_rows, n_cols, c_in, c_out, accumulate, dtype, workspace,
+                              workspace_bytes, st);
+}
+
 }  // extern "C"

@@ -189,3 +189,46 @@ extern "C" PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_r
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
+
+// The same regions moved by the copy engines instead of SMs: one 2-D copy per region whose
+// planes are evenly spaced rows of one pitch, one 3-D copy when each side's plane pitch is a
+// whole number of its row pitches, else one 2-D copy per plane. DMA copies run beside the
+// persistent kernels, which hold every SM's shared memory and would otherwise keep an SM copy
+// kernel waiting until they finish; so a band copied on a side stream overlaps the compute on
+// the main stream. Each copy is one call (no batched copy API).
+extern "C" PF_API int pf_copy_regions_dma(const pf_copy_region* regions, int32_t n_regions, void* stream) {
+  if (n_regions < 0) return fail(PF_EINVAL_ARG, "n_regions %d < 0", n_regions);
+  if (n_regions > 0 && regions == nullptr) return fail(PF_EINVAL_ARG, "null region list");
+  cudaStream_t st = (cudaStream_t)stream;
+  for (int i = 0; i < n_regions; ++i) {
+    const pf_copy_region& r = regions[i];
+    if (r.planes < 0 || r.rows < 0 || r.row_bytes < 0) return fail(PF_EINVAL_SHAPE, "region %d: negative size", i);
+    if (r.planes == 0 || r.rows == 0 || r.row_bytes == 0) continue;
+    if (r.src == nullptr || r.dst == nullptr) return fail(PF_EINVAL_ARG, "region %d: null pointer", i);
+    const int64_t sp = r.rows > 1 ? r.src_pitch : r.row_bytes, dp = r.rows > 1 ? r.dst_pitch : r.row_bytes;
+    if (sp < r.row_bytes || dp < r.row_bytes) return fail(PF_EINVAL_SHAPE, "region %d: row pitch smaller than the row", i);
+    if (r.planes > 1 && (r.src_plane_pitch < r.rows * sp || r.dst_plane_pitch < r.rows * dp))
+      return fail(PF_EINVAL_SHAPE, "region %d: plane pitch smaller than the plane", i);
+    PF_LAUNCH_SCOPE_WORK(st, "dma_copy_regions", (double)r.planes * r.rows * r.row_bytes, 'b');
+    if (r.planes == 1 || (r.src_plane_pitch == r.rows * sp && r.dst_plane_pitch == r.rows * dp)) {
+      // the planes are consecutive rows of one 2-D box
+      PF_CUDA_TRY(cudaMemcpy2DAsync(r.dst, (size_t)dp, r.src, (size_t)sp, (size_t)r.row_bytes,
+                                    (size_t)(r.rows * r.planes), cudaMemcpyDefault, st));
+    } else if (r.src_plane_pitch % sp == 0 && r.dst_plane_pitch % dp == 0) {
+      cudaMemcpy3DParms p;
+      memset(&p, 0, sizeof(p));
+      p.srcPtr = make_cudaPitchedPtr(const_cast<void*>(r.src), (size_t)sp, (size_t)r.row_bytes,
+                                     (size_t)(r.src_plane_pitch / sp));
+      p.dstPtr = make_cudaPitchedPtr(r.dst, (size_t)dp, (size_t)r.row_bytes, (size_t)(r.dst_plane_pitch / dp));
+      p.extent = make_cudaExtent((size_t)r.row_bytes, (size_t)r.rows, (size_t)r.planes);
+      p.kind = cudaMemcpyDefault;
+      PF_CUDA_TRY(cudaMemcpy3DAsync(&p, st));
+    } else {
+      for (int64_t pl = 0; pl < r.planes; ++pl)
+        PF_CUDA_TRY(cudaMemcpy2DAsync((char*)r.dst + pl * r.dst_plane_pitch, (size_t)dp,
+                                      (const char*)r.src + pl * r.src_plane_pitch, (size_t)sp, (size_t)r.row_bytes,
+                                      (size_t)r.rows, cudaMemcpyDefault, st));
+    }
+  }
+  return PF_OK;
+}

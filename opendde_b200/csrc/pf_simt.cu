@@ -1133,6 +1133,48 @@ int apb_rows(const pf_apb_params* p, const void* s_in, void* s_out, const float*
                               q0, nq, c_s, H, acc, ar, st);
 }
 
+// ---------------------------------------------------------------- row projections, pair LN + linear
+template <class T>
+int gemm_rows(const T* a, int64_t lda, const T* w, float* c, int64_t m, int n, int k, cudaStream_t st) {
+  return gemm<T, T>(a, 0, lda, w, 0, k, c, 0, n, 1, 1, m, n, k, 1.f, 0, st);
+}
+template int gemm_rows<float>(const float*, int64_t, const float*, float*, int64_t, int, int, cudaStream_t);
+template int gemm_rows<__nv_bfloat16>(const __nv_bfloat16*, int64_t, const __nv_bfloat16*, float*, int64_t, int, int,
+                                      cudaStream_t);
+
+size_t pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in, int c_out) {
+  Arena ar(nullptr, 0);
+  ar.take<float>((size_t)n_rows * n_cols * c_in);
+  ar.take<float>((size_t)n_rows * n_cols * c_out);
+  return ar.used;
+}
+
+template <class T>
+static int pair_ln_linear_t(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows,
+                            int64_t n_cols, int c_in, int c_out, int acc, Arena& ar, cudaStream_t st) {
+  const int64_t P = n_rows * n_cols;
+  float* y = ar.take<float>((size_t)P * c_in);
+  float* o = ar.take<float>((size_t)P * c_out);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "pair LN-linear workspace too small");
+  PF_TRY((ln_view<T, float>((const T*)zi.ptr, zi.row_stride, zi.col_stride, n_rows, n_cols, c_in, p->ln_w, p->ln_b,
+                            1e-5f, y, c_in, st)));
+  PF_TRY((gemm<float, T>(y, 0, c_in, (const T*)p->w, 0, c_in, o, 0, c_out, 1, 1, P, c_out, c_in, 1.f, 0, st)));
+  {
+    PF_LAUNCH_SCOPE(st, "k_combine_view");
+    k_combine_view<T><<<nblk(P * c_out, 256), 256, 0, st>>>((T*)zo.ptr, zo.row_stride, zo.col_stride, n_rows, n_cols,
+                                                          c_out, o, nullptr, acc);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows, int64_t n_cols,
+                   int c_in, int c_out, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32) return pair_ln_linear_t<float>(p, zi, zo, n_rows, n_cols, c_in, c_out, acc, ar, st);
+  return pair_ln_linear_t<__nv_bfloat16>(p, zi, zo, n_rows, n_cols, c_in, c_out, acc, ar, st);
+}
+
 // ---------------------------------------------------------------- OuterProductMean
 // norm[i*n_cols + j] = sum_s mask(s, row0 + i) mask(s, col0 + j) + eps, 16 x 16 outputs per CTA,
 // the mask rows staged 64 sequences at a time (the reference's einsum "...abc,...adc->...bdc").

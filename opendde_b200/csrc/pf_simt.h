@@ -63,5 +63,21 @@ int opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_view 
 int opm_norm(pf_mask_view m, int64_t n_seq, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, float eps,
              float* norm, cudaStream_t st);
 
+// c[m][n] = sum_k a[m*lda + k] w[n*k + k'] (fp32 result; a and w in the storage type)
+template <class T>
+int gemm_rows(const T* a, int64_t lda, const T* w, float* c, int64_t m, int n, int k, cudaStream_t st);
+// z_out (+)= W LN(z_in) on pair views (fp32 arithmetic)
+size_t pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in, int c_out);
+int pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows, int64_t n_cols,
+                   int c_in, int c_out, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace simt
+
+namespace trunk {
+// the trunk's pair input on a tile (pf_trunk.cu)
+size_t init_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int r_max, int s_max);
+int init(const pf_trunk_init_params* p, const void* s, int64_t s_stride, pf_token_ids ids, pf_mask_view bonds,
+         pf_pair_view zo, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int c_s, int c_z, int r_max,
+         int s_max, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+}  // namespace trunk
 }  // namespace pf

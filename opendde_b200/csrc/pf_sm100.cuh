@@ -15,6 +15,8 @@ namespace sm100 {
 // Bit 0: a bounded wait gave up. Once it is set, every later bounded wait in the process
 // returns at once, so a faulty pipeline drains instead of spinning. Bit 1: a triangle-attention
 // logit overflowed the f16 logit accumulator (reported only; the kernels run to completion).
+// Bit 2: a kernel's shared-memory layout did not fit the dynamic shared memory it was given (it
+// returned before starting; reported only).
 // The host reads the word with pf_device_status() (or a stream-ordered copy,
 // pf_device_status_async) and clears it.
 struct DeviceStatus {

@@ -85,5 +85,11 @@ int rows_opm(const pf_opm_params* p, pf_pair_view m, pf_mask_view mask, pf_pair_
              int64_t row0, int64_t nr, int64_t col0, int64_t nc, int c_m, int C, int c_z, float eps, int acc,
              void* ws, size_t ws_bytes, cudaStream_t st);
 
+// z_out (+)= W LN(z_in) on pair views (bf16): a LayerNorm pass and one row GEMM
+bool rows_pair_ln_linear_supported(int c_in, int c_out);
+size_t rows_pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in);
+int rows_pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows,
+                        int64_t n_cols, int c_in, int c_out, int acc, void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace tc
 }  // namespace pf

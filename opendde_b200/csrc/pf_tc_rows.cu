@@ -1182,6 +1182,37 @@ int rows_transition(const pf_transition_params* p, const void* x, int64_t xs, vo
   return rowgemm<E_RESID>(h, hid, rows, hid, p->w_o, c, ro, "k_rowgemm_resid", status, st);
 }
 
+// ---------------------------------------------------------------- pair LN + linear (recycling)
+bool rows_pair_ln_linear_supported(int c_in, int c_out) {
+  return c_in >= 8 && c_in % 8 == 0 && c_in <= 1024 && c_out >= 8 && c_out % 8 == 0 && c_out <= 1024;
+}
+
+size_t rows_pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in) {
+  return align_up((size_t)n_rows * n_cols * c_in * 2, 256);
+}
+
+int rows_pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows,
+                        int64_t n_cols, int c_in, int c_out, int acc, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (ws_bytes < rows_pair_ln_linear_ws_bytes(n_rows, n_cols, c_in))
+    return fail(PF_EWORKSPACE, "pair LN-linear workspace too small");
+  PF_TRY(check_view(zi, "pair LN-linear z_in"));
+  PF_TRY(check_view(zo, "pair LN-linear z_out"));
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  __nv_bfloat16* ln = (__nv_bfloat16*)ws;
+  PF_TRY(ln_pos((const __nv_bfloat16*)zi.ptr, zi.row_stride, zi.col_stride, n_rows, n_cols, c_in, p->ln_w, p->ln_b,
+                ln, st));
+  RowArgs ro{};
+  ro.n_out = c_out;
+  ro.bn = pick_bn(c_out, 16);
+  ro.e_cols = n_cols;
+  ro.out = (__nv_bfloat16*)zo.ptr;
+  ro.rs = zo.row_stride;
+  ro.cs = zo.col_stride;
+  ro.accumulate = acc;
+  return rowgemm<E_RESID>(ln, c_in, n_rows * n_cols, c_in, p->w, c_out, ro, "k_rowgemm_resid", status, st);
+}
+
 // ---------------------------------------------------------------- OuterProductMean
 bool rows_opm_supported(int c_m, int c_hidden, int c_z) {
   return c_m >= 8 && c_m % 8 == 0 && c_m <= 1024 && c_hidden == 32 && c_z >= 8 && c_z % 8 == 0 && c_z <= 1024;

@@ -400,11 +400,14 @@ __global__ void __launch_bounds__(192, 1) k_trimul_bgemm(const __grid_constant__
 // warpgroup k & 1, which owns shared-memory stage k & 1 and TMEM columns [256 w, 256 w + 256)).
 //   warp 0      TMA producer: W_g, W_z once; per tile the z tile (K-major SW128) and the x tile
 //               (channel-major box, 128 channels x 128 positions) into the warpgroup's stage
-//   warp 1      MMA issuer: gate = W_g LN_in(z) into cols +128, acc = W_z LN_out(x) into cols +0
+//   warp 1      MMA issuer: gate = W_g LN_in(z) into cols +128, acc = W_z LN_out(x) into cols +0;
+//               the MMA completion frees the input stage, so the next tiles load during the
+//               epilogue
 //   warps 2-9   two warpgroups; thread = position. x column -> registers -> LN_out(x) written
 //               K-major into the x buffer; LN_in(z) in place in the z buffer; epilogue
 //               acc * sigmoid(gate) (+ residual read back from global, an L2 hit) written into
-//               the z buffer, which is then TMA-stored.
+//               the shared output stage (handed between the warpgroups by out_free), which is
+//               then TMA-stored.
 struct OutArgs {
   int64_t n_i, n_j, tiles_per_row, n_tiles;
   const float *ln_in_w, *ln_in_b, *ln_out_w, *ln_out_b;
@@ -414,10 +417,18 @@ struct OutArgs {
   unsigned int* status;
 };
 
+// W_g, W_z; two input stages (z tile + x tile) freed when their MMAs complete; one output stage
+// shared by the two warpgroups (items alternate, so it is handed over by the out_free barrier).
+// This fills the 227 KB limit: the launch asks for all of it, and the kernel checks that the
+// 1 KB-aligned layout fits in what it got (the dynamic region starts 1 KB-aligned after the
+// block's reserved shared memory; if it did not, the kernel reports and returns).
 constexpr uint32_t O_WG = 0, O_WZ = 32768, O_STAGE = 65536, O_STAGE_BYTES = 65536;
-constexpr uint32_t O_LN = O_STAGE + 2 * O_STAGE_BYTES;  // 4 x 128 fp32 LayerNorm parameters
+constexpr uint32_t O_OUT = O_STAGE + 2 * O_STAGE_BYTES;
+constexpr uint32_t O_LN = O_OUT + 32768;  // 4 x 128 fp32 LayerNorm parameters
 constexpr uint32_t O_BAR = O_LN + 2048;
 constexpr uint32_t OUT_SMEM = O_BAR + 256;
+constexpr uint32_t OUT_SMEM_ALLOC = 232448;
+static_assert(OUT_SMEM <= OUT_SMEM_ALLOC, "dynamic shared memory limit");
 
 __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ CUtensorMap tzg,
                                                        const __grid_constant__ CUtensorMap tx,
@@ -435,9 +446,14 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
   auto empty = [&](int w) { return bars + 24 + 8 * w; };
   auto ready = [&](int w) { return bars + 40 + 8 * w; };
   auto done = [&](int w) { return bars + 56 + 8 * w; };
+  const uint32_t out_free = bars + 80;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + O_BAR + 128);
   float* lnp = reinterpret_cast<float*>(g + O_LN);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if ((base - raw) + OUT_SMEM > OUT_SMEM_ALLOC) {  // uniform over the block: nothing was started
+    if (tid == 0) atomicOr(args.status, 4u);  // report-only bit: the layout did not fit
+    return;
+  }
 
   if (tid == 0) {
     mbar_init(wbar, 1);
@@ -448,6 +464,7 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
       mbar_init(done(w), 1);
     }
     mbar_init(bars + 72, 1);
+    mbar_init(out_free, 1);
     fence_barrier_init();
   }
   for (int c = tid; c < 128; c += blockDim.x) {
@@ -504,6 +521,7 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
         tile::umma_k128(tmem + w * 256 + 128, sZ, base + O_WG, 16384, idesc_f16(128, 128, true));
         tile::umma_k128(tmem + w * 256, sX, base + O_WZ, 16384, idesc_f16(128, 128, true));
         umma_commit(done(w));
+        umma_commit(empty(w));  // the stage is free once these MMAs have read it
       }
       umma_commit(bars + 72);  // drain: every MMA complete before TMEM is released
       mbar_wait_drain(bars + 72, 0);
@@ -516,7 +534,6 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
     const uint32_t lane_base = (uint32_t)(q * 32) << 16;
     uint8_t* zt = g + O_STAGE + wg * O_STAGE_BYTES;
     uint8_t* xt = zt + 32768;
-    const uint32_t st = base + O_STAGE + wg * O_STAGE_BYTES;
     for (int64_t k = wg;; k += 2) {
       const int64_t t = blockIdx.x + k * G;
       if (t >= args.n_tiles) break;
@@ -562,6 +579,8 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
       tc_fence_after();
 #pragma unroll
       for (int c = 8; c < 16; ++c) old[c] = rd ? __ldg(zp + c) : make_uint4(0, 0, 0, 0);
+      // the output stage: the previous item's TMA store (the other warpgroup's) has read it
+      if (k > 0) mbar_wait(out_free, (uint32_t)((k - 1) & 1), args.status);
 #pragma unroll
       for (int cc = 0; cc < CH; cc += 16) {
         uint32_t av[16], gv[16];
@@ -571,7 +590,7 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           const int chunk = (cc >> 3) + e;
-          uint4* dst = reinterpret_cast<uint4*>(zt + tile::chunk_off(row, chunk));
+          uint4* dst = reinterpret_cast<uint4*>(g + O_OUT + tile::chunk_off(row, chunk));
           float u[8];
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
@@ -591,11 +610,11 @@ __global__ void __launch_bounds__(320, 1) k_trimul_out(const __grid_constant__ C
       fence_proxy_async_smem();
       named_bar_sync(1 + wg, 128);
       if (leader) {
-        tma_store_3d(&tzo, st, 0, j0, i);
-        tma_store_3d(&tzo, st + 16384, 64, j0, i);
+        tma_store_3d(&tzo, base + O_OUT, 0, j0, i);
+        tma_store_3d(&tzo, base + O_OUT + 16384, 64, j0, i);
         bulk_commit_group();
         bulk_wait_group_read0();
-        mbar_arrive(empty(wg));
+        mbar_arrive(out_free);
       }
     }
     if (leader) bulk_wait_group0();
@@ -667,7 +686,7 @@ int ensure_attrs() {
   return once_per_device(done, []() -> int {
     PF_TRY(set_smem(k_trimul_proj, PROJ_SMEM + 1024));
     PF_TRY(set_smem(k_trimul_bgemm, GEMM_SMEM + 1024));
-    PF_TRY(set_smem(k_trimul_out, OUT_SMEM + 1024));
+    PF_TRY(set_smem(k_trimul_out, OUT_SMEM_ALLOC));
     return PF_OK;
   });
 }
@@ -756,7 +775,7 @@ int launch_contract_out(const pf_trimul_params* p, const __nv_bfloat16* a, int64
     const bool resid_apart = acc && (zo.ptr != zg.ptr || zo.row_stride != zg.row_stride);
     const double bytes = 2.0 * (double)n_i * n_j * (CH + CH + (resid_apart ? CH : 0) + CH);
     PF_LAUNCH_SCOPE_WORK(st, "k_trimul_out", bytes, 'b');
-    k_trimul_out<<<(unsigned)grid_o, 320, OUT_SMEM + 1024, st>>>(tzg, txm, tzo, twz, twg, oa);
+    k_trimul_out<<<(unsigned)grid_o, 320, OUT_SMEM_ALLOC, st>>>(tzg, txm, tzo, twz, twg, oa);
   }
   PF_CHECK_LAUNCH();
   return PF_OK;

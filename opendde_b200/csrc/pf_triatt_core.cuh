@@ -5,11 +5,12 @@
 // walks items w = blockIdx.x, blockIdx.x + gridDim.x, ... and a key-tile "step" stream runs
 // through a 3-stage TMA ring continuously across items. The two rows of an item share the
 // triangle-bias tile (bias[h][j][k] does not depend on i).
-// Warp roles (320 threads):
+// Warp roles (352 threads):
 //   warps 0-3  softmax for row A (thread = query; TMEM lanes 0..127)
 //   warps 4-7  softmax for row B
 //   warp 8     TMA producer: per step the bias tile, K, V^T and key-mask rows of both rows
-//   warp 9     MMA issuer (single thread) and TMEM owner
+//   warp 9     S issuer (one thread) and TMEM owner
+//   warp 10    P.V issuer (one thread)
 // TMEM (per row R, base 256*R): S [0,128) f16 accumulator (one value per column), P [128,192)
 // (f16, two per column), [O | l] [192,240) fp32, Q [240,256) (f16, two per column).
 //   S = Q K^T           A = Q (TMEM), B = K tile (smem, 64B swizzle), f16 x f16 -> f16
@@ -42,7 +43,7 @@ struct CoreArgs {
 #ifndef PF_CORE_FMA_PAIRS
 #define PF_CORE_FMA_PAIRS 4
 #endif
-constexpr int CORE_THREADS = 320;
+constexpr int CORE_THREADS = 352;
 constexpr int CORE_STAGES = 3;
 // per-stage layout (bytes from the stage base)
 constexpr uint32_t CS_KA = 0;                  // 128 x 64 B (SW64) f16
@@ -207,7 +208,7 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       mbar_init(bars + 96 + 8 * r, 4);    // S read / Q written
       mbar_init(bars + 112 + 8 * r, 4);   // O/L read out, free for the next item
     }
-    mbar_init(bars + 128, 1);             // drain
+    mbar_init(bars + 128, 2);             // drain (one commit per MMA issuer)
     fence_barrier_init();
   }
   if (warp == 9) {
@@ -260,9 +261,14 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         }
       }
     }
-  } else if (warp == 9) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == 9 || warp == 10) {
+    // ------------------------------------------------------------ MMA issuers
+    // warp 9 issues every S = Q K^T, warp 10 every [O | l] += P [V^T; 1]^T; both walk the same
+    // step sequence. With S and P.V in separate threads, a row's next S waits only for that
+    // row's softmax to read the current S, never for the other row's P (the rows stay
+    // decoupled without polling).
     if (lane == 0) {
+      const bool s_issuer = warp == 9;
       constexpr uint32_t id_s = idesc_f16_f16acc(128, 128);               // f16 x f16 -> f16
       constexpr uint32_t id_o = idesc_f16(128, 48, false);                // f16 x f16 -> fp32
       uint32_t ns[2] = {0, 0};   // S issued per row (sfree phases)
@@ -292,9 +298,11 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
       if (w < a.n_items) {
         it = decode_item<NH>(a, w);
         kt = next_tile(it.fa, it.fb, 0, n_tiles);
-        ok = mbar_wait(bar_full0, 0, a.status);
-        tc_fence_after();
-        for (int r = 0; r < (it.has_b ? 2 : 1) && ok; ++r) issue_s(r, 0);
+        if (s_issuer) {
+          ok = mbar_wait(bar_full0, 0, a.status);
+          tc_fence_after();
+          for (int r = 0; r < (it.has_b ? 2 : 1) && ok; ++r) issue_s(r, 0);
+        }
       }
       bool first = true;
       while (w < a.n_items && ok) {
@@ -314,38 +322,43 @@ __global__ void __launch_bounds__(CORE_THREADS, 1) k_triatt_core(const __grid_co
         }
         const bool more = w2 < a.n_items;
         const int nr = it.has_b ? 2 : 1;
-        // 1. S of the next step, for each row as soon as it has read this step's S
-        if (more) {
-          const uint32_t s2 = (step + 1) % CORE_STAGES;
-          ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
-          tc_fence_after();
-          for (int r = 0; r < (it2.has_b ? 2 : 1) && ok; ++r) issue_s(r, s2);
-        }
-        // 2. P.V of this step, for each row once its P is written
-        for (int r = 0; r < nr && ok; ++r) {
-          const uint32_t tb_r = tmem + 256u * r;
-          ok = mbar_wait(bars + 64 + 8 * r, np[r] & 1, a.status);
-          if (first && ni[r] > 0) ok = ok && mbar_wait(bars + 112 + 8 * r, (ni[r] - 1) & 1, a.status);
-          tc_fence_after();
-          const uint64_t dv = dV0 + s * kStageD + (r ? kRowVD : 0);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            // key step kk: atom kk/4 (6 KB apart), 32 B into the 128 B swizzle row per step
-            const uint64_t d = dv + (uint64_t)((kk >> 2) * (CS_VT_ATOM >> 4) + (kk & 3) * 2);
-            umma_f16_ts(tb_r + T_O, tb_r + T_P + kk * 8, d, id_o, (!first || kk > 0) ? 1u : 0u);
+        if (s_issuer) {
+          // S of the next step, for each row as soon as it has read this step's S
+          if (more) {
+            const uint32_t s2 = (step + 1) % CORE_STAGES;
+            ok = ok && mbar_wait(bar_full0 + 8 * s2, ((step + 1) / CORE_STAGES) & 1, a.status);
+            tc_fence_after();
+            for (int r = 0; r < (it2.has_b ? 2 : 1) && ok; ++r) issue_s(r, s2);
           }
-          umma_commit(bars + 80 + 8 * r);
-          np[r] += 1;
-          if (first) ni[r] += 1;
+        } else {
+          // P.V of this step, for each row once its P is written
+          for (int r = 0; r < nr && ok; ++r) {
+            const uint32_t tb_r = tmem + 256u * r;
+            ok = mbar_wait(bars + 64 + 8 * r, np[r] & 1, a.status);
+            if (first && ni[r] > 0) ok = ok && mbar_wait(bars + 112 + 8 * r, (ni[r] - 1) & 1, a.status);
+            tc_fence_after();
+            const uint64_t dv = dV0 + s * kStageD + (r ? kRowVD : 0);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              // key step kk: atom kk/4 (6 KB apart), 32 B into the 128 B swizzle row per step
+              const uint64_t d = dv + (uint64_t)((kk >> 2) * (CS_VT_ATOM >> 4) + (kk & 3) * 2);
+              umma_f16_ts(tb_r + T_O, tb_r + T_P + kk * 8, d, id_o, (!first || kk > 0) ? 1u : 0u);
+            }
+            umma_commit(bars + 80 + 8 * r);
+            np[r] += 1;
+            if (first) ni[r] += 1;
+          }
+          // the stage's K tiles were read by this step's S (done: the softmax read S before
+          // writing P) and its V tiles by these P.V MMAs
+          umma_commit(bar_empty0 + 8 * s);
         }
-        umma_commit(bar_empty0 + 8 * s);
         w = w2;
         it = it2;
         kt = kt2;
         first = first2;
         ++step;
       }
-      umma_commit(bars + 128);  // drain: every MMA complete before TMEM is released
+      umma_commit(bars + 128);  // drain (count 2): every MMA of both issuers complete
       mbar_wait_drain(bars + 128, 0);
     }
   } else {

@@ -5,6 +5,7 @@ from .config import FOLDCP_ENVIRONMENT_KEYS, FOLDCP_MESH_KEY, FoldCPConfig, appl
 from .layout import FoldCP2DLayout
 from .mesh import FoldCPProcessMesh, clear_mesh_cache
 from .opm import outer_product_mean_local_update
+from .trunk_init import apply_trunk_z_cycle_local, build_trunk_z_init_local
 from .pair_sharding import (
     FoldCPPairShardSpec,
     gather_pair_tensor,
@@ -35,5 +36,6 @@ __all__ = [
     "distributed_attention_pair_bias_update", "distributed_pair_transition_update",
     "distributed_pairformer_block_pair_update", "distributed_pairformer_stack_pair_update",
     "distributed_pairformer_stack_single_bridge_update", "distributed_triangle_attention_update",
-    "distributed_triangle_multiplication_update", "outer_product_mean_local_update",
+    "distributed_triangle_multiplication_update", "outer_product_mean_local_update", "build_trunk_z_init_local",
+    "apply_trunk_z_cycle_local",
 ]

@@ -209,10 +209,24 @@ def windows_for(mesh, slot_bytes: int, device: torch.device) -> PeerWindows:
     return w
 
 
+COPY_KEY = "OPENDDE_B200_FOLDCP_COPY"
+
+
+def copy_engine() -> str:
+    """Who moves the band bytes: ``"sm"`` (the pf_copy_regions kernel, default) or ``"dma"``
+    (the GPU's copy engines, pf_copy_regions_dma: no SMs, so a side-stream band copy runs beside
+    the persistent kernels)."""
+    v = os.environ.get(COPY_KEY, "sm").strip().lower() or "sm"
+    if v not in ("sm", "dma"):
+        raise ValueError(f"{COPY_KEY} must be 'sm' or 'dma', got {v!r}")
+    return v
+
+
 def peer_copy_gbs(mesh, device: torch.device, reps: int = 5) -> float:
-    """Bandwidth of the band copies' transport, measured with the band-copy kernel itself: every
-    rank at once loads one whole slot of the next rank's window into local memory
-    (``pf_copy_regions``, 4 KB rows) ``reps`` times; returns this rank's GB/s of peer reads.
+    """Bandwidth of the band copies' transport, measured with the band copy itself (the kernel,
+    or the copy engines under ``OPENDDE_B200_FOLDCP_COPY=dma``): every rank at once copies one
+    whole slot of the next rank's window into local memory (4 KB rows) ``reps`` times; returns
+    this rank's GB/s of peer reads.
     Collective over the mesh's CP group (its windows must exist: run one op first)."""
     w = _WINDOWS.get(_window_key(mesh))
     if w is None or w.numel < 2:
@@ -222,13 +236,14 @@ def peer_copy_gbs(mesh, device: torch.device, reps: int = 5) -> float:
     rows = w.slot_bytes // row
     dst = torch.empty(rows * row, dtype=torch.uint8, device=device)
     plan = [(src, dst.data_ptr(), 1, rows, row, row, row, 0, 0)]
-    kernels.copy_regions(plan)                      # warm
+    dma = copy_engine() == "dma"
+    kernels.copy_regions(plan, dma=dma)             # warm
     torch.cuda.synchronize(device)
     dist.barrier(group=w.group)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(reps):
-        kernels.copy_regions(plan)
+        kernels.copy_regions(plan, dma=dma)
     e1.record()
     torch.cuda.synchronize(device)
     dist.barrier(group=w.group)
@@ -251,8 +266,9 @@ class PeerExchange(DistExchange):
         self._windows_fn = windows_fn
 
     def _copy(self, plan: List[CopyRegion]) -> None:
-        """Execute a copy plan (one pf_copy_regions launch per 32 boxes on the current stream)."""
-        kernels.copy_regions(plan)
+        """Execute a copy plan on the current stream: by the band-copy kernel (one launch per 32
+        boxes), or by the copy engines when ``OPENDDE_B200_FOLDCP_COPY=dma``."""
+        kernels.copy_regions(plan, dma=copy_engine() == "dma")
         is_remote = getattr(getattr(self, "_w", None), "is_remote", None)
         for r in plan:
             n = r[2] * r[3] * r[4]

@@ -211,6 +211,43 @@ def opm(pack: WeightPack, m: torch.Tensor, mask: Optional[torch.Tensor], z_out: 
                                  code, ws.data_ptr(), ws.numel(), stream_ptr()))
 
 
+def trunk_init(pack: WeightPack, s_init: torch.Tensor, ids, token_bonds: Optional[torch.Tensor],
+               z_out: torch.Tensor, row0: int, col0: int, r_max: int, s_max: int) -> None:
+    """z_out [R, C, c_z] = the trunk's pair input on rows [row0, row0 + R) x cols [col0, col0 + C)
+    (see pf_trunk_init_fwd). ``ids``: int32 CUDA tensors asym_id, residue_index, entity_id,
+    token_index, sym_id (in that order)."""
+    require_cuda(s_init, z_out, token_bonds, *ids)
+    code = dtype_code(s_init)
+    if z_out.dtype != s_init.dtype or s_init.stride(-1) != 1:
+        raise TypeError("s_init (contiguous channels) and the pair output must share the storage dtype")
+    n_token, c_s = s_init.shape
+    n_rows, n_cols, c_z = z_out.shape
+    nbytes = _abi.workspace_bytes("pf_trunk_init_workspace_size", n_rows, n_cols, c_s, c_z, r_max, s_max, code)
+    ws = workspace(nbytes, s_init.device)
+    tid = _abi.TokenIds(*[t.data_ptr() for t in ids])
+    check(_abi.load().pf_trunk_init_fwd(ctypes.byref(pack.struct), s_init.data_ptr(), s_init.stride(0), tid,
+                                        mask_view(token_bonds), pair_view(z_out), n_token, row0, n_rows, col0,
+                                        n_cols, c_s, c_z, r_max, s_max, code, ws.data_ptr(), ws.numel(),
+                                        stream_ptr()))
+
+
+def pair_ln_linear(pack: WeightPack, z_in: torch.Tensor, z_out: torch.Tensor, accumulate: bool) -> None:
+    """z_out (+)= W LN(z_in) over the positions of two pair views (see pf_pair_ln_linear_fwd)."""
+    require_cuda(z_in, z_out)
+    code = dtype_code(z_in)
+    if z_out.dtype != z_in.dtype:
+        raise TypeError("pair views must share the dtype")
+    n_rows, n_cols, c_in = z_in.shape
+    c_out = z_out.shape[2]
+    if z_out.shape[:2] != (n_rows, n_cols):
+        raise ValueError("pair views must cover the same positions")
+    nbytes = _abi.workspace_bytes("pf_pair_ln_linear_workspace_size", n_rows, n_cols, c_in, c_out, code)
+    ws = workspace(nbytes, z_in.device)
+    check(_abi.load().pf_pair_ln_linear_fwd(ctypes.byref(pack.struct), pair_view(z_in), pair_view(z_out), n_rows,
+                                            n_cols, c_in, c_out, int(accumulate), code, ws.data_ptr(), ws.numel(),
+                                            stream_ptr()))
+
+
 def apb(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, z: Optional[torch.Tensor],
         bias: Optional[torch.Tensor], heads: int, accumulate: bool) -> None:
     """s_out (+)= AttentionPairBias(s_in, z) (bias from z when ``bias`` is None)."""
@@ -250,11 +287,16 @@ def apb_rows(pack: WeightPack, s_in: torch.Tensor, s_out: torch.Tensor, bias: to
                                       heads, int(accumulate), code, ws.data_ptr(), ws.numel(), stream_ptr()))
 
 
-def copy_regions(regions) -> None:
+def copy_regions(regions, dma: bool = False) -> None:
     """Copy byte boxes ``(src_ptr, dst_ptr, planes, rows, row_bytes, src_pitch, dst_pitch,
-    src_plane_pitch, dst_plane_pitch)`` on the current stream, one kernel launch per
-    PF_MAX_COPY_REGIONS boxes (sources may be peers' windows)."""
+    src_plane_pitch, dst_plane_pitch)`` on the current stream (sources may be peers' windows):
+    by a kernel, one launch per PF_MAX_COPY_REGIONS boxes, or (``dma``) by the copy engines."""
     lib = _abi.load()
+    if dma:
+        if regions:
+            arr = (_abi.CopyRegion * len(regions))(*[_abi.CopyRegion(*r) for r in regions])
+            check(lib.pf_copy_regions_dma(arr, len(regions), stream_ptr()))
+        return
     step = _abi.PF_MAX_COPY_REGIONS
     for i in range(0, len(regions), step):
         chunk = regions[i:i + step]

@@ -82,11 +82,14 @@ def test_cp_fp32_matches_oracle(shape, transport, cuda_device):
         assert max_abs(s2, s_ref) <= 1e-4
 
 
+@pytest.mark.parametrize("dma", [False, True])
 @pytest.mark.parametrize("unit", [16, 8, 4, 1])
-def test_copy_regions_every_vector_width(unit, cuda_device):
-    """pf_copy_regions moves 2D rectangles at the widest common alignment (16/8/4/1 bytes)."""
+def test_copy_regions_every_vector_width(unit, dma, cuda_device):
+    """pf_copy_regions moves 2D rectangles at the widest common alignment (16/8/4/1 bytes);
+    pf_copy_regions_dma moves the same boxes by the copy engines (one 2-D copy for evenly spaced
+    planes, a 3-D copy for plane pitches that are whole numbers of rows, else a copy per plane)."""
     from opendde_b200 import kernels
-    size = 4 << 20
+    size = 8 << 20
     g = torch.Generator().manual_seed(7)
     src = torch.randint(0, 255, (size,), generator=g, dtype=torch.uint8).to(cuda_device)
     dst = torch.zeros_like(src)
@@ -95,7 +98,9 @@ def test_copy_regions_every_vector_width(unit, cuda_device):
     boxes = [(u, 1, 100, 37 * u, 103 * u, 70 * u, 0, 0),
              (64 * u, 1, 3, 4097 * u, 4099 * u, 4098 * u, 0, 0),
              (2 * u, 1, 1, 25000 * u, 25000 * u, 25000 * u, 0, 0),
-             (3 * u, 5, 7, 11 * u, 13 * u, 12 * u, 97 * u, 89 * u)]
+             (3 * u, 5, 7, 11 * u, 13 * u, 12 * u, 97 * u, 89 * u),
+             (5 * u, 3, 4, 10 * u, 12 * u, 16 * u, 72 * u, 80 * u),     # plane pitches: whole rows
+             (7 * u, 2, 3, 8 * u, 9 * u, 10 * u, 27 * u, 30 * u)]        # planes evenly spaced
     regions, want = [], dst.clone()
     for i, (off, planes, rows, row_bytes, sp, dp, spp, dpp) in enumerate(boxes):
         s_off, d_off = off, off + (1 << 20) * i
@@ -106,6 +111,27 @@ def test_copy_regions_every_vector_width(unit, cuda_device):
             for r in range(rows):
                 so, do = s_off + c * spp + r * sp, d_off + c * dpp + r * dp
                 want[do:do + row_bytes] = src[so:so + row_bytes]
-    kernels.copy_regions(regions)
+    kernels.copy_regions(regions, dma=dma)
     torch.cuda.synchronize()
     assert torch.equal(dst, want)
+
+
+@pytest.mark.parametrize("overlap", ["0", "2"])
+def test_cp_bf16_copy_engine_transport(overlap, cuda_device, monkeypatch):
+    """The peer transport with the bands moved by the copy engines (and, overlap 2, the attention
+    band in two chunks on the side stream) matches the single-device stack."""
+    monkeypatch.setenv("OPENDDE_B200_FOLDCP_COPY", "dma")
+    monkeypatch.setenv("OPENDDE_B200_FOLDCP_OVERLAP", overlap)
+    n = 300
+    stack, _ = _stack(1, cuda_device)
+    g = torch.Generator().manual_seed(1)
+    z = torch.randn((n, n, 128), generator=g).to(cuda_device, torch.bfloat16)
+    s = torch.randn((n, 384), generator=g).to(cuda_device, torch.bfloat16)
+    mask = ragged_pair_mask(n, seed=3, drop=0.2, full_rows=[5]).to(cuda_device)
+    with torch.no_grad():
+        s1, z1 = stack(s, z, mask)
+    outs = _cp((2, 4), stack, s, z, mask, "peer")
+    assert _abi.device_status(clear=True) == 0
+    for s2, z2 in outs:
+        assert rel_l2(z2, z1) <= 5e-3
+        assert rel_l2(s2, s1) <= 5e-3

@@ -68,3 +68,27 @@ def test_outer_product_mean_parameter_names_match_reference():
     assert tuple(mod.linear_out.weight.shape) == (int(rec["c_z"]), int(rec["c_hidden"]) ** 2)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         mod(torch.zeros(3, 5, int(rec["c_m"])))
+
+
+def test_trunk_init_module_api():
+    """RelativePositionEncoding keeps the reference's parameter name and shape; the lazy (id)
+    features are the only input form; CPU tensors are rejected (no CPU fallback)."""
+    from opendde_b200.model import RelativePositionEncoding, trunk_pair_init
+    from opendde_b200.model.primitives import LinearNoBias
+    rec = np.load(f"{GOLDEN_DIR}/trunk/trunk_init_n23.npz")
+    relpe = RelativePositionEncoding(r_max=int(rec["r_max"]), s_max=int(rec["s_max"]), c_z=int(rec["c_z"]))
+    assert [n for n, _ in relpe.named_parameters()] == ["linear_no_bias.weight"]
+    i = list(rec["param_names"]).index("relative_position_encoding.linear_no_bias.weight")
+    assert relpe.linear_no_bias.weight.shape[1] == 4 * int(rec["r_max"]) + 2 * int(rec["s_max"]) + 7
+    n, c_s, c_z = 5, int(rec["c_s"]), int(rec["c_z"])
+    d = {"asym_id": torch.zeros(n, dtype=torch.long), "residue_index": torch.arange(n),
+         "entity_id": torch.zeros(n, dtype=torch.long), "token_index": torch.arange(n),
+         "sym_id": torch.zeros(n, dtype=torch.long)}
+    feats = relpe.generate_relp(d)["relp"]
+    assert feats.shape == (n, n, relpe.linear_no_bias.weight.shape[1]) and i >= 0
+    z1, z2, bond = LinearNoBias(c_s, c_z), LinearNoBias(c_s, c_z), LinearNoBias(1, c_z)
+    with pytest.raises(RuntimeError, match="no CPU fallback"):
+        trunk_pair_init(torch.zeros(n, c_s), z1, z2, relpe, bond, feats, None)
+    with pytest.raises(TypeError, match="lazy"):
+        from opendde_b200.model.trunk_init import _relp_features
+        _relp_features(torch.zeros(n, n, 23))
