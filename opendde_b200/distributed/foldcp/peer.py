@@ -394,6 +394,56 @@ class PeerExchange(DistExchange):
         _, side = _projection_side_bytes(spec, planes, elem)
         return max(local.numel() * elem, 2 * side)
 
+    def trimul_chunks(self, local: torch.Tensor, spec: FoldCPPairShardSpec, transposed: bool, c_h: int,
+                      project: Callable[[int, int, int], None], parts: Sequence[Range], rows_b: Range,
+                      consume: Callable[[int, torch.Tensor, torch.Tensor, int], None]) -> None:
+        """trimul_bands with the a band requested as consecutive row chunks ``parts``, overlapped:
+        after the projections and the barrier, a side stream copies the b band and then chunk
+        after chunk of a, while ``consume(i, a_i, b, Np)`` enqueues chunk i's contraction and
+        epilogue on the current stream behind chunk i's copy. All buffers are allocated before
+        the side stream forks."""
+        elem = local.element_size()
+        ld_t, side = _projection_side_bytes(spec, c_h, elem)
+        w = self._windows_fn(self.mesh, self._slot_need(local, spec, c_h), local.device)
+        self._w = w
+        slot = w.slot
+        w.slot ^= 1
+        ptrs = w.slot_ptrs(slot)
+        me = self.mesh.cp_rank
+        project(ptrs[me], ptrs[me] + side, ld_t)
+        w.barrier()
+        n_pad = spec.n_padded
+        ld_b = _round8(n_pad)
+        b = local.new_empty((c_h, rows_b[1] - rows_b[0], ld_b))
+        outs = [local.new_empty((c_h, hi - lo, ld_b)) for lo, hi in parts]
+        plans = [projection_copy_plan(spec, self.layout, rows_b, transposed, ptrs, side, c_h, elem, ld_t,
+                                      b.data_ptr(), ld_b)]
+        plans[0] += projection_copy_plan(spec, self.layout, parts[0], transposed, ptrs, 0, c_h, elem, ld_t,
+                                         outs[0].data_ptr(), ld_b)
+        for (lo, hi), out in zip(parts[1:], outs[1:]):
+            plans.append(projection_copy_plan(spec, self.layout, (lo, hi), transposed, ptrs, 0, c_h, elem, ld_t,
+                                              out.data_ptr(), ld_b))
+        if local.is_cuda:
+            main = torch.cuda.current_stream(local.device)
+            side_st = self._side_stream(local.device)
+            side_st.wait_stream(main)
+            done = []
+            with torch.cuda.stream(side_st):
+                for plan in plans:
+                    if plan:
+                        self._copy(plan)
+                    ev = torch.cuda.Event()
+                    ev.record(side_st)
+                    done.append(ev)
+            for i, out in enumerate(outs):
+                main.wait_event(done[i])
+                consume(i, out, b, n_pad)
+            return
+        for i, (plan, out) in enumerate(zip(plans, outs)):
+            if plan:
+                self._copy(plan)
+            consume(i, out, b, n_pad)
+
     def trimul_bands(self, local: torch.Tensor, spec: FoldCPPairShardSpec, transposed: bool, c_h: int,
                      project: Callable[[int, int, int], None], rows_a: Range, rows_b: Range):
         """The triangle-update operand bands from the peers' projections.

@@ -176,8 +176,10 @@ OVERLAP_KEY = "OPENDDE_B200_FOLDCP_OVERLAP"
 
 
 def overlap_chunks() -> int:
-    """Row chunks of the overlapped attention band exchange (``OPENDDE_B200_FOLDCP_OVERLAP``;
-    0 or 1: one band per op, the default)."""
+    """Row chunks of the overlapped band exchanges of triangle attention and the triangle update
+    (``OPENDDE_B200_FOLDCP_OVERLAP``; 0 or 1: one band per op, the default). The overlap is real
+    with the copy-engine transport (``OPENDDE_B200_FOLDCP_COPY=dma``); band-copy kernels wait
+    for the persistent kernels' SMs."""
     v = os.environ.get(OVERLAP_KEY, "").strip()
     if not v:
         return 0
@@ -204,6 +206,22 @@ def _trimul(module, z_local, ctx: FoldCPPairContext, ops) -> None:
         # on x = z^T: a(i, k) = a(z(k, i)), so the tile is projected through a transposed view.
         mt = m[r0:r1, c0:c1]
         zt, mt = (z_local, mt) if module._outgoing else (z_local.transpose(0, 1), mt.t())
+        chunks = overlap_chunks()
+        if chunks > 1 and hasattr(ex, "trimul_chunks"):
+            # the a band (output rows) in chunks: chunk i's copy on a side stream overlaps the
+            # contraction and epilogue of chunk i-1 (every output row needs the whole b band)
+            step = -(-(r1 - r0) // chunks)
+            parts = [(a_, min(a_ + step, r1)) for a_ in range(r0, r1, step)]
+
+            def consume(i, a_i, b_full, n_k):
+                lo, hi = parts[i]
+                rows = z_local[lo - r0:hi - r0]
+                ops.trimul_combine(module, a_i, b_full, n_k, rows, rows)
+
+            ex.trimul_chunks(z_local, spec, transposed=not module._outgoing, c_h=module.c_hidden,
+                             project=lambda pa, pb, ld: ops.trimul_project(module, zt, mt, pa, pb, ld),
+                             parts=parts, rows_b=(c0, c1), consume=consume)
+            return
         a, b, n_k = ex.trimul_bands(
             z_local, spec, transposed=not module._outgoing, c_h=module.c_hidden,
             project=lambda pa, pb, ld: ops.trimul_project(module, zt, mt, pa, pb, ld),

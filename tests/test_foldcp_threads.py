@@ -113,8 +113,9 @@ def test_cp_single_ops_reference_return_convention(shape):
 @pytest.mark.parametrize("shape", [(1, 2), (2, 2), (2, 4)])
 @pytest.mark.parametrize("chunks", [2, 3])
 def test_cp_stack_overlapped_attention_chunks(shape, chunks, monkeypatch):
-    """The chunked attention band exchange (side-stream overlap on GPUs) computes the same
-    stack: every chunk of attention rows gets its own band and the shared bias rows."""
+    """The chunked band exchanges (side-stream overlap on GPUs) compute the same stack: every
+    chunk of attention rows gets its own band and the shared bias rows, and every chunk of the
+    triangle update's output rows its own a band next to the whole b band."""
     monkeypatch.setenv("OPENDDE_B200_FOLDCP_OVERLAP", str(chunks))
     torch.manual_seed(0)
     stack, p = _stack(1)
