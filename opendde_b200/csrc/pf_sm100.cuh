@@ -146,6 +146,11 @@ __device__ __forceinline__ void bulk_wait_group_read0() {
 }
 // Wait until the committed bulk stores are complete.
 __device__ __forceinline__ void bulk_wait_group0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Bring one 128-byte line into L2 ahead of its use (no register result, nothing to wait for).
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"((uint64_t)p));
+}
+
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"((uint64_t)map) : "memory");
 }

@@ -286,6 +286,27 @@ __device__ __forceinline__ uint4 pack8_f16(const float* f) {
   return make_uint4(pack_f16(f[0], f[1]), pack_f16(f[2], f[3]), pack_f16(f[4], f[5]), pack_f16(f[6], f[7]));
 }
 
+// Lines the epilogue of a tile will read (the residual row and the gate row of E_RESID), sent to
+// L2 before the tile's accumulator is ready. With one thread per position and every thread
+// reading its own row, the reads otherwise reach DRAM with only a few 16-byte loads in flight
+// per SM: the accumulating epilogue ran 20x slower than the storing one (6.7 vs 0.32 ms for
+// 2.36M rows of 128 channels).
+template <int E>
+__device__ __forceinline__ void row_prefetch(const RowArgs& a, bool valid, int64_t p, int64_t r, int64_t c, int n0) {
+  if constexpr (E == E_RESID) {
+    if (!valid || n0 >= a.n_out) return;
+    const int bytes = (a.n_out - n0 < a.bn ? a.n_out - n0 : a.bn) * 2;
+    if (a.accumulate) {
+      const char* o = reinterpret_cast<const char*>(a.out + r * a.rs + c * a.cs + n0);
+      for (int b = 0; b < bytes; b += 128) prefetch_l2(o + b);
+    }
+    if (a.gate) {
+      const char* g = reinterpret_cast<const char*>(a.gate + p * a.ldg + n0);
+      for (int b = 0; b < bytes; b += 128) prefetch_l2(g + b);
+    }
+  }
+}
+
 // Epilogue of one 128 x bn accumulator: thread = one position (TMEM lane), taddr = its lane's
 // address at column 0 of the accumulator. Every tcgen05.ld is executed by all 32 lanes.
 template <int E>
@@ -310,14 +331,27 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
     }
   } else if constexpr (E == E_STORE || E == E_RESID) {
     for (int cc = 0; cc < a.bn; cc += 32) {
-      uint32_t v[32];
-      tmem_ld32(taddr + cc, v);
-      tmem_ld_wait();
       const int n = n0 + cc;
-      if (!valid || n >= a.n_out) continue;
       // columns of this tile (bn is a multiple of 16, not of 32) that exist
       int cnt = a.n_out - n < 32 ? a.n_out - n : 32;
       if (a.bn - cc < cnt) cnt = a.bn - cc;
+      // E_RESID: the chunk's residual and gate vectors, all in flight before the TMEM load
+      uint4 oq[4], gq[4];
+      if constexpr (E == E_RESID) {
+        if (valid && cnt == 32) {
+          const uint4* o4 = reinterpret_cast<const uint4*>(a.out + r * a.rs + c * a.cs + n);
+          const uint4* g4 = a.gate ? reinterpret_cast<const uint4*>(a.gate + p * a.ldg + n) : nullptr;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            oq[e] = a.accumulate ? o4[e] : make_uint4(0u, 0u, 0u, 0u);
+            gq[e] = g4 ? g4[e] : make_uint4(0u, 0u, 0u, 0u);
+          }
+        }
+      }
+      uint32_t v[32];
+      tmem_ld32(taddr + cc, v);
+      tmem_ld_wait();
+      if (!valid || n >= a.n_out) continue;
       float f[32];
 #pragma unroll
       for (int e = 0; e < 32; ++e) f[e] = __uint_as_float(v[e]);
@@ -353,8 +387,7 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
 #pragma unroll
             for (int u = 0; u < 8; ++u) y[u] = f[8 * e + u];
             if (gp) {
-              const uint4 gq = reinterpret_cast<const uint4*>(gp)[e];
-              const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
+              const uint32_t gw[4] = {gq[e].x, gq[e].y, gq[e].z, gq[e].w};
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 y[2 * u] *= bf16lo(gw[u]);
@@ -362,8 +395,7 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
               }
             }
             if (a.accumulate) {
-              const uint4 oq = reinterpret_cast<const uint4*>(o)[e];
-              const uint32_t ow[4] = {oq.x, oq.y, oq.z, oq.w};
+              const uint32_t ow[4] = {oq[e].x, oq[e].y, oq[e].z, oq[e].w};
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 y[2 * u] += bf16lo(ow[u]);
@@ -599,8 +631,6 @@ __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUte
       const int64_t mt = t / a.n_tiles;
       const int n0 = (int)(t % a.n_tiles) * a.bn;
       const uint32_t b = j & 1;
-      mbar_wait(acc_full(b), (j >> 1) & 1, a.status);
-      tc_fence_after();
       bool valid;
       int64_t p, r, c;
       if constexpr (AM == A_OUTER) {
@@ -614,6 +644,9 @@ __global__ void __launch_bounds__(192, 1) k_rowgemm(const __grid_constant__ CUte
         r = valid ? p / a.e_cols : 0;
         c = valid ? p - r * a.e_cols : 0;
       }
+      row_prefetch<E>(a, valid, p, r, c, n0);  // overlaps the wait for this tile's MMAs
+      mbar_wait(acc_full(b), (j >> 1) & 1, a.status);
+      tc_fence_after();
       row_epilogue<E>(a, tmem + 256 * b + ((uint32_t)(q * 32) << 16), valid, p, r, c, n0);
       tc_fence_before();
       __syncwarp();
