@@ -398,6 +398,79 @@ def run_op_workload(args, kind):
     }), flush=True)
 
 
+# ------------------------------------------------------------------------------ heads
+def run_heads_workload(args):
+    """The pair work downstream of the stack at N = --n-token on the trunk's pair width, bf16, one
+    GPU: the distogram logits + contact probabilities (96 bins), the confidence head's pair input
+    and its pae / pde logits (64 bins each, fp32 out), and the diffusion pair conditioning
+    (c_z -> 128). ms per call through the module API (inputs resident) and every kernel's fraction
+    of the measured HBM (or bf16) peak from the library's per-launch work and CUDA-event times."""
+    from opendde_b200 import _abi
+    from opendde_b200.model import ConfidencePairHead, DiffusionPairConditioning, DistogramHead
+    from opendde_b200.model.trunk_init import LazyRelativePositionEncodingFeatures
+    from opendde_b200.utils import seeded_init_
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = load_peaks()
+    n, c_s_in = args.n, 449
+    g = torch.Generator().manual_seed(1)
+    z = torch.randn((n, n, C_Z), generator=g).to(dev, torch.bfloat16)
+    s_in = torch.randn((n, c_s_in), generator=g).to(dev, torch.bfloat16)
+    coords = (torch.randn((n, 3), generator=g) * 20.0).to(dev)
+    chains = torch.arange(n) * 4 // n
+    ids = [t.to(dev) for t in (chains, torch.arange(n) - chains * 300, chains % 2, torch.arange(n), chains // 2)]
+    relp = LazyRelativePositionEncodingFeatures(*ids, r_max=32, s_max=2)
+    dh, ch = DistogramHead(C_Z, 96), ConfidencePairHead(c_z=C_Z, c_s_inputs=c_s_in)
+    dc = DiffusionPairConditioning(C_Z, 128)
+    for i, m in enumerate((dh, ch, dc)):
+        seeded_init_(m, seed=i)
+        m.to(dev)
+    zp = torch.empty_like(z)
+    ops = [("distogram", lambda: dh.contact_probs(z, 2.25, 25.75, 96, 8.0)),
+           ("confidence_pair_input", lambda: ch.embed_pair_tile(s_in, coords, z, zp)),
+           ("confidence_pae_pde", lambda: ch.pair_logits(zp)),
+           ("diffusion_pair_cond", lambda: dc.prepare_cache(relp, z))]
+    rows = []
+    st = torch.cuda.current_stream()
+    with ClockSampler(0) as clk:
+        for name, fn in ops:
+            with torch.no_grad():
+                for _ in range(args.warmup):
+                    fn()
+                torch.cuda.synchronize()
+                _abi.profile_enable(True)
+                _abi.profile_report()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                for _ in range(args.steps):
+                    fn()
+                e1.record(st)
+                torch.cuda.synchronize()
+                _abi.profile_enable(False)
+                prof = _abi.profile_report()
+            ents = {}
+            for k, (launches, total, work, unit) in prof.items():
+                e = kernel_entry(k, launches, total, work, unit, peaks)
+                ents[k] = {"ms_per_call": total / args.steps, "launches_per_call": launches / args.steps,
+                           "bound": e and e["bound"], "achieved": e and e["achieved"], "frac": e and e["frac"],
+                           "unit": e and e["unit"]}
+            rows.append({"op": name, "ms_per_call": e0.elapsed_time(e1) / args.steps, "kernels": ents})
+    assert _abi.device_status() == 0, "a device-side bounded wait timed out"
+    value = sum(r["ms_per_call"] for r in rows)
+    dom = max(((k, v) for r in rows for k, v in r["kernels"].items()), key=lambda kv: kv[1]["ms_per_call"])
+    print(json.dumps({
+        "metric": "ms for the pair heads and the diffusion pair conditioning after the trunk, bf16",
+        "value": value, "unit": "ms", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": value, "higher_is_better": False, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic: z ~ N(0,1), s_inputs ~ N(0,1), coordinates ~ N(0, 20 A), four chains; seeded weights",
+        "config": {"workload": f"pair_heads_N{n}", "n_token": n, "c_z": C_Z, "distogram_bins": 96,
+                   "pae_pde_bins": 64, "c_z_pair_diffusion": 128,
+                   "l2": "inputs larger than L2 (pair tensor %d MB)" % (n * n * C_Z * 2 // 10**6)},
+        "dominant_kernel": {"kernel": dom[0], **dom[1]}, "ops": rows, "clocks": clk.summary(),
+    }), flush=True)
+
+
 # ------------------------------------------------------------------------------ main
 def main():
     ap = argparse.ArgumentParser()
@@ -405,9 +478,10 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=["trunk", "c1", "c2"], default="trunk",
+    ap.add_argument("--workload", choices=["trunk", "c1", "c2", "heads"], default="trunk",
                     help="trunk: the 48-block trunk (the headline); c1 / c2: standalone triangle attention / "
-                         "triangle multiplicative update at their configurations (1 GPU)")
+                         "triangle multiplicative update at their configurations (1 GPU); heads: the pair "
+                         "heads and the diffusion pair conditioning after the trunk (1 GPU)")
     # "--n-token" first: torchrun resolves abbreviated options even after the script name, and a
     # bare "--n" is ambiguous to it
     ap.add_argument("--n-token", "--n", dest="n", type=int, default=N_TOKEN)
@@ -430,7 +504,10 @@ def main():
     cores = os.cpu_count() or 1
     if args.workload != "trunk" and args.impl == "ours":
         if rank == 0:
-            run_op_workload(args, args.workload)
+            if args.workload == "heads":
+                run_heads_workload(args)
+            else:
+                run_op_workload(args, args.workload)
         return
 
     if args.impl == "reference":

@@ -347,6 +347,85 @@ PF_API int pf_pair_ln_linear_fwd(const pf_pair_linear_params* w, pf_pair_view z_
                                  int64_t n_cols, int32_t c_in, int32_t c_out, int32_t accumulate, int32_t dtype,
                                  void* workspace, size_t workspace_bytes, void* stream);
 
+/* ---- Pair heads and pair conditioning downstream of the stack ----------------------------
+ * pf_pair_head_fwd: per-position bin logits of a pair tile (n_rows x n_cols positions of c_z
+ * channels, n_bins outputs), in one of three forms:
+ *   PF_HEAD_PLAIN    logits = W LN(z) + b               ConfidenceHead pae (confidence.py:599-601)
+ *   PF_HEAD_SYM_IN   logits = W LN(z + z^T) + b         ConfidenceHead pde (confidence.py:602-606)
+ *   PF_HEAD_SYM_OUT  logits = (W z + b) + (W z^T + b)   DistogramHead.forward (head.py:33-46)
+ * zt is the view whose (r, s) element is z^T at the tile's position (r, s), i.e. z(col, row):
+ * the transposed view of the plane on one GPU, or the reciprocal rectangle (viewed transposed)
+ * under Fold-CP (distogram.py:22-50, foldcp/confidence.py:22-29); unused by PLAIN. ln_w / ln_b:
+ * the LayerNorm's affine parameters (PLAIN, SYM_IN; NULL = 1 / 0), unused by SYM_OUT; b NULL =
+ * no bias. logits is a pair view of n_bins (<= 256) channels stored as logits_dtype (PF_F32: the
+ * confidence heads' fp32 outputs; or the stack dtype). contact (optional, fp32 at
+ * contact + r*contact_rs + s*contact_cs) = the sum of softmax(logits) over the first contact_bins
+ * bins (the bins whose top <= thres, foldcp/distogram.py:159-166). bf16 on tcgen05 (LayerNorm /
+ * transposed-sum pass + row GEMM with the bias and the softmax in its epilogue); fp32 on the SIMT
+ * kernels. */
+enum { PF_HEAD_PLAIN = 0, PF_HEAD_SYM_IN = 1, PF_HEAD_SYM_OUT = 2 };
+typedef struct {
+  const float* ln_w; const float* ln_b;  /* [c_z] LayerNorm parameters, or NULL              */
+  const void* w;                         /* [n_bins, c_z]                                    */
+  const float* b;                        /* [n_bins] bias, or NULL                           */
+} pf_pair_head_params;
+
+PF_API int pf_pair_head_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t n_bins, int32_t dtype,
+                                       size_t* bytes);
+PF_API int pf_pair_head_fwd(const pf_pair_head_params* w, int32_t mode, pf_pair_view z, pf_pair_view zt,
+                            int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t n_bins, pf_pair_view logits,
+                            int32_t logits_dtype, float* contact, int64_t contact_rs, int64_t contact_cs,
+                            int32_t contact_bins, int32_t dtype, void* workspace, size_t workspace_bytes,
+                            void* stream);
+
+/* pf_confidence_pair_init_fwd: the ConfidenceHead's pair input on a tile, rows
+ * [row0, row0 + n_rows) x cols [col0, col0 + n_cols) of n_token:
+ *   z_out(i, j) = z_trunk(i, j) + W_s2 s_inputs(i) + W_s1 s_inputs(j)
+ *                 + W_d one_hot(d_ij) + W_d0 d_ij,  d_ij = |x_i - x_j|,
+ *   one_hot_b(d) = (d > lower_b) * (d < upper_b)
+ * (confidence.py:289-296, 540-572; the Fold-CP local form foldcp/confidence.py:81-148 and
+ * confidence.py:177-202). coords: fp32 [n_token][3] representative-atom positions; 1..64 distance
+ * bins. z_out may alias z_trunk. */
+typedef struct {
+  const void* w_s1; const void* w_s2;    /* [c_z, c_s_inputs] linear_no_bias_s1 / s2         */
+  const void* w_d;                       /* [c_z, n_dist_bins] linear_no_bias_d               */
+  const void* w_d0;                      /* [c_z, 1] linear_no_bias_d_wo_onehot               */
+  const float* lower_bins; const float* upper_bins;  /* [n_dist_bins]                         */
+} pf_confidence_init_params;
+
+PF_API int pf_confidence_pair_init_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_s_inputs, int32_t c_z,
+                                                  int32_t n_dist_bins, int32_t dtype, size_t* bytes);
+PF_API int pf_confidence_pair_init_fwd(const pf_confidence_init_params* w, const void* s_inputs, int64_t s_stride,
+                                       const float* coords, pf_pair_view z_trunk, pf_pair_view z_out, int64_t n_token,
+                                       int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols,
+                                       int32_t c_s_inputs, int32_t c_z, int32_t n_dist_bins, int32_t dtype,
+                                       void* workspace, size_t workspace_bytes, void* stream);
+
+/* pf_diffusion_pair_cond_fwd: the pair half of DiffusionConditioning on a tile (prepare_cache and
+ * _apply_pair_z_transitions, diffusion.py:828-847, 1019-1040; the Fold-CP local form
+ * prepare_cache_foldcp_local, :906-1017):
+ *   x    = c_z == c_zd ? z_trunk : W_zt LN_zt(z_trunk)        (layernorm_z_trunk has no offset)
+ *   pair = W_z LN_z([x | relpe(i, j)])                         (relpe from the token ids, as in
+ *                                                               pf_trunk_init_fwd; no offset)
+ *   pair += transition_z1(pair); pair += transition_z2(pair)   (n = 2)
+ * z_out: the tile of c_zd channels (16-byte aligned positions); it may alias z_trunk when
+ * c_z == c_zd (z_trunk is consumed before z_out is written). */
+typedef struct {
+  const float* ln_zt_w;                  /* [c_z]  layernorm_z_trunk.weight (c_z != c_zd)     */
+  const void* w_zt;                      /* [c_zd, c_z] linear_no_bias_z_trunk (c_z != c_zd)  */
+  const void* w_relp;                    /* [c_zd, 4 r_max + 2 s_max + 7] relpe.linear_no_bias */
+  const float* ln_z_w;                   /* [2 c_zd] layernorm_z.weight                        */
+  const void* w_z;                       /* [c_zd, 2 c_zd] linear_no_bias_z                    */
+  pf_transition_params t1, t2;           /* transition_z1 / transition_z2                      */
+} pf_diffusion_pair_params;
+
+PF_API int pf_diffusion_pair_cond_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t c_zd,
+                                                 int32_t r_max, int32_t s_max, int32_t dtype, size_t* bytes);
+PF_API int pf_diffusion_pair_cond_fwd(const pf_diffusion_pair_params* w, pf_pair_view z_trunk, pf_token_ids ids,
+                                      pf_pair_view z_out, int64_t n_token, int64_t row0, int64_t n_rows, int64_t col0,
+                                      int64_t n_cols, int32_t c_z, int32_t c_zd, int32_t r_max, int32_t s_max,
+                                      int32_t dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---- Fold-CP band exchange through peer memory ------------------------------------------
  * Replace the reference's ring / transpose band exchanges over NCCL send/receive
  * (opendde/distributed/foldcp/comm.py:26-184, used by real_pairformer.py:1226-1404 and

@@ -54,7 +54,13 @@ EXPORTED = (
     "pf_trunk_init_workspace_size", "pf_trunk_init_fwd", "pf_pair_ln_linear_workspace_size",
     "pf_pair_ln_linear_fwd",
     "pf_copy_regions_dma",
+    "pf_pair_head_workspace_size", "pf_pair_head_fwd",
+    "pf_confidence_pair_init_workspace_size", "pf_confidence_pair_init_fwd",
+    "pf_diffusion_pair_cond_workspace_size", "pf_diffusion_pair_cond_fwd",
 )
+
+# pf_pair_head_fwd forms (include/pairformer_b200.h)
+PF_HEAD_PLAIN, PF_HEAD_SYM_IN, PF_HEAD_SYM_OUT = 0, 1, 2
 
 
 class PFError(RuntimeError):
@@ -114,6 +120,19 @@ class TokenIds(Structure):
 
 class PairLinearParams(Structure):
     _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w")]
+
+
+class PairHeadParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_w", "ln_b", "w", "b")]
+
+
+class ConfidenceInitParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("w_s1", "w_s2", "w_d", "w_d0", "lower_bins", "upper_bins")]
+
+
+class DiffusionPairParams(Structure):
+    _fields_ = [(n, c_void_p) for n in ("ln_zt_w", "w_zt", "w_relp", "ln_z_w", "w_z")] + [
+        ("t1", TransitionParams), ("t2", TransitionParams)]
 
 
 _lib = None
@@ -189,6 +208,19 @@ def load(path: str = LIB_PATH):
         "pf_pair_ln_linear_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
         "pf_pair_ln_linear_fwd": ([POINTER(PairLinearParams), PairView, PairView, c_int64, c_int64, c_int32, c_int32,
                                    c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_pair_head_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_pair_head_fwd": ([POINTER(PairHeadParams), c_int32, PairView, PairView, c_int64, c_int64, c_int32, c_int32,
+                              PairView, c_int32, c_void_p, c_int64, c_int64, c_int32, c_int32, c_void_p, c_size_t,
+                              c_void_p], c_int),
+        "pf_confidence_pair_init_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
+        "pf_confidence_pair_init_fwd": ([POINTER(ConfidenceInitParams), c_void_p, c_int64, c_void_p, PairView,
+                                         PairView, c_int64, c_int64, c_int64, c_int64, c_int64, c_int32, c_int32,
+                                         c_int32, c_int32, c_void_p, c_size_t, c_void_p], c_int),
+        "pf_diffusion_pair_cond_workspace_size": ([c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32, sz],
+                                                  c_int),
+        "pf_diffusion_pair_cond_fwd": ([POINTER(DiffusionPairParams), PairView, TokenIds, PairView, c_int64, c_int64,
+                                        c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                        c_void_p, c_size_t, c_void_p], c_int),
         "pf_opm_workspace_size": ([c_int64, c_int64, c_int64, c_int64, c_int32, c_int32, c_int32, c_int32, sz], c_int),
         "pf_opm_fwd": ([POINTER(OpmParams), PairView, MaskView, PairView, c_int64, c_int64, c_int64, c_int64, c_int64,
                         c_int64, c_int32, c_int32, c_int32, c_float, c_int32, c_int32, c_void_p, c_size_t, c_void_p],

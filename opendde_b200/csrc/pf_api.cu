@@ -628,4 +628,144 @@ int pf_pair_ln_linear_fwd(const pf_pair_linear_params* w, pf_pair_view z_in, pf_
                               workspace_bytes, st);
 }
 
+// ------------------------------------------------------------------ pair heads and conditioning
+static bool pair_head_rows(int c_z, int n_bins, int dtype) {
+  return dtype == PF_BF16 && !force_simt() && tc::rows_pair_head_supported(c_z, n_bins);
+}
+
+int pf_pair_head_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t n_bins, int32_t dtype,
+                                size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || n_bins <= 0) return fail(PF_EINVAL_SHAPE, "pair head: bad sizes");
+  *bytes = pair_head_rows(c_z, n_bins, dtype) ? tc::rows_pair_head_ws_bytes(n_rows, n_cols, c_z)
+                                              : simt::pair_head_ws_bytes(n_rows, n_cols, c_z, n_bins);
+  return PF_OK;
+}
+
+int pf_pair_head_fwd(const pf_pair_head_params* w, int32_t mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows,
+                     int64_t n_cols, int32_t c_z, int32_t n_bins, pf_pair_view logits, int32_t logits_dtype,
+                     float* contact, int64_t contact_rs, int64_t contact_cs, int32_t contact_bins, int32_t dtype,
+                     void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  PF_TRY(check_dtype(logits_dtype));
+  if (mode != PF_HEAD_PLAIN && mode != PF_HEAD_SYM_IN && mode != PF_HEAD_SYM_OUT)
+    return fail(PF_EINVAL_ARG, "pair head: unknown mode %d", mode);
+  if (!w || !w->w) return fail(PF_EINVAL_ARG, "pair head: null weight pointer");
+  if (!view_ok(z) || !view_ok(logits) || (mode != PF_HEAD_PLAIN && !view_ok(zt)))
+    return fail(PF_EINVAL_ARG, "pair head: bad view");
+  if (dtype == PF_F32 && logits_dtype != PF_F32) return fail(PF_EINVAL_DTYPE, "pair head: fp32 input needs fp32 logits");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_z > 1024 || n_bins <= 0 || n_bins > 256)
+    return fail(PF_EINVAL_SHAPE, "pair head: bad sizes c_z=%d n_bins=%d (1..256 bins)", c_z, n_bins);
+  if (contact && (contact_bins < 0 || contact_bins > n_bins || contact_rs < 0 || contact_cs < 0))
+    return fail(PF_EINVAL_ARG, "pair head: contact_bins %d outside [0, %d] or bad contact strides", contact_bins,
+                n_bins);
+  const size_t lsz = logits_dtype == PF_F32 ? 4 : 2;
+  if (((uintptr_t)logits.ptr) % lsz) return fail(PF_EINVAL_ARG, "pair head: misaligned logits");
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_pair_head_workspace_size(n_rows, n_cols, c_z, n_bins, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "pair head"));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (pair_head_rows(c_z, n_bins, dtype)) {
+    set_path("tc.rows");
+    return tc::rows_pair_head(w, mode, z, zt, n_rows, n_cols, c_z, n_bins, logits, logits_dtype == PF_F32, contact,
+                              contact_rs, contact_cs, contact_bins, workspace, workspace_bytes, st);
+  }
+  set_path("simt");
+  return simt::pair_head(w, mode, z, zt, n_rows, n_cols, c_z, n_bins, logits, logits_dtype == PF_F32, contact,
+                         contact_rs, contact_cs, contact_bins, dtype, workspace, workspace_bytes, st);
+}
+
+int pf_confidence_pair_init_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_s_inputs, int32_t c_z,
+                                           int32_t n_dist_bins, int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_s_inputs <= 0 || c_z <= 0 || n_dist_bins < 0)
+    return fail(PF_EINVAL_SHAPE, "confidence pair init: bad sizes");
+  *bytes = heads::conf_init_ws_bytes(n_rows, n_cols, c_z, n_dist_bins);
+  return PF_OK;
+}
+
+static int check_pair_io(const pf_pair_view& a, const pf_pair_view& b, int dtype, const char* what) {
+  const size_t esz = dtype == PF_F32 ? 4 : 2;
+  for (const pf_pair_view* v : {&a, &b})
+    if (((uintptr_t)v->ptr) % 16 || (v->row_stride * esz) % 16 || (v->col_stride * esz) % 16)
+      return fail(PF_EINVAL_SHAPE, "%s: pair views need 16-byte aligned positions", what);
+  return PF_OK;
+}
+
+static int check_tile(int64_t n_token, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, const char* what) {
+  if (row0 < 0 || n_rows < 0 || row0 + n_rows > n_token || col0 < 0 || n_cols < 0 || col0 + n_cols > n_token)
+    return fail(PF_EINVAL_SHAPE, "%s: tile rows [%lld, %lld) x cols [%lld, %lld) outside %lld tokens", what,
+                (long long)row0, (long long)(row0 + n_rows), (long long)col0, (long long)(col0 + n_cols),
+                (long long)n_token);
+  return PF_OK;
+}
+
+int pf_confidence_pair_init_fwd(const pf_confidence_init_params* w, const void* s_inputs, int64_t s_stride,
+                                const float* coords, pf_pair_view z_trunk, pf_pair_view z_out, int64_t n_token,
+                                int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int32_t c_s_inputs,
+                                int32_t c_z, int32_t n_dist_bins, int32_t dtype, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_s1 || !w->w_s2 || !w->w_d || !w->w_d0 || !w->lower_bins || !w->upper_bins || !s_inputs || !coords)
+    return fail(PF_EINVAL_ARG, "confidence pair init: null weight, bins, s_inputs or coords");
+  if (!view_ok(z_trunk) || !view_ok(z_out)) return fail(PF_EINVAL_ARG, "confidence pair init: bad view");
+  if (n_token < 0 || c_s_inputs <= 0 || c_s_inputs > 4096 || c_z <= 0 || c_z > 1024 || c_z % 8 || n_dist_bins < 1 ||
+      n_dist_bins > 64 || s_stride < c_s_inputs)
+    return fail(PF_EINVAL_SHAPE,
+                "confidence pair init: bad sizes c_s_inputs=%d c_z=%d (a multiple of 8) bins=%d (1..64)", c_s_inputs,
+                c_z, n_dist_bins);
+  PF_TRY(check_tile(n_token, row0, n_rows, col0, n_cols, "confidence pair init"));
+  PF_TRY(check_pair_io(z_trunk, z_out, dtype, "confidence pair init"));
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  size_t need;
+  PF_TRY(pf_confidence_pair_init_workspace_size(n_rows, n_cols, c_s_inputs, c_z, n_dist_bins, dtype, &need));
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "confidence pair init"));
+  set_path("simt");
+  return heads::conf_init(w, s_inputs, s_stride, coords, z_trunk, z_out, row0, n_rows, col0, n_cols, c_s_inputs, c_z,
+                          n_dist_bins, dtype, workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+int pf_diffusion_pair_cond_workspace_size(int64_t n_rows, int64_t n_cols, int32_t c_z, int32_t c_zd, int32_t r_max,
+                                          int32_t s_max, int32_t dtype, size_t* bytes) {
+  PF_TRY(check_dtype(dtype));
+  if (!bytes) return fail(PF_EINVAL_ARG, "bytes is NULL");
+  if (n_rows < 0 || n_cols < 0 || c_z <= 0 || c_zd <= 0 || r_max < 0 || s_max < 0)
+    return fail(PF_EINVAL_SHAPE, "diffusion pair: bad sizes");
+  *bytes = heads::diffusion_ws_bytes(n_rows, n_cols, c_z, c_zd, r_max, s_max, dtype);
+  return PF_OK;
+}
+
+int pf_diffusion_pair_cond_fwd(const pf_diffusion_pair_params* w, pf_pair_view z_trunk, pf_token_ids ids,
+                               pf_pair_view z_out, int64_t n_token, int64_t row0, int64_t n_rows, int64_t col0,
+                               int64_t n_cols, int32_t c_z, int32_t c_zd, int32_t r_max, int32_t s_max, int32_t dtype,
+                               void* workspace, size_t workspace_bytes, void* stream) {
+  PF_TRY(check_dtype(dtype));
+  if (!w || !w->w_relp || !w->ln_z_w || !w->w_z || !w->t1.w_a || !w->t1.w_b || !w->t1.w_o || !w->t2.w_a ||
+      !w->t2.w_b || !w->t2.w_o)
+    return fail(PF_EINVAL_ARG, "diffusion pair: null weight pointer");
+  if (c_z != c_zd && (!w->ln_zt_w || !w->w_zt))
+    return fail(PF_EINVAL_ARG, "diffusion pair: c_z %d != c_zd %d needs layernorm_z_trunk and linear_no_bias_z_trunk",
+                c_z, c_zd);
+  if (!ids.asym_id || !ids.residue_index || !ids.entity_id || !ids.token_index || !ids.sym_id)
+    return fail(PF_EINVAL_ARG, "diffusion pair: null token id array");
+  if (!view_ok(z_trunk) || !view_ok(z_out)) return fail(PF_EINVAL_ARG, "diffusion pair: bad view");
+  if (n_token < 0 || c_z <= 0 || c_z > 1024 || c_z % 8 || c_zd <= 0 || c_zd > 512 || c_zd % 8 || r_max < 0 ||
+      r_max > 1024 || s_max < 0 || s_max > 1024)
+    return fail(PF_EINVAL_SHAPE,
+                "diffusion pair: bad sizes c_z=%d c_zd=%d (multiples of 8, c_zd <= 512) r_max=%d s_max=%d", c_z, c_zd,
+                r_max, s_max);
+  PF_TRY(check_tile(n_token, row0, n_rows, col0, n_cols, "diffusion pair"));
+  PF_TRY(check_pair_io(z_trunk, z_out, dtype, "diffusion pair"));
+  if (n_rows == 0 || n_cols == 0) return PF_OK;
+  const size_t need = heads::diffusion_ws_bytes(n_rows, n_cols, c_z, c_zd, r_max, s_max, dtype);
+  PF_TRY(check_ws(workspace, workspace_bytes, need, "diffusion pair"));
+  PF_TRY(heads::diffusion(w, z_trunk, ids, z_out, row0, n_rows, col0, n_cols, c_z, c_zd, r_max, s_max, dtype,
+                          workspace, workspace_bytes, (cudaStream_t)stream));
+  set_path(dtype == PF_BF16 && !force_simt() ? "tc.rows" : "simt");
+  return PF_OK;
+}
+
 }  // extern "C"

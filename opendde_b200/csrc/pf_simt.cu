@@ -1175,6 +1175,144 @@ int pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view
   return pair_ln_linear_t<__nv_bfloat16>(p, zi, zo, n_rows, n_cols, c_in, c_out, acc, ar, st);
 }
 
+// ---------------------------------------------------------------- pair heads
+// out[p*c + ch] = (LN unless norm = 0)(x(r, s) + (y ? y(r, s) : 0)), fp32; one warp per position
+template <class T>
+__global__ void k_head_in(const T* __restrict__ x, int64_t rs, int64_t cs, const T* __restrict__ y, int64_t yrs,
+                          int64_t ycs, int norm, int64_t n_rows, int64_t n_cols, int c,
+                          const float* __restrict__ gamma, const float* __restrict__ beta, float* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pos >= n_rows * n_cols) return;
+  const int64_t r = pos / n_cols, s = pos - r * n_cols;
+  const T* xp = x + r * rs + s * cs;
+  const T* yp = y ? y + r * yrs + s * ycs : nullptr;
+  constexpr int MAXV = 32;  // c <= 1024
+  const int per = (c + 31) / 32;
+  float v[MAXV];
+  float sum = 0.f;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (t < per) {
+      const int ch = t * 32 + lane;
+      v[t] = ch < c ? to_f(xp[ch]) + (yp ? to_f(yp[ch]) : 0.f) : 0.f;
+      sum += v[t];
+    }
+  }
+  float mean = 0.f, rstd = 1.f;
+  if (norm) {
+    mean = warp_sum(sum) / (float)c;
+    float sq = 0.f;
+#pragma unroll
+    for (int t = 0; t < MAXV; ++t) {
+      if (t < per) {
+        const int ch = t * 32 + lane;
+        const float d = ch < c ? v[t] - mean : 0.f;
+        sq += d * d;
+      }
+    }
+    rstd = 1.0f / sqrtf(warp_sum(sq) / (float)c + 1e-5f);
+  }
+  float* op = out + pos * c;
+#pragma unroll
+  for (int t = 0; t < MAXV; ++t) {
+    if (t < per) {
+      const int ch = t * 32 + lane;
+      if (ch < c) {
+        float o = v[t];
+        if (norm) {
+          o = (o - mean) * rstd;
+          if (gamma) o *= gamma[ch];
+          if (beta) o += beta[ch];
+        }
+        op[ch] = o;
+      }
+    }
+  }
+}
+
+// logits(r, s, n) = acc[p*nb + n] + bscale * bias[n]; contact(r, s) = the softmax mass of the
+// first cbins bins. One warp per position.
+template <class TO>
+__global__ void k_head_out(const float* __restrict__ acc, int64_t n_rows, int64_t n_cols, int nb,
+                           const float* __restrict__ bias, float bscale, TO* __restrict__ lo, int64_t lrs,
+                           int64_t lcs, float* __restrict__ contact, int64_t crs, int64_t ccs, int cbins) {
+  const int lane = threadIdx.x & 31;
+  const int64_t pos = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (pos >= n_rows * n_cols) return;
+  const int64_t r = pos / n_cols, s = pos - r * n_cols;
+  const float* ap = acc + pos * nb;
+  TO* op = lo + r * lrs + s * lcs;
+  float mx = -INFINITY;
+  for (int n = lane; n < nb; n += 32) {
+    const float y = ap[n] + (bias ? bscale * bias[n] : 0.f);
+    op[n] = from_f<TO>(y);
+    mx = fmaxf(mx, y);
+  }
+  if (!contact) return;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float tot = 0.f, sel = 0.f;
+  for (int n = lane; n < nb; n += 32) {
+    const float e = expf(ap[n] + (bias ? bscale * bias[n] : 0.f) - mx);
+    tot += e;
+    if (n < cbins) sel += e;
+  }
+  tot = warp_sum(tot);
+  sel = warp_sum(sel);
+  if (lane == 0) contact[r * crs + s * ccs] = sel / tot;
+}
+
+size_t pair_head_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int n_bins) {
+  Arena ar(nullptr, 0);
+  ar.take<float>((size_t)n_rows * n_cols * c_z);
+  ar.take<float>((size_t)n_rows * n_cols * n_bins);
+  return ar.used;
+}
+
+template <class T>
+static int pair_head_t(const pf_pair_head_params* p, int mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows,
+                       int64_t n_cols, int c_z, int nb, pf_pair_view lo, int lo_f32, float* contact, int64_t crs,
+                       int64_t ccs, int cbins, Arena& ar, cudaStream_t st) {
+  const int64_t P = n_rows * n_cols;
+  float* a = ar.take<float>((size_t)P * c_z);
+  float* acc = ar.take<float>((size_t)P * nb);
+  if (!ar.ok()) return fail(PF_EWORKSPACE, "pair head workspace too small");
+  if (P == 0) return PF_OK;
+  {
+    PF_LAUNCH_SCOPE(st, "k_head_in");
+    k_head_in<T><<<nblk(P, 8), 256, 0, st>>>((const T*)z.ptr, z.row_stride, z.col_stride,
+                                             mode == PF_HEAD_PLAIN ? nullptr : (const T*)zt.ptr, zt.row_stride,
+                                             zt.col_stride, mode != PF_HEAD_SYM_OUT, n_rows, n_cols, c_z, p->ln_w,
+                                             p->ln_b, a);
+  }
+  PF_CHECK_LAUNCH();
+  PF_TRY((gemm<float, T>(a, 0, c_z, (const T*)p->w, 0, c_z, acc, 0, nb, 1, 1, P, nb, c_z, 1.f, 0, st)));
+  const float bscale = mode == PF_HEAD_SYM_OUT ? 2.f : 1.f;
+  {
+    PF_LAUNCH_SCOPE(st, "k_head_out");
+    if (lo_f32)
+      k_head_out<float><<<nblk(P, 8), 256, 0, st>>>(acc, n_rows, n_cols, nb, p->b, bscale, (float*)lo.ptr,
+                                                    lo.row_stride, lo.col_stride, contact, crs, ccs, cbins);
+    else
+      k_head_out<T><<<nblk(P, 8), 256, 0, st>>>(acc, n_rows, n_cols, nb, p->b, bscale, (T*)lo.ptr, lo.row_stride,
+                                                lo.col_stride, contact, crs, ccs, cbins);
+  }
+  PF_CHECK_LAUNCH();
+  return PF_OK;
+}
+
+int pair_head(const pf_pair_head_params* p, int mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows, int64_t n_cols,
+              int c_z, int n_bins, pf_pair_view lo, int lo_f32, float* contact, int64_t crs, int64_t ccs, int cbins,
+              int dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
+  Arena ar(ws, ws_bytes);
+  if (dtype == PF_F32)
+    return pair_head_t<float>(p, mode, z, zt, n_rows, n_cols, c_z, n_bins, lo, lo_f32, contact, crs, ccs, cbins, ar,
+                              st);
+  return pair_head_t<__nv_bfloat16>(p, mode, z, zt, n_rows, n_cols, c_z, n_bins, lo, lo_f32, contact, crs, ccs, cbins,
+                                    ar, st);
+}
+
 // ---------------------------------------------------------------- OuterProductMean
 // norm[i*n_cols + j] = sum_s mask(s, row0 + i) mask(s, col0 + j) + eps, 16 x 16 outputs per CTA,
 // the mask rows staged 64 sequences at a time (the reference's einsum "...abc,...adc->...bdc").

@@ -71,7 +71,25 @@ size_t pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in, int c_o
 int pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows, int64_t n_cols,
                    int c_in, int c_out, int acc, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// bin logits of a pair tile (pf_pair_head_fwd), fp32 arithmetic
+size_t pair_head_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int n_bins);
+int pair_head(const pf_pair_head_params* p, int mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows, int64_t n_cols,
+              int c_z, int n_bins, pf_pair_view lo, int lo_f32, float* contact, int64_t crs, int64_t ccs, int cbins,
+              int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+
 }  // namespace simt
+
+namespace heads {
+// the confidence head's pair input and the diffusion pair conditioning on a tile (pf_heads.cu)
+size_t conf_init_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int n_bins);
+int conf_init(const pf_confidence_init_params* p, const void* s, int64_t s_stride, const float* coords,
+              pf_pair_view zi, pf_pair_view zo, int64_t row0, int64_t n_rows, int64_t col0, int64_t n_cols, int c_s,
+              int c_z, int n_bins, int dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t diffusion_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z, int c_zd, int r_max, int s_max, int dtype);
+int diffusion(const pf_diffusion_pair_params* p, pf_pair_view zt, pf_token_ids ids, pf_pair_view zo, int64_t row0,
+              int64_t n_rows, int64_t col0, int64_t n_cols, int c_z, int c_zd, int r_max, int s_max, int dtype,
+              void* ws, size_t ws_bytes, cudaStream_t st);
+}  // namespace heads
 
 namespace trunk {
 // the trunk's pair input on a tile (pf_trunk.cu)

@@ -91,5 +91,14 @@ size_t rows_pair_ln_linear_ws_bytes(int64_t n_rows, int64_t n_cols, int c_in);
 int rows_pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair_view zo, int64_t n_rows,
                         int64_t n_cols, int c_in, int c_out, int acc, void* ws, size_t ws_bytes, cudaStream_t st);
 
+// bin logits of a pair tile (pf_pair_head_fwd, bf16): one LayerNorm / transposed-sum pass and one
+// row GEMM whose epilogue adds the bias and forms the softmax contact sum
+bool rows_pair_head_supported(int c_z, int n_bins);
+size_t rows_pair_head_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z);
+int rows_pair_head(const pf_pair_head_params* p, int mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows,
+                   int64_t n_cols, int c_z, int n_bins, pf_pair_view lo, int lo_f32, float* contact,
+                   int64_t contact_rs, int64_t contact_cs, int contact_bins, void* ws, size_t ws_bytes,
+                   cudaStream_t st);
+
 }  // namespace tc
 }  // namespace pf

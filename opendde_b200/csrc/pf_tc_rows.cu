@@ -43,11 +43,13 @@ constexpr int RD = 32;  // attention head dimension
 
 // ------------------------------------------------------------------ LayerNorm of pair views
 // out[p*c + ch] = LN(x(r, s))[ch], p = r*n_cols + s; x(r, s) = x + r*rs + s*cs (elements),
-// channels contiguous. L lanes per position (a power of two <= 16), each lane holding up to
-// MAXV 16-byte vectors (8 channels each) between the passes.
+// channels contiguous. With a second view y: LN(x(r, s) + y(r, s)) (the sum held in bf16
+// between the passes); norm = 0: the plain x (+ y), no LayerNorm. L lanes per position (a power
+// of two <= 16), each lane holding up to MAXV 16-byte vectors (8 channels each) between the passes.
 template <int L, int MAXV>
 __global__ void __launch_bounds__(256) k_ln_pos(const __nv_bfloat16* __restrict__ x, int64_t rs, int64_t cs,
-                                                int64_t n_rows, int64_t n_cols, int c,
+                                                const __nv_bfloat16* __restrict__ y, int64_t yrs, int64_t ycs,
+                                                int norm, int64_t n_rows, int64_t n_cols, int c,
                                                 const float* __restrict__ gamma, const float* __restrict__ beta,
                                                 __nv_bfloat16* __restrict__ out) {
   const int64_t per_block = 256 / L;
@@ -58,9 +60,11 @@ __global__ void __launch_bounds__(256) k_ln_pos(const __nv_bfloat16* __restrict_
   uint4 v[MAXV];
   float sum = 0.f;
   const __nv_bfloat16* src = x;
+  const __nv_bfloat16* src2 = y;
   if (live) {
     const int64_t r = p / n_cols, s = p - r * n_cols;
     src = x + r * rs + s * cs;
+    if (y) src2 = y + r * yrs + s * ycs;
   }
 #pragma unroll
   for (int t = 0; t < MAXV; ++t) {
@@ -68,10 +72,27 @@ __global__ void __launch_bounds__(256) k_ln_pos(const __nv_bfloat16* __restrict_
     v[t] = make_uint4(0u, 0u, 0u, 0u);
     if (live && vi < nvec) {
       v[t] = *reinterpret_cast<const uint4*>(src + vi * 8);
+      if (y) {
+        const uint4 u = *reinterpret_cast<const uint4*>(src2 + vi * 8);
+        const uint32_t wx[4] = {v[t].x, v[t].y, v[t].z, v[t].w}, wy[4] = {u.x, u.y, u.z, u.w};
+        uint32_t ws[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ws[e] = pack_bf16(bf16lo(wx[e]) + bf16lo(wy[e]), bf16hi(wx[e]) + bf16hi(wy[e]));
+        v[t] = make_uint4(ws[0], ws[1], ws[2], ws[3]);
+      }
       const uint32_t w[4] = {v[t].x, v[t].y, v[t].z, v[t].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) sum += bf16lo(w[e]) + bf16hi(w[e]);
     }
+  }
+  if (!norm) {  // uniform over the block: no lane reaches the shuffles below
+    if (!live) return;
+#pragma unroll
+    for (int t = 0; t < MAXV; ++t) {
+      const int vi = t * L + sub;
+      if (vi < nvec) *reinterpret_cast<uint4*>(out + p * c + vi * 8) = v[t];
+    }
+    return;
   }
 #pragma unroll
   for (int o = L / 2; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
@@ -224,7 +245,9 @@ constexpr uint32_t R_B_BYTES = RB_NMAX * RB_K * 2;  // 32 KB
 constexpr uint32_t R_STAGE = R_A_BYTES + R_B_BYTES;
 constexpr uint32_t R_SMEM = R_STAGES * R_STAGE + 256;
 
-enum Epi : int { E_STORE = 0, E_AB = 1, E_RESID = 2, E_SWIGLU = 3, E_QKVG = 4, E_HBIAS = 5, E_STOREF = 6, E_OPMAB = 7 };
+enum Epi : int {
+  E_STORE = 0, E_AB = 1, E_RESID = 2, E_SWIGLU = 3, E_QKVG = 4, E_HBIAS = 5, E_STOREF = 6, E_OPMAB = 7, E_HEAD = 8
+};
 // A operand: contiguous rows (A_ROWS), or the outer products X[(i, c)][(j, e)] of
 // OuterProductMean read as rows (i, j) of K = (c, e) through a 4-D tensor map (A_OUTER)
 enum AMode : int { A_ROWS = 0, A_OUTER = 1 };
@@ -277,6 +300,12 @@ struct RowArgs {
   int64_t hs, bias_rs;
   int bias_f16;
   float bias_scale;
+  // E_HEAD: y = acc + bias_scale * colbias[n] (colbias may be null) stored at
+  // (outf or out) + r*rs + c*cs + n; contact[r*contact_rs + c*contact_cs] = sum over n <
+  // contact_bins of softmax(y) (one output tile: bn >= n_out)
+  float* contact;
+  int64_t contact_rs, contact_cs;
+  int contact_bins;
 };
 
 __device__ __forceinline__ uint4 pack8_bf16(const float* f) {
@@ -508,6 +537,72 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
         o[1] = pack8_bf16(f + 8);
       }
     }
+  } else if constexpr (E == E_HEAD) {
+    float mx = -INFINITY;
+#pragma unroll 1
+    for (int cc = 0; cc < a.bn; cc += 16) {
+      uint32_t v[16];
+      tmem_ld16(taddr + cc, v);
+      tmem_ld_wait();
+      const int n = n0 + cc;
+      if (!valid || n >= a.n_out) continue;
+      const int cnt = a.n_out - n < 16 ? a.n_out - n : 16;
+      float f[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        f[e] = __uint_as_float(v[e]);
+        if (a.colbias && e < cnt) f[e] = fmaf(a.bias_scale, a.colbias[n + e], f[e]);
+      }
+      const int64_t off = r * a.rs + c * a.cs + n;
+      if (a.outf) {
+        float* o = a.outf + off;
+        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            reinterpret_cast<float4*>(o)[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e < cnt) o[e] = f[e];
+        }
+      } else {
+        __nv_bfloat16* o = a.out + off;
+        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+          reinterpret_cast<uint4*>(o)[0] = pack8_bf16(f);
+          reinterpret_cast<uint4*>(o)[1] = pack8_bf16(f + 8);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if (e < cnt) o[e] = __float2bfloat16_rn(f[e]);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (e < cnt) mx = fmaxf(mx, f[e]);
+    }
+    if (a.contact) {
+      // second pass over the accumulator: sum of exp over all bins and over the contact bins
+      float tot = 0.f, sel = 0.f;
+#pragma unroll 1
+      for (int cc = 0; cc < a.bn; cc += 16) {
+        uint32_t v[16];
+        tmem_ld16(taddr + cc, v);
+        tmem_ld_wait();
+        const int n = n0 + cc;
+        if (!valid || n >= a.n_out) continue;
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          if (n + e < a.n_out) {
+            float y = __uint_as_float(v[e]);
+            if (a.colbias) y = fmaf(a.bias_scale, a.colbias[n + e], y);
+            const float ex = exp2f((y - mx) * LOG2E_R);
+            tot += ex;
+            if (n + e < a.contact_bins) sel += ex;
+          }
+        }
+      }
+      if (valid) a.contact[r * a.contact_rs + c * a.contact_cs] = sel / tot;
+    }
   } else {  // E_HBIAS
     uint32_t v[16];
     tmem_ld16(taddr, v);
@@ -683,6 +778,7 @@ int ensure_attrs() {
     PF_TRY(set_smem(k_rowgemm<E_STOREF, A_ROWS>, R_SMEM + 1024));
     PF_TRY(set_smem(k_rowgemm<E_OPMAB, A_ROWS>, R_SMEM + 1024));
     PF_TRY(set_smem(k_rowgemm<E_RESID, A_OUTER>, R_SMEM + 1024));
+    PF_TRY(set_smem(k_rowgemm<E_HEAD, A_ROWS>, R_SMEM + 1024));
     PF_TRY(set_smem(k_ln_cmajor, CM_MAX_C * 128 * 2));
     return PF_OK;
   });
@@ -698,8 +794,10 @@ int check_view(const pf_pair_view& v, const char* what) {
 }
 
 // LayerNorm of the positions (r < n_rows, s < n_cols) of a bf16 view into rows of c channels.
-int ln_pos(const __nv_bfloat16* x, int64_t rs, int64_t cs, int64_t n_rows, int64_t n_cols, int c, const float* g,
-           const float* b, __nv_bfloat16* out, cudaStream_t st) {
+// With y (and its strides): of x + y; norm = 0: the plain x (+ y), no LayerNorm.
+int ln_pos2(const __nv_bfloat16* x, int64_t rs, int64_t cs, const __nv_bfloat16* y, int64_t yrs, int64_t ycs,
+            int norm, int64_t n_rows, int64_t n_cols, int c, const float* g, const float* b, __nv_bfloat16* out,
+            cudaStream_t st) {
   const int64_t P = n_rows * n_cols;
   if (P == 0) return PF_OK;
   const int nvec = c / 8;
@@ -707,8 +805,9 @@ int ln_pos(const __nv_bfloat16* x, int64_t rs, int64_t cs, int64_t n_rows, int64
   while (L * 2 <= nvec && L < 16) L *= 2;
   const int maxv = (nvec + L - 1) / L;
   const unsigned grid = (unsigned)((P + 256 / L - 1) / (256 / L));
-  PF_LAUNCH_SCOPE_WORK(st, "k_ln_pos", 4.0 * (double)P * c, 'b');
-#define PF_LNPOS(LL, MV) k_ln_pos<LL, MV><<<grid, 256, 0, st>>>(x, rs, cs, n_rows, n_cols, c, g, b, out)
+  PF_LAUNCH_SCOPE_WORK(st, "k_ln_pos", (y ? 6.0 : 4.0) * (double)P * c, 'b');
+#define PF_LNPOS(LL, MV) \
+  k_ln_pos<LL, MV><<<grid, 256, 0, st>>>(x, rs, cs, y, yrs, ycs, norm, n_rows, n_cols, c, g, b, out)
   if (L == 16) {
     if (maxv <= 1) PF_LNPOS(16, 1);
     else if (maxv <= 2) PF_LNPOS(16, 2);
@@ -728,6 +827,11 @@ int ln_pos(const __nv_bfloat16* x, int64_t rs, int64_t cs, int64_t n_rows, int64
 #undef PF_LNPOS
   PF_CHECK_LAUNCH();
   return PF_OK;
+}
+
+int ln_pos(const __nv_bfloat16* x, int64_t rs, int64_t cs, int64_t n_rows, int64_t n_cols, int c, const float* g,
+           const float* b, __nv_bfloat16* out, cudaStream_t st) {
+  return ln_pos2(x, rs, cs, nullptr, 0, 0, 1, n_rows, n_cols, c, g, b, out, st);
 }
 
 int ln_cmajor(const __nv_bfloat16* x, int64_t ld, int64_t n_i, int64_t n_j, int c, const float* g, const float* b,
@@ -813,7 +917,12 @@ int rowgemm(const __nv_bfloat16* A, int64_t lda, int64_t n_pos, int k, const voi
   PF_TRY(ensure_attrs());
   const int64_t grid = ra.n_work < sm_count() ? ra.n_work : sm_count();
   {
-    PF_LAUNCH_SCOPE_WORK(st, name, 2.0 * (double)n_pos * ra.n_out * k, 'f');
+    // the head GEMM (a few dozen bins per position) is bound by its bytes: the A rows read, the
+    // logits and contact probabilities written
+    const double work = E == E_HEAD ? (double)n_pos * (2.0 * k + (ra.outf ? 4.0 : 2.0) * ra.n_out +
+                                                       (ra.contact ? 4.0 : 0.0))
+                                    : 2.0 * (double)n_pos * ra.n_out * k;
+    PF_LAUNCH_SCOPE_WORK(st, name, work, E == E_HEAD ? 'b' : 'f');
     k_rowgemm<E, A_ROWS><<<(unsigned)grid, 192, R_SMEM + 1024, st>>>(ta, tb, ra);
   }
   PF_CHECK_LAUNCH();
@@ -1244,6 +1353,50 @@ int rows_pair_ln_linear(const pf_pair_linear_params* p, pf_pair_view zi, pf_pair
   ro.cs = zo.col_stride;
   ro.accumulate = acc;
   return rowgemm<E_RESID>(ln, c_in, n_rows * n_cols, c_in, p->w, c_out, ro, "k_rowgemm_resid", status, st);
+}
+
+// ---------------------------------------------------------------- pair heads
+bool rows_pair_head_supported(int c_z, int n_bins) {
+  return c_z >= 8 && c_z % 8 == 0 && c_z <= 1024 && n_bins >= 1 && n_bins <= RB_NMAX;
+}
+
+size_t rows_pair_head_ws_bytes(int64_t n_rows, int64_t n_cols, int c_z) {
+  return align_up((size_t)n_rows * n_cols * c_z * 2, 256);
+}
+
+// A = LN(z) / LN(z + zt) / (z + zt) per position (k_ln_pos), then logits = A W^T + s b with the
+// softmax contact sum in the epilogue (k_rowgemm<E_HEAD>, one output tile of <= 256 bins).
+int rows_pair_head(const pf_pair_head_params* p, int mode, pf_pair_view z, pf_pair_view zt, int64_t n_rows,
+                   int64_t n_cols, int c_z, int n_bins, pf_pair_view lo, int lo_f32, float* contact,
+                   int64_t contact_rs, int64_t contact_cs, int contact_bins, void* ws, size_t ws_bytes,
+                   cudaStream_t st) {
+  if (ws_bytes < rows_pair_head_ws_bytes(n_rows, n_cols, c_z)) return fail(PF_EWORKSPACE, "pair head workspace too small");
+  PF_TRY(check_view(z, "pair head z"));
+  if (mode != PF_HEAD_PLAIN) PF_TRY(check_view(zt, "pair head zt"));
+  unsigned int* status;
+  PF_TRY(device_status_ptr(&status));
+  __nv_bfloat16* a = (__nv_bfloat16*)ws;
+  const bool sym = mode != PF_HEAD_PLAIN;
+  PF_TRY(ln_pos2((const __nv_bfloat16*)z.ptr, z.row_stride, z.col_stride, sym ? (const __nv_bfloat16*)zt.ptr : nullptr,
+                 zt.row_stride, zt.col_stride, mode != PF_HEAD_SYM_OUT, n_rows, n_cols, c_z, p->ln_w, p->ln_b, a, st));
+  RowArgs ro{};
+  ro.n_out = n_bins;
+  ro.bn = pick_bn(n_bins, 16);
+  ro.e_cols = n_cols;
+  ro.rs = lo.row_stride;
+  ro.cs = lo.col_stride;
+  if (lo_f32)
+    ro.outf = (float*)lo.ptr;
+  else
+    ro.out = (__nv_bfloat16*)lo.ptr;
+  ro.colbias = p->b;
+  ro.n_colbias = p->b ? n_bins : 0;
+  ro.bias_scale = mode == PF_HEAD_SYM_OUT ? 2.f : 1.f;
+  ro.contact = contact;
+  ro.contact_rs = contact_rs;
+  ro.contact_cs = contact_cs;
+  ro.contact_bins = contact_bins;
+  return rowgemm<E_HEAD>(a, c_z, n_rows * n_cols, c_z, p->w, n_bins, ro, "k_rowgemm_head", status, st);
 }
 
 // ---------------------------------------------------------------- OuterProductMean

@@ -4,6 +4,14 @@
 from .config import FOLDCP_ENVIRONMENT_KEYS, FOLDCP_MESH_KEY, FoldCPConfig, apply_foldcp_config
 from .layout import FoldCP2DLayout
 from .mesh import FoldCPProcessMesh, clear_mesh_cache
+from .heads import (
+    confidence_pair_input_local,
+    confidence_pair_logits_local,
+    diffusion_prepare_cache_local,
+    distogram_contact_probs_local,
+    distributed_confidence_pair_logits,
+    distributed_distogram_contact_probs,
+)
 from .opm import outer_product_mean_local_update
 from .trunk_init import apply_trunk_z_cycle_local, build_trunk_z_init_local
 from .pair_sharding import (
@@ -37,5 +45,7 @@ __all__ = [
     "distributed_pairformer_block_pair_update", "distributed_pairformer_stack_pair_update",
     "distributed_pairformer_stack_single_bridge_update", "distributed_triangle_attention_update",
     "distributed_triangle_multiplication_update", "outer_product_mean_local_update", "build_trunk_z_init_local",
-    "apply_trunk_z_cycle_local",
+    "apply_trunk_z_cycle_local", "distogram_contact_probs_local", "distributed_distogram_contact_probs",
+    "confidence_pair_logits_local", "distributed_confidence_pair_logits", "confidence_pair_input_local",
+    "diffusion_prepare_cache_local",
 ]

@@ -336,3 +336,73 @@ def trimul_combine(pack: WeightPack, a: torch.Tensor, b: torch.Tensor, n_k: int,
     check(_abi.load().pf_trimul_combine(ctypes.byref(pack.struct), a.data_ptr(), b.data_ptr(), ld, n_i, n_j, n_k,
                                         pair_view(zg), pair_view(zo), c_z, c_h, int(accumulate), code,
                                         ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def pair_head(pack: WeightPack, mode: int, z: torch.Tensor, zt: Optional[torch.Tensor], logits: torch.Tensor,
+              contact: Optional[torch.Tensor] = None, contact_bins: int = 0) -> None:
+    """logits [R, C, n_bins] (fp32, or z's dtype) of a pair tile and optionally the contact
+    probabilities [R, C] (fp32): see pf_pair_head_fwd. ``zt`` holds z^T at the tile's positions
+    (forms PF_HEAD_SYM_IN / PF_HEAD_SYM_OUT)."""
+    require_cuda(z, zt, logits, contact)
+    code = dtype_code(z)
+    lcode = dtype_code(logits)
+    n_rows, n_cols, c_z = z.shape
+    n_bins = logits.shape[2]
+    if logits.shape[:2] != (n_rows, n_cols) or (zt is not None and zt.shape != z.shape):
+        raise ValueError("pair head views must cover the same positions")
+    if zt is not None and zt.dtype != z.dtype:
+        raise TypeError("z and zt must share the dtype")
+    if contact is not None and (contact.dtype != torch.float32 or tuple(contact.shape) != (n_rows, n_cols)):
+        raise ValueError("contact must be a float32 [R, C] tensor")
+    nbytes = _abi.workspace_bytes("pf_pair_head_workspace_size", n_rows, n_cols, c_z, n_bins, code)
+    ws = workspace(nbytes, z.device)
+    ztv = pair_view(zt) if zt is not None else PairView(None, 0, 0)
+    crs, ccs = (contact.stride(0), contact.stride(1)) if contact is not None else (0, 0)
+    check(_abi.load().pf_pair_head_fwd(ctypes.byref(pack.struct), mode, pair_view(z), ztv, n_rows, n_cols, c_z,
+                                       n_bins, pair_view(logits), lcode, _ptr(contact), crs, ccs, contact_bins, code,
+                                       ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def confidence_pair_init(pack: WeightPack, s_inputs: torch.Tensor, coords: torch.Tensor, z_trunk: torch.Tensor,
+                         z_out: torch.Tensor, row0: int, col0: int, n_dist_bins: int) -> None:
+    """z_out [R, C, c_z] = the confidence head's pair input on rows [row0, row0 + R) x cols
+    [col0, col0 + C) (see pf_confidence_pair_init_fwd); z_out may be z_trunk."""
+    require_cuda(s_inputs, coords, z_trunk, z_out)
+    code = dtype_code(z_trunk)
+    if z_out.dtype != z_trunk.dtype or s_inputs.dtype != z_trunk.dtype or s_inputs.stride(-1) != 1:
+        raise TypeError("s_inputs (contiguous channels) and the pair views must share the storage dtype")
+    if coords.dtype != torch.float32 or not coords.is_contiguous() or coords.shape[-1] != 3:
+        raise ValueError("coords must be a contiguous float32 [N_token, 3] tensor")
+    n_token, c_s = s_inputs.shape
+    n_rows, n_cols, c_z = z_out.shape
+    if z_trunk.shape != z_out.shape:
+        raise ValueError("z_trunk and z_out must cover the same positions")
+    nbytes = _abi.workspace_bytes("pf_confidence_pair_init_workspace_size", n_rows, n_cols, c_s, c_z, n_dist_bins,
+                                  code)
+    ws = workspace(nbytes, z_out.device)
+    check(_abi.load().pf_confidence_pair_init_fwd(ctypes.byref(pack.struct), s_inputs.data_ptr(), s_inputs.stride(0),
+                                                  coords.data_ptr(), pair_view(z_trunk), pair_view(z_out), n_token,
+                                                  row0, n_rows, col0, n_cols, c_s, c_z, n_dist_bins, code,
+                                                  ws.data_ptr(), ws.numel(), stream_ptr()))
+
+
+def diffusion_pair_cond(pack: WeightPack, z_trunk: torch.Tensor, ids, z_out: torch.Tensor, row0: int, col0: int,
+                        n_token: int, r_max: int, s_max: int) -> None:
+    """z_out [R, C, c_zd] = the diffusion pair conditioning on rows [row0, row0 + R) x cols
+    [col0, col0 + C) (see pf_diffusion_pair_cond_fwd). ``ids``: int32 CUDA tensors asym_id,
+    residue_index, entity_id, token_index, sym_id."""
+    require_cuda(z_trunk, z_out, *ids)
+    code = dtype_code(z_trunk)
+    if z_out.dtype != z_trunk.dtype:
+        raise TypeError("pair views must share the dtype")
+    n_rows, n_cols, c_z = z_trunk.shape
+    c_zd = z_out.shape[2]
+    if z_out.shape[:2] != (n_rows, n_cols):
+        raise ValueError("z_trunk and z_out must cover the same positions")
+    nbytes = _abi.workspace_bytes("pf_diffusion_pair_cond_workspace_size", n_rows, n_cols, c_z, c_zd, r_max, s_max,
+                                  code)
+    ws = workspace(nbytes, z_out.device)
+    tid = _abi.TokenIds(*[t.data_ptr() for t in ids])
+    check(_abi.load().pf_diffusion_pair_cond_fwd(ctypes.byref(pack.struct), pair_view(z_trunk), tid,
+                                                 pair_view(z_out), n_token, row0, n_rows, col0, n_cols, c_z, c_zd,
+                                                 r_max, s_max, code, ws.data_ptr(), ws.numel(), stream_ptr()))

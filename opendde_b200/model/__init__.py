@@ -1,4 +1,5 @@
 """Module mirror of opendde.model (Pairformer pair stack only)."""
+from .heads import ConfidencePairHead, DiffusionPairConditioning, DistogramHead  # noqa: F401
 from .outer_product_mean import OuterProductMean  # noqa: F401
 from .pairformer import PairformerBlock, PairformerStack  # noqa: F401
 from .primitives import Linear, LinearNoBias, Transition  # noqa: F401
