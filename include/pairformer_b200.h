@@ -68,8 +68,13 @@ typedef struct {
 
 PF_API int pf_abi_version(void);
 PF_API const char* pf_last_error_string(void);
-/* Options: PF_OPT_FORCE_SIMT=1 routes bf16 requests to the generic SIMT kernels (testing). */
+/* Options: PF_OPT_FORCE_SIMT=1 routes bf16 requests to the generic SIMT kernels (testing).
+ * PF_OPT_SM_RESERVE=r (0..64, per calling thread; 0 = default): the persistent tensor-core kernels
+ * this thread launches afterwards use r fewer CTAs than the device has SMs, and pf_copy_regions
+ * launches at most 8 r CTAs, so that a band copy enqueued on another stream runs on the r free
+ * SMs beside them (the Fold-CP overlapped band exchange). No reference counterpart. */
 #define PF_OPT_FORCE_SIMT 1
+#define PF_OPT_SM_RESERVE 2
 PF_API int pf_set_option(int option, int64_t value);
 /* Name of the kernel family the last call on this thread dispatched to ("tc" or "simt"). */
 PF_API const char* pf_last_path(void);

@@ -27,6 +27,7 @@ PF_EWORKSPACE = 8
 PF_F32 = 0
 PF_BF16 = 1
 PF_OPT_FORCE_SIMT = 1
+PF_OPT_SM_RESERVE = 2
 
 _STATUS_NAMES = {
     PF_EINVAL_SHAPE: "PF_EINVAL_SHAPE", PF_EINVAL_DTYPE: "PF_EINVAL_DTYPE",
@@ -246,6 +247,12 @@ def last_path() -> str:
 
 def set_force_simt(flag: bool) -> None:
     check(load().pf_set_option(PF_OPT_FORCE_SIMT, 1 if flag else 0))
+
+
+def set_sm_reserve(n: int) -> None:
+    """Leave ``n`` SMs out of the persistent kernels this thread launches next (see
+    PF_OPT_SM_RESERVE); 0 restores every SM."""
+    check(load().pf_set_option(PF_OPT_SM_RESERVE, int(n)))
 
 
 def device_status(clear: bool = False) -> int:

@@ -13,6 +13,7 @@
 #include "pf_common.cuh"
 #include "pf_simt.h"
 #include "pf_tc.h"
+#include "pf_tmap.h"
 
 namespace pf {
 
@@ -67,6 +68,11 @@ const char* pf_last_path(void) { return g_path; }
 int pf_set_option(int option, int64_t value) {
   if (option == PF_OPT_FORCE_SIMT) {
     g_force_simt = value ? 1 : 0;
+    return PF_OK;
+  }
+  if (option == PF_OPT_SM_RESERVE) {
+    if (value < 0 || value > 64) return fail(PF_EINVAL_ARG, "SM reserve %lld outside [0, 64]", (long long)value);
+    set_sm_reserve((int)value);
     return PF_OK;
   }
   return fail(PF_EINVAL_ARG, "unknown option %d", option);

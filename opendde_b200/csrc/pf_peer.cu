@@ -16,6 +16,7 @@
 
 #include "pf_common.cuh"
 #include "pf_prof.h"
+#include "pf_tmap.h"
 
 namespace pf {
 namespace {
@@ -175,7 +176,10 @@ extern "C" PF_API int pf_copy_regions(const pf_copy_region* regions, int32_t n_r
   PF_CUDA_TRY(cudaGetDevice(&dev));
   PF_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t items = bs.item_start[n];
-  const int grid = (int)(items < (int64_t)sms * 4 ? items : (int64_t)sms * 4);
+  // with an SM reserve set, at most 8 CTAs per reserved SM, so that the copy fits beside the
+  // persistent kernels that leave those SMs free
+  const int64_t cap = sm_reserve() > 0 ? (int64_t)sm_reserve() * 8 : (int64_t)sms * 4;
+  const int grid = (int)(items < cap ? items : cap);
   cudaStream_t st = (cudaStream_t)stream;
   double copied = 0.0;  // bytes copied (each read once from its source, written once)
   for (int i = 0; i < n; ++i) copied += (double)live[i].planes * live[i].rows * live[i].row_bytes;

@@ -538,71 +538,70 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
       }
     }
   } else if constexpr (E == E_HEAD) {
-    float mx = -INFINITY;
+    // one pass over the accumulator in 32-column chunks: store the logits and keep an online
+    // softmax (running max, and the sums over all bins and over the contact bins, rescaled when
+    // the max grows)
+    float mx = -INFINITY, tot = 0.f, sel = 0.f;
 #pragma unroll 1
-    for (int cc = 0; cc < a.bn; cc += 16) {
-      uint32_t v[16];
-      tmem_ld16(taddr + cc, v);
+    for (int cc = 0; cc < a.bn; cc += 32) {
+      uint32_t v[32];
+      tmem_ld32(taddr + cc, v);
       tmem_ld_wait();
       const int n = n0 + cc;
       if (!valid || n >= a.n_out) continue;
-      const int cnt = a.n_out - n < 16 ? a.n_out - n : 16;
-      float f[16];
+      int cnt = a.n_out - n < 32 ? a.n_out - n : 32;
+      if (a.bn - cc < cnt) cnt = a.bn - cc;
+      float f[32];
+      float cm = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < 16; ++e) {
+      for (int e = 0; e < 32; ++e) {
         f[e] = __uint_as_float(v[e]);
-        if (a.colbias && e < cnt) f[e] = fmaf(a.bias_scale, a.colbias[n + e], f[e]);
+        if (e < cnt) {
+          if (a.colbias) f[e] = fmaf(a.bias_scale, a.colbias[n + e], f[e]);
+          cm = fmaxf(cm, f[e]);
+        }
       }
       const int64_t off = r * a.rs + c * a.cs + n;
       if (a.outf) {
         float* o = a.outf + off;
-        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+        if (cnt == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
+          for (int e = 0; e < 8; ++e)
             reinterpret_cast<float4*>(o)[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
+          for (int e = 0; e < 32; ++e)
             if (e < cnt) o[e] = f[e];
         }
       } else {
         __nv_bfloat16* o = a.out + off;
-        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-          reinterpret_cast<uint4*>(o)[0] = pack8_bf16(f);
-          reinterpret_cast<uint4*>(o)[1] = pack8_bf16(f + 8);
+        if (cnt == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(o)[e] = pack8_bf16(f + 8 * e);
         } else {
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
+          for (int e = 0; e < 32; ++e)
             if (e < cnt) o[e] = __float2bfloat16_rn(f[e]);
         }
       }
+      if (a.contact) {
+        const float nm = fmaxf(mx, cm);
+        const float scale = exp2f((mx - nm) * LOG2E_R);  // 0 on the first chunk (mx = -inf)
+        float ct = 0.f, cs = 0.f;
 #pragma unroll
-      for (int e = 0; e < 16; ++e)
-        if (e < cnt) mx = fmaxf(mx, f[e]);
-    }
-    if (a.contact) {
-      // second pass over the accumulator: sum of exp over all bins and over the contact bins
-      float tot = 0.f, sel = 0.f;
-#pragma unroll 1
-      for (int cc = 0; cc < a.bn; cc += 16) {
-        uint32_t v[16];
-        tmem_ld16(taddr + cc, v);
-        tmem_ld_wait();
-        const int n = n0 + cc;
-        if (!valid || n >= a.n_out) continue;
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          if (n + e < a.n_out) {
-            float y = __uint_as_float(v[e]);
-            if (a.colbias) y = fmaf(a.bias_scale, a.colbias[n + e], y);
-            const float ex = exp2f((y - mx) * LOG2E_R);
-            tot += ex;
-            if (n + e < a.contact_bins) sel += ex;
+        for (int e = 0; e < 32; ++e) {
+          if (e < cnt) {
+            const float ex = exp2f((f[e] - nm) * LOG2E_R);
+            ct += ex;
+            if (n + e < a.contact_bins) cs += ex;
           }
         }
+        tot = fmaf(tot, scale, ct);
+        sel = fmaf(sel, scale, cs);
+        mx = nm;
       }
-      if (valid) a.contact[r * a.contact_rs + c * a.contact_cs] = sel / tot;
     }
+    if (a.contact && valid) a.contact[r * a.contact_rs + c * a.contact_cs] = sel / tot;
   } else {  // E_HBIAS
     uint32_t v[16];
     tmem_ld16(taddr, v);

@@ -49,7 +49,12 @@ int device_status_ptr(unsigned int** out) {
   return PF_OK;
 }
 
-int64_t sm_count() {
+static thread_local int g_sm_reserve = 0;
+
+void set_sm_reserve(int r) { g_sm_reserve = r < 0 ? 0 : r; }
+int sm_reserve() { return g_sm_reserve; }
+
+int64_t device_sm_count() {
   static std::atomic<int> n[64];
   int dev = 0;
   cudaGetDevice(&dev);
@@ -61,6 +66,13 @@ int64_t sm_count() {
     n[dev].store(v, std::memory_order_relaxed);
   }
   return v;
+}
+
+// The persistent kernels' grid: every SM, less the ones this thread reserved for a band copy
+// that runs beside them (pf_set_option(PF_OPT_SM_RESERVE, r)).
+int64_t sm_count() {
+  const int64_t v = device_sm_count() - g_sm_reserve;
+  return v < 1 ? 1 : v;
 }
 
 int current_device(int* dev) {

@@ -21,7 +21,10 @@ int make_tmap(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* ba
 int device_status_ptr(unsigned int** out);
 
 // Number of SMs of the current device (persistent grids are sized by it).
-int64_t sm_count();
+int64_t sm_count();         // SMs for persistent grids (less the reserve of the calling thread)
+int64_t device_sm_count();  // all SMs of the current device
+void set_sm_reserve(int r);
+int sm_reserve();
 
 // Ordinal of the current device, checked against the per-device tables (< 64).
 int current_device(int* dev);

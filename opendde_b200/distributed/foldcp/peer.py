@@ -22,6 +22,7 @@ back to the NCCL transport with ``=nccl``.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 from typing import Callable, Dict, List, Sequence, Tuple
@@ -222,6 +223,34 @@ def copy_engine() -> str:
     return v
 
 
+RESERVE_KEY = "OPENDDE_B200_FOLDCP_RESERVE_SMS"
+
+
+def reserve_sms() -> int:
+    """SMs the overlapped band exchanges leave to the band-copy kernel while a chunk computes
+    (``OPENDDE_B200_FOLDCP_RESERVE_SMS``, default 0). The persistent kernels otherwise hold every
+    SM, and a copy kernel launched beside them waits for their end."""
+    v = os.environ.get(RESERVE_KEY, "").strip()
+    n = int(v) if v else 0
+    if not 0 <= n <= 64:
+        raise ValueError(f"{RESERVE_KEY} must be in [0, 64], got {v!r}")
+    return n
+
+
+@contextlib.contextmanager
+def sm_reserve(n: int):
+    """Launches inside use ``n`` fewer SMs for their persistent grids (the library's
+    PF_OPT_SM_RESERVE on this thread); nothing changes for n = 0."""
+    if n <= 0:
+        yield
+        return
+    _abi.set_sm_reserve(n)
+    try:
+        yield
+    finally:
+        _abi.set_sm_reserve(0)
+
+
 def peer_copy_gbs(mesh, device: torch.device, reps: int = 5) -> float:
     """Bandwidth of the band copies' transport, measured with the band copy itself (the kernel,
     or the copy engines under ``OPENDDE_B200_FOLDCP_COPY=dma``): every rank at once copies one
@@ -298,25 +327,35 @@ class PeerExchange(DistExchange):
         stream forks, so no memory the current stream still uses is handed to it."""
         plans, outs, bias = self._publish_and_plan(local, spec, needs, (bias_tile, transposed, bias_rows))
         if local.is_cuda and any(plans):
-            main = torch.cuda.current_stream(local.device)
-            side = self._side_stream(local.device)
-            side.wait_stream(main)
-            done = []
-            with torch.cuda.stream(side):
-                for plan in plans:
-                    if plan:
-                        self._copy(plan)
-                    ev = torch.cuda.Event()
-                    ev.record(side)
-                    done.append(ev)
-            for i, out in enumerate(outs):
-                main.wait_event(done[i])
-                consume(i, out, bias)
+            self._overlap(local.device, plans, lambda i: consume(i, outs[i], bias))
             return
         for i, (plan, out) in enumerate(zip(plans, outs)):
             if plan:
                 self._copy(plan)
             consume(i, out, bias)
+
+    def _overlap(self, device, plans, consume_i) -> None:
+        """Copy plan after plan on a side stream while ``consume_i(i)`` enqueues chunk i's compute
+        on the current stream behind copy i. With an SM reserve (``reserve_sms``, SM copies only),
+        the copies after the first and the compute of every chunk but the last run with that many
+        SMs left out of the persistent grids, so that copy i + 1 runs beside compute i."""
+        r = reserve_sms() if copy_engine() == "sm" else 0
+        main = torch.cuda.current_stream(device)
+        side = self._side_stream(device)
+        side.wait_stream(main)
+        done = []
+        with torch.cuda.stream(side):
+            for i, plan in enumerate(plans):
+                if plan:
+                    with sm_reserve(r if i > 0 else 0):
+                        self._copy(plan)
+                ev = torch.cuda.Event()
+                ev.record(side)
+                done.append(ev)
+        for i in range(len(plans)):
+            main.wait_event(done[i])
+            with sm_reserve(r if i < len(plans) - 1 else 0):
+                consume_i(i)
 
     def _side_stream(self, device) -> "torch.cuda.Stream":
         st = getattr(self, "_side", None)
@@ -424,20 +463,7 @@ class PeerExchange(DistExchange):
             plans.append(projection_copy_plan(spec, self.layout, (lo, hi), transposed, ptrs, 0, c_h, elem, ld_t,
                                               out.data_ptr(), ld_b))
         if local.is_cuda:
-            main = torch.cuda.current_stream(local.device)
-            side_st = self._side_stream(local.device)
-            side_st.wait_stream(main)
-            done = []
-            with torch.cuda.stream(side_st):
-                for plan in plans:
-                    if plan:
-                        self._copy(plan)
-                    ev = torch.cuda.Event()
-                    ev.record(side_st)
-                    done.append(ev)
-            for i, out in enumerate(outs):
-                main.wait_event(done[i])
-                consume(i, out, b, n_pad)
+            self._overlap(local.device, plans, lambda i: consume(i, outs[i], b, n_pad))
             return
         for i, (plan, out) in enumerate(zip(plans, outs)):
             if plan:

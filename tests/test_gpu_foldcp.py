@@ -135,3 +135,26 @@ def test_cp_bf16_copy_engine_transport(overlap, cuda_device, monkeypatch):
     for s2, z2 in outs:
         assert rel_l2(z2, z1) <= 5e-3
         assert rel_l2(s2, s1) <= 5e-3
+
+
+def test_cp_bf16_sm_reserve_overlap(cuda_device, monkeypatch):
+    """The overlapped band exchange with SMs reserved for the copy kernel (persistent grids of
+    148 - 16 CTAs while a chunk computes): the same z and s as the same overlap without the
+    reserve, bit for bit (the grid size changes which CTA computes a tile, not the tile), and the
+    single-device stack's within tolerance."""
+    n = 300
+    stack, _ = _stack(1, cuda_device)
+    g = torch.Generator().manual_seed(2)
+    z = torch.randn((n, n, 128), generator=g).to(cuda_device, torch.bfloat16)
+    s = torch.randn((n, 384), generator=g).to(cuda_device, torch.bfloat16)
+    mask = ragged_pair_mask(n, seed=3, drop=0.2, full_rows=[5]).to(cuda_device)
+    with torch.no_grad():
+        s1, z1 = stack(s, z, mask)
+    monkeypatch.setenv("OPENDDE_B200_FOLDCP_OVERLAP", "3")
+    base = _cp((2, 4), stack, s, z, mask, "peer")
+    monkeypatch.setenv("OPENDDE_B200_FOLDCP_RESERVE_SMS", "16")
+    outs = _cp((2, 4), stack, s, z, mask, "peer")
+    assert _abi.device_status(clear=True) == 0
+    for (s2, z2), (sb, zb) in zip(outs, base):
+        assert torch.equal(z2, zb) and torch.equal(s2, sb)
+        assert rel_l2(z2, z1) <= 5e-3 and rel_l2(s2, s1) <= 5e-3
