@@ -538,66 +538,75 @@ __device__ __forceinline__ void row_epilogue(const RowArgs& a, uint32_t taddr, b
       }
     }
   } else if constexpr (E == E_HEAD) {
-    // one pass over the accumulator in 32-column chunks: store the logits and keep an online
+    // one pass over the accumulator in 16-column chunks: store the logits and keep an online
     // softmax (running max, and the sums over all bins and over the contact bins, rescaled when
     // the max grows)
     float mx = -INFINITY, tot = 0.f, sel = 0.f;
 #pragma unroll 1
-    for (int cc = 0; cc < a.bn; cc += 32) {
-      uint32_t v[32];
-      tmem_ld32(taddr + cc, v);
-      tmem_ld_wait();
+    for (int cc = 0; cc < a.bn; cc += 16) {
       const int n = n0 + cc;
-      if (!valid || n >= a.n_out) continue;
-      int cnt = a.n_out - n < 32 ? a.n_out - n : 32;
-      if (a.bn - cc < cnt) cnt = a.bn - cc;
-      float f[32];
-      float cm = -INFINITY;
+      const int cnt = a.n_out - n < 16 ? (a.n_out - n > 0 ? a.n_out - n : 0) : 16;
+      // the chunk's bias values in flight before the TMEM load's wait
+      float bias[16];
 #pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        f[e] = __uint_as_float(v[e]);
-        if (e < cnt) {
-          if (a.colbias) f[e] = fmaf(a.bias_scale, a.colbias[n + e], f[e]);
-          cm = fmaxf(cm, f[e]);
-        }
-      }
+      for (int e = 0; e < 16; ++e) bias[e] = (a.colbias && e < cnt) ? a.bias_scale * a.colbias[n + e] : 0.f;
+      uint32_t v[16];
+      tmem_ld16(taddr + cc, v);
+      tmem_ld_wait();
+      if (!valid || cnt == 0) continue;
+      float f[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]) + bias[e];
       const int64_t off = r * a.rs + c * a.cs + n;
       if (a.outf) {
         float* o = a.outf + off;
-        if (cnt == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
+          for (int e = 0; e < 4; ++e)
             reinterpret_cast<float4*>(o)[e] = make_float4(f[4 * e], f[4 * e + 1], f[4 * e + 2], f[4 * e + 3]);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
+          for (int e = 0; e < 16; ++e)
             if (e < cnt) o[e] = f[e];
         }
       } else {
         __nv_bfloat16* o = a.out + off;
-        if (cnt == 32 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
-#pragma unroll
-          for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(o)[e] = pack8_bf16(f + 8 * e);
+        if (cnt == 16 && (reinterpret_cast<uintptr_t>(o) & 15) == 0) {
+          reinterpret_cast<uint4*>(o)[0] = pack8_bf16(f);
+          reinterpret_cast<uint4*>(o)[1] = pack8_bf16(f + 8);
         } else {
 #pragma unroll
-          for (int e = 0; e < 32; ++e)
+          for (int e = 0; e < 16; ++e)
             if (e < cnt) o[e] = __float2bfloat16_rn(f[e]);
         }
       }
       if (a.contact) {
-        const float nm = fmaxf(mx, cm);
-        const float scale = exp2f((mx - nm) * LOG2E_R);  // 0 on the first chunk (mx = -inf)
-        float ct = 0.f, cs = 0.f;
+        // trees (depth 4) rather than 16-long chains: four epilogue warps per SM leave latency
+        // exposed
+        float t[16];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          if (e < cnt) {
-            const float ex = exp2f((f[e] - nm) * LOG2E_R);
-            ct += ex;
-            if (n + e < a.contact_bins) cs += ex;
-          }
+        for (int e = 0; e < 16; ++e) t[e] = e < cnt ? f[e] : -INFINITY;
+#pragma unroll
+        for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+          for (int e = 0; e < w; ++e) t[e] = fmaxf(t[e], t[e + w]);
+        const float nm = fmaxf(mx, t[0]);
+        const float scale = ex2_approx((mx - nm) * LOG2E_R);  // 0 on the first chunk (mx = -inf)
+        float ex[16], es[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          ex[e] = e < cnt ? ex2_approx((f[e] - nm) * LOG2E_R) : 0.f;
+          es[e] = n + e < a.contact_bins ? ex[e] : 0.f;
         }
-        tot = fmaf(tot, scale, ct);
-        sel = fmaf(sel, scale, cs);
+#pragma unroll
+        for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+          for (int e = 0; e < w; ++e) {
+            ex[e] += ex[e + w];
+            es[e] += es[e + w];
+          }
+        tot = fmaf(tot, scale, ex[0]);
+        sel = fmaf(sel, scale, es[0]);
         mx = nm;
       }
     }
