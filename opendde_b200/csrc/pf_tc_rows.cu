@@ -140,53 +140,77 @@ __global__ void __launch_bounds__(256) k_ln_pos(const __nv_bfloat16* __restrict_
   }
 }
 
-// out[(i*n_j + j)*c + ch] = LN over ch of x[(ch*n_i + i)*ld + j]. One CTA of 128 threads per
-// (i, 128 j); the tile is staged in shared memory ([ch][128] bf16) by coalesced loads.
-__global__ void __launch_bounds__(128) k_ln_cmajor(const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t n_i,
+// out[(i*n_j + j)*c + ch] = LN over ch of x[(ch*n_i + i)*ld + j]. One CTA of 256 threads per
+// (i, 64 j): the [ch][64] bf16 tile is loaded into shared memory one 128-byte channel row per
+// warp instruction, then four threads per position each sum a quarter of the channels; the four
+// partial sums (then the four partial squared deviations) are combined through shared memory. A thread per position over all c channels (the previous form) left a c-long dependent
+// chain and, with c * 256 B of shared memory per 128 positions, two CTAs per SM at c = 384.
+constexpr int CM_J = 64;
+__global__ void __launch_bounds__(256) k_ln_cmajor(const __nv_bfloat16* __restrict__ x, int64_t ld, int64_t n_i,
                                                    int64_t n_j, int c, const float* __restrict__ gamma,
                                                    const float* __restrict__ beta, __nv_bfloat16* __restrict__ out) {
-  extern __shared__ __nv_bfloat16 tile[];
-  const int64_t tpr = (n_j + 127) / 128;
+  extern __shared__ __nv_bfloat16 tile[];  // [c][CM_J]
+  __shared__ float red[2][4][CM_J];
+  const int64_t tpr = (n_j + CM_J - 1) / CM_J;
   const int64_t i = blockIdx.x / tpr;
-  const int64_t j = (blockIdx.x % tpr) * 128 + threadIdx.x;
-  const bool live = j < n_j;
-  const int t = threadIdx.x;
-  float sum = 0.f;
-  const __nv_bfloat16* src = x + i * ld + (live ? j : 0);
+  const int64_t j0 = (blockIdx.x % tpr) * CM_J;
   const int64_t plane = n_i * ld;
+  {
+    // load: warp w takes channels w, w + 8, ...; lane l the positions j0 + 2l, j0 + 2l + 1 (one
+    // 128-byte row of a channel per warp instruction, bf16 pairs; ld and j0 are even)
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    const int64_t jj = j0 + 2 * l;
+    const __nv_bfloat16* src = x + i * ld + jj;
+    uint32_t* t32 = reinterpret_cast<uint32_t*>(tile);
+    if (jj + 1 < n_j) {
 #pragma unroll 8
-  for (int ch = 0; ch < c; ++ch) {
-    const __nv_bfloat16 v = live ? src[ch * plane] : __float2bfloat16_rn(0.f);
-    tile[ch * 128 + t] = v;
-    sum += __bfloat162float(v);
-  }
-  if (!live) return;  // no block-wide barrier follows: each thread reads only its own column
-  const float mean = sum / (float)c;
-  float sq = 0.f;
-  for (int ch = 0; ch < c; ++ch) {
-    const float d = __bfloat162float(tile[ch * 128 + t]) - mean;
-    sq = fmaf(d, d, sq);
-  }
-  const float rstd = rsqrtf(sq / (float)c + 1e-5f);
-  __nv_bfloat16* dst = out + (i * n_j + j) * c;
-  for (int ch0 = 0; ch0 < c; ch0 += 8) {
-    uint32_t o4[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const int ch = ch0 + e * 2;
-      float y0 = (__bfloat162float(tile[ch * 128 + t]) - mean) * rstd;
-      float y1 = (__bfloat162float(tile[(ch + 1) * 128 + t]) - mean) * rstd;
-      if (gamma) {
-        y0 *= gamma[ch];
-        y1 *= gamma[ch + 1];
+      for (int ch = w; ch < c; ch += 8) t32[ch * (CM_J / 2) + l] = *reinterpret_cast<const uint32_t*>(src + ch * plane);
+    } else {
+      for (int ch = w; ch < c; ch += 8) {
+        const uint32_t lo = jj < n_j ? (uint32_t)__bfloat16_as_ushort(src[ch * plane]) : 0u;
+        t32[ch * (CM_J / 2) + l] = lo;
       }
-      if (beta) {
-        y0 += beta[ch];
-        y1 += beta[ch + 1];
-      }
-      o4[e] = pack_bf16(y0, y1);
     }
-    *reinterpret_cast<uint4*>(dst + ch0) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+  }
+  __syncthreads();
+  const int jl = threadIdx.x & (CM_J - 1), part = threadIdx.x >> 6;
+  const int64_t j = j0 + jl;
+  const bool live = j < n_j;
+  const int cq = c >> 2, ch0 = part * cq;
+  float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int k = 0; k < cq; ++k) s4[k & 3] += __bfloat162float(tile[(ch0 + k) * CM_J + jl]);
+  red[0][part][jl] = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+  __syncthreads();
+  const float mean = ((red[0][0][jl] + red[0][1][jl]) + (red[0][2][jl] + red[0][3][jl])) / (float)c;
+  float q4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+  for (int k = 0; k < cq; ++k) {
+    const float d = __bfloat162float(tile[(ch0 + k) * CM_J + jl]) - mean;
+    q4[k & 3] = fmaf(d, d, q4[k & 3]);
+  }
+  red[1][part][jl] = (q4[0] + q4[1]) + (q4[2] + q4[3]);
+  __syncthreads();
+  if (!live) return;  // no barrier follows
+  const float var = ((red[1][0][jl] + red[1][1][jl]) + (red[1][2][jl] + red[1][3][jl])) / (float)c;
+  const float rstd = rsqrtf(var + 1e-5f);
+  __nv_bfloat16* dst = out + (i * n_j + j) * c + ch0;
+  auto y_of = [&](int ch) {
+    float y = (__bfloat162float(tile[ch * CM_J + jl]) - mean) * rstd;
+    if (gamma) y *= gamma[ch];
+    if (beta) y += beta[ch];
+    return y;
+  };
+  if ((cq & 7) == 0) {  // 16-byte stores (the part's start is 16-byte aligned)
+    for (int k = 0; k < cq; k += 8) {
+      uint32_t o4[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) o4[e] = pack_bf16(y_of(ch0 + k + 2 * e), y_of(ch0 + k + 2 * e + 1));
+      *reinterpret_cast<uint4*>(dst + k) = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    }
+  } else {  // c % 8 == 0 makes cq even: 4-byte stores
+    for (int k = 0; k < cq; k += 2)
+      *reinterpret_cast<uint32_t*>(dst + k) = pack_bf16(y_of(ch0 + k), y_of(ch0 + k + 1));
   }
 }
 
@@ -772,7 +796,7 @@ int set_smem(K kernel, uint32_t bytes) {
   return PF_OK;
 }
 
-constexpr int CM_MAX_C = 768;  // k_ln_cmajor: c * 256 B of shared memory
+constexpr int CM_MAX_C = 768;  // k_ln_cmajor: c * 2 * CM_J B of shared memory
 
 int ensure_attrs() {
   static std::atomic<unsigned long long> done{0};
@@ -787,7 +811,7 @@ int ensure_attrs() {
     PF_TRY(set_smem(k_rowgemm<E_OPMAB, A_ROWS>, R_SMEM + 1024));
     PF_TRY(set_smem(k_rowgemm<E_RESID, A_OUTER>, R_SMEM + 1024));
     PF_TRY(set_smem(k_rowgemm<E_HEAD, A_ROWS>, R_SMEM + 1024));
-    PF_TRY(set_smem(k_ln_cmajor, CM_MAX_C * 128 * 2));
+    PF_TRY(set_smem(k_ln_cmajor, CM_MAX_C * CM_J * 2));
     return PF_OK;
   });
 }
@@ -847,10 +871,10 @@ int ln_cmajor(const __nv_bfloat16* x, int64_t ld, int64_t n_i, int64_t n_j, int 
   if (n_i * n_j == 0) return PF_OK;
   if (c > CM_MAX_C || c % 8) return fail(PF_EUNSUPPORTED, "LayerNorm over %d channel-major channels", c);
   PF_TRY(ensure_attrs());
-  const int64_t blocks = n_i * ((n_j + 127) / 128);
+  const int64_t blocks = n_i * ((n_j + CM_J - 1) / CM_J);
   if (blocks > 0x7fffffffll) return fail(PF_EUNSUPPORTED, "LayerNorm grid too large");
   PF_LAUNCH_SCOPE_WORK(st, "k_ln_cmajor", 4.0 * (double)n_i * n_j * c, 'b');
-  k_ln_cmajor<<<(unsigned)blocks, 128, (size_t)c * 128 * 2, st>>>(x, ld, n_i, n_j, c, g, b, out);
+  k_ln_cmajor<<<(unsigned)blocks, 256, (size_t)c * CM_J * 2, st>>>(x, ld, n_i, n_j, c, g, b, out);
   PF_CHECK_LAUNCH();
   return PF_OK;
 }
