@@ -135,24 +135,33 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
     }
   } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issuer
-    // Order per chunk hc: ab(t, hc) for each tile, then out(t, hc) for each tile, so one
-    // tile's ab MMAs run while the other tile's warpgroup is busy with its silu.
+    // Per chunk hc and tile t: ab(t, hc + 1) as soon as t's warpgroup has read ab(t, hc) out of
+    // TMEM, then out(t, hc) once it has written h(t, hc): the next chunk's ab MMAs run while the
+    // warpgroup is still turning the current chunk into h, and the other tile's work fills the
+    // rest.
     if (lane == 0) {
       constexpr uint32_t id_ab = idesc_f16(128, 128, true);
       constexpr uint32_t id_o = idesc_f16(128, 128, true);
       bool ok = true;
       for (int t = 0; t < ntile; ++t) ok = mbar_wait(b_ln(t), 0, a.status) && ok;  // LN(x) in smem
+      ok = mbar_wait(b_wf(0), 0, a.status) && ok;
+      for (int t = 0; t < ntile; ++t) {
+        tc_fence_after();
+        tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, base + S_W, 16384, id_ab);
+        umma_commit(b_abf(t));
+      }
       for (int hc = 0; hc < NCHUNK; ++hc) {
-        const int s = hc & 1;
-        const uint32_t w = base + S_W + s * S_W_SLOT;
-        ok = mbar_wait(b_wf(s), (hc >> 1) & 1, a.status) && ok;
+        const int s = hc & 1, s1 = (hc + 1) & 1;
+        const uint32_t w = base + S_W + s * S_W_SLOT, w1 = base + S_W + s1 * S_W_SLOT;
+        const bool next = hc + 1 < NCHUNK;
+        if (next) ok = mbar_wait(b_wf(s1), ((hc + 1) >> 1) & 1, a.status) && ok;
         for (int t = 0; t < ntile; ++t) {
-          if (hc > 0) ok = mbar_wait(b_abe(t), (hc - 1) & 1, a.status) && ok;  // D_ab read out
-          tc_fence_after();
-          tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, w, 16384, id_ab);
-          umma_commit(b_abf(t));
-        }
-        for (int t = 0; t < ntile; ++t) {
+          if (next) {
+            ok = mbar_wait(b_abe(t), hc & 1, a.status) && ok;  // ab(t, hc) read out
+            tc_fence_after();
+            tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, w1, 16384, id_ab);
+            umma_commit(b_abf(t));
+          }
           ok = mbar_wait(b_hf(t), hc & 1, a.status) && ok;
           tc_fence_after();
           const uint32_t hb = base + S_H + t * 16384, wo = w + 32768;
@@ -162,7 +171,7 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
                      id_o, (hc > 0 || kk > 0) ? 1u : 0u);
           umma_commit(b_he(t));  // h buffer of tile t free when this MMA finishes
         }
-        umma_commit(b_we(s));  // weight slot s free (its ab and out MMAs are done)
+        umma_commit(b_we(s));  // weight slot s free (chunk hc's ab and out MMAs are done)
       }
       for (int t = 0; t < ntile; ++t) umma_commit(b_out(t));
       umma_commit(b_drain);  // drain: every MMA complete before TMEM is released
