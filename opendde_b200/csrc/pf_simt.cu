@@ -423,11 +423,17 @@ __global__ void __launch_bounds__(64) k_attn_split(const float* __restrict__ q, 
                                                    int64_t kv_ps, const float* __restrict__ bias, int64_t b_hs,
                                                    int64_t b_rs, int64_t n_q, int64_t n_keys, int64_t per_split,
                                                    float inv_sqrt_d_div, int H, float* __restrict__ part) {
-  __shared__ float Ks[64][D + 1];
-  __shared__ float Vs[64][D + 1];
+  // 32-key tiles: K, V and the 64 queries' bias rows of the tile staged in shared memory (the
+  // bias by 128-byte rows, consecutive keys on consecutive threads), then per query all 32 logits
+  // at once, one running-max update per tile, the exponentials and the P.V accumulation.
+  constexpr int KT = 32;
+  __shared__ float Ks[KT][D + 1];
+  __shared__ float Vs[KT][D + 1];
+  __shared__ float Bs[64][KT + 1];
   const int h = blockIdx.y;
   const int64_t sp = blockIdx.z;
-  const int64_t j = (int64_t)blockIdx.x * 64 + threadIdx.x;
+  const int64_t j0 = (int64_t)blockIdx.x * 64;
+  const int64_t j = j0 + threadIdx.x;
   const bool active = j < n_q;
   float qv[D];
   const float* qp = q + (active ? j : 0) * q_ps + h * D;
@@ -441,39 +447,56 @@ __global__ void __launch_bounds__(64) k_attn_split(const float* __restrict__ q, 
   const int64_t kb1 = kb0 + per_split < n_keys ? kb0 + per_split : n_keys;
   const float* kb = k + h * D;
   const float* vb = v + h * D;
-  for (int64_t k0 = kb0; k0 < kb1; k0 += 64) {
+  const int tk = threadIdx.x & (KT - 1), half = threadIdx.x >> 5;
+  for (int64_t k0 = kb0; k0 < kb1; k0 += KT) {
     __syncthreads();
     {
-      const int64_t kk = k0 + threadIdx.x;
-      if (kk < kb1) {
+      // K and V of the tile: consecutive threads take consecutive floats of each key's D values
 #pragma unroll
-        for (int t = 0; t < D; ++t) {
-          Ks[threadIdx.x][t] = kb[kk * kv_ps + t];
-          Vs[threadIdx.x][t] = vb[kk * kv_ps + t];
-        }
+      for (int idx = threadIdx.x; idx < KT * D; idx += 64) {
+        const int kt = idx / D, t = idx - kt * D;
+        const int64_t kr = k0 + kt;
+        Ks[kt][t] = kr < kb1 ? kb[kr * kv_ps + t] : 0.f;
+        Vs[kt][t] = kr < kb1 ? vb[kr * kv_ps + t] : 0.f;
       }
+      const int64_t kk = k0 + tk;
+      const float* bcol = bias + (int64_t)h * b_hs + k0 + tk;
+      for (int qq = half; qq < 64; qq += 2)
+        Bs[qq][tk] = (kk < kb1 && j0 + qq < n_q) ? bcol[(j0 + qq) * b_rs] : 0.f;
     }
     __syncthreads();
     if (!active) continue;
     const int64_t rem = kb1 - k0;
-    const int nk = rem < 64 ? (int)rem : 64;
-    const float* brow = bias + (int64_t)h * b_hs + j * b_rs + k0;
-    for (int t = 0; t < nk; ++t) {
-      float s = 0.f;
+    const int nk = rem < KT ? (int)rem : KT;
+    float sc[KT];
+    float tmax = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < D; ++e) s = fmaf(qv[e], Ks[t][e], s);
-      s = s + brow[t];
-      if (s > mrun) {
-        const float corr = expf(mrun - s);  // exp(-inf) = 0 on the first key
-        l *= corr;
+    for (int t = 0; t < KT; ++t) {
+      float s = -INFINITY;
+      if (t < nk) {
+        float d0 = 0.f;
 #pragma unroll
-        for (int e = 0; e < D; ++e) acc[e] *= corr;
-        mrun = s;
+        for (int e = 0; e < D; ++e) d0 = fmaf(qv[e], Ks[t][e], d0);
+        s = d0 + Bs[threadIdx.x][t];
       }
-      const float pexp = expf(s - mrun);
-      l += pexp;
+      sc[t] = s;
+      tmax = fmaxf(tmax, s);
+    }
+    if (tmax > mrun) {
+      const float corr = expf(mrun - tmax);  // exp(-inf) = 0 on the first tile
+      l *= corr;
 #pragma unroll
-      for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[t][e], acc[e]);
+      for (int e = 0; e < D; ++e) acc[e] *= corr;
+      mrun = tmax;
+    }
+#pragma unroll
+    for (int t = 0; t < KT; ++t) {
+      if (t < nk) {
+        const float pexp = expf(sc[t] - mrun);
+        l += pexp;
+#pragma unroll
+        for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[t][e], acc[e]);
+      }
     }
   }
   if (!active) return;
