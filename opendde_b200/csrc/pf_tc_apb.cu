@@ -8,6 +8,7 @@
 #include "pf_prof.h"
 #include "pf_sm100.cuh"
 #include "pf_tc.h"
+#include "pf_tile_common.cuh"
 #include "pf_tmap.h"
 
 namespace pf {
@@ -17,7 +18,9 @@ using namespace sm100;
 namespace {
 
 constexpr int C = 128, HB = 16, TILE = 128;
-constexpr uint32_t APB_SMEM = 32768 + 4096 + 64;
+// z tile 32 KB, W 4 KB, LayerNorm parameters 1 KB, barriers and the TMEM slot
+constexpr uint32_t S_LNP = 36864, S_BAR = S_LNP + 1024;
+constexpr uint32_t APB_SMEM = S_BAR + 64;
 
 struct ApbArgs {
   int64_t n_rows, n_cols, tiles_per_row;
@@ -27,14 +30,17 @@ struct ApbArgs {
   unsigned int* status;
 };
 
-__global__ void __launch_bounds__(128) k_apb_bias(const __grid_constant__ CUtensorMap tz,
-                                                  const __grid_constant__ CUtensorMap tw, const ApbArgs a) {
+// The row is held as 64 registers of bf16 pairs (the tile helpers of the fused kernels), so that
+// four CTAs fit per SM and their TMA loads, LayerNorms and stores overlap.
+__global__ void __launch_bounds__(128, 3) k_apb_bias(const __grid_constant__ CUtensorMap tz,
+                                                     const __grid_constant__ CUtensorMap tw, const ApbArgs a) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
-  const uint32_t sA = base, sB = base + 32768, bar_load = base + 36864, bar_mma = bar_load + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + 36864 + 16);
+  const uint32_t sA = base, sB = base + 32768, bar_load = base + S_BAR, bar_mma = bar_load + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + S_BAR + 16);
+  float* lnp = reinterpret_cast<float*>(g + S_LNP);
   const int tid = threadIdx.x, warp = tid >> 5;
   const int64_t t = blockIdx.x;
   const int64_t r = t / a.tiles_per_row;
@@ -44,6 +50,8 @@ __global__ void __launch_bounds__(128) k_apb_bias(const __grid_constant__ CUtens
     mbar_init(bar_mma, 1);
     fence_barrier_init();
   }
+  lnp[tid] = a.ln_w ? a.ln_w[tid] : 1.f;
+  lnp[C + tid] = a.ln_b ? a.ln_b[tid] : 0.f;
   if (warp == 0) {
     tmem_alloc(smem_u32(tmem_slot), 32);
     tmem_relinquish();
@@ -61,42 +69,11 @@ __global__ void __launch_bounds__(128) k_apb_bias(const __grid_constant__ CUtens
   }
   mbar_wait(bar_load, 0, a.status);
   {
-    float v[C];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint4 q = *reinterpret_cast<const uint4*>(g + (j >> 3) * 16384 + sw128_off(tid, j & 7));
-      v[j * 8 + 0] = bf16lo(q.x); v[j * 8 + 1] = bf16hi(q.x);
-      v[j * 8 + 2] = bf16lo(q.y); v[j * 8 + 3] = bf16hi(q.y);
-      v[j * 8 + 4] = bf16lo(q.z); v[j * 8 + 5] = bf16hi(q.z);
-      v[j * 8 + 6] = bf16lo(q.w); v[j * 8 + 7] = bf16hi(q.w);
-    }
-    float sm = 0.f;
-#pragma unroll
-    for (int c = 0; c < C; ++c) sm += v[c];
-    const float mean = sm * (1.0f / C);
-    float sq = 0.f;
-#pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const float d = v[c] - mean;
-      sq += d * d;
-    }
-    const float rstd = rsqrtf(sq * (1.0f / C) + 1e-5f);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      float y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const int c = j * 8 + e;
-        float val = (v[c] - mean) * rstd;
-        if (a.ln_w) val *= __ldg(a.ln_w + c);
-        if (a.ln_b) val += __ldg(a.ln_b + c);
-        y[e] = val;
-      }
-      uint4 q;
-      q.x = pack_bf16(y[0], y[1]); q.y = pack_bf16(y[2], y[3]);
-      q.z = pack_bf16(y[4], y[5]); q.w = pack_bf16(y[6], y[7]);
-      *reinterpret_cast<uint4*>(g + (j >> 3) * 16384 + sw128_off(tid, j & 7)) = q;
-    }
+    uint32_t zr[64];
+    float m, rs;
+    tile::load_row(g, tid, zr);
+    tile::row_stats(zr, 1e-5f, m, rs);
+    tile::store_norm_row(g, tid, zr, m, rs, lnp, lnp + C);
   }
   fence_proxy_async_smem();
   __syncthreads();
