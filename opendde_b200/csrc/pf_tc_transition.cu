@@ -8,7 +8,8 @@
 //   h(chunk)        = silu(a) * b  -> bf16 -> shared memory (SW128 K-major)
 //   out            += h(chunk) W_o(:, chunk)^T             UMMA 128x128x64  -> TMEM
 // Warps 0-3 / 4-7: tile A / tile B (thread = row): LayerNorm prologue, silu per chunk, final
-// residual epilogue (TMA store). Warp 8: TMA producer (x tiles, weight-chunk ring of 2 slots).
+// residual epilogue (TMA store). Warp 8: TMA producer (x tiles; the [W_a;W_b] chunks in a ring
+// of 3 slots, the W_o chunks in a ring of 2).
 // Warp 9: MMA issuer. While one warpgroup turns a chunk into h, the tensor core works on the
 // other tile, so the SiLU and the MMAs overlap.
 // Reference: opendde/model/modules/primitives.py:182-217.
@@ -29,13 +30,19 @@ namespace {
 constexpr int C = 128, HID = 512, CHUNK = 64, NCHUNK = HID / CHUNK, TILE = 128;
 
 // shared memory (offsets from the 1 KB aligned base)
-constexpr uint32_t S_X = 0;                   // 2 tiles x 32 KB: x, LN(x) in place, then the output tile
-constexpr uint32_t S_W = 65536;               // 2 slots x 48 KB: [W_a;W_b] 2 atoms x 128 rows (32 KB) + W_o 128 rows x 128 B (16 KB)
-constexpr uint32_t S_W_SLOT = 49152;
-constexpr uint32_t S_H = S_W + 2 * S_W_SLOT;  // 2 tiles x 16 KB: h 128 rows x 64 (128 B)
-constexpr uint32_t S_LN = S_H + 2 * 16384;    // LayerNorm weight and bias (fp32)
+// Two weight rings: [W_a;W_b] of a chunk (2 atoms x 128 rows, 32 KB) three deep, W_o of a chunk
+// (128 rows x 128 B, 16 KB) two deep, so that a chunk's [W_a;W_b] is in flight while the two
+// chunks before it are still in use (one 48 KB slot pair per chunk, two deep, put the next chunk's
+// L2 load on the path of every chunk).
+constexpr int NWAB = 3, NWO = 2;
+constexpr uint32_t S_X = 0;                          // 2 tiles x 32 KB: x, LN(x) in place, then the output tile
+constexpr uint32_t S_WAB = 65536, WAB_SLOT = 32768;
+constexpr uint32_t S_WO = S_WAB + NWAB * WAB_SLOT, WO_SLOT = 16384;
+constexpr uint32_t S_H = S_WO + NWO * WO_SLOT;       // 2 tiles x 16 KB: h 128 rows x 64 (128 B)
+constexpr uint32_t S_LN = S_H + 2 * 16384;           // LayerNorm weight and bias (fp32)
 constexpr uint32_t S_BAR = S_LN + 1024;
 constexpr uint32_t TR_SMEM = S_BAR + 256;
+static_assert(TR_SMEM + 1024 <= 232448, "transition shared memory");
 
 struct TrArgs {
   int64_t rows;
@@ -74,10 +81,12 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
   auto b_hf = [&](int t) { return bars + 64 + 8 * t; };
   auto b_he = [&](int t) { return bars + 80 + 8 * t; };
   auto b_out = [&](int t) { return bars + 96 + 8 * t; };
-  auto b_wf = [&](int s) { return bars + 112 + 8 * s; };
-  auto b_we = [&](int s) { return bars + 128 + 8 * s; };
-  const uint32_t b_drain = bars + 144;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + S_BAR + 192);
+  auto b_abw_f = [&](int s) { return bars + 112 + 8 * s; };  // [W_a;W_b] slot full / empty
+  auto b_abw_e = [&](int s) { return bars + 136 + 8 * s; };
+  auto b_ow_f = [&](int s) { return bars + 160 + 8 * s; };   // W_o slot full / empty
+  auto b_ow_e = [&](int s) { return bars + 176 + 8 * s; };
+  const uint32_t b_drain = bars + 192;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g + S_BAR + 224);
   float* lnp = reinterpret_cast<float*>(g + S_LN);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t r0 = (int64_t)blockIdx.x * (2 * TILE);
@@ -93,8 +102,14 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
       mbar_init(b_hf(t), 4);
       mbar_init(b_he(t), 1);
       mbar_init(b_out(t), 1);
-      mbar_init(b_wf(t), 1);
-      mbar_init(b_we(t), 1);
+    }
+    for (int k = 0; k < NWAB; ++k) {
+      mbar_init(b_abw_f(k), 1);
+      mbar_init(b_abw_e(k), 1);
+    }
+    for (int k = 0; k < NWO; ++k) {
+      mbar_init(b_ow_f(k), 1);
+      mbar_init(b_ow_e(k), 1);
     }
     mbar_init(b_drain, 1);
     fence_barrier_init();
@@ -121,16 +136,19 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
         tma_load_2d(base + S_X + t * 32768 + 16384, &tx, b_x(t), 64, (int)(r0 + t * TILE));
       }
       for (int hc = 0; hc < NCHUNK; ++hc) {
-        const int s = hc & 1;
-        if (hc >= 2 && !mbar_wait(b_we(s), ((hc - 2) >> 1) & 1, a.status)) break;
-        const uint32_t w = base + S_W + s * S_W_SLOT;
-        mbar_arrive_expect_tx(b_wf(s), S_W_SLOT);
+        const int sa = hc % NWAB, na = hc / NWAB;  // slot, and its use number
+        if (na > 0 && !mbar_wait(b_abw_e(sa), (na - 1) & 1, a.status)) break;
+        const uint32_t w = base + S_WAB + sa * WAB_SLOT;
+        mbar_arrive_expect_tx(b_abw_f(sa), WAB_SLOT);
         // atom k (K 64k..64k+63): rows 0..63 = W_a chunk, rows 64..127 = W_b chunk
-        tma_load_2d(w, &twa, b_wf(s), 0, hc * CHUNK);
-        tma_load_2d(w + 8192, &twb, b_wf(s), 0, hc * CHUNK);
-        tma_load_2d(w + 16384, &twa, b_wf(s), 64, hc * CHUNK);
-        tma_load_2d(w + 16384 + 8192, &twb, b_wf(s), 64, hc * CHUNK);
-        tma_load_2d(w + 32768, &two, b_wf(s), hc * CHUNK, 0);  // W_o[:, chunk] 128 rows x 64
+        tma_load_2d(w, &twa, b_abw_f(sa), 0, hc * CHUNK);
+        tma_load_2d(w + 8192, &twb, b_abw_f(sa), 0, hc * CHUNK);
+        tma_load_2d(w + 16384, &twa, b_abw_f(sa), 64, hc * CHUNK);
+        tma_load_2d(w + 16384 + 8192, &twb, b_abw_f(sa), 64, hc * CHUNK);
+        const int so = hc % NWO, no = hc / NWO;
+        if (no > 0 && !mbar_wait(b_ow_e(so), (no - 1) & 1, a.status)) break;
+        mbar_arrive_expect_tx(b_ow_f(so), WO_SLOT);
+        tma_load_2d(base + S_WO + so * WO_SLOT, &two, b_ow_f(so), hc * CHUNK, 0);  // W_o[:, chunk] 128 x 64
       }
     }
   } else if (warp == 9) {
@@ -144,17 +162,19 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
       constexpr uint32_t id_o = idesc_f16(128, 128, true);
       bool ok = true;
       for (int t = 0; t < ntile; ++t) ok = mbar_wait(b_ln(t), 0, a.status) && ok;  // LN(x) in smem
-      ok = mbar_wait(b_wf(0), 0, a.status) && ok;
+      ok = mbar_wait(b_abw_f(0), 0, a.status) && ok;
       for (int t = 0; t < ntile; ++t) {
         tc_fence_after();
-        tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, base + S_W, 16384, id_ab);
+        tile::umma_k128(tmem + 256 * t, base + S_X + t * 32768, base + S_WAB, 16384, id_ab);
         umma_commit(b_abf(t));
       }
+      umma_commit(b_abw_e(0));  // [W_a;W_b] of chunk 0 free once both tiles' ab MMAs are done
       for (int hc = 0; hc < NCHUNK; ++hc) {
-        const int s = hc & 1, s1 = (hc + 1) & 1;
-        const uint32_t w = base + S_W + s * S_W_SLOT, w1 = base + S_W + s1 * S_W_SLOT;
+        const int s1 = (hc + 1) % NWAB, so = hc % NWO;
+        const uint32_t w1 = base + S_WAB + s1 * WAB_SLOT, wo = base + S_WO + so * WO_SLOT;
         const bool next = hc + 1 < NCHUNK;
-        if (next) ok = mbar_wait(b_wf(s1), ((hc + 1) >> 1) & 1, a.status) && ok;
+        if (next) ok = mbar_wait(b_abw_f(s1), ((hc + 1) / NWAB) & 1, a.status) && ok;
+        ok = mbar_wait(b_ow_f(so), (hc / NWO) & 1, a.status) && ok;
         for (int t = 0; t < ntile; ++t) {
           if (next) {
             ok = mbar_wait(b_abe(t), hc & 1, a.status) && ok;  // ab(t, hc) read out
@@ -164,14 +184,15 @@ __global__ void __launch_bounds__(320, 1) k_transition(const __grid_constant__ C
           }
           ok = mbar_wait(b_hf(t), hc & 1, a.status) && ok;
           tc_fence_after();
-          const uint32_t hb = base + S_H + t * 16384, wo = w + 32768;
+          const uint32_t hb = base + S_H + t * 16384;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             umma_f16(tmem + 256 * t + 128, sdesc(hb + kk * 32, 1024, SWZ_128B), sdesc(wo + kk * 32, 1024, SWZ_128B),
                      id_o, (hc > 0 || kk > 0) ? 1u : 0u);
           umma_commit(b_he(t));  // h buffer of tile t free when this MMA finishes
         }
-        umma_commit(b_we(s));  // weight slot s free (chunk hc's ab and out MMAs are done)
+        if (next) umma_commit(b_abw_e(s1));  // [W_a;W_b] of chunk hc + 1 free after its ab MMAs
+        umma_commit(b_ow_e(so));             // W_o of chunk hc free after its out MMAs
       }
       for (int t = 0; t < ntile; ++t) umma_commit(b_out(t));
       umma_commit(b_drain);  // drain: every MMA complete before TMEM is released
