@@ -112,3 +112,28 @@ def test_bf16_tensor_core_path_vs_simt_path(kind, n, cuda_device):
     assert _abi.device_status(clear=True) == 0
     err = rel_l2(got_tc, got_simt)
     assert err <= 1e-2, f"{kind}: tc vs simt rel-L2 {err:.3e}"
+
+
+@pytest.mark.parametrize("reserve", [0, 64])
+def test_bf16_transition_persistent_pairs(reserve, cuda_device):
+    """The persistent transition walks several 256-row pairs per CTA (299^2 rows = 349 pairs +
+    57 rows: ~2.4 pairs per CTA on 148 SMs, ~4.2 with 64 SMs reserved) and ends on a one-tile
+    pair: bit-identical to the run on every SM, and within the bf16 bar of the SIMT path."""
+    mod, params, s, z, mask = _case("transition", 299)
+    mod = cuda_module(mod, params, cuda_device)
+    base = cuda_op("transition", mod, s, z, mask, cuda_device, torch.bfloat16)
+    _abi.set_sm_reserve(reserve)
+    try:
+        got = cuda_op("transition", mod, s, z, mask, cuda_device, torch.bfloat16)
+        assert _abi.last_path() == "tc"
+    finally:
+        _abi.set_sm_reserve(0)
+    assert _abi.device_status(clear=True) == 0
+    assert torch.equal(got, base)
+    _abi.set_force_simt(True)
+    try:
+        want = cuda_op("transition", mod, s, z, mask, cuda_device, torch.bfloat16)
+    finally:
+        _abi.set_force_simt(False)
+    err = rel_l2(got, want)
+    assert err <= 1e-2, f"transition tc vs simt rel-L2 {err:.3e}"
