@@ -314,7 +314,7 @@ __global__ void __launch_bounds__(352, 1) k_transition(const __grid_constant__ C
           const uint4 o = old[chunk];
           float u[8];
 #pragma unroll
-          for (int k = 0; k < 8; ++k) u[k] = __uint_as_float(ov[e * 8 + k]);
+          for (int v = 0; v < 8; ++v) u[v] = __uint_as_float(ov[e * 8 + v]);
           u[0] += bf16lo(o.x); u[1] += bf16hi(o.x); u[2] += bf16lo(o.y); u[3] += bf16hi(o.y);
           u[4] += bf16lo(o.z); u[5] += bf16hi(o.z); u[6] += bf16lo(o.w); u[7] += bf16hi(o.w);
           uint4 wv;
