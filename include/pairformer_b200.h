@@ -229,7 +229,8 @@ PF_API int pf_triatt_fwd(const pf_triatt_params* w, pf_pair_view zs, pf_mask_vie
 /* ---- Transition (LN -> SiLU(W_a y) * (W_b y) -> W_out) ------------------------------------
  * Replaces Transition.forward (opendde/model/modules/primitives.py:182-217) and the Fold-CP
  * distributed_pair_transition_update (real_pairformer.py:1405, local in inference).
- * x and out are [rows, c] with row strides x_stride/out_stride (elements); out may alias x.
+ * x and out are [rows, c] with row strides x_stride/out_stride (elements); out may be x itself
+ * (same pointer and stride: the in-place update) or disjoint from it, not partly overlapping.
  * out = (accumulate ? out : 0) + Transition(x). */
 typedef struct {
   const float* ln_w; const float* ln_b;   /* [c]        layernorm1        */
