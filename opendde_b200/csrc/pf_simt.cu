@@ -425,11 +425,16 @@ __global__ void __launch_bounds__(64) k_attn_split(const float* __restrict__ q, 
                                                    float inv_sqrt_d_div, int H, float* __restrict__ part) {
   // 32-key tiles: K, V and the 64 queries' bias rows of the tile staged in shared memory (the
   // bias by 128-byte rows, consecutive keys on consecutive threads), then per query all 32 logits
-  // at once, one running-max update per tile, the exponentials and the P.V accumulation.
+  // at once, one running-max update per tile, the exponentials and the P.V accumulation. The
+  // tiles are copied with cp.async (4-byte copies, zero-filled past the key range) into two
+  // buffers where both fit in the 48 KB of static shared memory, so the next tile's loads are in
+  // flight during the current tile's math; otherwise into one.
   constexpr int KT = 32;
-  __shared__ float Ks[KT][D + 1];
-  __shared__ float Vs[KT][D + 1];
-  __shared__ float Bs[64][KT + 1];
+  constexpr int TILE_BYTES = (2 * KT * (D + 1) + 64 * (KT + 1)) * 4;
+  constexpr int NB = 2 * TILE_BYTES <= 48 * 1024 ? 2 : 1;
+  __shared__ float Ks[NB][KT][D + 1];
+  __shared__ float Vs[NB][KT][D + 1];
+  __shared__ float Bs[NB][64][KT + 1];
   const int h = blockIdx.y;
   const int64_t sp = blockIdx.z;
   const int64_t j0 = (int64_t)blockIdx.x * 64;
@@ -447,57 +452,77 @@ __global__ void __launch_bounds__(64) k_attn_split(const float* __restrict__ q, 
   const int64_t kb1 = kb0 + per_split < n_keys ? kb0 + per_split : n_keys;
   const float* kb = k + h * D;
   const float* vb = v + h * D;
+  const float* bh = bias + (int64_t)h * b_hs;
   const int tk = threadIdx.x & (KT - 1), half = threadIdx.x >> 5;
-  for (int64_t k0 = kb0; k0 < kb1; k0 += KT) {
-    __syncthreads();
-    {
-      // K and V of the tile: consecutive threads take consecutive floats of each key's D values
+  // one 4-byte asynchronous copy; src_bytes = 0 writes a zero (the source is then not read)
+  auto cp4 = [](float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(valid ? 4 : 0)
+                 : "memory");
+  };
+  // copies of the tile starting at key kt0 into buffer b, as one commit group
+  auto prefetch = [&](int64_t kt0, int b) {
+    for (int idx = threadIdx.x; idx < KT * D; idx += 64) {
+      const int kt = idx / D, t = idx - kt * D;
+      const int64_t kr = kt0 + kt;
+      const bool ok = kr < kb1;
+      cp4(&Ks[b][kt][t], ok ? kb + kr * kv_ps + t : kb, ok);
+      cp4(&Vs[b][kt][t], ok ? vb + kr * kv_ps + t : vb, ok);
+    }
+    const int64_t kk = kt0 + tk;
+    for (int qq = half; qq < 64; qq += 2) {
+      const bool ok = kk < kb1 && j0 + qq < n_q;
+      cp4(&Bs[b][qq][tk], ok ? bh + (j0 + qq) * b_rs + kk : bh, ok);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (kb0 < kb1) prefetch(kb0, 0);
+  int it = 0;
+  for (int64_t k0 = kb0; k0 < kb1; k0 += KT, ++it) {
+    const int b = NB == 2 ? (it & 1) : 0;
+    if (NB == 1 && it > 0) prefetch(k0, 0);  // the trailing barrier freed the one buffer
+    if (NB == 2 && k0 + KT < kb1) {
+      prefetch(k0 + KT, b ^ 1);  // the other buffer: freed by the previous tile's trailing barrier
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();  // this tile's copies, from every thread, are in shared memory
+    if (active) {
+      const int64_t rem = kb1 - k0;
+      const int nk = rem < KT ? (int)rem : KT;
+      float sc[KT];
+      float tmax = -INFINITY;
 #pragma unroll
-      for (int idx = threadIdx.x; idx < KT * D; idx += 64) {
-        const int kt = idx / D, t = idx - kt * D;
-        const int64_t kr = k0 + kt;
-        Ks[kt][t] = kr < kb1 ? kb[kr * kv_ps + t] : 0.f;
-        Vs[kt][t] = kr < kb1 ? vb[kr * kv_ps + t] : 0.f;
+      for (int t = 0; t < KT; ++t) {
+        float s = -INFINITY;
+        if (t < nk) {
+          float d0 = 0.f;
+#pragma unroll
+          for (int e = 0; e < D; ++e) d0 = fmaf(qv[e], Ks[b][t][e], d0);
+          s = d0 + Bs[b][threadIdx.x][t];
+        }
+        sc[t] = s;
+        tmax = fmaxf(tmax, s);
       }
-      const int64_t kk = k0 + tk;
-      const float* bcol = bias + (int64_t)h * b_hs + k0 + tk;
-      for (int qq = half; qq < 64; qq += 2)
-        Bs[qq][tk] = (kk < kb1 && j0 + qq < n_q) ? bcol[(j0 + qq) * b_rs] : 0.f;
-    }
-    __syncthreads();
-    if (!active) continue;
-    const int64_t rem = kb1 - k0;
-    const int nk = rem < KT ? (int)rem : KT;
-    float sc[KT];
-    float tmax = -INFINITY;
+      if (tmax > mrun) {
+        const float corr = expf(mrun - tmax);  // exp(-inf) = 0 on the first tile
+        l *= corr;
 #pragma unroll
-    for (int t = 0; t < KT; ++t) {
-      float s = -INFINITY;
-      if (t < nk) {
-        float d0 = 0.f;
-#pragma unroll
-        for (int e = 0; e < D; ++e) d0 = fmaf(qv[e], Ks[t][e], d0);
-        s = d0 + Bs[threadIdx.x][t];
+        for (int e = 0; e < D; ++e) acc[e] *= corr;
+        mrun = tmax;
       }
-      sc[t] = s;
-      tmax = fmaxf(tmax, s);
-    }
-    if (tmax > mrun) {
-      const float corr = expf(mrun - tmax);  // exp(-inf) = 0 on the first tile
-      l *= corr;
 #pragma unroll
-      for (int e = 0; e < D; ++e) acc[e] *= corr;
-      mrun = tmax;
-    }
+      for (int t = 0; t < KT; ++t) {
+        if (t < nk) {
+          const float pexp = expf(sc[t] - mrun);
+          l += pexp;
 #pragma unroll
-    for (int t = 0; t < KT; ++t) {
-      if (t < nk) {
-        const float pexp = expf(sc[t] - mrun);
-        l += pexp;
-#pragma unroll
-        for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[t][e], acc[e]);
+          for (int e = 0; e < D; ++e) acc[e] = fmaf(pexp, Vs[b][t][e], acc[e]);
+        }
       }
     }
+    __syncthreads();  // every thread is done with buffer b before it is refilled
   }
   if (!active) return;
   float* out = part + ((sp * H + h) * n_q + j) * (D + 2);
